@@ -1,0 +1,242 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference.
+
+Run in a container that has the reference checkout (read-only) and
+``transformers``::
+
+    PYTHONPATH=<reference checkout> python tests/golden/make_golden.py
+
+Each fixture stores seeded inputs (or the seed that regenerates them) and the
+outputs of the reference's OWN functions, imported from the checkout:
+
+* ``yarn.pt``      transformers ``ROPE_INIT_FUNCTIONS['yarn']`` (Dream's rotary)
+* ``pool.pt``      ``ops/chunk_attn_pool_gqa_tilelang.py:17 _compact_pool_torch``
+* ``drop.pt``      ``dream_dllm_hils/kernel_utils.py:102 remote_drop_mask``
+* ``route.pt``     ``dream_dllm_hils/routing.py:52 route_topk_g7(training=False)``
+* ``weights.pt``   ``dream_dllm_hils/attention.py:126 _route_weights_torch``
+* ``selected.pt``  ``ops/hils_fwd_bwd_head.py:21 hils_torch_ref``
+* ``qcal.pt``      ``attention.py:41-63`` RoPE / inverse RoPE + ``qcal.py:22 rms_norm``
+* ``local_mask.pt`` ``dream_dllm_hils/local_attention.py:35-64`` K/V masking + window
+* ``layer.pt``     a whole route layer composed from the functions above (the
+  flash-attn local branch, GPU-only in the reference, comes from the oracle)
+
+The fixtures are consumed by ``tests/test_oracle_golden.py`` (CPU) and by the
+GPU parity tests; nothing at test time reads the reference checkout.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from oracle import route_layer as orc  # noqa: E402
+
+
+def _save(name, obj):
+    path = os.path.join(HERE, name)
+    torch.save(obj, path)
+    print(f"wrote {name}: {os.path.getsize(path) / 1024:.1f} KiB")
+
+
+def gen_yarn():
+    from transformers import Qwen2Config
+    from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+
+    cfg = Qwen2Config(
+        hidden_size=3584, num_attention_heads=28, num_key_value_heads=4,
+        max_position_embeddings=16384, rope_theta=1.0e6,
+        rope_scaling={"rope_type": "yarn", "factor": 8.0,
+                      "original_max_position_embeddings": 2048},
+    )
+    inv_freq, af = ROPE_INIT_FUNCTIONS["yarn"](cfg, "cpu")
+    _save("yarn.pt", {"inv_freq": inv_freq.float(), "attention_factor": float(af),
+                      "dim": 128, "base": 1.0e6, "factor": 8.0, "orig": 2048})
+
+
+def gen_pool():
+    from ops.chunk_attn_pool_gqa_tilelang import _compact_pool_torch
+
+    g = torch.Generator().manual_seed(11)
+    b, c, s, hkv, gg, d = 1, 6, 64, 2, 7, 128
+    mu = (torch.randn(b, c, hkv, gg, d, generator=g)).bfloat16()
+    k = (torch.randn(b, c, s, hkv, d, generator=g) / math.sqrt(d)).bfloat16()
+    valid = torch.ones(b, c, s, dtype=torch.bool)
+    valid[:, 1, ::5] = False          # ragged validity
+    valid[:, 3, :-1] = False          # chunk with only its landmark valid -> zeros
+    valid[:, 4, 0] = False            # first slot invalid
+    lmk, ent = _compact_pool_torch(mu, k, valid, 1.0 / math.sqrt(d))
+    _save("pool.pt", {"mu_q": mu, "k_chunked": k, "key_valid": valid, "lmk": lmk, "entropy": ent})
+
+
+def gen_drop():
+    from dream_dllm_hils.kernel_utils import remote_drop_mask
+
+    b, l = 2, 1024
+    valid = torch.ones(b, l, dtype=torch.bool)
+    valid[0, 128:191] = False          # chunk 2 of batch 0: only its landmark stays valid
+    valid[1, 640:] = False             # ragged tail in batch 1
+    out = {}
+    for w in (0, 63, 64, 256, 1280):
+        out[w] = remote_drop_mask(valid, w, 64).bool()
+    _save("drop.pt", {"key_valid": valid, "masks": out})
+
+
+def gen_route():
+    from dream_dllm_hils.routing import route_topk_g7
+
+    g = torch.Generator().manual_seed(74)
+    b, l, c, hkv, gg, d, topk = 1, 300, 40, 1, 7, 128, 32
+    q = torch.randn(b, l, hkv * gg, d, generator=g).bfloat16()
+    lmk = torch.randn(b, c, hkv, gg, d, generator=g).bfloat16()
+    lse = torch.randn(b, l, hkv, gg, generator=g)
+    bias = torch.randn(b, c, hkv, gg, generator=g)
+    drop = torch.zeros(b, l, c, dtype=torch.int32)
+    drop[:, ::11, 3] = 1
+    drop[:, 7, :20] = 1               # 20 available chunks -> 12 slots of -1
+    drop[:, 9, :] = 1                 # nothing routable
+    idx, sc = route_topk_g7(q, lmk, lse, bias, drop, topk, 64, 512, training=False)
+    _save("route.pt", {"q": q, "lmk": lmk, "local_lse": lse, "bias": bias, "drop": drop,
+                       "topk": topk, "indices": idx, "scores": sc})
+
+
+def gen_weights():
+    from dream_dllm_hils.attention import _route_weights_torch
+
+    r = torch.load(os.path.join(HERE, "route.pt"))
+    b, l, hq, k = r["scores"].shape
+    g = torch.Generator().manual_seed(5)
+    local_lse = torch.randn(b, l, hq, generator=g)
+    outs = {}
+    for off, sc in ((0.0, 1.0), (0.3, 1.7)):
+        rw, lw = _route_weights_torch(
+            r["scores"], r["indices"], r["bias"].contiguous(), local_lse, temperature=1.0,
+            gate_offset=torch.tensor(off), gate_scale=torch.tensor(sc))
+        outs[(off, sc)] = (rw, lw)
+    _save("weights.pt", {"local_lse": local_lse, "outs": outs})
+
+
+def gen_selected():
+    from ops.hils_fwd_bwd_head import hils_torch_ref
+
+    g = torch.Generator().manual_seed(79)
+    b, lq, lk, hkv, gg, d, topk, s = 1, 48, 1024, 1, 7, 128, 8, 64
+    q = torch.randn(b, lq, hkv * gg, d, generator=g).bfloat16()
+    k = torch.randn(b, lk, hkv, d, generator=g).bfloat16()
+    v = torch.randn(b, lk, hkv, d, generator=g).bfloat16()
+    c = lk // s
+    idx = torch.stack([torch.randperm(c, generator=g)[:topk].sort().values for _ in range(lq)])
+    idx = idx.view(b, lq, hkv, topk).to(torch.int32)
+    idx[:, 5, :, 5:] = -1
+    idx[:, 6] = -1
+    w = torch.softmax(torch.randn(b, lq, hkv * gg, topk, generator=g), -1).bfloat16()
+    out = hils_torch_ref(q, k, v, w, idx, chunk_size=s, sm_scale=d ** -0.5, block_q=1)
+    _save("selected.pt", {"q": q, "k": k, "v": v, "weights": w, "indices": idx, "out": out})
+
+
+def gen_qcal():
+    from dream_dllm_hils.attention import apply_rotary_pos_emb, invert_rotary_pos_emb
+    from dream_dllm_hils.qcal import rms_norm
+
+    yarn = torch.load(os.path.join(HERE, "yarn.pt"))
+    g = torch.Generator().manual_seed(3)
+    b, l, hq, d = 1, 128, 4, 128
+    pos = orc.landmark_position_ids(b, l)
+    cos, sin = orc.rope_cos_sin(pos, yarn["inv_freq"], yarn["attention_factor"], torch.bfloat16)
+    q = (torch.randn(b, l, hq, d, generator=g) / math.sqrt(d)).bfloat16()
+    delta = (torch.randn(b, l, hq, d, generator=g) * 0.05).bfloat16()
+    q_roped, _ = apply_rotary_pos_emb(q.transpose(1, 2), q.transpose(1, 2), cos, sin)
+    q_roped = q_roped.transpose(1, 2).contiguous()
+    unrot = invert_rotary_pos_emb(q_roped.transpose(1, 2), cos, sin).transpose(1, 2)
+    comb = rms_norm(unrot + delta, torch.ones(d), 1e-6)
+    rq, _ = apply_rotary_pos_emb(comb.transpose(1, 2), comb.transpose(1, 2), cos, sin)
+    _save("qcal.pt", {"q": q, "delta": delta, "position_ids": pos, "cos": cos, "sin": sin,
+                      "q_roped": q_roped, "unrot": unrot.contiguous(),
+                      "route_q": rq.transpose(1, 2).contiguous()})
+
+
+def gen_local_mask():
+    from dream_dllm_hils.local_attention import _apply_key_valid, _flash_window, _window_key_valid
+
+    g = torch.Generator().manual_seed(9)
+    b, l, hkv, d = 1, 256, 1, 8
+    k = torch.randn(b, l, hkv, d, generator=g).bfloat16()
+    v = torch.randn(b, l, hkv, d, generator=g).bfloat16()
+    valid = torch.ones(b, l, dtype=torch.bool)
+    valid[:, 100:110] = False
+    out = {}
+    for skip in (False, True):
+        vmask = _window_key_valid(valid, chunk_size=64, skip_inert_slots=skip)
+        mk, mv = _apply_key_valid(k, v, vmask)
+        out[skip] = {"valid": vmask, "k": mk, "v": mv, "window": _flash_window(256, skip, 64)}
+    _save("local_mask.pt", {"k": k, "v": v, "key_valid": valid, "out": out})
+
+
+def gen_layer():
+    """Whole route layer, composed from the reference's functions in the order
+    of ``attention.py:1358-1774`` (bf16 RoPE chain of the live path)."""
+    from dream_dllm_hils.attention import (
+        _route_weights_torch, apply_rotary_pos_emb, invert_rotary_pos_emb)
+    from dream_dllm_hils.kernel_utils import remote_drop_mask
+    from dream_dllm_hils.qcal import rms_norm
+    from dream_dllm_hils.routing import route_topk_g7
+    from ops.chunk_attn_pool_gqa_tilelang import _compact_pool_torch
+    from ops.hils_fwd_bwd_head import hils_torch_ref
+
+    cfg = orc.MRSAConfig(q_heads=7, kv_heads=1, rope_precision="bf16")
+    b, l, hidden, seed = 1, 1024, 512, 1234
+    inp = orc.make_route_layer_inputs(b, l, cfg, hidden=hidden, seed=seed)
+    yarn = torch.load(os.path.join(HERE, "yarn.pt"))
+    cos, sin = orc.rope_cos_sin(inp["position_ids"], yarn["inv_freq"], yarn["attention_factor"],
+                                torch.bfloat16)
+    qt, kt = apply_rotary_pos_emb(inp["q_pre"].transpose(1, 2), inp["k_pre"].transpose(1, 2), cos, sin)
+    q, k, v = qt.transpose(1, 2).contiguous(), kt.transpose(1, 2).contiguous(), inp["v"]
+    hq, hkv, d, chunk = 7, 1, 128, 64
+    c = l // chunk
+    valid = inp["key_valid"]
+    local_o, local_lse = orc.local_attention(q, k, v, valid, 256, chunk, True)
+    # Q-Cal (attention.py:458-503)
+    t = torch.nn.functional.linear(inp["hidden"], inp["w_in"])
+    delta = torch.nn.functional.linear(t, inp["w_out"]).view(b, l, hq, d)
+    unrot = invert_rotary_pos_emb(q.transpose(1, 2), cos, sin).transpose(1, 2)
+    comb = rms_norm(unrot + delta, inp["norm_weight"], 1e-6)
+    rqt, _ = apply_rotary_pos_emb(comb.transpose(1, 2), comb.transpose(1, 2), cos, sin)
+    route_q = rqt.transpose(1, 2).contiguous()
+    mu = route_q[:, chunk - 1::chunk].reshape(b, c, hkv, 7, d)
+    lmk, ent = _compact_pool_torch(mu, k.reshape(b, c, chunk, hkv, d), valid.reshape(b, c, chunk),
+                                   1.0 / math.sqrt(d))
+    prior = ent * inp["entropy_bias_scale"].view(1, 1, hkv, 7)
+    drop = remote_drop_mask(valid, 256, chunk)
+    idx, sc = route_topk_g7(route_q, lmk, local_lse.reshape(b, l, hkv, 7), prior.contiguous(), drop,
+                            32, chunk, 256, training=False)
+    rw, lw = _route_weights_torch(sc, idx, prior.contiguous(), local_lse.float().contiguous(),
+                                  temperature=1.0, gate_offset=torch.tensor(0.0),
+                                  gate_scale=torch.tensor(1.0))
+    remote = hils_torch_ref(q, k, v, rw, idx.to(torch.int32), chunk_size=chunk,
+                            sm_scale=d ** -0.5, block_q=1).to(torch.bfloat16)
+    out = (remote.float() + lw.float()[..., None] * local_o.float()).to(torch.bfloat16)
+    rows = torch.arange(7, l, 8)      # every 8th row, landmark rows (63 mod 64) included
+    _save("layer.pt", {"seed": seed, "batch": b, "seq_len": l, "hidden": hidden,
+                       "q_heads": hq, "kv_heads": hkv, "rows": rows, "q": q[:, rows],
+                       "k": k[:, rows], "route_q": route_q[:, rows],
+                       "lmk": lmk, "entropy": ent, "indices": idx, "scores": sc,
+                       "remote_weights": rw, "local_weight": lw, "local_lse": local_lse,
+                       "out": out})
+
+
+if __name__ == "__main__":
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gen_yarn()
+    gen_pool()
+    gen_drop()
+    gen_route()
+    gen_weights()
+    gen_selected()
+    gen_qcal()
+    gen_local_mask()
+    gen_layer()
+    print("done")
