@@ -1,0 +1,191 @@
+/*
+ * mrsa.h -- C ABI of the B200 (sm_100a) MRSA route-layer / SWA-layer forward.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream, launches on that stream, never allocates, frees or synchronises,
+ * and returns 0 or a negative MRSA_ERR_* code (no exceptions, no aborts).
+ * Tensors are dense row-major in the reference's BLHD layouts:
+ *   q            [B, L, Hq, D]   bf16        (Hq = Hkv * G, D = 128)
+ *   k, v         [B, L, Hkv, D]  bf16
+ *   key_valid    [B, L]          uint8 (0/1), NULL = every key valid
+ *   landmarks    [B, C, Hkv, G, D] bf16      (C = L / 64 chunks)
+ *   prior/entropy[B, C, Hkv, G]  fp32
+ *   local_lse    [B, L, Hq]      fp32 (natural log)
+ *   indices      [B, L, Hkv, K]  int32, ascending, -1 last
+ *   scores / remote weights [B, L, Hq, K] bf16; local weight [B, L, Hq] bf16
+ * Pointers must be 16-byte aligned.  Stateless and re-entrant: any host
+ * thread, any stream.
+ */
+#ifndef MRSA_B200_H
+#define MRSA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* mrsa_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+enum {
+  MRSA_OK = 0,
+  MRSA_ERR_NULL = -1,      /* a required pointer is NULL */
+  MRSA_ERR_SHAPE = -2,     /* inconsistent or unsupported shape */
+  MRSA_ERR_ALIGN = -3,     /* a pointer is not 16-byte aligned */
+  MRSA_ERR_LAUNCH = -4,    /* CUDA rejected the launch */
+  MRSA_ERR_ARG = -5,       /* bad scalar argument */
+  MRSA_ERR_WORKSPACE = -6  /* workspace missing or too small */
+};
+
+enum { MRSA_BF16 = 0, MRSA_F32 = 1 };                 /* cos/sin and score dtypes */
+enum { MRSA_WEIGHTS_AFFINE = 0, MRSA_WEIGHTS_SOFTMAX = 1 };
+
+const char* mrsa_strerror(int code);
+int mrsa_abi_version(void);
+
+/* YaRN inverse frequencies [dim/2] and attention factor, host-side.
+ * Replaces transformers ROPE_INIT_FUNCTIONS['yarn'] as used by Dream's rotary
+ * module (dream_dllm_hils/train_fulltext.py:2873-2888). */
+int mrsa_yarn_inv_freq(int dim, double base, double factor, int orig_max_pos, double beta_fast,
+                       double beta_slow, int truncate, float* inv_freq_out,
+                       float* attention_factor_out);
+
+/* fp32 rotate-half RoPE on one or two BLHD bf16 tensors (x1 may be NULL).
+ * cos/sin come either from position_ids [B,L] int64 + inv_freq [D/2] fp32 +
+ * attention_factor (HF rotary rule: fp32 pos*inv_freq, cos*factor), or from
+ * explicit cos/sin [B,L,D] of dtype cs_dtype.  y may alias x.
+ * Replaces ops/rope_tilelang_fp32.py:84 rope_rotary_pos_emb and :173
+ * single_tensor_rope_autograd (forward), and the torch RoPE of
+ * dream_dllm_hils/attention.py:41-52 / :384-393. */
+int mrsa_rope(const void* x0, void* y0, int64_t heads0, const void* x1, void* y1, int64_t heads1,
+              const int64_t* position_ids, const float* inv_freq, float attention_factor,
+              const void* cos, const void* sin, int cs_dtype, int64_t batch, int64_t seq_len,
+              int64_t head_dim, mrsa_stream_t stream);
+
+/* Q-Cal routing query: route_q = rope(rmsnorm(invrope(q) + scale*bf16(bf16(h W_in^T) W_out^T))),
+ * q the RoPE'd query, h [B,L,hidden], W_in [rank,hidden], W_out [Hq*D,rank] bf16,
+ * norm_weight [D] fp32, cos/sin from position_ids (as in mrsa_rope).
+ * Replaces _qcal_delta + _finish_calibrated_query (dream_dllm_hils/attention.py:458-511). */
+int mrsa_qcal_route_query(const void* hidden, const void* q, const void* w_in, const void* w_out,
+                          const float* norm_weight, float eps, float scale,
+                          const int64_t* position_ids, const float* inv_freq,
+                          float attention_factor, void* route_q, int64_t batch, int64_t seq_len,
+                          int64_t hidden_size, int64_t rank, int64_t q_heads, int64_t head_dim,
+                          mrsa_stream_t stream);
+
+/* Landmark attention pool + entropy prior.  mu_q element (b,c,h,g,d) is read at
+ * mu_q + b*mu_stride_b + c*mu_stride_c + (h*G+g)*D + d (elements); k [B,C*64,Hkv,D].
+ * Writes landmarks, entropy, optionally prior = entropy*bias_scale[h*G+g] and
+ * chunk_ok [B,C] (1 = chunk has a valid non-landmark key).
+ * Replaces ops/chunk_attn_pool_gqa_tilelang.py:425 chunk_attn_pool_gqa (forward). */
+int mrsa_chunk_pool(const void* mu_q, int64_t mu_stride_b, int64_t mu_stride_c, const void* k,
+                    const uint8_t* key_valid, float sm_scale, const float* bias_scale,
+                    void* landmarks, float* entropy, float* prior, uint8_t* chunk_ok,
+                    int64_t batch, int64_t chunks, int64_t kv_heads, int64_t groups,
+                    int64_t head_dim, mrsa_stream_t stream);
+
+/* Dense 1 = drop mask [B,L,C] int32 (chunk overlaps the chunk-aligned local
+ * window or has no valid non-landmark key).
+ * Replaces dream_dllm_hils/kernel_utils.py:102 remote_drop_mask (allowed_mask=None). */
+int mrsa_remote_drop_mask(const uint8_t* key_valid, int32_t* out, int64_t batch, int64_t seq_len,
+                          int64_t window, int64_t chunk, mrsa_stream_t stream);
+
+/* Post-softmax max-pooled top-K chunk routing + optional route weights.
+ * route_q [B,Lq,Hq,D] (query rows at global positions q_offset..), landmarks
+ * [B,C,Hkv,G,D] (lmk_per_qhead=1) or [B,C,Hkv,D] (0), local_lse [B,Lq,Hq],
+ * bias [B,C,Hq] or NULL.  Dropped chunks: drop_mask [B,Lq,C] int32 if given,
+ * else the inline rule from chunk_ok [B,C] (NULL = all valid) and window
+ * (window < 0: nothing dropped).  scores_out dtype: scores_dtype.
+ * remote_w/local_w (both or neither) get the route weights of
+ * mode MRSA_WEIGHTS_AFFINE (_route_weights_torch with gate scale/offset) or
+ * MRSA_WEIGHTS_SOFTMAX (route_weights).
+ * Replaces ops/topk_head_softmax.py:15 ref_softmax_topk_max_pooling and :1242
+ * online_softmax_topk_head (post_softmax, non-causal), dream_dllm_hils/routing.py:52
+ * route_topk_g7, and fuses dream_dllm_hils/attention.py:126 _route_weights_torch. */
+int mrsa_route_topk(const void* route_q, const void* landmarks, int lmk_per_qhead,
+                    const float* local_lse, const float* bias, const int32_t* drop_mask,
+                    const uint8_t* chunk_ok, int64_t window, int64_t q_offset,
+                    int32_t* indices, void* scores_out, int scores_dtype, void* remote_w,
+                    void* local_w, int weight_mode, float temperature, float gate_scale,
+                    float gate_offset, int64_t batch, int64_t q_len, int64_t chunks,
+                    int64_t kv_heads, int64_t groups, int64_t head_dim, int64_t topk,
+                    mrsa_stream_t stream);
+
+/* Route weights from scores [B,L,Hq,K] bf16, indices [B,L,Hkv,K] int32,
+ * prior [B,C,Hkv,G] fp32, local_lse [B,L,Hq] fp32.
+ * Replaces ops/hils_bidir_route_weights_tilelang.py:276 route_weights (any K<=32)
+ * and dream_dllm_hils/attention.py:126 _route_weights_torch (no Gumbel / value bonus). */
+int mrsa_route_weights(const void* scores, const int32_t* indices, const float* prior,
+                       const float* local_lse, void* remote_w, void* local_w, int weight_mode,
+                       float temperature, float gate_scale, float gate_offset, int64_t batch,
+                       int64_t seq_len, int64_t chunks, int64_t kv_heads, int64_t groups,
+                       int64_t topk, mrsa_stream_t stream);
+
+/* Bidirectional banded GQA attention: query row i (global position q_offset+i)
+ * attends keys j with |pos_i - j| <= window.  Keys that are invalid or, with
+ * skip_inert, landmark slots ((j+1)%chunk==0) have K and V treated as zero
+ * (logit 0, no value).  Writes out [B,Lq,Hq,D] bf16 and lse [B,Lq,Hq] fp32 (or NULL).
+ * Replaces dream_dllm_hils/local_attention.py:110 bidir_local_attention (flash-attn
+ * window (W,W)) and, with skip_inert=0, the SWA layer's call at attention.py:1210. */
+int mrsa_local_attention(const void* q, const void* k, const void* v, const uint8_t* key_valid,
+                         void* out, float* lse, int64_t window, int skip_inert, int64_t chunk,
+                         float sm_scale, int64_t batch, int64_t q_len, int64_t kv_len,
+                         int64_t q_offset, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                         mrsa_stream_t stream);
+
+/* Weighted per-chunk-softmax attention over the selected chunks, optionally
+ * fused with the local branch: out = bf16(bf16(remote) + local_w*local) when
+ * local_out and local_w are given, else bf16(remote).
+ * weights [B,Lq,Hq,K] bf16, indices [B,Lq,Hkv,K] int32, k/v [B,Lk,Hkv,D].
+ * Replaces ops/hils_fwd_bwd_head.py:1113 HiLS_block_M_head (forward),
+ * dream_dllm_hils/routing.py:305 selected_attention_g7 and
+ * ops/hils_bidir_output_fusion_tilelang.py:138 fuse_hils_outputs. */
+int mrsa_selected_attention(const void* q, const void* k, const void* v, const uint8_t* key_valid,
+                            const void* weights, const int32_t* indices, const void* local_out,
+                            const void* local_w, void* out, float sm_scale, int mask_last_token,
+                            int64_t batch, int64_t q_len, int64_t kv_len, int64_t kv_heads,
+                            int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk,
+                            mrsa_stream_t stream);
+
+/* out = bf16(remote + local_w * local) over rows = B*L*H, each of head_dim.
+ * Replaces ops/hils_bidir_output_fusion_tilelang.py:138 fuse_hils_outputs. */
+int mrsa_fuse_outputs(const void* remote, const void* local, const void* local_w, void* out,
+                      int64_t rows, int64_t head_dim, mrsa_stream_t stream);
+
+/* ---------------------------------------------------------------- layers */
+typedef struct {
+  /* inputs (device) */
+  const void* q_pre;          /* [B,L,Hq,D] bf16, before RoPE */
+  const void* k_pre;          /* [B,L,Hkv,D] bf16, before RoPE */
+  const void* v;              /* [B,L,Hkv,D] bf16 */
+  const void* hidden;         /* [B,L,hidden] bf16 (Q-Cal input) */
+  const int64_t* position_ids;/* [B,L] */
+  const uint8_t* key_valid;   /* [B,L] or NULL */
+  const float* inv_freq;      /* [D/2] */
+  const void* w_in;           /* [rank,hidden] bf16 */
+  const void* w_out;          /* [Hq*D,rank] bf16 */
+  const float* norm_weight;   /* [D] */
+  const float* bias_scale;    /* [Hq] entropy_bias_scale */
+  /* output */
+  void* out;                  /* [B,L,Hq,D] bf16, pre o_proj */
+  /* scalars */
+  float attention_factor, rms_eps, qcal_scale, temperature, gate_scale, gate_offset;
+  int64_t batch, seq_len, q_heads, kv_heads, head_dim, hidden_size, rank;
+  int64_t topk, local_window;
+} mrsa_route_layer_args;
+
+/* Bytes of workspace mrsa_route_layer_forward needs (256-byte aligned pieces). */
+size_t mrsa_route_layer_workspace_size(const mrsa_route_layer_args* a);
+
+/* Whole route layer on one device: RoPE, local branch, Q-Cal, landmark pool,
+ * routing + weights, selected attention fused with the local branch.
+ * Replaces KernelDreamFullHiLSAttention.forward (dream_dllm_hils/attention.py:1313-1774)
+ * from the projected q/k/v/h to the input of o_proj. */
+int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* workspace, size_t ws_bytes,
+                             mrsa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MRSA_B200_H */

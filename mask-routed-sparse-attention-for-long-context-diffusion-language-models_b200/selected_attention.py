@@ -1,0 +1,122 @@
+"""Selected-chunk attention (+ local merge) on the B200 kernel.
+
+Drop-ins for ``ops/hils_fwd_bwd_head.py:1113 HiLS_block_M_head`` (forward),
+``dream_dllm_hils/routing.py:305 selected_attention_g7`` / ``:330
+selected_attention_g7_cached`` and
+``ops/hils_bidir_output_fusion_tilelang.py:138 fuse_hils_outputs``.  No
+physical G=8 / power-of-two top-k padding is needed: the kernel takes the
+logical group size (<= 8) and any top-k <= 32.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_LOGICAL_G = 7
+
+
+def selected_attention(q, k, v, weights, indices, key_valid=None, *, chunk: int = 64,
+                       local_out=None, local_weight=None, mask_last_token=True, sm_scale=None,
+                       out=None):
+    """``out = sum_k w_k softmax_chunk(q.K_k/sqrt(D)) V_k`` (bf16), fused with
+    ``+ local_weight * local_out`` when those are given."""
+    b, lq, hq, d = q.shape
+    lk, hkv = k.shape[1], k.shape[2]
+    topk = indices.shape[-1]
+    dev = q.device
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    w = weights.to(torch.bfloat16).contiguous()
+    idx = indices.to(device=dev, dtype=torch.int32).contiguous()
+    kv = None if key_valid is None else key_valid.to(device=dev, dtype=torch.bool).contiguous()
+    lo = None if local_out is None else local_out.contiguous()
+    lw = None if local_weight is None else local_weight.to(torch.bfloat16).contiguous()
+    if out is None:
+        out = torch.empty_like(q)
+    scale = float(d) ** -0.5 if sm_scale is None else float(sm_scale)
+    _lib.call("mrsa_selected_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
+              _lib.ptr(w), _lib.ptr(idx), _lib.ptr(lo), _lib.ptr(lw), _lib.ptr(out), scale,
+              int(bool(mask_last_token)), b, lq, lk, hkv, hq // hkv, d, topk, int(chunk),
+              _lib.stream_of(q))
+    return out
+
+
+def _validate_g7(q, k, v, weights, indices, key_valid, chunk_size):
+    # mirrors dream_dllm_hils/routing.py:368-425
+    if q.ndim != 4 or k.ndim != 4:
+        raise ValueError(f"q and k must be BLHD tensors, got {tuple(q.shape)} and {tuple(k.shape)}")
+    batch, query_len, h_q, dim = q.shape
+    if k.shape[0] != batch or k.shape[-1] != dim:
+        raise ValueError(f"incompatible q/k shapes {tuple(q.shape)} and {tuple(k.shape)}")
+    kv_len, h_kv = k.shape[1:3]
+    if h_q != h_kv * _LOGICAL_G:
+        raise ValueError(f"Dream G7 requires h_q == 7 * h_kv, got h_q={h_q}, h_kv={h_kv}")
+    if v.shape != k.shape:
+        raise ValueError(f"v shape {tuple(v.shape)} must match k shape {tuple(k.shape)}")
+    selected = indices.shape[-1]
+    if indices.shape != (batch, query_len, h_kv, selected):
+        raise ValueError(f"invalid indices shape {tuple(indices.shape)}")
+    if weights.shape != (batch, query_len, h_q, selected):
+        raise ValueError(f"invalid weights shape {tuple(weights.shape)}")
+    if key_valid.shape != (batch, kv_len):
+        raise ValueError(f"invalid key_valid shape {tuple(key_valid.shape)}")
+    if kv_len % chunk_size != 0:
+        raise ValueError(f"cache length {kv_len} must be divisible by chunk_size={chunk_size}")
+    if q.dtype != torch.bfloat16 or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("selected attention requires BF16 q, k, and v")
+    if q.device != k.device or v.device != q.device:
+        raise ValueError("q, k, and v must share a device")
+    if weights.device != q.device or indices.device != q.device:
+        raise ValueError("weights and indices must share the q device")
+    if key_valid.device != q.device:
+        raise ValueError("key_valid must share the q device")
+    if selected <= 0:
+        raise ValueError("selected attention requires at least one chunk slot")
+
+
+def selected_attention_g7(q, k, v, weights, indices, key_valid, chunk_size, training,
+                          token_keep=None):
+    """Selected-chunk attention with compact KV (``dream_dllm_hils/routing.py:305``)."""
+    _validate_g7(q, k, v, weights, indices, key_valid, chunk_size)
+    if token_keep is not None:
+        raise ValueError("token_keep (token refinement) is not supported by the B200 kernel")
+    return selected_attention(q, k, v, weights, indices, key_valid, chunk=chunk_size)
+
+
+def selected_attention_g7_cached(q, k, v, weights, indices, key_valid, chunk_size, token_keep=None):
+    """Partial queries against a full K/V cache (``dream_dllm_hils/routing.py:330``)."""
+    return selected_attention_g7(q, k, v, weights, indices, key_valid, chunk_size, False, token_keep)
+
+
+def HiLS_block_M_head(q, k, v, weights, indices, block_size=64, sm_scale=None, block_M=None,
+                      mask_last_token=True, dtype="bfloat16", accum_dtype="float", num_threads=None,
+                      num_threads_fwd=None, num_threads_bwd=None, is_training=True, slope=None,
+                      key_valid=None, token_keep=None):
+    """Forward of ``ops/hils_fwd_bwd_head.py:1113`` (q may carry padded heads;
+    padded weights are zero)."""
+    if slope is not None or token_keep is not None:
+        raise ValueError("ALiBi slope / token_keep are not supported by the B200 kernel")
+    hq, hkv = q.shape[2], k.shape[2]
+    if hq % hkv or hq // hkv > 8:
+        raise ValueError("the B200 kernel supports query groups of at most 8 heads")
+    return selected_attention(q, k, v, weights, indices, key_valid, chunk=block_size,
+                              mask_last_token=mask_last_token, sm_scale=sm_scale)
+
+
+def fuse_hils_outputs(remote_output, local_output, local_weight):
+    """``bf16(remote + local_weight * local)`` (fp32 math)."""
+    # mirrors ops/hils_bidir_output_fusion_tilelang.py:101-135
+    if remote_output.shape != local_output.shape or remote_output.ndim != 4:
+        raise ValueError("remote_output and local_output must be matching BLHD tensors")
+    if local_weight.shape != remote_output.shape[:-1]:
+        raise ValueError("local_weight must be [B,L,H]")
+    if not (remote_output.dtype == local_output.dtype == local_weight.dtype == torch.bfloat16):
+        raise ValueError("fuse_hils_outputs requires BF16 tensors")
+    if not (remote_output.is_contiguous() and local_output.is_contiguous() and local_weight.is_contiguous()):
+        raise ValueError("fuse_hils_outputs requires contiguous tensors")
+    out = torch.empty_like(remote_output)
+    b, l, h, d = remote_output.shape
+    _lib.call("mrsa_fuse_outputs", _lib.ptr(remote_output), _lib.ptr(local_output),
+              _lib.ptr(local_weight), _lib.ptr(out), b * l * h, d, _lib.stream_of(out))
+    return out

@@ -50,6 +50,8 @@ __all__ = [
     "route_layer_forward",
     "swa_layer_forward",
     "topk_set_agreement",
+    "route_keys",
+    "route_scores_at",
 ]
 
 
@@ -288,6 +290,34 @@ def route_topk_blocked(route_q: torch.Tensor, lmks5: torch.Tensor, local_lse4: t
     return torch.cat(out_i, 1), torch.cat(out_s, 1)
 
 
+def route_keys(route_q: torch.Tensor, lmks5: torch.Tensor, local_lse4: torch.Tensor,
+               prior_bias: torch.Tensor, drop_mask: torch.Tensor) -> torch.Tensor:
+    """The max-pooled selection key ``[B,L,Hkv,C]`` of :func:`route_topk`
+    (dropped chunks ``-inf``), for gap-aware selection comparisons."""
+    b, l, hq, d = route_q.shape
+    c, hkv, g = lmks5.shape[1:4]
+    raw = torch.einsum("blhgd,bchgd->blhgc", route_q.float().view(b, l, hkv, g, d),
+                       lmks5.float()) * (1.0 / math.sqrt(d))
+    x = raw + prior_bias.float().permute(0, 2, 3, 1)[:, None]
+    total = torch.logaddexp(local_lse4.float(), torch.logsumexp(x, dim=-1))
+    key = (x - total[..., None]).max(dim=3).values
+    return key.masked_fill(drop_mask.bool()[:, :, None, :], float("-inf"))
+
+
+def route_scores_at(route_q: torch.Tensor, lmks5: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+    """Raw scaled scores ``[B,L,Hq,K]`` (bf16, ``-inf`` at ``-1``) of given
+    selections, as :func:`route_topk` gathers them."""
+    b, l, hq, d = route_q.shape
+    c, hkv, g = lmks5.shape[1:4]
+    k = indices.shape[-1]
+    raw = torch.einsum("blhgd,bchgd->blhgc", route_q.float().view(b, l, hkv, g, d),
+                       lmks5.float()) * (1.0 / math.sqrt(d))
+    idx = indices.long()
+    sc = torch.gather(raw, -1, idx.clamp_min(0)[:, :, :, None, :].expand(b, l, hkv, g, k))
+    sc = sc.masked_fill(idx[:, :, :, None, :] < 0, float("-inf"))
+    return sc.reshape(b, l, hq, k).to(route_q.dtype)
+
+
 def route_weights_affine(scores: torch.Tensor, indices: torch.Tensor, prior_bias: torch.Tensor,
                          local_lse: torch.Tensor, *, temperature: float = 1.0,
                          gate_offset: float = 0.0, gate_scale: float = 1.0):
@@ -463,15 +493,18 @@ def make_route_layer_inputs(batch: int, seq_len: int, cfg: MRSAConfig = MRSAConf
 
 
 def route_layer_forward(inp: dict, cfg: MRSAConfig = MRSAConfig(), *, keep: bool = True,
-                        query_slice: slice | None = None):
+                        query_slice: slice | None = None, indices: torch.Tensor | None = None):
     """Route-layer forward from post-projection q/k/v/h to the pre-``o_proj``
     output, in the order of ``KernelDreamFullHiLSAttention.forward``
     (``dream_dllm_hils/attention.py:1358-1774``): RoPE, local branch, Q-Cal,
     landmark pool + entropy prior, drop mask, routing, route weights,
     selected attention, fusion.  ``query_slice`` restricts the per-query
     stages (local, routing, weights, selected, fusion) to a query range, the
-    landmark pool still covers every chunk.  Returns a dict of every
-    intermediate (``keep``) plus ``out``.
+    landmark pool still covers every chunk.  ``indices`` (for the sliced rows)
+    replaces the oracle's own selection -- scores, weights and outputs are
+    then evaluated on those chunks, which decouples near-tie selection flips
+    from the attention comparison.  Returns a dict of every intermediate
+    (``keep``) plus ``out``.
     """
     chunk, d = cfg.chunk, cfg.head_dim
     q_pre, k_pre, v = inp["q_pre"], inp["k_pre"], inp["v"]
@@ -503,12 +536,16 @@ def route_layer_forward(inp: dict, cfg: MRSAConfig = MRSAConfig(), *, keep: bool
     local_o, local_lse = _local_rows(q, k, v, key_valid, cfg.local_window, chunk, True, qs)
     drop = remote_drop_mask(key_valid, cfg.local_window, chunk)[:, qs]
     idx, scores = route_topk_blocked(route_q[:, qs], lmk, local_lse.view(b, -1, hkv, g), prior, drop, cfg.topk)
+    if indices is not None:
+        idx = indices.long().cpu()
+        scores = route_scores_at(route_q[:, qs], lmk, idx)
     rw, lw = route_weights_affine(scores, idx, prior, local_lse, temperature=cfg.route_temperature,
                                   gate_offset=inp["gate_offset"], gate_scale=inp["gate_scale"])
     remote = _selected_rows(q, k, v, rw, idx, key_valid, chunk, qs)
     out = fuse_outputs(remote, local_o, lw)
     res = {"out": out}
     if keep:
+        res.update(route_key=route_keys(route_q[:, qs], lmk, local_lse.view(b, -1, hkv, g), prior, drop))
         res.update(q=q, k=k, route_q=route_q, lmk=lmk, entropy=entropy, prior_bias=prior,
                    local_out=local_o, local_lse=local_lse, indices=idx, scores=scores,
                    remote_weights=rw, local_weight=lw, remote_out=remote, cos=cos, sin=sin)
