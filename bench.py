@@ -1,0 +1,355 @@
+"""MRSA route-layer forward benchmark (BASELINE metric: route-layer fwd tokens/s, bf16).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N=1 runs configs[1]: B=1, L=16384 (256 chunks), 28/4 heads, d=128, Q-Cal
+hidden 3584 / rank 64, top-32 of 64-token chunks + local radius 256, YaRN-8
+fp32 RoPE, seeded N(0,1) activations (N(0,1)/sqrt(128) for q/k/v).  N>1
+(torchrun) shards one sequence of L = 16384*N tokens into contiguous query
+blocks of 16384 per GPU with NCCL all-gathers of K/V and chunk summaries
+(N=8: configs[4], L=131072), i.e. weak scaling in query rows.  A step is one
+route-layer forward from the projected q/k/v/h to the o_proj input.  Inputs
+(q 117 MB + h 117 MB + k/v 33 MB per 16k tokens) are larger than L2 (126 MB).
+
+``--impl reference`` times the reference's PyTorch path restated on the CPU
+(``oracle/``; the reference is Python and its checkout is not on the GPU
+host) with all host threads, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L_PER_GPU = 16384
+HQ, HKV, D, HIDDEN, RANK, TOPK, CHUNK, WLOC = 28, 4, 128, 3584, 64, 32, 64, 256
+METRIC = "MRSA route-layer fwd tokens/s (bf16)"
+
+
+def algorithmic(l_local: int, l_total: int):
+    """Algorithmic FLOPs of one route-layer forward over ``l_local`` query rows
+    with ``l_total`` keys (BASELINE.md section 3 formulas)."""
+    c = l_total // CHUNK
+    f_sel = l_local * HQ * TOPK * CHUNK * D * 4
+    w = WLOC + CHUNK - 1
+    band = l_local * (2 * w + 1) - (w * (w + 1) if l_local == l_total else 0)
+    f_loc = HQ * D * 4 * band
+    f_route = l_local * HQ * c * D * 2
+    f_qcal = l_local * (HIDDEN * RANK * 2 + RANK * HQ * D * 2)
+    return {"selected_attention": f_sel, "local_attention": f_loc, "route": 2 * f_route,
+            "qcal": f_qcal, "route_one_pass": f_route}
+
+
+def stage_bytes(l: int):
+    """Compulsory HBM bytes of the memory-bound stages."""
+    c = l // CHUNK
+    return {"rope": l * (HQ + HKV) * D * 2 * 2,
+            "pool": l * HKV * D * 2 + c * HQ * D * 2 * 2 + c * HQ * 8,
+            "qcal": l * HIDDEN * 2 + 2 * l * HQ * D * 2}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(l_local: int, rank: int, dev):
+    """Seeded synthetic inputs of this rank's rows (distributions of configs[0])."""
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    q = torch.randn(1, l_local, HQ, D, device=dev, generator=g).div_(math.sqrt(D)).bfloat16()
+    k = torch.randn(1, l_local, HKV, D, device=dev, generator=g).div_(math.sqrt(D)).bfloat16()
+    v = torch.randn(1, l_local, HKV, D, device=dev, generator=g).div_(math.sqrt(D)).bfloat16()
+    h = torch.randn(1, l_local, HIDDEN, device=dev, generator=g).bfloat16()
+    gw = torch.Generator(device=dev).manual_seed(7)          # weights identical on every rank
+    w_in = (torch.randn(RANK, HIDDEN, device=dev, generator=gw) * 0.02).bfloat16()
+    w_out = (torch.randn(HQ * D, RANK, device=dev, generator=gw) * 0.02).bfloat16()
+    role = (torch.randn(HIDDEN, device=dev, generator=gw) * 0.02).bfloat16()
+    i = torch.arange(rank * l_local, (rank + 1) * l_local, device=dev)
+    h[0, (i + 1) % CHUNK == 0] += role                        # landmark role offset
+    pos = (i - i // CHUNK).view(1, -1).contiguous()
+    valid = torch.ones(1, l_local, dtype=torch.bool, device=dev)
+    return {"q_pre": q, "k_pre": k, "v": v, "hidden": h, "position_ids": pos, "key_valid": valid,
+            "w_in": w_in, "w_out": w_out}
+
+
+def cpu_route_layer_rate(l_total: int, q_small: int, q_big: int):
+    """Oracle (the reference's PyTorch path on the CPU) timed on two query
+    slices; tokens/s of a whole layer from the linear model t(Q) = a + b*Q."""
+    from oracle import route_layer as orc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = orc.MRSAConfig()
+    inp = orc.make_route_layer_inputs(1, l_total, cfg, hidden=HIDDEN, seed=0)
+    mid = l_total // 2
+
+    def run(nq):
+        t0 = time.perf_counter()
+        orc.route_layer_forward(inp, cfg, keep=False, query_slice=slice(mid, mid + nq))
+        return time.perf_counter() - t0
+
+    a_s, b_s = run(q_small), run(q_big)
+    slope = max((b_s - a_s) / (q_big - q_small), 1e-12)
+    fixed = max(a_s - slope * q_small, 0.0)
+    return l_total / (fixed + slope * l_total), {"fixed_s": fixed, "per_query_s": slope}
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the oracle port on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    l_total = L_PER_GPU * world
+    from oracle import route_layer as orc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = orc.MRSAConfig()
+    inp = orc.make_route_layer_inputs(1, l_total, cfg, hidden=HIDDEN, seed=0)
+    mid, q_step, q_small = l_total // 2, 128, 32
+
+    def run(nq):
+        t0 = time.perf_counter()
+        orc.route_layer_forward(inp, cfg, keep=False, query_slice=slice(mid, mid + nq))
+        return time.perf_counter() - t0
+
+    small = [run(q_small) for _ in range(max(1, args.warmup))]
+    steps = [run(q_step) for _ in range(args.steps)]
+    a_s, b_s = statistics.median(small), statistics.median(steps)
+    slope = max((b_s - a_s) / (q_step - q_small), 1e-12)
+    fixed = max(a_s - slope * q_small, 0.0)
+    value = l_total / (fixed + slope * l_total)
+    cores = torch.get_num_threads()
+    sample = (f"oracle route layer at L={l_total}: {q_step}-query slice per step "
+              f"({q_small}-query slices in warm-up) extrapolated to all {l_total} queries "
+              f"with t = a + b*Q (a={fixed:.3f}s, b={slope * 1e3:.3f}ms/query)")
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * l_total / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"route-layer fwd B=1 L={l_total} 28/4 heads d=128 top-32x64 + local-256",
+                       "global_batch": 1, "seq_len": l_total, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seq-per-gpu", type=int, default=L_PER_GPU)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import __graft_entry__
+
+    mrsa = __graft_entry__.load_package()
+    mrsa.load_library()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    lq = args.seq_per_gpu
+    l_total = lq * world
+    inp = make_inputs(lq, rank, dev)
+    layer = mrsa.RouteLayer(inp["w_in"], inp["w_out"])
+    if world > 1:
+        from mrsa_b200.shard import ShardedRouteLayer
+
+        runner = ShardedRouteLayer(layer)
+    else:
+        runner = layer
+    names = ("q_pre", "k_pre", "v", "hidden", "position_ids", "key_valid")
+    x = [inp[n] for n in names]
+    out = torch.empty_like(inp["q_pre"])
+
+    def step():
+        runner(*x, out=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = ClockSampler(local) if rank == 0 else None
+    if clk:
+        clk.start()
+        time.sleep(0.3)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = clk.stop() if clk else None
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    ms_step = ms / args.steps
+    value = l_total / (ms_step / 1e3)
+
+    # ---- e2e through the public API with pinned host buffers ---------------
+    host = [t.cpu().pin_memory() for t in x]
+    dev_in = [torch.empty_like(t) for t in x]
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for d_, h_ in zip(dev_in, host):
+            d_.copy_(h_, non_blocking=True)
+        runner(*dev_in, out=out)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e2 = max(3, args.steps // 2)
+    e0.record(stream)
+    for _ in range(e2):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = t.item()
+    e2e_value = l_total / (ms_e2e / e2 / 1e3)
+
+    # ---- per-kernel times, roofline of the dominant kernel -----------------
+    hbm, tflops, peak_kind = load_peaks()
+    stages, roof = None, None
+    if world == 1:
+        stages = layer.stage_times(*x[:5], x[5], reps=5)
+        dom = max(stages, key=stages.get)
+        flops = algorithmic(lq, l_total)
+        byts = stage_bytes(lq)
+        if dom in ("selected_attention", "local_attention", "route"):
+            ach = flops[dom] / (stages[dom] * 1e-3) / 1e12
+            roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tflops,
+                    "unit": "TFLOP/s", "frac": ach / tflops, "traffic": None,
+                    "peak_kind": f"{peak_kind} bf16 burst"}
+        else:
+            ach = byts[dom] / (stages[dom] * 1e-3) / 1e9
+            roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                    "frac": ach / hbm, "traffic": None, "peak_kind": f"{peak_kind} HBM copy"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": (f"route-layer fwd B=1 L={l_total} (query blocks of {lq} per GPU) "
+                                        "28/4 heads d=128 top-32x64 + local-256, Q-Cal 3584->64, YaRN-8"),
+                           "global_batch": 1, "seq_len": l_total, "parallelism": f"seq{world}",
+                           "l2": "inputs larger than L2 (267 MB per 16k tokens)"},
+                "roofline": roof, "stage_ms": stages,
+                "gpu_launches": args.steps * 6,
+                "clocks": clocks,
+                "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
+                        "d2h_bytes_per_step": d2h * world, "steps": e2}}
+        if world == 1 and not args.no_cpu_baseline:
+            rate, info = cpu_route_layer_rate(l_total, 32, 160)
+            line["cpu_baseline"] = {
+                "value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                "sample": (f"oracle route layer at L={l_total}, 32- and 160-query slices, "
+                           f"extrapolated t = a + b*Q (a={info['fixed_s']:.2f}s, "
+                           f"b={info['per_query_s'] * 1e3:.2f}ms/query)")}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -64,6 +64,39 @@ __device__ __forceinline__ void mma_bf16(float* c, const uint32_t* a, uint32_t b
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// fp16 operands (P.V runs in fp16: P keeps 11 significant bits instead of
+// bf16's 8, and bf16 V converts to fp16 exactly inside the fp16 range).
+__device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// bf16x2 word -> f16x2 word (saturating at +-65504)
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t u) {
+  const float lo = __uint_as_float(u << 16), hi = __uint_as_float(u & 0xffff0000u);
+  return pack_f16x2(lo, hi);
+}
+// Convert a 64-row x 128-column bf16 tile in shared memory to fp16 in place,
+// cooperatively over `nthreads` threads.
+__device__ __forceinline__ void tile_bf16_to_f16(void* tile, int tid, int nthreads) {
+  uint4* t = reinterpret_cast<uint4*>(tile);
+  for (int i = tid; i < 64 * 128 / 8; i += nthreads) {
+    uint4 v = t[i];
+    v.x = bf16x2_to_f16x2(v.x);
+    v.y = bf16x2_to_f16x2(v.y);
+    v.z = bf16x2_to_f16x2(v.z);
+    v.w = bf16x2_to_f16x2(v.w);
+    t[i] = v;
+  }
+}
+
 // 128-byte row of 8 16-byte pieces, XOR-swizzled by row to spread ldmatrix
 // row reads over all banks.  `piece` indexes 16-byte units inside the row.
 __device__ __forceinline__ int swz(int row, int piece) { return (piece ^ (row & 7)); }

@@ -4,6 +4,8 @@
 // zeroed keys keep logit 0 in the softmax, keys with |i-j| > window are out.
 // Tile: 64 query rows of one query head per CTA (4 warps x 16 rows), 64-key
 // tiles streamed by cp.async (double buffered); online softmax in registers.
+// P.V runs on fp16 operands (V converted in shared memory; exact for |v| <
+// 65504, saturating beyond) so P keeps 11 significant bits.
 #include "common.cuh"
 
 using namespace mrsa;
@@ -93,6 +95,8 @@ __global__ void __launch_bounds__(NT) local_attn_kernel(
       cp_async_wait<0>();
     }
     __syncthreads();
+    tile_bf16_to_f16(sm.v[st], tid, NT);
+    __syncthreads();
     float s[BN / 8][4];
 #pragma unroll
     for (int n = 0; n < BN / 8; ++n)
@@ -158,17 +162,17 @@ __global__ void __launch_bounds__(NT) local_attn_kernel(
 #pragma unroll
     for (int kk = 0; kk < BN / 16; ++kk) {
       uint32_t pa[4];
-      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      pa[0] = pack_f16x2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_f16x2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_f16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_f16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
       for (int np = 0; np < D / 16; ++np) {
         uint32_t b0, b1, b2, b3;
         const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), p = np * 2 + (lane >> 4);
         ldsm_x4_t(b0, b1, b2, b3, vs + off128(r, p));
-        mma_bf16(o[2 * np], pa, b0, b1);
-        mma_bf16(o[2 * np + 1], pa, b2, b3);
+        mma_f16(o[2 * np], pa, b0, b1);
+        mma_f16(o[2 * np + 1], pa, b2, b3);
       }
     }
     __syncthreads();

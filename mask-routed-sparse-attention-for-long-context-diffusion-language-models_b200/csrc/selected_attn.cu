@@ -2,8 +2,9 @@
 // local branch.  Semantics of the HiLS forward (ops/hils_fwd_bwd_head.py:21-93
 // torch reference, kernel :423-559): every selected chunk is normalised on
 // its own (landmark slot 63 and invalid keys masked), its probabilities are
-// scaled by the route weight and rounded to bf16, and P.V accumulates in
-// fp32; the epilogue applies fuse_hils_outputs
+// scaled by the route weight, and P.V accumulates in fp32 on fp16 operands
+// (the reference rounds P to bf16; fp16 keeps 3 more bits, and bf16 V
+// converts to fp16 exactly for |v| < 65504); the epilogue applies fuse_hils_outputs
 // (ops/hils_bidir_output_fusion_tilelang.py:15-37): bf16(bf16(remote) + w_l*local).
 //
 // CTA = 16 queries x one KV head.  Each warp owns a fixed pair of queries,
@@ -156,6 +157,8 @@ __global__ void __launch_bounds__(NT, 2) selected_attn_kernel(SelArgs a) {
       cp_async_wait<0>();
     }
     __syncthreads();
+    tile_bf16_to_f16(sm.v[st], tid, NT);
+    __syncthreads();
     const int c = sm.ulist[u];
     const uint32_t ma = __ballot_sync(0xffffffffu, ia == c);
     const uint32_t mb = __ballot_sync(0xffffffffu, ib == c);
@@ -223,17 +226,17 @@ __global__ void __launch_bounds__(NT, 2) selected_attn_kernel(SelArgs a) {
 #pragma unroll
       for (int kk = 0; kk < S / 16; ++kk) {
         uint32_t pa[4];
-        pa[0] = pack_bf16x2(s[2 * kk][0] * f0, s[2 * kk][1] * f0);
-        pa[1] = pack_bf16x2(s[2 * kk][2] * f1, s[2 * kk][3] * f1);
-        pa[2] = pack_bf16x2(s[2 * kk + 1][0] * f0, s[2 * kk + 1][1] * f0);
-        pa[3] = pack_bf16x2(s[2 * kk + 1][2] * f1, s[2 * kk + 1][3] * f1);
+        pa[0] = pack_f16x2(s[2 * kk][0] * f0, s[2 * kk][1] * f0);
+        pa[1] = pack_f16x2(s[2 * kk][2] * f1, s[2 * kk][3] * f1);
+        pa[2] = pack_f16x2(s[2 * kk + 1][0] * f0, s[2 * kk + 1][1] * f0);
+        pa[3] = pack_f16x2(s[2 * kk + 1][2] * f1, s[2 * kk + 1][3] * f1);
 #pragma unroll
         for (int np = 0; np < D / 16; ++np) {
           uint32_t b0, b1, b2, b3;
           const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), p = np * 2 + (lane >> 4);
           ldsm_x4_t(b0, b1, b2, b3, vs + off128(r, p));
-          mma_bf16(o[2 * np], pa, b0, b1);
-          mma_bf16(o[2 * np + 1], pa, b2, b3);
+          mma_f16(o[2 * np], pa, b0, b1);
+          mma_f16(o[2 * np + 1], pa, b2, b3);
         }
       }
     }

@@ -141,40 +141,71 @@ class RouteLayer:
         if key_valid is not None and key_valid.shape != (b, l):
             raise ValueError("key_valid must be [B, L]")
 
+    # ------------------------------------------------------------------ timing
+    STAGES = ("rope", "local_attention", "qcal", "pool", "route", "selected_attention")
+
+    def stage_times(self, q_pre, k_pre, v, hidden, position_ids, key_valid=None, reps: int = 5):
+        """Average device milliseconds of each of the six kernels of the fused
+        path, from CUDA events on the current stream around each launch."""
+        res = None
+        for _ in range(reps + 1):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.STAGES) + 1)]
+            self._forward_stages(q_pre, k_pre, v, hidden, position_ids, key_valid, events=ev)
+            torch.cuda.synchronize()
+            t = [ev[i].elapsed_time(ev[i + 1]) for i in range(len(self.STAGES))]
+            if res is None:
+                res = [0.0] * len(t)          # first pass warms the allocator
+            else:
+                res = [a + b for a, b in zip(res, t)]
+        return {n: v / reps for n, v in zip(self.STAGES, res)}
+
     # ------------------------------------------------------------------ staged
-    def _forward_stages(self, q_pre, k_pre, v, hidden, position_ids, key_valid):
+    def _forward_stages(self, q_pre, k_pre, v, hidden, position_ids, key_valid, events=None):
         c = self.cfg
+        mark = (lambda i: events[i].record()) if events is not None else (lambda i: None)
         b, l, hq, d = q_pre.shape
         hkv = k_pre.shape[2]
         g = hq // hkv
         nc = l // c.chunk
         dev = q_pre.device
         st = _lib.stream_of(q_pre)
+        local_out = torch.empty_like(q_pre)
+        local_lse = torch.empty(b, l, hq, device=dev, dtype=torch.float32)
+        route_q = torch.empty_like(q_pre)
+        lmk = torch.empty(b, nc, hkv, g, d, device=dev, dtype=torch.bfloat16)
+        ent = torch.empty(b, nc, hkv, g, device=dev, dtype=torch.float32)
+        prior = torch.empty_like(ent)
+        chunk_ok = torch.empty(b, nc, device=dev, dtype=torch.uint8)
+        out = torch.empty_like(q_pre)
+        mark(0)
         q, k = yarn_rope_qk(q_pre, k_pre, position_ids, self.inv_freq, self.attention_factor)
-        local_out, local_lse = window_attention(q, k, v, key_valid, c.local_window + c.chunk - 1,
-                                                skip_inert=True, chunk=c.chunk)
-        route_q = torch.empty_like(q)
+        mark(1)
+        window_attention(q, k, v, key_valid, c.local_window + c.chunk - 1, skip_inert=True,
+                         chunk=c.chunk, out=local_out, lse=local_lse)
+        mark(2)
         _lib.call("mrsa_qcal_route_query", _lib.ptr(hidden), _lib.ptr(q), _lib.ptr(self.w_in),
                   _lib.ptr(self.w_out), _lib.ptr(self.norm_weight), float(c.rms_eps),
                   float(c.qcal_scale), _lib.ptr(position_ids), _lib.ptr(self.inv_freq),
                   float(self.attention_factor), _lib.ptr(route_q), b, l, hidden.shape[-1],
                   self.w_in.shape[0], hq, d, st)
-        lmk = torch.empty(b, nc, hkv, g, d, device=dev, dtype=torch.bfloat16)
-        ent = torch.empty(b, nc, hkv, g, device=dev, dtype=torch.float32)
-        prior = torch.empty_like(ent)
-        chunk_ok = torch.empty(b, nc, device=dev, dtype=torch.uint8)
+        mark(3)
         mu = route_q[:, c.chunk - 1:]
         _lib.call("mrsa_chunk_pool", C.c_void_p(mu.data_ptr()), l * hq * d, c.chunk * hq * d,
                   _lib.ptr(k), _lib.ptr(key_valid), d ** -0.5, _lib.ptr(self.bias_scale),
                   _lib.ptr(lmk), _lib.ptr(ent), _lib.ptr(prior), _lib.ptr(chunk_ok),
                   b, nc, hkv, g, d, st)
+        mark(4)
         idx, scores, rw, lw = route_topk_fused(route_q, lmk, local_lse, prior, chunk_ok, c.topk,
                                                c.local_window, temperature=c.route_temperature,
                                                gate_scale=self.gate_scale,
                                                gate_offset=self.gate_offset)
+        mark(5)
+        selected_attention(q, k, v, rw, idx, key_valid, chunk=c.chunk, local_out=local_out,
+                           local_weight=lw, out=out)
+        mark(6)
+        if events is not None:
+            return None
         remote = selected_attention(q, k, v, rw, idx, key_valid, chunk=c.chunk)
-        out = selected_attention(q, k, v, rw, idx, key_valid, chunk=c.chunk, local_out=local_out,
-                                 local_weight=lw)
         return {"q": q, "k": k, "route_q": route_q, "local_out": local_out, "local_lse": local_lse,
                 "lmk": lmk, "entropy": ent, "prior_bias": prior, "chunk_ok": chunk_ok,
                 "indices": idx, "scores": scores, "remote_weights": rw, "local_weight": lw,

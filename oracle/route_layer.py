@@ -603,10 +603,10 @@ def topk_set_agreement(key: torch.Tensor, idx_a: torch.Tensor, idx_b: torch.Tens
     t33 = srt[..., topk] if c > topk else torch.full(key.shape[:-1], float("-inf"))
 
     def member(idx):
-        m = torch.zeros(*key.shape, dtype=torch.bool)
-        ok = idx >= 0
-        m.scatter_(-1, idx.clamp_min(0).long(), ok)
-        return m
+        # scatter_add: "-1" slots map to chunk 0 with weight 0 and never erase it
+        m = torch.zeros(*key.shape, dtype=torch.int32)
+        m.scatter_add_(-1, idx.clamp_min(0).long(), (idx >= 0).to(torch.int32))
+        return m > 0
 
     ma, mb = member(idx_a), member(idx_b)
     must_in = (key >= t33[..., None] + gap) & torch.isfinite(key)

@@ -27,13 +27,15 @@ def close_bf16(got, ref, max_abs=MAX_ABS, mean_rel=MEAN_REL):
     assert d.max().item() <= max_abs and rel <= mean_rel, (d.max().item(), rel)
 
 
-def ulp_close(got, ref, frac=1e-3):
+def ulp_close(got, ref, frac=1e-3, floor=2.0 ** -20):
     """bf16 results of fp32 math done in a different order: at most one ulp
-    apart, and almost always identical."""
+    apart (or ``floor`` apart where cancellation leaves a result near zero),
+    and almost always identical."""
     got, ref = got.float().cpu(), ref.float().cpu()
     d = (got - ref).abs()
-    ulp = ref.abs().clamp_min(1e-30) * 2.0 ** -7
-    assert (d <= ulp + 1e-30).all(), d.max().item()
+    _, e = torch.frexp(torch.maximum(got.abs(), ref.abs()))
+    ulp = torch.ldexp(torch.ones_like(d), e - 8)          # bf16 spacing at that magnitude
+    assert ((d <= ulp) | (d <= floor)).all(), d.max().item()
     assert (d > 0).float().mean().item() <= frac
 
 
@@ -233,7 +235,8 @@ def _check_layer(mrsa, dev, l, cfg, hidden, seed, sl, key_valid=None, batch=1, m
     ulp_close(st["q"], ref["q"])
     ulp_close(st["k"], ref["k"])
     rq_rows = torch.arange(cfg.chunk - 1, l, cfg.chunk)
-    close_bf16(st["route_q"][:, rq_rows], ref["route_q"][:, rq_rows], max_abs=3e-2, mean_rel=2e-3)
+    # route_q is RMS-normalised (|x| up to ~8): one bf16 ulp there is 3.1e-2
+    close_bf16(st["route_q"][:, rq_rows], ref["route_q"][:, rq_rows], max_abs=6.5e-2, mean_rel=2e-3)
     close_bf16(st["lmk"], ref["lmk"], max_abs=2e-2, mean_rel=2e-3)
     torch.testing.assert_close(st["entropy"].cpu(), ref["entropy"], atol=2e-3, rtol=1e-3)
     close_bf16(st["local_out"][:, sl], ref["local_out"])
