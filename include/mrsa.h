@@ -185,6 +185,24 @@ size_t mrsa_route_layer_workspace_size(const mrsa_route_layer_args* a);
 int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* workspace, size_t ws_bytes,
                              mrsa_stream_t stream);
 
+/* Size of the device scratch built into the library for
+ * mrsa_route_layer_forward_noalloc (held by every GPU that loads it). */
+#define MRSA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* The route layer of mrsa_route_layer_forward for callers that cannot
+ * allocate device memory (a plugin inside a framework that owns all device
+ * allocations, a server with a fixed memory pool, code running while a stream
+ * is recorded).  It has no counterpart in the reference.  Instead of a caller
+ * workspace it uses MRSA_NOALLOC_SCRATCH_BYTES of scratch inside the library
+ * image: problems whose mrsa_route_layer_workspace_size exceeds that (about
+ * 1200 tokens of the Dream shape) are rejected with MRSA_ERR_WORKSPACE before
+ * anything runs.  Runs on the current device; its first call on a device
+ * looks up the scratch address (cudaGetSymbolAddress), so make that first
+ * call before any stream capture.  All calls on a device share the scratch:
+ * calls whose GPU work overlaps race, so order them on one stream.  Nothing
+ * in the scratch needs to start at zero.  Allocates and frees nothing. */
+int mrsa_route_layer_forward_noalloc(const mrsa_route_layer_args* a, mrsa_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,7 @@ _SIGS = {
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_route_layer_workspace_size": [_vp],
     "mrsa_route_layer_forward": [_vp, _vp, _sz, _vp],
+    "mrsa_route_layer_forward_noalloc": [_vp, _vp],
 }
 _RESTYPE = {"mrsa_strerror": C.c_char_p, "mrsa_route_layer_workspace_size": _sz}
 
