@@ -13,7 +13,7 @@
  *   local_lse    [B, L, Hq]      fp32 (natural log)
  *   indices      [B, L, Hkv, K]  int32, ascending, -1 last
  *   scores / remote weights [B, L, Hq, K] bf16; local weight [B, L, Hq] bf16
- * Pointers must be 16-byte aligned.  Stateless and re-entrant: any host
+ * Pointers (key_valid included) must be 16-byte aligned.  Stateless and re-entrant: any host
  * thread, any stream.
  */
 #ifndef MRSA_B200_H
@@ -147,6 +147,13 @@ int mrsa_selected_attention(const void* q, const void* k, const void* v, const u
                             int64_t batch, int64_t q_len, int64_t kv_len, int64_t kv_heads,
                             int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk,
                             mrsa_stream_t stream);
+
+/* Bit mask of device-side failures recorded since the last clear: bit 0 = a
+ * selected-attention CTA gave up waiting on one of its internal barriers (its
+ * output rows are then incomplete).  Synchronises the current device; with
+ * clear != 0 also resets the mask.  Negative on a CUDA error.  Replaces the
+ * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
+int mrsa_device_error_flags(int clear);
 
 /* out = bf16(remote + local_w * local) over rows = B*L*H, each of head_dim.
  * Replaces ops/hils_bidir_output_fusion_tilelang.py:138 fuse_hils_outputs. */

@@ -40,6 +40,7 @@ _SIGS = {
     "mrsa_selected_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _int,
                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
+    "mrsa_device_error_flags": [_int],
     "mrsa_route_layer_workspace_size": [_vp],
     "mrsa_route_layer_forward": [_vp, _vp, _sz, _vp],
     "mrsa_route_layer_forward_noalloc": [_vp, _vp],

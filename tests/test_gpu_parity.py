@@ -314,3 +314,9 @@ def test_swa_layer_matches_oracle(mrsa, dev):
     ro, rl = orc._local_rows(q, k, inp["v"], inp["key_valid"], 1280, 64, False, sl)
     close_bf16(out[:, sl], ro)
     torch.testing.assert_close(lse[:, sl].cpu(), rl, atol=5e-4, rtol=1e-5)
+
+
+def test_no_device_side_wait_gave_up(mrsa, dev):
+    """every bounded in-kernel wait of the runs above completed"""
+    torch.cuda.synchronize()
+    assert mrsa._lib.load().mrsa_device_error_flags(1) == 0
