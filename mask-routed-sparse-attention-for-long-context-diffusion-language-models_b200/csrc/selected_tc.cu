@@ -11,17 +11,25 @@
 // O^T in tensor memory: TMEM lane = output dim (128 lanes), column 8*q + g =
 // (query, head).  The CTA walks the union of its queries' chunk lists; per
 // chunk the queries that selected it ("owners", up to 8 per work item) are
-// compacted into the rows of one MMA tile:
+// gathered into the rows of one MMA tile:
 //   S[64 x 64]        = Q_own[64 x 128] . K_c^T         (UMMA M=64,  N=64)
 //   P                 = per-row softmax of S times the route weight (hi + lo)
 //   O_part^T[128 x N] = V_c^T[128 x 64] . P^T           (UMMA M=128, N=8*owners)
 //   O^T[:, 8q..8q+7] += O_part^T[:, 8j..8j+7]           (TMEM read-modify-write)
-// Warp roles: 0-3 and 4-7 are two groups that take alternate work items
-// (softmax with TMEM lane = S row, then the read-modify-write with TMEM lane
-// = dim; the read-modify-writes are chained item by item); warp 8 is the
-// loader (owner compaction + TMA of K, V and the owners' Q rows into
-// 128-byte-swizzled tiles, three stages); warp 9 issues the MMAs.  Every
-// mbarrier wait is bounded and a shared abort flag unwinds all roles.
+// The tensor pipe retires about one MMA instruction per 44 cycles for these
+// small shapes, so an item costs 16 MMAs (8 for S, 4 hi + 4 lo for P.V) and
+// everything else runs beside it:
+//   warps 0-3   accumulate: the read-modify-write of every item, in order,
+//               one quadrant of output dims each; then the epilogue;
+//   warps 4-11  softmax, two groups of four taking alternate items; each S row
+//               is read by two threads (32 columns each) with 16x32bx2 loads;
+//   warp 12     loader: owner lists into an item ring, TMA of the K and V tile
+//               (one 4-D box each) and of each owner's 8 query rows (3-D box);
+//   warp 13     MMA issue (one thread), descriptors hoisted per item.
+// Owner j of an item goes to S row slot 2*(j%4) + j/4, so the first four
+// owners land in four different TMEM quadrants and four softmax warps share
+// the rows.  Every mbarrier wait is bounded and a shared abort flag unwinds all
+// roles; an aborted CTA waits (bounded) for its own copies and MMAs in flight.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -38,30 +46,37 @@ constexpr int QB = 32;            // queries per CTA (== warp size: one loader l
 constexpr int GMAX = 8;           // head rows per query in the MMA tile
 constexpr int OWN = 8;            // owners per work item (64 S rows)
 constexpr int NST = 3;            // load stages
+constexpr int RING = 8;           // item-ring entries (>= NST + 3)
 constexpr int D = kHeadDim, S = kChunk, KMAX = 32;
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 448;
+constexpr int W_SMX = 4, W_LOAD = 12, W_MMA = 13;
 constexpr int kAccCols = QB * GMAX;          // 256
 constexpr int kSCol = 256, kPCol = 384;      // S[2] at 256/320, partial[2] at 384/448
 
+struct Item {
+  int n;                          // owners
+  int u;                          // union index (key mask)
+  uint8_t oq[OWN];                // owner query (CTA-local), compact order
+  uint8_t slot[OWN];              // owner's slot in its chunk list (route weight)
+};
+
 struct __align__(1024) TcSmem {
-  unsigned char kt[NST][16384];   // K tile: 2 sub-tiles [64 keys x 64 dims] (K-major SW128)
+  unsigned char kt[NST][16384];   // K tile: [half][64 keys][64 dims], 128-byte swizzled
   unsigned char vt[NST][16384];   // V tile, same layout, read as V^T (MN-major)
-  unsigned char at[NST][16384];   // owner Q rows: 2 sub-tiles [64 rows x 64 dims]
-  unsigned char ph[2][8192];      // P hi: [64 rows x 64 keys]
+  unsigned char at[NST][16384];   // owner Q rows: 8 slots x [half][8 rows][64 dims]
+  unsigned char ph[2][8192];      // P hi: [64 rows x 64 keys], row 8j+g = owner j head g
   unsigned char pl[2][8192];      // P lo
-  __nv_bfloat16 w[QB][GMAX][KMAX];
-  int idx[QB][KMAX + 1];          // padded: lane-per-query reads are bank-conflict free
-  int ulist[QB * KMAX];
+  float w[QB][GMAX][KMAX];        // route weights; a chunk's repeats summed into its first slot
   unsigned long long vmask[QB * KMAX];   // per union chunk: bit s = key s usable
-  unsigned long long kvmask[NST];
-  int item_own_q[NST][OWN];       // owner query (CTA-local) per compact group
-  int item_own_slot[NST][OWN];
-  int item_n[NST];
-  uint64_t bar_full[NST], bar_kvfree[NST], bar_sdone[2], bar_pready[2], bar_pvdone[2], bar_rmw[2];
+  int2 ulist[QB * KMAX];          // per union chunk: (chunk, owner-query mask)
+  Item ring[RING];
+  uint64_t bar_full[NST], bar_free[NST], bar_sdone[2], bar_pready[2], bar_pvdone[2], bar_partfree[2];
+  uint64_t bar_ring[RING], bar_mma_drain;
   uint32_t tmem_base;
   int nu, n_items, abort_flag;
-  uint32_t bitmap[64];            // C <= 2048 chunks
 };
+// one CTA per SM: the tile set plus 1 KB of alignment slack fits the 227 KB opt-in limit
+static_assert(sizeof(TcSmem) + 1024 <= 232448, "selected-attention shared memory over budget");
 
 struct TcArgs {
   const __nv_bfloat16* w;
@@ -82,15 +97,27 @@ __device__ int g_tc_error;
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ int swz_off(int row, int piece) { return row * 128 + ((piece ^ (row & 7)) << 4); }
 
+__device__ __forceinline__ bool aborted(TcSmem& sm) { return *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0; }
+
 __device__ __forceinline__ bool wait_bar(TcSmem& sm, uint64_t* bar, uint32_t parity) {
   // bounded wait that also gives up when another role has aborted
   for (int round = 0; round < 4000; ++round) {
     if (tc::mbar_wait(su32(bar), parity, 1000u)) return true;
-    if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) return false;
+    if (aborted(sm)) return false;
   }
   *reinterpret_cast<volatile int*>(&sm.abort_flag) = 1;
   return false;
 }
+
+// The same wait taken by a whole warp: every lane gets the same answer, so the
+// warp stays converged for the collective operations that follow.
+__device__ __forceinline__ bool wait_bar_warp(TcSmem& sm, uint64_t* bar, uint32_t parity) {
+  const bool ok = wait_bar(sm, bar, parity);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// UMMA descriptor start-address field advance for a byte offset.
+__device__ __forceinline__ uint64_t adv(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
 
 __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -101,10 +128,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   const int hk = blockIdx.y, b = blockIdx.z;
   const int64_t q0 = static_cast<int64_t>(blockIdx.x) * QB;
   const int G = a.G, K = a.K, C = a.C, Hq = a.Hkv * a.G;
-  const int nwords = (C + 31) >> 5;
+  // set-up tables live in the Q staging area, which is idle until the loader starts:
+  // per-chunk owner masks, and the chunk lists (read once more by the loader)
+  uint32_t* ownmask = reinterpret_cast<uint32_t*>(&sm.at[0][0]);
+  int (*idx)[KMAX + 1] = reinterpret_cast<int (*)[KMAX + 1]>(&sm.at[1][0]);
 
   // ---------------- set-up: chunk lists, weights, union of chunks ----------
-  for (int e = tid; e < 64; e += NTHREADS) sm.bitmap[e] = 0u;
+  if (warp == W_LOAD && lane == 0) {
+    tc::prefetch_tensormap(&tm_k);
+    tc::prefetch_tensormap(&tm_v);
+    tc::prefetch_tensormap(&tm_q);
+  }
+  for (int e = tid; e < C; e += NTHREADS) ownmask[e] = 0u;
   for (int e = tid; e < QB * KMAX; e += NTHREADS) {
     const int qi = e / KMAX, kk = e % KMAX;
     int c = -1;
@@ -112,25 +147,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       c = a.indices[((b * a.Lq + q0 + qi) * a.Hkv + hk) * K + kk];
       if (c >= C) c = -1;
     }
-    sm.idx[qi][kk] = c < 0 ? -1 : c;
+    idx[qi][kk] = c < 0 ? -1 : c;
   }
   for (int e = tid; e < QB * GMAX * KMAX; e += NTHREADS) {
     const int qi = e / (GMAX * KMAX), g = (e / KMAX) % GMAX, kk = e % KMAX;
-    __nv_bfloat16 wv = f2bf(0.f);
-    if (g < G && kk < K && q0 + qi < a.Lq) wv = a.w[((b * a.Lq + q0 + qi) * Hq + hk * G + g) * K + kk];
+    float wv = 0.f;
+    if (g < G && kk < K && q0 + qi < a.Lq) wv = bf2f(a.w[((b * a.Lq + q0 + qi) * Hq + hk * G + g) * K + kk]);
     sm.w[qi][g][kk] = wv;
   }
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
       tc::mbar_init(su32(&sm.bar_full[s]), 1);
-      tc::mbar_init(su32(&sm.bar_kvfree[s]), 1);
+      tc::mbar_init(su32(&sm.bar_free[s]), 1);
     }
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(su32(&sm.bar_sdone[s]), 1);
       tc::mbar_init(su32(&sm.bar_pready[s]), 4);
       tc::mbar_init(su32(&sm.bar_pvdone[s]), 1);
-      tc::mbar_init(su32(&sm.bar_rmw[s]), 4);
+      tc::mbar_init(su32(&sm.bar_partfree[s]), 4);
     }
+    for (int r = 0; r < RING; ++r) tc::mbar_init(su32(&sm.bar_ring[r]), 1);
+    tc::mbar_init(su32(&sm.bar_mma_drain), 1);
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -139,39 +176,39 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     tc::tmem_relinquish();
   }
   __syncthreads();
+  // A chunk listed more than once by a query: the slots share one softmax, so
+  // their weights are summed (in slot order) into the first slot.
   for (int e = tid; e < QB * KMAX; e += NTHREADS) {
-    const int c = sm.idx[e / KMAX][e % KMAX];
-    if (c >= 0) atomicOr(&sm.bitmap[c >> 5], 1u << (c & 31));
+    const int qi = e / KMAX, kk = e % KMAX, c = idx[qi][kk];
+    bool first = c >= 0;
+    for (int k2 = 0; k2 < kk && first; ++k2) first = idx[qi][k2] != c;
+    if (!first) continue;
+    for (int k2 = kk + 1; k2 < KMAX; ++k2) {
+      if (idx[qi][k2] != c) continue;
+      for (int g = 0; g < G; ++g) sm.w[qi][g][kk] += sm.w[qi][g][k2];
+    }
   }
   __syncthreads();
-  if (warp == 8) {
-    // compact the union bitmap into an ascending chunk list, then count work items
-    int base = 0;
-    for (int wb = 0; wb < nwords; wb += 32) {
-      const uint32_t word = (wb + lane < nwords) ? sm.bitmap[wb + lane] : 0u;
-      const int cnt = __popc(word);
-      int incl = cnt;
+  // owner mask per chunk (the loader picks each query's first slot of a chunk)
+  for (int e = tid; e < QB * KMAX; e += NTHREADS) {
+    const int c = idx[e / KMAX][e % KMAX];
+    if (c >= 0) atomicOr(&ownmask[c], 1u << (e / KMAX));
+  }
+  __syncthreads();
+  if (warp == W_LOAD) {
+    // compact into an ascending (chunk, owners) list and count work items
+    int base = 0, items = 0;
+    for (int c0 = 0; c0 < C; c0 += 32) {
+      const uint32_t m = c0 + lane < C ? ownmask[c0 + lane] : 0u;
+      const uint32_t nz = __ballot_sync(0xffffffffu, m != 0u);
+      if (m != 0u) {
+        sm.ulist[base + __popc(nz & ((1u << lane) - 1u))] = make_int2(c0 + lane, static_cast<int>(m));
+        items += (__popc(m) + OWN - 1) / OWN;
+      }
+      base += __popc(nz);
+    }
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      int pos = base + incl - cnt;
-      uint32_t bits = word;
-      while (bits) {
-        sm.ulist[pos++] = ((wb + lane) << 5) + (__ffs(bits) - 1);
-        bits &= bits - 1;
-      }
-      base += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    __syncwarp();
-    int items = 0;
-    for (int u = 0; u < base; ++u) {
-      const int c = sm.ulist[u];
-      bool own = false;
-      for (int kk = 0; kk < K; ++kk) own |= sm.idx[lane][kk] == c;   // K <= 32
-      items += (__popc(__ballot_sync(0xffffffffu, own)) + OWN - 1) / OWN;
-    }
+    for (int o = 16; o > 0; o >>= 1) items += __shfl_xor_sync(0xffffffffu, items, o);
     if (lane == 0) {
       sm.nu = base;
       sm.n_items = items;
@@ -183,7 +220,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   __syncthreads();
   for (int e = tid; e < sm.nu * 4; e += NTHREADS) {
     const int u = e >> 2, qt = e & 3;
-    const int64_t j0 = static_cast<int64_t>(sm.ulist[u]) * S + qt * 16;
+    const int64_t j0 = static_cast<int64_t>(sm.ulist[u].x) * S + qt * 16;
     unsigned long long m = 0xFFFFull;
     if (a.key_valid != nullptr) {
       const uint4 raw = *reinterpret_cast<const uint4*>(a.key_valid + b * a.Lk + j0);
@@ -203,25 +240,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     for (int c = 0; c < kAccCols; c += 8) tc::tmem_st8(tbase + lane_off + c, z);
     tc::tmem_wait_st();
   }
+  tc::fence_proxy_async();                   // set-up writes to the staging area precede TMA writes
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const int n_items = sm.n_items;
   const float sl2 = a.sm_scale * kLog2e;
 
-  if (warp == 8) {
+  if (warp == W_LOAD) {
     // ============================ loader =====================================
+    int myc[KMAX];                           // this lane's (query's) chunk list
+#pragma unroll
+    for (int kk = 0; kk < KMAX; ++kk) myc[kk] = idx[lane][kk];
+    tc::fence_proxy_async();                 // these reads precede TMA writes to the same area
     int item = 0;
-    for (int u = 0; u < sm.nu && item < n_items; ++u) {
-      const int c = sm.ulist[u];
-      int my_slot = -1;
-      for (int kk = 0; kk < K; ++kk)
-        if (my_slot < 0 && sm.idx[lane][kk] == c) my_slot = kk;
-      uint32_t owners = __ballot_sync(0xffffffffu, my_slot >= 0);
+    bool ok = true;
+    for (int u = 0; ok && u < sm.nu; ++u) {
+      const int2 ue = sm.ulist[u];
+      const int c = ue.x;
+      uint32_t owners = static_cast<uint32_t>(ue.y);
+      int my_slot = 0;
+#pragma unroll
+      for (int kk = KMAX - 1; kk >= 0; --kk) my_slot = myc[kk] == c ? kk : my_slot;
       while (owners) {
-        const int ls = item % NST;
-        if (item >= NST && !wait_bar(sm, &sm.bar_kvfree[ls], ((item - NST) / NST) & 1)) {
-          u = sm.nu;
+        const int st = item % NST, r = item % RING;
+        if (item >= NST && !wait_bar_warp(sm, &sm.bar_free[st], ((item / NST) - 1) & 1)) {
+          ok = false;
           break;
         }
         int n = 0;
@@ -229,143 +273,176 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         for (uint32_t m = owners; m && n < OWN; m &= m - 1, ++n) grp |= m & (~m + 1);
         owners &= ~grp;
         const bool mine = (grp >> lane) & 1u;
-        const int pos = __popc(grp & ((1u << lane) - 1u));
+        const int j = __popc(grp & ((1u << lane) - 1u));
         if (mine) {
-          sm.item_own_q[ls][pos] = lane;
-          sm.item_own_slot[ls][pos] = my_slot;
+          sm.ring[r].oq[j] = static_cast<uint8_t>(lane);
+          sm.ring[r].slot[j] = static_cast<uint8_t>(my_slot);
         }
-        const int64_t j0 = static_cast<int64_t>(c) * S;
         if (lane == 0) {
-          sm.item_n[ls] = n;
-          sm.kvmask[ls] = sm.vmask[u];
+          sm.ring[r].n = n;
+          sm.ring[r].u = u;
         }
         __syncwarp();
+        const uint32_t bar = su32(&sm.bar_full[st]);
         if (lane == 0) {
-          const uint32_t bar = su32(&sm.bar_full[ls]);
+          tc::mbar_arrive(su32(&sm.bar_ring[r]));
           tc::mbar_arrive_expect_tx(bar, 2u * 16384u + static_cast<uint32_t>(n) * 2048u);
-          const int ky = static_cast<int>(b * a.Lk + j0);
-          for (int h = 0; h < 2; ++h) {
-            tc::tma_load_2d(su32(sm.kt[ls] + h * 8192), &tm_k, hk * D + 64 * h, ky, bar);
-            tc::tma_load_2d(su32(sm.vt[ls] + h * 8192), &tm_v, hk * D + 64 * h, ky, bar);
-          }
-          for (int j = 0; j < n; ++j) {
-            const int qy = static_cast<int>((b * a.Lq + q0 + sm.item_own_q[ls][j]) * Hq + hk * G);
-            for (int h = 0; h < 2; ++h)
-              tc::tma_load_2d(su32(sm.at[ls] + h * 8192 + j * 1024), &tm_q, 64 * h, qy, bar);
-          }
+          const int ky = static_cast<int>(b * a.Lk + static_cast<int64_t>(c) * S);
+          tc::tma_load_4d(su32(sm.kt[st]), &tm_k, 0, ky, 0, hk, bar);
+          tc::tma_load_4d(su32(sm.vt[st]), &tm_v, 0, ky, 0, hk, bar);
+        }
+        __syncwarp();
+        if (mine) {
+          const int slot = 2 * (j & 3) + (j >> 2);
+          const int qy = static_cast<int>((b * a.Lq + q0 + lane) * Hq + hk * G);
+          tc::tma_load_3d(su32(sm.at[st] + slot * 2048), &tm_q, 0, qy, 0, bar);
         }
         ++item;
       }
     }
-  } else if (warp == 9) {
+    // wait (bounded, even after an abort) for this CTA's copies in flight
+    if (lane == 0) {
+      for (int it = item - NST < 0 ? 0 : item - NST; it < item; ++it)
+        tc::mbar_wait(su32(&sm.bar_full[it % NST]), (it / NST) & 1);
+    }
+    __syncwarp();
+  } else if (warp == W_MMA) {
     // ============================ MMA issue ==================================
     if (lane == 0) {
-      const uint32_t id_s = tc::idesc_bf16_f32(64, 64, 0, 0);
+      constexpr uint32_t id_s = tc::idesc_bf16_f32(64, 64, 0, 0);
+      const uint64_t dq0 = tc::smem_desc_sw128(su32(sm.at[0]), 16, 2048);
+      const uint64_t dk0 = tc::smem_desc_sw128(su32(sm.kt[0]), 16, 1024);
+      const uint64_t dv0 = tc::smem_desc_sw128(su32(sm.vt[0]), 8192, 1024);
+      const uint64_t dh0 = tc::smem_desc_sw128(su32(sm.ph[0]), 16, 1024);
+      const uint64_t dl0 = tc::smem_desc_sw128(su32(sm.pl[0]), 16, 1024);
       auto issue_s = [&](int it) -> bool {
-        const int ls = it % NST, s2 = it & 1;
-        if (!wait_bar(sm, &sm.bar_full[ls], (it / NST) & 1)) return false;
+        const int st = it % NST, s2 = it & 1;
+        if (!wait_bar(sm, &sm.bar_full[st], (it / NST) & 1)) return false;
         tc::fence_after_sync();
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = tc::smem_desc_sw128(su32(sm.at[ls] + (kk >> 2) * 8192 + (kk & 3) * 32), 16, 1024);
-          const uint64_t bd = tc::smem_desc_sw128(su32(sm.kt[ls] + (kk >> 2) * 8192 + (kk & 3) * 32), 16, 1024);
-          tc::mma_bf16_ss(tbase + kSCol + 64 * s2, ad, bd, id_s, kk > 0);
-        }
+        const uint64_t da = adv(dq0, st * 16384), db = adv(dk0, st * 16384);
+        const uint32_t dS = tbase + kSCol + 64 * s2;
+        tc::mma_bf16<false>(dS, da, db, id_s);
+#pragma unroll
+        for (int kk = 1; kk < 8; ++kk)
+          tc::mma_bf16<true>(dS, adv(da, (kk >> 2) * 1024 + (kk & 3) * 32), adv(db, (kk >> 2) * 8192 + (kk & 3) * 32),
+                             id_s);
         tc::mma_commit(su32(&sm.bar_sdone[s2]));
         return true;
       };
       bool ok = true;
       for (int it = 0; ok && it < n_items && it < 2; ++it) ok = issue_s(it);
       for (int it = 0; ok && it < n_items; ++it) {
-        const int ls = it % NST, s2 = it & 1;
+        const int st = it % NST, s2 = it & 1;
         if (!wait_bar(sm, &sm.bar_pready[s2], (it >> 1) & 1)) break;
+        if (it >= 2 && !wait_bar(sm, &sm.bar_partfree[s2], ((it >> 1) - 1) & 1)) break;
         tc::fence_after_sync();
-        const int np = ((8 * sm.item_n[ls] + 15) / 16) * 16;
+        const int np = ((8 * sm.ring[it % RING].n + 15) / 16) * 16;
         const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
-        for (int part = 0; part < 2; ++part) {
-          const unsigned char* pt = part ? sm.pl[s2] : sm.ph[s2];
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = tc::smem_desc_sw128(su32(sm.vt[ls] + kk * 2048), 8192, 1024);
-            const uint64_t bd = tc::smem_desc_sw128(su32(pt + kk * 32), 16, 1024);
-            tc::mma_bf16_ss(tbase + kPCol + 64 * s2, ad, bd, id_o, part > 0 || kk > 0);
-          }
-        }
+        const uint64_t dv = adv(dv0, st * 16384), dh = adv(dh0, s2 * 8192), dl = adv(dl0, s2 * 8192);
+        const uint32_t dP = tbase + kPCol + 64 * s2;
+        tc::mma_bf16<false>(dP, dv, dh, id_o);
+#pragma unroll
+        for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dh, kk * 32), id_o);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
         tc::mma_commit(su32(&sm.bar_pvdone[s2]));
-        tc::mma_commit(su32(&sm.bar_kvfree[ls]));
+        tc::mma_commit(su32(&sm.bar_free[st]));
         if (it + 2 < n_items) ok = issue_s(it + 2);
       }
+      // every MMA issued by this thread has completed once this phase lands
+      tc::mma_commit(su32(&sm.bar_mma_drain));
+      tc::mbar_wait(su32(&sm.bar_mma_drain), 0);
     }
     __syncwarp();
-  } else {
-    // ============================ item groups (warps 0-3, 4-7) ===============
-    const int grp = warp >> 2, wq = warp & 3;
-    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const int row = wq * 16 + lane;          // S row of this thread's TMEM lane (M=64 layout)
+  } else if (warp >= W_SMX) {
+    // ============================ softmax (warps 4-7, 8-11) ==================
+    const int grp = (warp - W_SMX) >> 2, q = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int t = lane & 15, hf = lane >> 4;
+    const int jrow = t < 8 ? q : q + 4;      // owner (compact index) of this thread's row
+    const int g = t & 7;
     for (int it = grp; it < n_items; it += 2) {
-      const int ls = it % NST, s2 = it & 1;
-      if (!wait_bar(sm, &sm.bar_sdone[s2], (it >> 1) & 1)) break;
+      const int s2 = it & 1, r = it % RING;
+      if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
+      const int n = sm.ring[r].n;
+      const bool row_on = jrow < n;
+      float w = 0.f;
+      uint32_t km = 0u;
+      if (row_on) {
+        if (g < G) w = sm.w[sm.ring[r].oq[jrow]][g][sm.ring[r].slot[jrow]];
+        const unsigned long long vm = sm.vmask[sm.ring[r].u];
+        km = static_cast<uint32_t>(hf ? (vm >> 32) : vm);
+      }
+      if (!wait_bar_warp(sm, &sm.bar_sdone[s2], (it >> 1) & 1)) break;
       tc::fence_after_sync();
-      const int n = sm.item_n[ls];
-      int oq[OWN];
-#pragma unroll
-      for (int j = 0; j < OWN; ++j) oq[j] = j < n ? sm.item_own_q[ls][j] : 0;
-      // ---- softmax: one S row per thread (lanes 0-15 of each warp) ----
-      if (wq * 16 < 8 * n) {
-        uint32_t r[64];
-#pragma unroll
-        for (int c = 0; c < 64; c += 16)
-          tc::tmem_ld16(tbase + lane_off + kSCol + 64 * s2 + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
+      uint32_t x[32];
+      if (q < n) {                           // warp-uniform: this quadrant holds rows
+        tc::tmem_ld_16x32bx2_x32(tbase + lane_off + kSCol + 64 * s2, x);
         tc::tmem_wait_ld();
-        const int j = row >> 3, g = row & 7;
-        if (lane < 16 && j < n && g < G) {
-          const float w = bf2f(sm.w[sm.item_own_q[ls][j]][g][sm.item_own_slot[ls][j]]);
-          const unsigned long long km = sm.kvmask[ls];
-          const uint32_t km_lo = static_cast<uint32_t>(km), km_hi = static_cast<uint32_t>(km >> 32);
-          float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      } else {
 #pragma unroll
-          for (int t = 0; t < 64; ++t) {
-            const uint32_t bit = t < 32 ? (km_lo >> t) & 1u : (km_hi >> (t - 32)) & 1u;
-            const float x = bit ? __uint_as_float(r[t]) * sl2 : -INFINITY;
-            r[t] = __float_as_uint(x);
-            mx4[t & 3] = fmaxf(mx4[t & 3], x);
-          }
-          const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-          const float base = mx == -INFINITY ? 0.f : mx;
-          float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < 32; ++c) x[c] = 0u;
+      }
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int t = 0; t < 64; ++t) {
-            const float e = fast_exp2(__uint_as_float(r[t]) - base);   // masked keys: 2^-inf = 0
-            r[t] = __float_as_uint(e);
-            sum4[t & 3] += e;
-          }
-          const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-          const float f = sum > 0.f ? w / sum : 0.f;
-          uint32_t hi[32], lo[32];
+      for (int c = 0; c < 32; ++c) {
+        const float v = ((km >> c) & 1u) ? __uint_as_float(x[c]) * sl2 : -INFINITY;
+        x[c] = __float_as_uint(v);
+        mx4[c & 3] = fmaxf(mx4[c & 3], v);
+      }
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float base = mx == -INFINITY ? 0.f : mx;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int h = 0; h < 32; ++h) {
-            const float p0 = __uint_as_float(r[2 * h]) * f;
-            const float p1 = __uint_as_float(r[2 * h + 1]) * f;
-            hi[h] = pack_bf16x2(p0, p1);
-            lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
-          }
+      for (int c = 0; c < 32; ++c) {
+        const float e = fast_exp2(__uint_as_float(x[c]) - base);   // masked keys: 2^-inf = 0
+        x[c] = __float_as_uint(e);
+        sum4[c & 3] += e;
+      }
+      float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+      const float f = sum > 0.f ? w / sum : 0.f;
+      uint32_t hi[16], lo[16];
 #pragma unroll
-          for (int p = 0; p < 8; ++p) {
-            *reinterpret_cast<uint4*>(sm.ph[s2] + swz_off(row, p)) =
-                make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
-            *reinterpret_cast<uint4*>(sm.pl[s2] + swz_off(row, p)) =
-                make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
-          }
+      for (int h = 0; h < 16; ++h) {
+        const float p0 = __uint_as_float(x[2 * h]) * f;
+        const float p1 = __uint_as_float(x[2 * h + 1]) * f;
+        hi[h] = pack_bf16x2(p0, p1);
+        lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+      }
+      // the P buffer is free once the P.V of item it-2 has completed
+      if (it >= 2 && !wait_bar_warp(sm, &sm.bar_pvdone[s2], ((it >> 1) - 1) & 1)) break;
+      if (row_on) {
+        const int row = 8 * jrow + g;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          *reinterpret_cast<uint4*>(sm.ph[s2] + swz_off(row, 4 * hf + p)) =
+              make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
+          *reinterpret_cast<uint4*>(sm.pl[s2] + swz_off(row, 4 * hf + p)) =
+              make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
         }
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[s2]));
-      // ---- read-modify-write of the owners' accumulator columns ----
-      if (!wait_bar(sm, &sm.bar_pvdone[s2], (it >> 1) & 1)) break;
-      if (it >= 1 && !wait_bar(sm, &sm.bar_rmw[(it - 1) & 1], ((it - 1) >> 1) & 1)) break;
-      tc::fence_after_sync();
+    }
+  } else {
+    // ============================ accumulate + epilogue (warps 0-3) ==========
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    for (int it = 0; it < n_items; ++it) {
+      const int s2 = it & 1, r = it % RING;
+      if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
+      const int n = sm.ring[r].n;
+      int oq[OWN];
 #pragma unroll
-      for (int j0 = 0; j0 < OWN; j0 += 4) {      // owners in batches of 4: loads, one wait, stores
+      for (int j = 0; j < OWN; ++j) oq[j] = sm.ring[r].oq[j];
+      if (!wait_bar_warp(sm, &sm.bar_pvdone[s2], (it >> 1) & 1)) break;
+      tc::fence_after_sync();
+      tc::tmem_wait_st();                    // previous item's accumulator stores have landed
+#pragma unroll
+      for (int j0 = 0; j0 < OWN; j0 += 4) {  // owners in batches of 4: loads, one wait, stores
         if (j0 >= n) break;
         uint32_t pv[4][8], acc[4][8];
 #pragma unroll
@@ -376,37 +453,36 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
           }
         }
         tc::tmem_wait_ld();
+        if (j0 + 4 >= n) {                   // last partial columns read: release the buffer
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(su32(&sm.bar_partfree[s2]));
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (j0 + j < n) {
 #pragma unroll
-            for (int t = 0; t < 8; ++t)
-              acc[j][t] = __float_as_uint(__uint_as_float(acc[j][t]) + __uint_as_float(pv[j][t]));
+            for (int c = 0; c < 8; ++c)
+              acc[j][c] = __float_as_uint(__uint_as_float(acc[j][c]) + __uint_as_float(pv[j][c]));
             tc::tmem_st8(tbase + lane_off + 8 * oq[j0 + j], acc[j]);
           }
         }
       }
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_rmw[s2]));
     }
-    // ---- epilogue: after every item's accumulate, each group writes 16 queries
-    asm volatile("bar.sync 1, 256;\n" ::: "memory");
-    tc::fence_after_sync();
-    if (!*reinterpret_cast<volatile int*>(&sm.abort_flag)) {
-      const int d = wq * 32 + lane;
-      for (int qi = grp * 16; qi < grp * 16 + 16; ++qi) {
+    tc::tmem_wait_st();
+    if (!__any_sync(0xffffffffu, aborted(sm))) {
+      const int d = warp * 32 + lane;
+      for (int qi = 0; qi < QB; ++qi) {
         const int64_t rowq = q0 + qi;
         uint32_t acc[8];
         tc::tmem_ld8(tbase + lane_off + 8 * qi, acc);
         tc::tmem_wait_ld();
         if (rowq >= a.Lq) continue;
-        for (int g = 0; g < G; ++g) {
-          const int64_t o = ((b * a.Lq + rowq) * Hq + hk * G + g) * (int64_t)D + d;
-          float r = round_bf16(__uint_as_float(acc[g]));
-          if (a.local_out) r += bf2f(a.local_w[(b * a.Lq + rowq) * Hq + hk * G + g]) * bf2f(a.local_out[o]);
-          a.out[o] = f2bf(r);
+        for (int gg = 0; gg < G; ++gg) {
+          const int64_t o = ((b * a.Lq + rowq) * Hq + hk * G + gg) * (int64_t)D + d;
+          float v = round_bf16(__uint_as_float(acc[gg]));
+          if (a.local_out) v += bf2f(a.local_w[(b * a.Lq + rowq) * Hq + hk * G + gg]) * bf2f(a.local_out[o]);
+          a.out[o] = f2bf(v);
         }
       }
     }
@@ -426,10 +502,9 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
-// 2-D bf16 tensor map over a row-major [rows x cols] matrix with row stride
-// `stride` elements, box [box_cols x box_rows], 128-byte swizzle.
-bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t stride,
-              uint32_t box_cols, uint32_t box_rows) {
+// bf16 tensor map with 128-byte swizzle over `rank` dims (innermost first).
+bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+              const cuuint32_t* box) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -438,12 +513,9 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, ui
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
   if (g_encode == nullptr) return false;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {stride * 2};
-  const cuuint32_t box[2] = {box_cols, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
+                  strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -468,11 +540,17 @@ extern "C" int mrsa_selected_attention(const void* q, const void* k, const void*
       (local_out && !aligned16(local_out)) || (key_valid && !aligned16(key_valid)))
     return MRSA_ERR_ALIGN;
   if (q_len == 0) return MRSA_OK;
+  // K, V: [B*Lk rows][Hkv*128] viewed as (dim-in-half, row, half, head): one box = one chunk tile.
+  // Q: [B*Lq*Hq rows][128] viewed as (dim-in-half, row, half): one box = 8 rows of one query.
   CUtensorMap tm_k, tm_v, tm_q;
-  const uint64_t hq = static_cast<uint64_t>(kv_heads * groups);
-  if (!make_map(&tm_k, k, kv_heads * D, batch * kv_len, kv_heads * D, 64, 64) ||
-      !make_map(&tm_v, v, kv_heads * D, batch * kv_len, kv_heads * D, 64, 64) ||
-      !make_map(&tm_q, q, D, batch * q_len * hq, D, 64, 8))
+  const cuuint64_t kv_dims[4] = {64, static_cast<cuuint64_t>(batch * kv_len), 2, static_cast<cuuint64_t>(kv_heads)};
+  const cuuint64_t kv_str[3] = {static_cast<cuuint64_t>(kv_heads * D * 2), 128, 256};
+  const cuuint32_t kv_box[4] = {64, 64, 2, 1};
+  const cuuint64_t q_dims[3] = {64, static_cast<cuuint64_t>(batch * q_len * kv_heads * groups), 2};
+  const cuuint64_t q_str[2] = {256, 128};
+  const cuuint32_t q_box[3] = {64, 8, 2};
+  if (!make_map(&tm_k, k, 4, kv_dims, kv_str, kv_box) || !make_map(&tm_v, v, 4, kv_dims, kv_str, kv_box) ||
+      !make_map(&tm_q, q, 3, q_dims, q_str, q_box))
     return MRSA_ERR_LAUNCH;
   TcArgs a;
   a.w = static_cast<const __nv_bfloat16*>(weights);

@@ -187,6 +187,44 @@ def test_selected_with_invalid_keys_matches_oracle(mrsa, dev):
     assert torch.equal(out[:, 0].cpu(), torch.zeros_like(out[:, 0].cpu()))
 
 
+@pytest.mark.parametrize("g,topk,lq", [(7, 32, 1000), (8, 13, 777), (3, 32, 96)])
+def test_selected_random_routing_duplicates_ragged(mrsa, dev, g, topk, lq):
+    """random chunk lists with empty (-1) and repeated slots, a query length that
+    is not a multiple of the 32-query block, batch 2, several group sizes; the
+    oracle (``hils_torch_ref`` semantics) counts a repeated chunk once per slot"""
+    gen = torch.Generator().manual_seed(1000 * g + topk)
+    b, lk, hkv, d = 2, 2048, 2, 128
+    c = lk // 64
+    q = torch.randn(b, lq, hkv * g, d, generator=gen).bfloat16()
+    k = torch.randn(b, lk, hkv, d, generator=gen).bfloat16()
+    v = torch.randn(b, lk, hkv, d, generator=gen).bfloat16()
+    idx = torch.randint(0, c, (b, lq, hkv, topk), generator=gen, dtype=torch.int32)
+    idx[torch.rand(idx.shape, generator=gen) < 0.1] = -1
+    idx[:, ::5, :, 1] = idx[:, ::5, :, 0]                    # repeated chunk in a query's list
+    idx[:, ::7, :, -1] = idx[:, ::7, :, 0]
+    w = torch.rand(b, lq, hkv * g, topk, generator=gen).bfloat16()
+    valid = torch.rand(b, lk, generator=gen) > 0.05
+    out = mrsa.selected_attention(q.to(dev), k.to(dev), v.to(dev), w.to(dev), idx.to(dev), valid.to(dev))
+    rows = torch.unique(torch.cat([torch.arange(0, lq, 37), torch.tensor([lq - 1, 0, 5, 35])]))
+    ref = orc.selected_attention(q[:, rows], k, v, w[:, rows], idx[:, rows], valid, 64, block=16)
+    close_bf16(out[:, rows.to(dev)], ref)
+
+
+def test_selected_all_queries_same_chunks(mrsa, dev):
+    """every query of a block selects the same chunks: items of 8 owners, 4 per chunk"""
+    gen = torch.Generator().manual_seed(5)
+    lq, lk, hkv, g, d, topk = 256, 4096, 4, 7, 128, 32
+    q = torch.randn(1, lq, hkv * g, d, generator=gen).bfloat16()
+    k = torch.randn(1, lk, hkv, d, generator=gen).bfloat16()
+    v = torch.randn(1, lk, hkv, d, generator=gen).bfloat16()
+    idx = (torch.arange(topk, dtype=torch.int32) * 2).expand(1, lq, hkv, -1).contiguous()
+    w = torch.randn(1, lq, hkv * g, topk, generator=gen).softmax(-1).bfloat16()
+    out = mrsa.selected_attention(q.to(dev), k.to(dev), v.to(dev), w.to(dev), idx.to(dev))
+    rows = torch.tensor([0, 31, 32, 100, 255])
+    ref = orc.selected_attention(q[:, rows], k, v, w[:, rows], idx[:, rows], None, 64, block=8)
+    close_bf16(out[:, rows.to(dev)], ref)
+
+
 @pytest.mark.parametrize("window,skip", [(256, True), (1280, False), (40, True)])
 def test_local_attention_matches_oracle(mrsa, dev, window, skip):
     gen = torch.Generator().manual_seed(window)
