@@ -16,16 +16,22 @@
 //   P                 = per-row softmax of S times the route weight (hi + lo)
 //   O_part^T[128 x N] = V_c^T[128 x 64] . P^T           (UMMA M=128, N=8*owners)
 //   O^T[:, 8q..8q+7] += O_part^T[:, 8j..8j+7]           (TMEM read-modify-write)
-// The tensor pipe retires about one MMA instruction per 44 cycles for these
-// small shapes, so an item costs 16 MMAs (8 for S, 4 hi + 4 lo for P.V) and
-// everything else runs beside it:
+// For these small shapes the tensor pipe retires about one MMA instruction per
+// 44 cycles (its shared-memory operand reads), so an item costs 16 MMAs and the
+// rest of the work runs beside them in a pipeline three items deep:
 //   warps 0-3   accumulate: the read-modify-write of every item, in order,
 //               one quadrant of output dims each; then the epilogue;
 //   warps 4-11  softmax, two groups of four taking alternate items; each S row
 //               is read by two threads (32 columns each) with 16x32bx2 loads;
-//   warp 12     loader: owner lists into an item ring, TMA of the K and V tile
-//               (one 4-D box each) and of each owner's 8 query rows (3-D box);
-//   warp 13     MMA issue (one thread), descriptors hoisted per item.
+//   warp 12     K/Q loader: owner lists into an item ring, TMA of the K tile
+//               (one 4-D box) and each owner's 8 query rows (3-D box); its
+//               stages are released when the item's S MMAs complete;
+//   warp 13     V loader: TMA of the V tile, stages released after P.V;
+//   warp 14     MMA issue: the warp stays converged and one elected lane
+//               issues (about a third cheaper than issuing from a lone lane).
+// TMEM: accumulators in columns 0-255, then four 64-column buffers; item i's S
+// lands in buffer i%4 and its P.V partial overwrites the same columns once the
+// softmax has read them, so S can run three items ahead of P.V.
 // Owner j of an item goes to S row slot 2*(j%4) + j/4, so the first four
 // owners land in four different TMEM quadrants and four softmax warps share
 // the rows.  Every mbarrier wait is bounded and a shared abort flag unwinds all
@@ -45,32 +51,35 @@ namespace {
 constexpr int QB = 32;            // queries per CTA (== warp size: one loader lane per query)
 constexpr int GMAX = 8;           // head rows per query in the MMA tile
 constexpr int OWN = 8;            // owners per work item (64 S rows)
-constexpr int NST = 3;            // load stages
-constexpr int RING = 8;           // item-ring entries (>= NST + 3)
+constexpr int NKQ = 3;            // K/Q load stages (released after S)
+constexpr int NV = 3;             // V load stages (released after P.V)
+constexpr int NBUF = 4;           // TMEM S/partial buffers; S runs NBUF-1 items ahead
+constexpr int RING = 16;          // item-ring entries
 constexpr int D = kHeadDim, S = kChunk, KMAX = 32;
-constexpr int NTHREADS = 448;
-constexpr int W_SMX = 4, W_LOAD = 12, W_MMA = 13;
+constexpr int NTHREADS = 480;
+constexpr int W_SMX = 4, W_LOADKQ = 12, W_LOADV = 13, W_MMA = 14;
 constexpr int kAccCols = QB * GMAX;          // 256
-constexpr int kSCol = 256, kPCol = 384;      // S[2] at 256/320, partial[2] at 384/448
+constexpr int kBufCol = 256;                 // buffer b at columns 256 + 64 b
 
 struct Item {
   int n;                          // owners
-  int u;                          // union index (key mask)
+  int u;                          // union index (chunk, key mask)
   uint8_t oq[OWN];                // owner query (CTA-local), compact order
   uint8_t slot[OWN];              // owner's slot in its chunk list (route weight)
 };
 
 struct __align__(1024) TcSmem {
-  unsigned char kt[NST][16384];   // K tile: [half][64 keys][64 dims], 128-byte swizzled
-  unsigned char vt[NST][16384];   // V tile, same layout, read as V^T (MN-major)
-  unsigned char at[NST][16384];   // owner Q rows: 8 slots x [half][8 rows][64 dims]
+  unsigned char kt[NKQ][16384];   // K tile: [half][64 keys][64 dims], 128-byte swizzled
+  unsigned char at[NKQ][16384];   // owner Q rows: 8 slots x [half][8 rows][64 dims]
+  unsigned char vt[NV][16384];    // V tile, K's layout, read as V^T (MN-major)
   unsigned char ph[2][8192];      // P hi: [64 rows x 64 keys], row 8j+g = owner j head g
   unsigned char pl[2][8192];      // P lo
   float w[QB][GMAX][KMAX];        // route weights; a chunk's repeats summed into its first slot
   unsigned long long vmask[QB * KMAX];   // per union chunk: bit s = key s usable
   int2 ulist[QB * KMAX];          // per union chunk: (chunk, owner-query mask)
   Item ring[RING];
-  uint64_t bar_full[NST], bar_free[NST], bar_sdone[2], bar_pready[2], bar_pvdone[2], bar_partfree[2];
+  uint64_t bar_kqfull[NKQ], bar_kqfree[NKQ], bar_vfull[NV], bar_vfree[NV];
+  uint64_t bar_sdone[NBUF], bar_pvdone[NBUF], bar_partfree[NBUF], bar_pready[2];
   uint64_t bar_ring[RING], bar_mma_drain;
   uint32_t tmem_base;
   int nu, n_items, abort_flag;
@@ -116,6 +125,18 @@ __device__ __forceinline__ bool wait_bar_warp(TcSmem& sm, uint64_t* bar, uint32_
   return __all_sync(0xffffffffu, ok);
 }
 
+// One lane of a converged warp (elect.sync).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 %%rx;\n\t.reg .pred %%px;\n\t"
+      "elect.sync %%rx|%%px, %1;\n\t"
+      "@%%px mov.s32 %0, 1;\n\t}\n"
+      : "+r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
+}
+
 // UMMA descriptor start-address field advance for a byte offset.
 __device__ __forceinline__ uint64_t adv(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
 
@@ -134,11 +155,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   int (*idx)[KMAX + 1] = reinterpret_cast<int (*)[KMAX + 1]>(&sm.at[1][0]);
 
   // ---------------- set-up: chunk lists, weights, union of chunks ----------
-  if (warp == W_LOAD && lane == 0) {
+  if (warp == W_LOADKQ && lane == 0) {
     tc::prefetch_tensormap(&tm_k);
-    tc::prefetch_tensormap(&tm_v);
     tc::prefetch_tensormap(&tm_q);
   }
+  if (warp == W_LOADV && lane == 0) tc::prefetch_tensormap(&tm_v);
   for (int e = tid; e < C; e += NTHREADS) ownmask[e] = 0u;
   for (int e = tid; e < QB * KMAX; e += NTHREADS) {
     const int qi = e / KMAX, kk = e % KMAX;
@@ -156,16 +177,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     sm.w[qi][g][kk] = wv;
   }
   if (tid == 0) {
-    for (int s = 0; s < NST; ++s) {
-      tc::mbar_init(su32(&sm.bar_full[s]), 1);
-      tc::mbar_init(su32(&sm.bar_free[s]), 1);
+    for (int s = 0; s < NKQ; ++s) {
+      tc::mbar_init(su32(&sm.bar_kqfull[s]), 1);
+      tc::mbar_init(su32(&sm.bar_kqfree[s]), 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NV; ++s) {
+      tc::mbar_init(su32(&sm.bar_vfull[s]), 1);
+      tc::mbar_init(su32(&sm.bar_vfree[s]), 1);
+    }
+    for (int s = 0; s < NBUF; ++s) {
       tc::mbar_init(su32(&sm.bar_sdone[s]), 1);
-      tc::mbar_init(su32(&sm.bar_pready[s]), 4);
       tc::mbar_init(su32(&sm.bar_pvdone[s]), 1);
       tc::mbar_init(su32(&sm.bar_partfree[s]), 4);
     }
+    for (int s = 0; s < 2; ++s) tc::mbar_init(su32(&sm.bar_pready[s]), 4);
     for (int r = 0; r < RING; ++r) tc::mbar_init(su32(&sm.bar_ring[r]), 1);
     tc::mbar_init(su32(&sm.bar_mma_drain), 1);
     sm.abort_flag = 0;
@@ -195,7 +220,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     if (c >= 0) atomicOr(&ownmask[c], 1u << (e / KMAX));
   }
   __syncthreads();
-  if (warp == W_LOAD) {
+  if (warp == W_LOADKQ) {
     // compact into an ascending (chunk, owners) list and count work items
     int base = 0, items = 0;
     for (int c0 = 0; c0 < C; c0 += 32) {
@@ -247,8 +272,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   const int n_items = sm.n_items;
   const float sl2 = a.sm_scale * kLog2e;
 
-  if (warp == W_LOAD) {
-    // ============================ loader =====================================
+  if (warp == W_LOADKQ) {
+    // ============================ K/Q loader =================================
     int myc[KMAX];                           // this lane's (query's) chunk list
 #pragma unroll
     for (int kk = 0; kk < KMAX; ++kk) myc[kk] = idx[lane][kk];
@@ -263,11 +288,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
 #pragma unroll
       for (int kk = KMAX - 1; kk >= 0; --kk) my_slot = myc[kk] == c ? kk : my_slot;
       while (owners) {
-        const int st = item % NST, r = item % RING;
-        if (item >= NST && !wait_bar_warp(sm, &sm.bar_free[st], ((item / NST) - 1) & 1)) {
-          ok = false;
-          break;
-        }
+        const int st = item % NKQ, r = item % RING;
+        // the item's owner list goes into the ring before the stage is free
         int n = 0;
         uint32_t grp = 0;
         for (uint32_t m = owners; m && n < OWN; m &= m - 1, ++n) grp |= m & (~m + 1);
@@ -283,13 +305,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
           sm.ring[r].u = u;
         }
         __syncwarp();
-        const uint32_t bar = su32(&sm.bar_full[st]);
+        if (lane == 0) tc::mbar_arrive(su32(&sm.bar_ring[r]));
+        if (item >= NKQ && !wait_bar_warp(sm, &sm.bar_kqfree[st], ((item / NKQ) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        const uint32_t bar = su32(&sm.bar_kqfull[st]);
         if (lane == 0) {
-          tc::mbar_arrive(su32(&sm.bar_ring[r]));
-          tc::mbar_arrive_expect_tx(bar, 2u * 16384u + static_cast<uint32_t>(n) * 2048u);
-          const int ky = static_cast<int>(b * a.Lk + static_cast<int64_t>(c) * S);
-          tc::tma_load_4d(su32(sm.kt[st]), &tm_k, 0, ky, 0, hk, bar);
-          tc::tma_load_4d(su32(sm.vt[st]), &tm_v, 0, ky, 0, hk, bar);
+          tc::mbar_arrive_expect_tx(bar, 16384u + static_cast<uint32_t>(n) * 2048u);
+          tc::tma_load_4d(su32(sm.kt[st]), &tm_k, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(c) * S), 0,
+                          hk, bar);
         }
         __syncwarp();
         if (mine) {
@@ -302,54 +327,84 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     }
     // wait (bounded, even after an abort) for this CTA's copies in flight
     if (lane == 0) {
-      for (int it = item - NST < 0 ? 0 : item - NST; it < item; ++it)
-        tc::mbar_wait(su32(&sm.bar_full[it % NST]), (it / NST) & 1);
+      for (int it = item - NKQ < 0 ? 0 : item - NKQ; it < item; ++it)
+        tc::mbar_wait(su32(&sm.bar_kqfull[it % NKQ]), (it / NKQ) & 1);
+    }
+    __syncwarp();
+  } else if (warp == W_LOADV) {
+    // ============================ V loader ===================================
+    int item = 0;
+    for (; item < n_items; ++item) {
+      const int st = item % NV, r = item % RING;
+      if (!wait_bar_warp(sm, &sm.bar_ring[r], (item / RING) & 1)) break;
+      if (item >= NV && !wait_bar_warp(sm, &sm.bar_vfree[st], ((item / NV) - 1) & 1)) break;
+      if (lane == 0) {
+        const int c = sm.ulist[sm.ring[r].u].x;
+        const uint32_t bar = su32(&sm.bar_vfull[st]);
+        tc::mbar_arrive_expect_tx(bar, 16384u);
+        tc::tma_load_4d(su32(sm.vt[st]), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(c) * S), 0,
+                        hk, bar);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      for (int it = item - NV < 0 ? 0 : item - NV; it < item; ++it)
+        tc::mbar_wait(su32(&sm.bar_vfull[it % NV]), (it / NV) & 1);
     }
     __syncwarp();
   } else if (warp == W_MMA) {
-    // ============================ MMA issue ==================================
-    if (lane == 0) {
-      constexpr uint32_t id_s = tc::idesc_bf16_f32(64, 64, 0, 0);
-      const uint64_t dq0 = tc::smem_desc_sw128(su32(sm.at[0]), 16, 2048);
-      const uint64_t dk0 = tc::smem_desc_sw128(su32(sm.kt[0]), 16, 1024);
-      const uint64_t dv0 = tc::smem_desc_sw128(su32(sm.vt[0]), 8192, 1024);
-      const uint64_t dh0 = tc::smem_desc_sw128(su32(sm.ph[0]), 16, 1024);
-      const uint64_t dl0 = tc::smem_desc_sw128(su32(sm.pl[0]), 16, 1024);
-      auto issue_s = [&](int it) -> bool {
-        const int st = it % NST, s2 = it & 1;
-        if (!wait_bar(sm, &sm.bar_full[st], (it / NST) & 1)) return false;
-        tc::fence_after_sync();
-        const uint64_t da = adv(dq0, st * 16384), db = adv(dk0, st * 16384);
-        const uint32_t dS = tbase + kSCol + 64 * s2;
+    // ============================ MMA issue (converged warp) =================
+    constexpr uint32_t id_s = tc::idesc_bf16_f32(64, 64, 0, 0);
+    const uint64_t dq0 = tc::smem_desc_sw128(su32(sm.at[0]), 16, 2048);
+    const uint64_t dk0 = tc::smem_desc_sw128(su32(sm.kt[0]), 16, 1024);
+    const uint64_t dv0 = tc::smem_desc_sw128(su32(sm.vt[0]), 8192, 1024);
+    const uint64_t dh0 = tc::smem_desc_sw128(su32(sm.ph[0]), 16, 1024);
+    const uint64_t dl0 = tc::smem_desc_sw128(su32(sm.pl[0]), 16, 1024);
+    auto issue_s = [&](int it) -> bool {
+      const int st = it % NKQ, bf = it % NBUF;
+      if (!wait_bar_warp(sm, &sm.bar_kqfull[st], (it / NKQ) & 1)) return false;
+      // the buffer's previous item (it - NBUF) must have had its partial read
+      if (it >= NBUF && !wait_bar_warp(sm, &sm.bar_partfree[bf], ((it / NBUF) - 1) & 1)) return false;
+      tc::fence_after_sync();
+      const uint64_t da = adv(dq0, st * 16384), db = adv(dk0, st * 16384);
+      const uint32_t dS = tbase + kBufCol + 64 * bf;
+      if (elect_one()) {
         tc::mma_bf16<false>(dS, da, db, id_s);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
           tc::mma_bf16<true>(dS, adv(da, (kk >> 2) * 1024 + (kk & 3) * 32), adv(db, (kk >> 2) * 8192 + (kk & 3) * 32),
                              id_s);
-        tc::mma_commit(su32(&sm.bar_sdone[s2]));
-        return true;
-      };
-      bool ok = true;
-      for (int it = 0; ok && it < n_items && it < 2; ++it) ok = issue_s(it);
-      for (int it = 0; ok && it < n_items; ++it) {
-        const int st = it % NST, s2 = it & 1;
-        if (!wait_bar(sm, &sm.bar_pready[s2], (it >> 1) & 1)) break;
-        if (it >= 2 && !wait_bar(sm, &sm.bar_partfree[s2], ((it >> 1) - 1) & 1)) break;
-        tc::fence_after_sync();
-        const int np = ((8 * sm.ring[it % RING].n + 15) / 16) * 16;
-        const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
-        const uint64_t dv = adv(dv0, st * 16384), dh = adv(dh0, s2 * 8192), dl = adv(dl0, s2 * 8192);
-        const uint32_t dP = tbase + kPCol + 64 * s2;
+        tc::mma_commit(su32(&sm.bar_sdone[bf]));
+        tc::mma_commit(su32(&sm.bar_kqfree[st]));
+      }
+      __syncwarp();
+      return true;
+    };
+    bool ok = true;
+    for (int it = 0; ok && it < n_items && it < NBUF - 1; ++it) ok = issue_s(it);
+    for (int it = 0; ok && it < n_items; ++it) {
+      const int sv = it % NV, bf = it % NBUF, p2 = it & 1;
+      if (!wait_bar_warp(sm, &sm.bar_pready[p2], (it >> 1) & 1)) break;
+      if (!wait_bar_warp(sm, &sm.bar_vfull[sv], (it / NV) & 1)) break;
+      tc::fence_after_sync();
+      const int np = ((8 * sm.ring[it % RING].n + 15) / 16) * 16;
+      const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
+      const uint64_t dv = adv(dv0, sv * 16384), dh = adv(dh0, p2 * 8192), dl = adv(dl0, p2 * 8192);
+      const uint32_t dP = tbase + kBufCol + 64 * bf;
+      if (elect_one()) {
         tc::mma_bf16<false>(dP, dv, dh, id_o);
 #pragma unroll
         for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dh, kk * 32), id_o);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
-        tc::mma_commit(su32(&sm.bar_pvdone[s2]));
-        tc::mma_commit(su32(&sm.bar_free[st]));
-        if (it + 2 < n_items) ok = issue_s(it + 2);
+        tc::mma_commit(su32(&sm.bar_pvdone[bf]));
+        tc::mma_commit(su32(&sm.bar_vfree[sv]));
       }
-      // every MMA issued by this thread has completed once this phase lands
+      __syncwarp();
+      if (it + NBUF - 1 < n_items) ok = issue_s(it + NBUF - 1);
+    }
+    // every MMA issued by this warp has completed once this phase lands
+    if (elect_one()) {
       tc::mma_commit(su32(&sm.bar_mma_drain));
       tc::mbar_wait(su32(&sm.bar_mma_drain), 0);
     }
@@ -362,47 +417,52 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     const int jrow = t < 8 ? q : q + 4;      // owner (compact index) of this thread's row
     const int g = t & 7;
     for (int it = grp; it < n_items; it += 2) {
-      const int s2 = it & 1, r = it % RING;
+      const int bf = it % NBUF, p2 = it & 1, r = it % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
       const int n = sm.ring[r].n;
       const bool row_on = jrow < n;
       float w = 0.f;
-      uint32_t km = 0u;
+      uint32_t km = 0xFFFFFFFFu;             // rows without an owner are computed and dropped
       if (row_on) {
         if (g < G) w = sm.w[sm.ring[r].oq[jrow]][g][sm.ring[r].slot[jrow]];
         const unsigned long long vm = sm.vmask[sm.ring[r].u];
         km = static_cast<uint32_t>(hf ? (vm >> 32) : vm);
       }
-      if (!wait_bar_warp(sm, &sm.bar_sdone[s2], (it >> 1) & 1)) break;
+      if (!wait_bar_warp(sm, &sm.bar_sdone[bf], (it / NBUF) & 1)) break;
       tc::fence_after_sync();
       uint32_t x[32];
       if (q < n) {                           // warp-uniform: this quadrant holds rows
-        tc::tmem_ld_16x32bx2_x32(tbase + lane_off + kSCol + 64 * s2, x);
+        tc::tmem_ld_16x32bx2_x32(tbase + lane_off + kBufCol + 64 * bf, x);
         tc::tmem_wait_ld();
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) x[c] = 0u;
       }
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // masked keys -> -inf; the common case (every key usable but possibly the
+      // last of the chunk) takes one select instead of 32
+      if (__all_sync(0xffffffffu, (km | 0x80000000u) == 0xFFFFFFFFu)) {
+        if (!(km >> 31)) x[31] = __float_as_uint(-INFINITY);
+      } else {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float v = ((km >> c) & 1u) ? __uint_as_float(x[c]) * sl2 : -INFINITY;
-        x[c] = __float_as_uint(v);
-        mx4[c & 3] = fmaxf(mx4[c & 3], v);
+        for (int c = 0; c < 32; ++c)
+          if (!((km >> c) & 1u)) x[c] = __float_as_uint(-INFINITY);
       }
-      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(x[c]));
+      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float base = mx == -INFINITY ? 0.f : mx;
+      const float nb = mx == -INFINITY ? 0.f : -mx * sl2;
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float e = fast_exp2(__uint_as_float(x[c]) - base);   // masked keys: 2^-inf = 0
+        const float e = fast_exp2(fmaf(__uint_as_float(x[c]), sl2, nb));   // masked keys: 2^-inf = 0
         x[c] = __float_as_uint(e);
         sum4[c & 3] += e;
       }
       float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-      const float f = sum > 0.f ? w / sum : 0.f;
+      const float f = sum > 0.f ? __fdividef(w, sum) : 0.f;
       uint32_t hi[16], lo[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
@@ -412,33 +472,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
       }
       // the P buffer is free once the P.V of item it-2 has completed
-      if (it >= 2 && !wait_bar_warp(sm, &sm.bar_pvdone[s2], ((it >> 1) - 1) & 1)) break;
+      if (it >= 2 && !wait_bar_warp(sm, &sm.bar_pvdone[(it - 2) % NBUF], ((it - 2) / NBUF) & 1)) break;
       if (row_on) {
         const int row = 8 * jrow + g;
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          *reinterpret_cast<uint4*>(sm.ph[s2] + swz_off(row, 4 * hf + p)) =
+          *reinterpret_cast<uint4*>(sm.ph[p2] + swz_off(row, 4 * hf + p)) =
               make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
-          *reinterpret_cast<uint4*>(sm.pl[s2] + swz_off(row, 4 * hf + p)) =
+          *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(row, 4 * hf + p)) =
               make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
         }
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[s2]));
+      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[p2]));
     }
   } else {
     // ============================ accumulate + epilogue (warps 0-3) ==========
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     for (int it = 0; it < n_items; ++it) {
-      const int s2 = it & 1, r = it % RING;
+      const int bf = it % NBUF, r = it % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
       const int n = sm.ring[r].n;
       int oq[OWN];
 #pragma unroll
       for (int j = 0; j < OWN; ++j) oq[j] = sm.ring[r].oq[j];
-      if (!wait_bar_warp(sm, &sm.bar_pvdone[s2], (it >> 1) & 1)) break;
+      if (!wait_bar_warp(sm, &sm.bar_pvdone[bf], (it / NBUF) & 1)) break;
       tc::fence_after_sync();
       tc::tmem_wait_st();                    // previous item's accumulator stores have landed
 #pragma unroll
@@ -448,7 +508,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (j0 + j < n) {
-            tc::tmem_ld8(tbase + lane_off + kPCol + 64 * s2 + 8 * (j0 + j), pv[j]);
+            tc::tmem_ld8(tbase + lane_off + kBufCol + 64 * bf + 8 * (j0 + j), pv[j]);
             tc::tmem_ld8(tbase + lane_off + 8 * oq[j0 + j], acc[j]);
           }
         }
@@ -456,7 +516,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         if (j0 + 4 >= n) {                   // last partial columns read: release the buffer
           tc::fence_before_sync();
           __syncwarp();
-          if (lane == 0) tc::mbar_arrive(su32(&sm.bar_partfree[s2]));
+          if (lane == 0) tc::mbar_arrive(su32(&sm.bar_partfree[bf]));
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
