@@ -109,7 +109,9 @@ __device__ __forceinline__ int swz_off(int row, int piece) { return row * 128 + 
 __device__ __forceinline__ bool aborted(TcSmem& sm) { return *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0; }
 
 __device__ __forceinline__ bool wait_bar(TcSmem& sm, uint64_t* bar, uint32_t parity) {
-  // bounded wait that also gives up when another role has aborted
+  // bounded wait that also gives up when another role has aborted; a phase
+  // that has already completed is seen by the cheap non-blocking test
+  if (tc::mbar_test(su32(bar), parity)) return true;
   for (int round = 0; round < 4000; ++round) {
     if (tc::mbar_wait(su32(bar), parity, 1000u)) return true;
     if (aborted(sm)) return false;
@@ -354,40 +356,48 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     __syncwarp();
   } else if (warp == W_MMA) {
     // ============================ MMA issue (converged warp) =================
+    // Per step: P.V of item it and S of item it+3 go out in one elected batch
+    // after all four of their waits, so the warp passes one fence and one
+    // convergence point per item.
     constexpr uint32_t id_s = tc::idesc_bf16_f32(64, 64, 0, 0);
     const uint64_t dq0 = tc::smem_desc_sw128(su32(sm.at[0]), 16, 2048);
     const uint64_t dk0 = tc::smem_desc_sw128(su32(sm.kt[0]), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(su32(sm.vt[0]), 8192, 1024);
     const uint64_t dh0 = tc::smem_desc_sw128(su32(sm.ph[0]), 16, 1024);
     const uint64_t dl0 = tc::smem_desc_sw128(su32(sm.pl[0]), 16, 1024);
-    auto issue_s = [&](int it) -> bool {
+    auto s_mmas = [&](int it) {
       const int st = it % NKQ, bf = it % NBUF;
-      if (!wait_bar_warp(sm, &sm.bar_kqfull[st], (it / NKQ) & 1)) return false;
-      // the buffer's previous item (it - NBUF) must have had its partial read
-      if (it >= NBUF && !wait_bar_warp(sm, &sm.bar_partfree[bf], ((it / NBUF) - 1) & 1)) return false;
-      tc::fence_after_sync();
       const uint64_t da = adv(dq0, st * 16384), db = adv(dk0, st * 16384);
       const uint32_t dS = tbase + kBufCol + 64 * bf;
-      if (elect_one()) {
-        tc::mma_bf16<false>(dS, da, db, id_s);
+      tc::mma_bf16<false>(dS, da, db, id_s);
 #pragma unroll
-        for (int kk = 1; kk < 8; ++kk)
-          tc::mma_bf16<true>(dS, adv(da, (kk >> 2) * 1024 + (kk & 3) * 32), adv(db, (kk >> 2) * 8192 + (kk & 3) * 32),
-                             id_s);
-        tc::mma_commit(su32(&sm.bar_sdone[bf]));
-        tc::mma_commit(su32(&sm.bar_kqfree[st]));
-      }
-      __syncwarp();
-      return true;
+      for (int kk = 1; kk < 8; ++kk)
+        tc::mma_bf16<true>(dS, adv(da, (kk >> 2) * 1024 + (kk & 3) * 32), adv(db, (kk >> 2) * 8192 + (kk & 3) * 32),
+                           id_s);
+      tc::mma_commit(su32(&sm.bar_sdone[bf]));
+      tc::mma_commit(su32(&sm.bar_kqfree[st]));
+    };
+    // S of item it is ready to go: its K/Q tiles landed and its buffer's previous partial was read
+    auto s_ready = [&](int it) -> bool {
+      if (!wait_bar_warp(sm, &sm.bar_kqfull[it % NKQ], (it / NKQ) & 1)) return false;
+      return it < NBUF || wait_bar_warp(sm, &sm.bar_partfree[it % NBUF], ((it / NBUF) - 1) & 1);
     };
     bool ok = true;
-    for (int it = 0; ok && it < n_items && it < NBUF - 1; ++it) ok = issue_s(it);
+    for (int it = 0; ok && it < n_items && it < NBUF - 1; ++it) {
+      ok = s_ready(it);
+      if (!ok) break;
+      tc::fence_after_sync();
+      if (elect_one()) s_mmas(it);
+      __syncwarp();
+    }
     for (int it = 0; ok && it < n_items; ++it) {
       const int sv = it % NV, bf = it % NBUF, p2 = it & 1;
+      const int nxt = it + NBUF - 1;
+      const int np = ((8 * sm.ring[it % RING].n + 15) / 16) * 16;
       if (!wait_bar_warp(sm, &sm.bar_pready[p2], (it >> 1) & 1)) break;
       if (!wait_bar_warp(sm, &sm.bar_vfull[sv], (it / NV) & 1)) break;
+      if (nxt < n_items && !s_ready(nxt)) break;
       tc::fence_after_sync();
-      const int np = ((8 * sm.ring[it % RING].n + 15) / 16) * 16;
       const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
       const uint64_t dv = adv(dv0, sv * 16384), dh = adv(dh0, p2 * 8192), dl = adv(dl0, p2 * 8192);
       const uint32_t dP = tbase + kBufCol + 64 * bf;
@@ -399,9 +409,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
         tc::mma_commit(su32(&sm.bar_pvdone[bf]));
         tc::mma_commit(su32(&sm.bar_vfree[sv]));
+        if (nxt < n_items) s_mmas(nxt);
       }
       __syncwarp();
-      if (it + NBUF - 1 < n_items) ok = issue_s(it + NBUF - 1);
     }
     // every MMA issued by this warp has completed once this phase lands
     if (elect_one()) {

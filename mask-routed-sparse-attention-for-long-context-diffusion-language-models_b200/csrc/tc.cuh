@@ -136,6 +136,18 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
 }
+// Non-blocking test of the phase with parity `parity` (about 15 cycles when it
+// has completed, against about 75 for a try_wait that succeeds).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
 // Bounded wait for the phase with parity `parity` to complete.  Returns false
 // after ~`max_iters` polls (each poll may suspend the thread briefly).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t max_iters = 4000000u) {
