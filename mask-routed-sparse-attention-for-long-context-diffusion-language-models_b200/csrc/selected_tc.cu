@@ -394,9 +394,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       const int sv = it % NV, bf = it % NBUF, p2 = it & 1;
       const int nxt = it + NBUF - 1;
       const int np = ((8 * sm.ring[it % RING].n + 15) / 16) * 16;
-      if (!wait_bar_warp(sm, &sm.bar_pready[p2], (it >> 1) & 1)) break;
-      if (!wait_bar_warp(sm, &sm.bar_vfull[sv], (it / NV) & 1)) break;
-      if (nxt < n_items && !s_ready(nxt)) break;
+      // fast path: the four phases this step needs are usually complete already;
+      // test them with independent non-blocking tests and one vote
+      bool rdy = tc::mbar_test(su32(&sm.bar_pready[p2]), (it >> 1) & 1) &
+                 tc::mbar_test(su32(&sm.bar_vfull[sv]), (it / NV) & 1);
+      if (nxt < n_items) {
+        rdy &= tc::mbar_test(su32(&sm.bar_kqfull[nxt % NKQ]), (nxt / NKQ) & 1);
+        if (nxt >= NBUF) rdy &= tc::mbar_test(su32(&sm.bar_partfree[nxt % NBUF]), ((nxt / NBUF) - 1) & 1);
+      }
+      if (!__all_sync(0xffffffffu, rdy)) {
+        if (!wait_bar_warp(sm, &sm.bar_pready[p2], (it >> 1) & 1)) break;
+        if (!wait_bar_warp(sm, &sm.bar_vfull[sv], (it / NV) & 1)) break;
+        if (nxt < n_items && !s_ready(nxt)) break;
+      }
       tc::fence_after_sync();
       const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
       const uint64_t dv = adv(dv0, sv * 16384), dh = adv(dh0, p2 * 8192), dl = adv(dl0, p2 * 8192);
