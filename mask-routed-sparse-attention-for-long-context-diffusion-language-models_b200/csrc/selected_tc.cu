@@ -20,7 +20,7 @@
 // 44 cycles (its shared-memory operand reads), so an item costs 16 MMAs and the
 // rest of the work runs beside them in a pipeline three items deep:
 //   warps 0-3   accumulate: the read-modify-write of every item, in order,
-//               one quadrant of output dims each; then the epilogue;
+//               one quadrant of output dims each;
 //   warps 4-11  softmax, two groups of four taking alternate items; each S row
 //               is read by two threads (32 columns each) with 16x32bx2 loads;
 //   warp 12     K/Q loader: owner lists into an item ring, TMA of the K tile
@@ -28,7 +28,9 @@
 //               stages are released when the item's S MMAs complete;
 //   warp 13     V loader: TMA of the V tile, stages released after P.V;
 //   warp 14     MMA issue: the warp stays converged and one elected lane
-//               issues (about a third cheaper than issuing from a lone lane).
+//               issues (about a third cheaper than issuing from a lone lane);
+//   warps 0-11  finally, the epilogue: bf16 rounding, the fused local-branch
+//               merge and the stores, three warps per TMEM quadrant.
 // TMEM: accumulators in columns 0-255, then four 64-column buffers; item i's S
 // lands in buffer i%4 and its P.V partial overwrites the same columns once the
 // softmax has read them, so S can run three items ahead of P.V.
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[p2]));
     }
   } else {
-    // ============================ accumulate + epilogue (warps 0-3) ==========
+    // ============================ accumulate (warps 0-3) =====================
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     for (int it = 0; it < n_items; ++it) {
       const int bf = it % NBUF, r = it % RING;
@@ -550,19 +552,50 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       }
     }
     tc::tmem_wait_st();
+  }
+
+  if (warp < W_LOADKQ) {
+    // ============================ epilogue (warps 0-11) ======================
+    // The softmax warps join the accumulate warps once the last item has been
+    // accumulated: three warps per TMEM quadrant, each taking batches of four
+    // queries whose local-branch inputs are loaded before the accumulators.
+    tc::fence_before_sync();
+    asm volatile("bar.sync 1, 384;\n" ::: "memory");
+    tc::fence_after_sync();
     if (!__any_sync(0xffffffffu, aborted(sm))) {
-      const int d = warp * 32 + lane;
-      for (int qi = 0; qi < QB; ++qi) {
-        const int64_t rowq = q0 + qi;
-        uint32_t acc[8];
-        tc::tmem_ld8(tbase + lane_off + 8 * qi, acc);
+      constexpr int EB = 4;
+      const int qd = warp & 3, part = warp >> 2;
+      const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+      const int d = qd * 32 + lane;
+      for (int q1 = part * EB; q1 < QB; q1 += 3 * EB) {
+        uint32_t acc[EB][8];
+        float lw[EB][GMAX], lo[EB][GMAX];
+#pragma unroll
+        for (int j = 0; j < EB; ++j) {
+          const int64_t rowq = q0 + q1 + j;
+#pragma unroll
+          for (int gg = 0; gg < GMAX; ++gg) {
+            lw[j][gg] = 0.f;
+            lo[j][gg] = 0.f;
+            if (a.local_out != nullptr && gg < G && rowq < a.Lq) {
+              const int64_t hrow = (b * a.Lq + rowq) * Hq + hk * G + gg;
+              lw[j][gg] = bf2f(a.local_w[hrow]);
+              lo[j][gg] = bf2f(a.local_out[hrow * D + d]);
+            }
+          }
+          tc::tmem_ld8(tbase + lane_off + 8 * (q1 + j), acc[j]);
+        }
         tc::tmem_wait_ld();
-        if (rowq >= a.Lq) continue;
-        for (int gg = 0; gg < G; ++gg) {
-          const int64_t o = ((b * a.Lq + rowq) * Hq + hk * G + gg) * (int64_t)D + d;
-          float v = round_bf16(__uint_as_float(acc[gg]));
-          if (a.local_out) v += bf2f(a.local_w[(b * a.Lq + rowq) * Hq + hk * G + gg]) * bf2f(a.local_out[o]);
-          a.out[o] = f2bf(v);
+#pragma unroll
+        for (int j = 0; j < EB; ++j) {
+          const int64_t rowq = q0 + q1 + j;
+          if (rowq >= a.Lq) continue;
+#pragma unroll
+          for (int gg = 0; gg < GMAX; ++gg) {
+            if (gg >= G) continue;
+            const int64_t o = ((b * a.Lq + rowq) * Hq + hk * G + gg) * (int64_t)D + d;
+            a.out[o] = f2bf(round_bf16(__uint_as_float(acc[j][gg])) + lw[j][gg] * lo[j][gg]);
+          }
         }
       }
     }
