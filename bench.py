@@ -210,6 +210,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-per-gpu", type=int, default=L_PER_GPU)
+    ap.add_argument("--profile", type=int, default=0, metavar="N",
+                    help="run N untimed fused layer forwards at the bench workload and exit "
+                         "(the target of the ncu captures summarised under profiles/)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -247,6 +250,13 @@ def main():
     def step():
         runner(*x, out=out)
 
+    if args.profile:
+        for _ in range(args.profile):
+            step()
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_forwards": args.profile, "seq_per_gpu": lq,
+                          "device_error_flags": mrsa._lib.load().mrsa_device_error_flags(1)}))
+        return
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
