@@ -100,6 +100,9 @@ int mrsa_remote_drop_mask(const uint8_t* key_valid, int32_t* out, int64_t batch,
  * remote_w/local_w (both or neither) get the route weights of
  * mode MRSA_WEIGHTS_AFFINE (_route_weights_torch with gate scale/offset) or
  * MRSA_WEIGHTS_SOFTMAX (route_weights).
+ * workspace: at least mrsa_route_topk_workspace_size() bytes of device memory
+ * (the fp32 max-pooled keys [B,Lq,Hkv,C]), 16-byte aligned; MRSA_ERR_WORKSPACE
+ * when missing or short.
  * Replaces ops/topk_head_softmax.py:15 ref_softmax_topk_max_pooling and :1242
  * online_softmax_topk_head (post_softmax, non-causal), dream_dllm_hils/routing.py:52
  * route_topk_g7, and fuses dream_dllm_hils/attention.py:126 _route_weights_torch. */
@@ -110,7 +113,12 @@ int mrsa_route_topk(const void* route_q, const void* landmarks, int lmk_per_qhea
                     void* local_w, int weight_mode, float temperature, float gate_scale,
                     float gate_offset, int64_t batch, int64_t q_len, int64_t chunks,
                     int64_t kv_heads, int64_t groups, int64_t head_dim, int64_t topk,
-                    mrsa_stream_t stream);
+                    void* workspace, size_t workspace_bytes, mrsa_stream_t stream);
+
+/* Device workspace bytes of mrsa_route_topk (0 for an invalid shape).  No
+ * reference counterpart: the reference materialises its scores instead. */
+size_t mrsa_route_topk_workspace_size(int64_t batch, int64_t q_len, int64_t chunks,
+                                      int64_t kv_heads);
 
 /* Route weights from scores [B,L,Hq,K] bf16, indices [B,L,Hkv,K] int32,
  * prior [B,C,Hkv,G] fp32, local_lse [B,L,Hq] fp32.
@@ -150,7 +158,8 @@ int mrsa_selected_attention(const void* q, const void* k, const void* v, const u
 
 /* Bit mask of device-side failures recorded since the last clear: bit 0 = a
  * selected-attention CTA gave up waiting on one of its internal barriers (its
- * output rows are then incomplete).  Synchronises the current device; with
+ * output rows are then incomplete); bit 1 = a routing key CTA did (its keys,
+ * hence its selections, are then incomplete).  Synchronises the current device; with
  * clear != 0 also resets the mask.  Negative on a CUDA error.  Replaces the
  * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
 int mrsa_device_error_flags(int clear);

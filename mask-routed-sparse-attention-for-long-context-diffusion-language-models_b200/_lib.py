@@ -32,7 +32,9 @@ _SIGS = {
                         _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_remote_drop_mask": [_vp, _vp, _i64, _i64, _i64, _i64, _vp],
     "mrsa_route_topk": [_vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _vp,
-                        _int, _f32, _f32, _f32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+                        _int, _f32, _f32, _f32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz,
+                        _vp],
+    "mrsa_route_topk_workspace_size": [_i64, _i64, _i64, _i64],
     "mrsa_route_weights": [_vp, _vp, _vp, _vp, _vp, _vp, _int, _f32, _f32, _f32,
                            _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_local_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _i64, _f32,
@@ -45,7 +47,8 @@ _SIGS = {
     "mrsa_route_layer_forward": [_vp, _vp, _sz, _vp],
     "mrsa_route_layer_forward_noalloc": [_vp, _vp],
 }
-_RESTYPE = {"mrsa_strerror": C.c_char_p, "mrsa_route_layer_workspace_size": _sz}
+_RESTYPE = {"mrsa_strerror": C.c_char_p, "mrsa_route_layer_workspace_size": _sz,
+            "mrsa_route_topk_workspace_size": _sz}
 
 EXPORTED = tuple(_SIGS)
 

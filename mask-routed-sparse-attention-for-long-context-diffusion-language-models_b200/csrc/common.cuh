@@ -114,6 +114,9 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Device error flag of the routing kernels (route.cu); -1 when unreadable.
+int route_error_flags(int clear);
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -143,7 +143,7 @@ const char* mrsa_strerror(int code) {
   }
 }
 
-int mrsa_abi_version(void) { return 1; }
+int mrsa_abi_version(void) { return 2; }
 
 int mrsa_yarn_inv_freq(int dim, double base, double factor, int orig_max_pos, double beta_fast,
                        double beta_slow, int truncate, float* inv_freq_out,

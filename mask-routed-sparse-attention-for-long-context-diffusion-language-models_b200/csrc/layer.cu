@@ -12,7 +12,7 @@ inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct LayerPlan {
   size_t q, k, route_q, lmk, entropy, prior, chunk_ok, local_out, local_lse, indices, scores,
-      remote_w, local_w, total;
+      remote_w, local_w, route_keys, total;
 };
 
 LayerPlan plan(const mrsa_route_layer_args* a) {
@@ -38,6 +38,7 @@ LayerPlan plan(const mrsa_route_layer_args* a) {
   p.scores = take(B * L * Hq * K * 2);
   p.remote_w = take(B * L * Hq * K * 2);
   p.local_w = take(B * L * Hq * 2);
+  p.route_keys = take(B * L * Hkv * C * 4);
   p.total = off;
   return p;
 }
@@ -80,6 +81,7 @@ extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* wo
   void* scores = ws + p.scores;
   void* remote_w = ws + p.remote_w;
   void* local_w = ws + p.local_w;
+  void* route_keys = ws + p.route_keys;
 
   const int64_t B = a->batch, L = a->seq_len, Hq = a->q_heads, Hkv = a->kv_heads,
                 D = a->head_dim, G = Hq / Hkv, C = L / mrsa::kChunk;
@@ -103,7 +105,7 @@ extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* wo
   rc = mrsa_route_topk(route_q, lmk, 1, local_lse, prior, nullptr, chunk_ok, a->local_window, 0,
                        indices, scores, MRSA_BF16, remote_w, local_w, MRSA_WEIGHTS_AFFINE,
                        a->temperature, a->gate_scale, a->gate_offset, B, L, C, Hkv, G, D,
-                       a->topk, stream);
+                       a->topk, route_keys, static_cast<size_t>(B * L * Hkv * C * 4), stream);
   if (rc) return rc;
   return mrsa_selected_attention(q, k, a->v, a->key_valid, remote_w, indices, local_out, local_w,
                                  a->out, sm_scale, 1, B, L, L, Hkv, G, D, a->topk, mrsa::kChunk,

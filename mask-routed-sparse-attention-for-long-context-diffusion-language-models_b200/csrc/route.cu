@@ -11,32 +11,54 @@
 // The drop rule of remote_drop_mask (dream_dllm_hils/kernel_utils.py:75-161) is
 // evaluated inline from chunk validity instead of a dense [L, C] mask.
 //
-// CTA = 16 queries x one KV head.  Warp g owns query head g of the group for
-// the two GEMM passes (mma.sync m16n8k16, landmarks read through L2); the
-// max-pooled keys of all chunks stay in shared memory; each warp then selects
-// the top-K of two queries with a 32-step radix search over order-preserving
-// integer keys, gathers raw scores for its selection and emits weights.
+// Two launches.
+// route_keys_kernel (tcgen05/TMEM): one CTA per 64 queries x one KV head keeps
+//   the G query tiles of its block in shared memory and streams 128-chunk
+//   landmark tiles by TMA.  S_g = Q_g . LMK_g^T runs as UMMA M=64, N=128, K=128
+//   into one of four 128-column TMEM buffers.  Pass 1 walks heads then tiles and
+//   folds each S tile into an online log-sum-exp per (query, head), giving T;
+//   pass 2 walks tiles then heads and keeps max_g (x - T_g) in registers, applies
+//   the drop rule and writes the fp32 keys [B, Lq, Hkv, C] to the workspace.
+//   Warps 0-7 read TMEM (two threads per S row, 32 columns each, via
+//   tcgen05.ld.16x32bx2), warp 8 issues the TMA copies, warp 9 the MMAs.
+// route_select_kernel: one warp per (query, KV head) holds that row's keys in
+//   registers, finds the K-th largest with a 32-step radix search over
+//   order-preserving integer keys, emits the indices in ascending chunk order
+//   (ties at the threshold: lowest chunk ids first), then computes the raw
+//   scores of its selection (lane = slot) and the route weights.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
+#include "tc.cuh"
 
 using namespace mrsa;
 
 namespace {
 
-constexpr int QB = 16;      // queries per CTA
-constexpr int NW = 8;       // warps per CTA
-constexpr int CT = 64;      // chunks per key tile in pass 2
 constexpr int D = kHeadDim;
 constexpr int kMaxChunks = 2048;
+constexpr int RQ = 64;            // queries per key CTA (UMMA M)
+constexpr int RN = 128;           // chunks per landmark tile (UMMA N)
+constexpr int RBUF = 4;           // TMEM S buffers of RN columns
+constexpr int RMAXST = 4;         // landmark stages (chosen at launch from the shared-memory budget)
+constexpr int RGMAX = 8;
+constexpr int R_THREADS = 320;    // warps 0-7 TMEM readers, 8 TMA, 9 MMA
+constexpr int R_W_LOAD = 8, R_W_MMA = 9;
+constexpr int kSmemLimit = 232448;
 
 struct RouteArgs {
   const __nv_bfloat16* rq;
   const __nv_bfloat16* lmk;
-  int lmk_g_stride;         // elements between query heads of one chunk/kv head (D or 0)
+  int lmk_per_qhead;
   const float* local_lse;
   const float* bias;
   const int32_t* drop;
   const uint8_t* chunk_ok;
   int64_t window, q_offset;
+  float* keys;              // workspace [B, Lq, Hkv, C]
   int32_t* indices;
   void* scores;
   int scores_f32;
@@ -46,8 +68,316 @@ struct RouteArgs {
   float temperature, gate_scale, gate_offset;
   int64_t Lq;
   int C, Hkv, G, K;
+  int nst;                  // landmark stages
   float sm_scale;
 };
+
+// Set (bit 0) when a key CTA gave up on a wait; read and cleared through
+// mrsa_device_error_flags().
+__device__ int g_route_error;
+
+// Misc shared state of the key kernel, after the query tiles and landmark stages.
+constexpr int RBR = 4;            // bias ring slots (one job's 128 bias values each)
+
+struct RouteMisc {
+  uint64_t lfull[RMAXST], lfree[RMAXST], sdone[RBUF], sfree[RBUF], qfull, mma_drain;
+  uint64_t bfull[RBR], bfree[RBR];
+  float bias[RBR][RN];             // bias of job j's head and tile in slot j % RBR
+  uint32_t tmem_base;
+  int abort_flag;
+  float T[RQ][RGMAX];              // T per (query, head), natural log
+  float part[2][RQ][RGMAX][2];     // pass-1 partials (max, sum) per column half, log2 domain
+  uint8_t chunk_ok[kMaxChunks];
+};
+
+__host__ __device__ constexpr size_t key_smem_bytes(int G, int nst) {
+  return static_cast<size_t>(G) * 16384 + static_cast<size_t>(nst) * 32768 + sizeof(RouteMisc) + 1024;
+}
+
+// Job j of the key kernel: pass 1 visits (head, tile) head-major, pass 2 tile-major.
+__device__ __forceinline__ void job_coords(int j, int G, int NT, int& g, int& t) {
+  if (j < G * NT) {
+    g = j / NT;
+    t = j % NT;
+  } else {
+    const int jj = j - G * NT;
+    t = jj / G;
+    g = jj % G;
+  }
+}
+
+__global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_l, RouteArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int G = a.G, C = a.C, NST = a.nst, Hq = a.Hkv * a.G;
+  unsigned char* qt = base;                                  // G x [half][64 rows][64 dims]
+  unsigned char* lt = base + G * 16384;                      // NST x [half][128 chunks][64 dims]
+  RouteMisc& ms = *reinterpret_cast<RouteMisc*>(lt + NST * 32768);
+  volatile int* abort_flag = &ms.abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * RQ;
+  const int NT = (C + RN - 1) / RN;
+  const int J = 2 * G * NT;
+
+  for (int c = tid; c < C; c += R_THREADS) ms.chunk_ok[c] = a.chunk_ok ? a.chunk_ok[(int64_t)b * C + c] : 1;
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      tc::mbar_init(tc::smem_addr(&ms.lfull[s]), 1);
+      tc::mbar_init(tc::smem_addr(&ms.lfree[s]), 1);
+    }
+    for (int s = 0; s < RBUF; ++s) {
+      tc::mbar_init(tc::smem_addr(&ms.sdone[s]), 1);
+      tc::mbar_init(tc::smem_addr(&ms.sfree[s]), 8);
+    }
+    for (int s = 0; s < RBR; ++s) {
+      tc::mbar_init(tc::smem_addr(&ms.bfull[s]), 1);
+      tc::mbar_init(tc::smem_addr(&ms.bfree[s]), 8);
+    }
+    tc::mbar_init(tc::smem_addr(&ms.qfull), 1);
+    tc::mbar_init(tc::smem_addr(&ms.mma_drain), 1);
+    ms.abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tc::smem_addr(&ms.tmem_base), 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = ms.tmem_base;
+
+  if (warp == R_W_LOAD) {
+    // ============================ TMA + bias ring =============================
+    const uint32_t qb = tc::smem_addr(&ms.qfull);
+    if (lane == 0) {
+      tc::prefetch_tensormap(&tm_q);
+      tc::prefetch_tensormap(&tm_l);
+      tc::mbar_arrive_expect_tx(qb, static_cast<uint32_t>(G) * 16384u);
+      for (int g = 0; g < G; ++g)
+        tc::tma_load_4d(tc::smem_addr(qt + g * 16384), &tm_q, 0, static_cast<int>(b * a.Lq + q0), 0, hk * G + g, qb);
+    }
+    __syncwarp();
+    int j = 0;
+    for (; j < J; ++j) {
+      const int st = j % NST, bs = j % RBR;
+      if (j >= NST && !tc::wait_bounded_warp(tc::smem_addr(&ms.lfree[st]), ((j / NST) - 1) & 1, abort_flag)) break;
+      int g, t;
+      job_coords(j, G, NT, g, t);
+      if (lane == 0) {
+        const uint32_t lb = tc::smem_addr(&ms.lfull[st]);
+        tc::mbar_arrive_expect_tx(lb, 32768u);
+        tc::tma_load_5d(tc::smem_addr(lt + st * 32768), &tm_l, 0, b * C + t * RN, 0, a.lmk_per_qhead ? g : 0, hk, lb);
+      }
+      // bias[c, hq] of the job's 128 chunks (stride Hq in memory) into its ring slot
+      float bv[RN / 32];
+#pragma unroll
+      for (int k = 0; k < RN / 32; ++k) {
+        const int c = t * RN + 32 * k + lane;
+        bv[k] = (a.bias != nullptr && c < C) ? a.bias[((int64_t)b * C + c) * Hq + hk * G + g] : 0.f;
+      }
+      if (j >= RBR && !tc::wait_bounded_warp(tc::smem_addr(&ms.bfree[bs]), ((j / RBR) - 1) & 1, abort_flag)) break;
+#pragma unroll
+      for (int k = 0; k < RN / 32; ++k) ms.bias[bs][32 * k + lane] = bv[k];
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&ms.bfull[bs]));
+    }
+    // wait (bounded, even after an abort) for the copies in flight
+    if (lane == 0) {
+      tc::mbar_wait(qb, 0);
+      for (int jj = j - NST < 0 ? 0 : j - NST; jj < j; ++jj) tc::mbar_wait(tc::smem_addr(&ms.lfull[jj % NST]), (jj / NST) & 1);
+    }
+    __syncwarp();
+  } else if (warp == R_W_MMA) {
+    // ============================ MMA (converged warp) ========================
+    constexpr uint32_t idesc = tc::idesc_bf16_f32(64, RN, 0, 0);
+    const uint64_t dq0 = tc::smem_desc_sw128(tc::smem_addr(qt), 16, 1024);
+    const uint64_t dl0 = tc::smem_desc_sw128(tc::smem_addr(lt), 16, 1024);
+    bool ok = tc::wait_bounded_warp(tc::smem_addr(&ms.qfull), 0, abort_flag);
+    for (int j = 0; ok && j < J; ++j) {
+      const int st = j % NST, bf = j % RBUF;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&ms.lfull[st]), (j / NST) & 1, abort_flag)) break;
+      if (j >= RBUF && !tc::wait_bounded_warp(tc::smem_addr(&ms.sfree[bf]), ((j / RBUF) - 1) & 1, abort_flag)) break;
+      tc::fence_after_sync();
+      int g, t;
+      job_coords(j, G, NT, g, t);
+      const uint64_t da = tc::desc_adv(dq0, g * 16384), db = tc::desc_adv(dl0, st * 32768);
+      const uint32_t dS = tbase + RN * bf;
+      if (tc::elect_one()) {
+        tc::mma_bf16<false>(dS, da, db, idesc);
+#pragma unroll
+        for (int kk = 1; kk < 8; ++kk)
+          tc::mma_bf16<true>(dS, tc::desc_adv(da, (kk >> 2) * 8192 + (kk & 3) * 32),
+                             tc::desc_adv(db, (kk >> 2) * 16384 + (kk & 3) * 32), idesc);
+        tc::mma_commit(tc::smem_addr(&ms.sdone[bf]));
+        tc::mma_commit(tc::smem_addr(&ms.lfree[st]));
+      }
+      __syncwarp();
+    }
+    if (tc::elect_one()) {
+      tc::mma_commit(tc::smem_addr(&ms.mma_drain));
+      tc::mbar_wait(tc::smem_addr(&ms.mma_drain), 0);
+    }
+    __syncwarp();
+  } else {
+    // ============================ TMEM readers (warps 0-7) ====================
+    // M=64 layout: S row r sits in lane (r % 16) of TMEM quadrant r / 16.  Warp
+    // w reads quadrant w % 4, tile columns [64 (w / 4), +64): lanes 0-15 the
+    // first 32 of those, lanes 16-31 the next 32.
+    const int qd = warp & 3, ch = warp >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
+    const int r = 16 * qd + (lane & 15);
+    const int cb = 64 * ch + 32 * (lane >> 4);              // first tile column of this thread
+    const int64_t rowq = q0 + r;
+    const bool row_ok = rowq < a.Lq;
+    const float scale = a.sm_scale;
+    bool ok = true;
+    int j = 0;
+    // S tile of job jj into s, this thread's bias values into bias; both slots released
+    auto read_tile = [&](int jj, uint32_t (&s)[32], float (&bias)[32]) -> bool {
+      const int bf = jj % RBUF, bs = jj % RBR;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&ms.bfull[bs]), (jj / RBR) & 1, abort_flag)) return false;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&ms.sdone[bf]), (jj / RBUF) & 1, abort_flag)) return false;
+      tc::fence_after_sync();
+      tc::tmem_ld_16x32bx2_x32(tbase + lane_off + RN * bf + 64 * ch, s);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(&ms.bias[bs][cb + i]);
+        bias[i] = v.x;
+        bias[i + 1] = v.y;
+        bias[i + 2] = v.z;
+        bias[i + 3] = v.w;
+      }
+      tc::tmem_wait_ld();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(tc::smem_addr(&ms.sfree[bf]));
+        tc::mbar_arrive(tc::smem_addr(&ms.bfree[bs]));
+      }
+      return true;
+    };
+    // ---- pass 1: online log-sum-exp (log2 domain) per (query, head)
+    for (int g = 0; ok && g < G; ++g) {
+      float m = -INFINITY, l = 0.f;
+      for (int t = 0; t < NT; ++t, ++j) {
+        float bias[32];
+        uint32_t s[32];
+        if (!(ok = read_tile(j, s, bias))) break;
+        float y[32], mb = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = t * RN + cb + i;
+          const float x = __uint_as_float(s[i]) * scale + bias[i];
+          y[i] = c < C ? x * kLog2e : -INFINITY;
+          mb = fmaxf(mb, y[i]);
+        }
+        if (mb > m) {
+          l = (m == -INFINITY) ? 0.f : l * fast_exp2(m - mb);
+          m = mb;
+        }
+        if (m != -INFINITY) {
+          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s4[i & 3] += fast_exp2(y[i] - m);
+          l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        }
+      }
+      if (!ok) break;
+      // combine the two column quarters held by this warp (lanes t, t+16)
+      const float mo = __shfl_xor_sync(0xffffffffu, m, 16), lo = __shfl_xor_sync(0xffffffffu, l, 16);
+      const float mn = fmaxf(m, mo);
+      l = (mn == -INFINITY) ? 0.f : l * fast_exp2(m - mn) + lo * fast_exp2(mo - mn);
+      m = mn;
+      if (lane < 16) {
+        ms.part[ch][r][g][0] = m;
+        ms.part[ch][r][g][1] = l;
+      }
+    }
+    // both column halves of a row meet in shared memory
+    asm volatile("bar.sync 1, 256;\n" ::: "memory");
+    if (ok && ch == 0 && lane < 16) {
+      for (int g = 0; g < G; ++g) {
+        const float m1 = ms.part[0][r][g][0], l1 = ms.part[0][r][g][1];
+        const float m2 = ms.part[1][r][g][0], l2 = ms.part[1][r][g][1];
+        const float mn = fmaxf(m1, m2);
+        const float lsum = (mn == -INFINITY) ? 0.f : l1 * fast_exp2(m1 - mn) + l2 * fast_exp2(m2 - mn);
+        const float lse = lsum > 0.f ? (mn + __log2f(lsum)) * kLn2 : -INFINITY;
+        const float loc = row_ok ? a.local_lse[((int64_t)b * a.Lq + rowq) * Hq + hk * G + g] : 0.f;
+        const float mx = fmaxf(loc, lse), mnv = fminf(loc, lse);
+        ms.T[r][g] = (mx == -INFINITY) ? -INFINITY : mx + log1pf(expf(mnv - mx));
+      }
+    }
+    asm volatile("bar.sync 1, 256;\n" ::: "memory");
+    // ---- pass 2: keys = max_g (x - T_g), the drop rule, fp32 keys to the workspace
+    int64_t clo = 1, chi = 0;                 // dropped chunk window [clo, chi] of this row
+    if (a.drop == nullptr && a.window >= 0) {
+      const int64_t pos = a.q_offset + rowq, L = static_cast<int64_t>(C) * kChunk;
+      int64_t lo = pos - a.window, hi = pos + a.window;
+      if (lo < 0) lo = 0;
+      if (hi > L - 1) hi = L - 1;
+      clo = lo / kChunk;
+      chi = hi / kChunk;
+    }
+    float* krow = a.keys + (((int64_t)b * a.Lq + rowq) * a.Hkv + hk) * C;
+    for (int t = 0; ok && t < NT; ++t) {
+      float key[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) key[i] = -INFINITY;
+      for (int g = 0; g < G; ++g, ++j) {
+        const float Tg = ms.T[r][g];
+        float bias[32];
+        uint32_t s[32];
+        if (!(ok = read_tile(j, s, bias))) break;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = __uint_as_float(s[i]) * scale + bias[i];
+          key[i] = fmaxf(key[i], x - Tg);
+        }
+      }
+      if (!ok || !row_ok) continue;
+      // dropped columns as a bit mask (bit i = column cb + i of this tile)
+      uint32_t dm = 0u;
+      if (a.drop != nullptr) {
+        const int32_t* dr = a.drop + ((int64_t)b * a.Lq + rowq) * C;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) {
+          const int c = t * RN + cb + i;
+          if (c < C && dr[c] != 0) dm |= 1u << i;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = t * RN + cb + i;
+          if (c < C && (ms.chunk_ok[c] == 0 || (c >= clo && c <= chi))) dm |= 1u << i;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if ((dm >> i) & 1u) key[i] = -INFINITY;
+      const int c0 = t * RN + cb;
+      if (c0 + 32 <= C && (C & 3) == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(krow + c0 + i) = make_float4(key[i], key[i + 1], key[i + 2], key[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i < C) krow[c0 + i] = key[i];
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (tid == 0 && ms.abort_flag) atomicOr(&g_route_error, 1);
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, 512);
+  }
+}
 
 // Route weights of one (query, head) row; lane k holds selected slot k.
 // r = raw score (already bf16-rounded) + bias, -inf for empty slots.
@@ -95,237 +425,105 @@ __device__ __forceinline__ void route_weights_row(float r, bool valid, float loc
   w_local = 1.0f - msig;
 }
 
-__device__ __forceinline__ bool dropped(const RouteArgs& a, int b, int64_t pos, int c,
-                                        const uint8_t* chunk_ok_s) {
-  if (a.drop != nullptr) return a.drop[((int64_t)b * a.Lq + (pos - a.q_offset)) * a.C + c] != 0;
-  if (chunk_ok_s[c] == 0) return true;
-  if (a.window < 0) return false;
-  const int64_t L = static_cast<int64_t>(a.C) * kChunk;
-  int64_t lo = pos - a.window, hi = pos + a.window;
-  if (lo < 0) lo = 0;
-  if (hi > L - 1) hi = L - 1;
-  return c >= lo / kChunk && c <= hi / kChunk;
-}
+constexpr int SEL_WARPS = 8;
+constexpr int SEL_CPL = kMaxChunks / 32;   // keys per lane at most
 
-__global__ void __launch_bounds__(NW * 32) route_kernel(RouteArgs a) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* keys = reinterpret_cast<float*>(smem_raw);                 // [QB][C]
-  float* xg = keys + QB * a.C;                                      // [NW][QB][CT]
-  float* Tsm = xg + NW * QB * CT;                                   // [QB][NW]
-  int* sel = reinterpret_cast<int*>(Tsm + QB * NW);                 // [QB][32]
-  uint8_t* chunk_ok_s = reinterpret_cast<uint8_t*>(sel + QB * 32);  // [C]
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g4 = lane >> 2, tq = lane & 3;
+// One warp per (query, KV head): top-K of the row's keys, raw scores, weights.
+__global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs a) {
+  __shared__ int sel_s[SEL_WARPS][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.y, b = blockIdx.z;
-  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * QB;
-  const int C = a.C, G = a.G, Hq = a.Hkv * a.G;
-
-  for (int c = tid; c < C; c += NW * 32)
-    chunk_ok_s[c] = a.chunk_ok ? a.chunk_ok[(int64_t)b * C + c] : 1;
-
-  const bool gemm_warp = warp < G;
-  const int hq = hk * G + warp;
-  const int64_t row0 = q0 + g4, row1 = q0 + g4 + 8;
-  const bool ok0 = row0 < a.Lq, ok1 = row1 < a.Lq;
-
-  uint32_t qa[D / 16][4];
-  if (gemm_warp) {
-    const __nv_bfloat16* r0p = a.rq + (((int64_t)b * a.Lq + (ok0 ? row0 : 0)) * Hq + hq) * D;
-    const __nv_bfloat16* r1p = a.rq + (((int64_t)b * a.Lq + (ok1 ? row1 : 0)) * Hq + hq) * D;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * SEL_WARPS + warp;
+  if (row >= a.Lq) return;
+  const int C = a.C, G = a.G, K = a.K, Hq = a.Hkv * a.G;
+  const int cpl = (C + 31) / 32;
+  const float* krow = a.keys + (((int64_t)b * a.Lq + row) * a.Hkv + hk) * C;
+  uint32_t u[SEL_CPL];
+  const uint32_t neg_inf_ord = f2ord(-INFINITY);
+  int nf = 0;
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const int c0 = ks * 16 + tq * 2;
-      qa[ks][0] = ok0 ? *reinterpret_cast<const uint32_t*>(r0p + c0) : 0u;
-      qa[ks][1] = ok1 ? *reinterpret_cast<const uint32_t*>(r1p + c0) : 0u;
-      qa[ks][2] = ok0 ? *reinterpret_cast<const uint32_t*>(r0p + c0 + 8) : 0u;
-      qa[ks][3] = ok1 ? *reinterpret_cast<const uint32_t*>(r1p + c0 + 8) : 0u;
+  for (int i = 0; i < SEL_CPL; ++i) {
+    const int c = i * 32 + lane;
+    u[i] = (i < cpl && c < C) ? f2ord(krow[c]) : 0u;
+    nf += u[i] > neg_inf_ord;
+  }
+  nf = __reduce_add_sync(0xffffffffu, nf);
+  const int keff = nf < K ? nf : K;
+  // radix search for the largest threshold with at least keff keys >= it
+  uint32_t thr = 0;
+  if (keff > 0) {
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = thr | (1u << bit);
+      int cnt = 0;
+#pragma unroll
+      for (int i = 0; i < SEL_CPL; ++i) cnt += (i < cpl) & (u[i] >= cand);
+      cnt = __reduce_add_sync(0xffffffffu, cnt);
+      if (cnt >= keff) thr = cand;
     }
   }
-  // landmark row pointer for chunk c of this warp's head
-  auto lmk_row = [&](int c) {
-    return a.lmk + (((int64_t)b * C + c) * a.Hkv + hk) * (int64_t)(a.lmk_g_stride ? G * D : D) +
-           (int64_t)warp * a.lmk_g_stride;
-  };
-  // S tile (16 queries x 8 chunks starting at c0), scaled; invalid chunk cols -> -inf
-  auto s_tile = [&](int c0, float* s) {
-    s[0] = s[1] = s[2] = s[3] = 0.f;
-    const int cc = c0 + g4;
-    const __nv_bfloat16* lp = lmk_row(cc < C ? cc : 0);
+  int ngt = 0;
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(lp + ks * 16 + tq * 2);
-      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(lp + ks * 16 + tq * 2 + 8);
-      mma_bf16(s, qa[ks], b0, b1);
-    }
+  for (int i = 0; i < SEL_CPL; ++i) ngt += (i < cpl) & (u[i] > thr);
+  ngt = keff > 0 ? __reduce_add_sync(0xffffffffu, ngt) : 0;
+  int need_eq = keff - ngt, taken = 0;
+  // ascending chunk order; ties at the threshold: lowest chunk ids first
 #pragma unroll
-    for (int i = 0; i < 4; ++i) s[i] *= a.sm_scale;
-  };
-  auto bias_of = [&](int c) -> float {
-    return a.bias ? a.bias[((int64_t)b * C + c) * Hq + hq] : 0.f;
-  };
-
-  // ---- pass 1: T = logaddexp(local_lse, logsumexp_c x) ----------------------
-  if (gemm_warp) {
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    for (int c0 = 0; c0 < C; c0 += 8) {
-      float s[4];
-      s_tile(c0, s);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = c0 + tq * 2 + (i & 1);
-        const float x = c < C ? s[i] + bias_of(c) : -INFINITY;
-        const int hr = i >> 1;
-        if (x > m[hr]) {
-          l[hr] = l[hr] * expf(m[hr] - x) + 1.f;
-          m[hr] = x;
-        } else if (x != -INFINITY) {
-          l[hr] += expf(x - m[hr]);
-        }
-      }
-    }
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
-#pragma unroll
-      for (int o = 1; o <= 2; o <<= 1) {
-        const float mo = __shfl_xor_sync(0xffffffffu, m[hr], o);
-        const float lo = __shfl_xor_sync(0xffffffffu, l[hr], o);
-        const float mn = fmaxf(m[hr], mo);
-        l[hr] = (mn == -INFINITY) ? 0.f : l[hr] * expf(m[hr] - mn) + lo * expf(mo - mn);
-        m[hr] = mn;
-      }
-      const float lse = (l[hr] > 0.f) ? m[hr] + logf(l[hr]) : -INFINITY;
-      const int64_t row = hr ? row1 : row0;
-      const bool ok = hr ? ok1 : ok0;
-      const float loc = ok ? a.local_lse[((int64_t)b * a.Lq + row) * Hq + hq] : 0.f;
-      const float mx = fmaxf(loc, lse), mnv = fminf(loc, lse);
-      const float T = (mx == -INFINITY) ? -INFINITY : mx + log1pf(expf(mnv - mx));
-      if (tq == 0) Tsm[(g4 + hr * 8) * NW + warp] = T;
-    }
+  for (int i = 0; i < SEL_CPL; ++i) {
+    if (i >= cpl || keff == 0) break;
+    const int c = i * 32 + lane;
+    const bool in = c < C;
+    const bool gt = in && u[i] > thr;
+    const bool eq = in && u[i] == thr;
+    const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
+    const int eq_before = __popc(eq_mask & ((1u << lane) - 1u));
+    const bool pick = gt || (eq && eq_before < need_eq);
+    need_eq -= __popc(eq_mask) < need_eq ? __popc(eq_mask) : need_eq;
+    const uint32_t pm = __ballot_sync(0xffffffffu, pick);
+    if (pick) sel_s[warp][taken + __popc(pm & ((1u << lane) - 1u))] = c;
+    taken += __popc(pm);
   }
-  __syncthreads();
-
-  // ---- pass 2: keys = max_g (x - T), dropped -> -inf -------------------------
-  for (int ct = 0; ct < C; ct += CT) {
-    if (gemm_warp) {
-      const float T0 = Tsm[g4 * NW + warp], T1 = Tsm[(g4 + 8) * NW + warp];
-#pragma unroll 2
-      for (int n = 0; n < CT / 8; ++n) {
-        const int c0 = ct + n * 8;
-        if (c0 >= C) break;
-        float s[4];
-        s_tile(c0, s);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int cl = n * 8 + tq * 2 + (i & 1);
-          const int c = ct + cl;
-          const float x = c < C ? s[i] + bias_of(c) : -INFINITY;
-          xg[(warp * QB + g4 + (i >> 1) * 8) * CT + cl] = x - ((i >> 1) ? T1 : T0);
-        }
-      }
-    }
-    __syncthreads();
-    for (int e = tid; e < QB * CT; e += NW * 32) {
-      const int qi = e / CT, cl = e % CT, c = ct + cl;
-      if (c >= C) continue;
-      float kmax = -INFINITY;
-      for (int gg = 0; gg < G; ++gg) kmax = fmaxf(kmax, xg[(gg * QB + qi) * CT + cl]);
-      const int64_t pos = a.q_offset + q0 + qi;
-      if (q0 + qi < a.Lq && dropped(a, b, pos, c, chunk_ok_s)) kmax = -INFINITY;
-      keys[qi * C + c] = kmax;
-    }
-    __syncthreads();
-  }
-
-  // ---- top-K per query: warp w -> queries w, w+8 ------------------------------
-  for (int qi = warp; qi < QB; qi += NW) {
-    const int64_t row = q0 + qi;
-    if (row >= a.Lq) continue;
-    const float* kr = keys + qi * C;
-    const uint32_t neg_inf_ord = f2ord(-INFINITY);
-    int nf = 0;
-    for (int c = lane; c < C; c += 32) nf += f2ord(kr[c]) > neg_inf_ord;
-    nf = __reduce_add_sync(0xffffffffu, nf);
-    const int keff = nf < a.K ? nf : a.K;
-    uint32_t thr = 0;
-    if (keff > 0) {
-      for (int bit = 31; bit >= 0; --bit) {
-        const uint32_t cand = thr | (1u << bit);
-        int cnt = 0;
-        for (int c = lane; c < C; c += 32) cnt += f2ord(kr[c]) >= cand;
-        cnt = __reduce_add_sync(0xffffffffu, cnt);
-        if (cnt >= keff) thr = cand;
-      }
-    }
-    int ngt = 0;
-    for (int c = lane; c < C; c += 32) ngt += f2ord(kr[c]) > thr;
-    ngt = keff > 0 ? __reduce_add_sync(0xffffffffu, ngt) : 0;
-    int need_eq = keff - ngt, taken = 0;
-    // ascending chunk order; ties at the threshold: lowest chunk ids first
-    for (int cb = 0; cb < C && keff > 0; cb += 32) {
-      const int c = cb + lane;
-      const uint32_t u = c < C ? f2ord(kr[c]) : 0u;
-      const bool gt = c < C && u > thr;
-      const bool eq = c < C && u == thr;
-      const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
-      const int eq_before = __popc(eq_mask & ((1u << lane) - 1u));
-      const bool pick = gt || (eq && eq_before < need_eq);
-      need_eq -= __popc(eq_mask) < need_eq ? __popc(eq_mask) : need_eq;
-      const uint32_t pm = __ballot_sync(0xffffffffu, pick);
-      if (pick) sel[qi * 32 + taken + __popc(pm & ((1u << lane) - 1u))] = c;
-      taken += __popc(pm);
-    }
-    __syncwarp();
-    for (int k = lane; k < a.K; k += 32) {
-      const int c = k < keff ? sel[qi * 32 + k] : -1;
-      if (k >= keff) sel[qi * 32 + k] = -1;
-      a.indices[(((int64_t)b * a.Lq + row) * a.Hkv + hk) * a.K + k] = c;
-    }
-  }
-  __syncthreads();
-
-  // ---- raw scores + route weights: warp g, lane = slot ------------------------
-  if (gemm_warp) {
-    for (int qi = 0; qi < QB; ++qi) {
-      const int64_t row = q0 + qi;
-      if (row >= a.Lq) break;
-      const int c = lane < a.K ? sel[qi * 32 + lane] : -1;
-      float raw = -INFINITY;
-      if (c >= 0) {
-        const __nv_bfloat16* qp = a.rq + (((int64_t)b * a.Lq + row) * Hq + hq) * D;
-        const __nv_bfloat16* lp = lmk_row(c);
-        float acc = 0.f;
+  __syncwarp();
+  const int csel = lane < keff ? sel_s[warp][lane] : -1;
+  if (lane < K) a.indices[(((int64_t)b * a.Lq + row) * a.Hkv + hk) * K + lane] = csel;
+  // raw scores of the selection (lane = slot) and route weights, head by head
+  for (int g = 0; g < G; ++g) {
+    const int hq = hk * G + g;
+    float raw = -INFINITY;
+    if (csel >= 0) {
+      const __nv_bfloat16* qp = a.rq + (((int64_t)b * a.Lq + row) * Hq + hq) * D;
+      const __nv_bfloat16* lp = a.lmk + (((int64_t)b * C + csel) * a.Hkv + hk) * (int64_t)(a.lmk_per_qhead ? G * D : D) +
+                                (a.lmk_per_qhead ? g * D : 0);
+      float acc = 0.f;
 #pragma unroll 4
-        for (int p = 0; p < D / 8; ++p) {
-          const uint4 qv = *reinterpret_cast<const uint4*>(qp + p * 8);
-          const uint4 lv = *reinterpret_cast<const uint4*>(lp + p * 8);
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&qv);
-          const uint32_t* lw = reinterpret_cast<const uint32_t*>(&lv);
+      for (int p = 0; p < D / 8; ++p) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(qp + p * 8);
+        const uint4 lv = *reinterpret_cast<const uint4*>(lp + p * 8);
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(&qv);
+        const uint32_t* lw = reinterpret_cast<const uint32_t*>(&lv);
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const float2 x = unpack_bf16x2(qw[w]), y = unpack_bf16x2(lw[w]);
-            acc = fmaf(x.x, y.x, acc);
-            acc = fmaf(x.y, y.y, acc);
-          }
+        for (int w = 0; w < 4; ++w) {
+          const float2 x = unpack_bf16x2(qw[w]), y = unpack_bf16x2(lw[w]);
+          acc = fmaf(x.x, y.x, acc);
+          acc = fmaf(x.y, y.y, acc);
         }
-        raw = acc * a.sm_scale;
       }
-      const int64_t o = (((int64_t)b * a.Lq + row) * Hq + hq) * a.K + lane;
-      if (lane < a.K) {
-        if (a.scores_f32) static_cast<float*>(a.scores)[o] = raw;
-        else static_cast<__nv_bfloat16*>(a.scores)[o] = f2bf(raw);
-      }
-      if (a.remote_w != nullptr) {
-        // the weights see the scores as the reference stores them (bf16)
-        const float sc = a.scores_f32 ? raw : round_bf16(raw);
-        const float r = c >= 0 ? sc + bias_of(c) : -INFINITY;
-        const float loc = a.local_lse[((int64_t)b * a.Lq + row) * Hq + hq];
-        float wr, wl;
-        route_weights_row(r, c >= 0, loc, a.K, a.weight_mode, a.temperature, a.gate_scale,
-                          a.gate_offset, wr, wl);
-        if (lane < a.K) a.remote_w[o] = f2bf(wr);
-        if (lane == 0) a.local_w[((int64_t)b * a.Lq + row) * Hq + hq] = f2bf(wl);
-      }
+      raw = acc * a.sm_scale;
+    }
+    const int64_t o = (((int64_t)b * a.Lq + row) * Hq + hq) * K + lane;
+    if (lane < K) {
+      if (a.scores_f32) static_cast<float*>(a.scores)[o] = raw;
+      else static_cast<__nv_bfloat16*>(a.scores)[o] = f2bf(raw);
+    }
+    if (a.remote_w != nullptr) {
+      // the weights see the scores as the reference stores them (bf16)
+      const float sc = a.scores_f32 ? raw : round_bf16(raw);
+      const float bias = (csel >= 0 && a.bias != nullptr) ? a.bias[((int64_t)b * C + csel) * Hq + hq] : 0.f;
+      const float rr = csel >= 0 ? sc + bias : -INFINITY;
+      const float loc = a.local_lse[((int64_t)b * a.Lq + row) * Hq + hq];
+      float wr, wl;
+      route_weights_row(rr, csel >= 0, loc, K, a.weight_mode, a.temperature, a.gate_scale, a.gate_offset, wr, wl);
+      if (lane < K) a.remote_w[o] = f2bf(wr);
+      if (lane == 0) a.local_w[((int64_t)b * a.Lq + row) * Hq + hq] = f2bf(wl);
     }
   }
 }
@@ -356,11 +554,32 @@ __global__ void route_weights_kernel(const __nv_bfloat16* __restrict__ scores,
   if (lane == 0) local_w[r] = f2bf(wl);
 }
 
-size_t route_smem_bytes(int C) {
-  return sizeof(float) * (QB * C + NW * QB * CT + QB * NW) + sizeof(int) * QB * 32 + C;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+              const cuuint32_t* box) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr) return false;
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
+                  strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
+
+extern "C" size_t mrsa_route_topk_workspace_size(int64_t batch, int64_t q_len, int64_t chunks,
+                                                 int64_t kv_heads) {
+  if (batch < 1 || q_len < 0 || chunks < 1 || kv_heads < 1) return 0;
+  return static_cast<size_t>(batch * q_len * kv_heads * chunks) * sizeof(float);
+}
 
 extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int lmk_per_qhead,
                                const float* local_lse, const float* bias, const int32_t* drop_mask,
@@ -369,29 +588,35 @@ extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int l
                                void* remote_w, void* local_w, int weight_mode, float temperature,
                                float gate_scale, float gate_offset, int64_t batch, int64_t q_len,
                                int64_t chunks, int64_t kv_heads, int64_t groups, int64_t head_dim,
-                               int64_t topk, mrsa_stream_t stream) {
+                               int64_t topk, void* workspace, size_t workspace_bytes,
+                               mrsa_stream_t stream) {
   if (!route_q || !landmarks || !local_lse || !indices || !scores_out) return MRSA_ERR_NULL;
   if ((remote_w == nullptr) != (local_w == nullptr)) return MRSA_ERR_NULL;
-  if (head_dim != D || groups < 1 || groups > NW || kv_heads < 1 || batch < 1 || q_len < 0 ||
+  if (head_dim != D || groups < 1 || groups > RGMAX || kv_heads < 1 || batch < 1 || q_len < 0 ||
       chunks < 1 || chunks > kMaxChunks || topk < 1 || topk > 32 || kv_heads > 65535 ||
-      batch > 65535 || q_offset < 0)
+      batch > 65535 || q_offset < 0 || batch * q_len * kv_heads * groups > 0x7fffffffLL ||
+      batch * chunks > 0x7fffffffLL)
     return MRSA_ERR_SHAPE;
   if (scores_dtype != MRSA_BF16 && scores_dtype != MRSA_F32) return MRSA_ERR_ARG;
   if (weight_mode != MRSA_WEIGHTS_AFFINE && weight_mode != MRSA_WEIGHTS_SOFTMAX) return MRSA_ERR_ARG;
   if (!(temperature > 0.f)) return MRSA_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(route_q) & 15u) || (reinterpret_cast<uintptr_t>(landmarks) & 15u))
+  if ((reinterpret_cast<uintptr_t>(route_q) & 15u) || (reinterpret_cast<uintptr_t>(landmarks) & 15u) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15u))
     return MRSA_ERR_ALIGN;
   if (q_len == 0) return MRSA_OK;
+  if (workspace == nullptr || workspace_bytes < mrsa_route_topk_workspace_size(batch, q_len, chunks, kv_heads))
+    return MRSA_ERR_WORKSPACE;
   RouteArgs a;
   a.rq = static_cast<const __nv_bfloat16*>(route_q);
   a.lmk = static_cast<const __nv_bfloat16*>(landmarks);
-  a.lmk_g_stride = lmk_per_qhead ? D : 0;
+  a.lmk_per_qhead = lmk_per_qhead ? 1 : 0;
   a.local_lse = local_lse;
   a.bias = bias;
   a.drop = drop_mask;
   a.chunk_ok = chunk_ok;
   a.window = window;
   a.q_offset = q_offset;
+  a.keys = static_cast<float*>(workspace);
   a.indices = indices;
   a.scores = scores_out;
   a.scores_f32 = scores_dtype == MRSA_F32;
@@ -407,15 +632,34 @@ extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int l
   a.G = static_cast<int>(groups);
   a.K = static_cast<int>(topk);
   a.sm_scale = 1.0f / sqrtf(static_cast<float>(D));
-  const size_t smem = route_smem_bytes(a.C);
-  if (cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  int nst = RMAXST;
+  while (nst > 2 && key_smem_bytes(a.G, nst) > static_cast<size_t>(kSmemLimit)) --nst;
+  a.nst = nst;
+  // route_q [B*Lq rows][Hq][128] as (dim-in-half, row, half, head): one box = 64 query rows of one head
+  // landmarks [B*C rows][Hkv][G'][128] as (dim-in-half, row, half, head-in-group, kv head): 128 chunks
+  const int64_t Hq = kv_heads * groups, Gl = lmk_per_qhead ? groups : 1;
+  CUtensorMap tm_q, tm_l;
+  const cuuint64_t q_dims[4] = {64, static_cast<cuuint64_t>(batch * q_len), 2, static_cast<cuuint64_t>(Hq)};
+  const cuuint64_t q_str[3] = {static_cast<cuuint64_t>(Hq * D * 2), 128, 256};
+  const cuuint32_t q_box[4] = {64, RQ, 2, 1};
+  const cuuint64_t l_dims[5] = {64, static_cast<cuuint64_t>(batch * chunks), 2, static_cast<cuuint64_t>(Gl),
+                                static_cast<cuuint64_t>(kv_heads)};
+  const cuuint64_t l_str[4] = {static_cast<cuuint64_t>(kv_heads * Gl * D * 2), 128, 256, static_cast<cuuint64_t>(Gl * D * 2)};
+  const cuuint32_t l_box[5] = {64, RN, 2, 1, 1};
+  if (!make_map(&tm_q, route_q, 4, q_dims, q_str, q_box) || !make_map(&tm_l, landmarks, 5, l_dims, l_str, l_box))
+    return MRSA_ERR_LAUNCH;
+  const size_t smem = key_smem_bytes(a.G, nst);
+  if (cudaFuncSetAttribute(route_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return MRSA_ERR_LAUNCH;
-  const int64_t blocks = (q_len + QB - 1) / QB;
-  if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
-  dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(kv_heads),
-            static_cast<unsigned>(batch));
-  route_kernel<<<grid, NW * 32, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t kblocks = (q_len + RQ - 1) / RQ;
+  dim3 kgrid(static_cast<unsigned>(kblocks), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
+  route_keys_kernel<<<kgrid, R_THREADS, smem, st>>>(tm_q, tm_l, a);
+  MRSA_CHECK_LAUNCH();
+  const int64_t sblocks = (q_len + SEL_WARPS - 1) / SEL_WARPS;
+  dim3 sgrid(static_cast<unsigned>(sblocks), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
+  route_select_kernel<<<sgrid, SEL_WARPS * 32, 0, st>>>(a);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
 }
@@ -443,3 +687,16 @@ extern "C" int mrsa_route_weights(const void* scores, const int32_t* indices, co
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
 }
+
+namespace mrsa {
+// Read (and optionally clear) the routing kernels' device error flag.
+int route_error_flags(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_route_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_route_error, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+}  // namespace mrsa

@@ -81,11 +81,13 @@ def _route(q5: torch.Tensor, k_lmks: torch.Tensor, lse: torch.Tensor, topk: int,
         mode, temp, gs, go = weights
         rw = torch.empty(b, l, hkv * g, topk, device=dev, dtype=torch.bfloat16)
         lw = torch.empty(b, l, hkv * g, device=dev, dtype=torch.bfloat16)
+    ws_bytes = _lib.load().mrsa_route_topk_workspace_size(b, l, s, hkv)
+    ws = torch.empty(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
     _lib.call("mrsa_route_topk", _lib.ptr(q), _lib.ptr(lm), per_q, _lib.ptr(lse_f), _lib.ptr(bias_f),
               _lib.ptr(drop), _lib.ptr(chunk_ok), int(window), int(q_offset), _lib.ptr(idx),
               _lib.ptr(sc), _lib.F32 if scores_dtype == torch.float32 else _lib.BF16,
               _lib.ptr(rw), _lib.ptr(lw), int(mode), float(temp), float(gs), float(go),
-              b, l, s, hkv, g, d, int(topk), _lib.stream_of(q))
+              b, l, s, hkv, g, d, int(topk), _lib.ptr(ws), ws.numel(), _lib.stream_of(q))
     return idx, sc, rw, lw
 
 

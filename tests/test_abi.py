@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(mrsa):
 
 def test_strerror_and_version(mrsa):
     lib = mrsa._lib.load()
-    assert lib.mrsa_abi_version() == 1
+    assert lib.mrsa_abi_version() == 2
     assert lib.mrsa_strerror(0) == b"ok"
     assert b"NULL" in lib.mrsa_strerror(-1)
     assert lib.mrsa_strerror(-99) == b"unknown error"
@@ -55,14 +55,19 @@ def test_bad_arguments_return_codes_without_device(mrsa):
     # topk > 32 and too many chunks are shape errors
     args = [dummy, dummy, 1, dummy, None, None, None, 256, 0, dummy, dummy, 0, None, None, 0, 1.0, 1.0,
             0.0, 1, 64, 4, 4, 7, 128]
-    assert lib.mrsa_route_topk(*args, 33, None) == -2
+    assert lib.mrsa_route_topk(*args, 33, dummy, 1 << 30, None) == -2
     args2 = list(args)
     args2[20] = 4096
-    assert lib.mrsa_route_topk(*args2, 32, None) == -2
+    assert lib.mrsa_route_topk(*args2, 32, dummy, 1 << 30, None) == -2
     # bad temperature
     args3 = list(args)
     args3[15] = 0.0
-    assert lib.mrsa_route_topk(*args3, 32, None) == -5
+    assert lib.mrsa_route_topk(*args3, 32, dummy, 1 << 30, None) == -5
+    # the keys workspace: B*Lq*Hkv*C fp32, refused when missing or short
+    assert lib.mrsa_route_topk_workspace_size(1, 64, 4, 4) == 64 * 4 * 4 * 4
+    assert lib.mrsa_route_topk_workspace_size(0, 64, 4, 4) == 0
+    assert lib.mrsa_route_topk(*args, 32, None, 0, None) == -6
+    assert lib.mrsa_route_topk(*args, 32, dummy, 64 * 4 * 4 * 4 - 1, None) == -6
     # selected attention: chunk must be 64, kv_len a multiple of it
     assert lib.mrsa_selected_attention(dummy, dummy, dummy, None, dummy, dummy, None, None, dummy, 0.1, 1,
                                        1, 64, 100, 4, 7, 128, 32, 64, None) == -2
@@ -83,8 +88,8 @@ def test_route_layer_workspace_size_formula(mrsa):
     n = lib.mrsa_route_layer_workspace_size(C.byref(a))
     l, hq, hkv, d, k, c = 16384, 28, 4, 128, 32, 256
     expect = (3 * l * hq * d * 2 + l * hkv * d * 2 + c * hq * d * 2 + 2 * c * hq * 4 + c
-              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2)
-    assert expect <= n <= expect + 13 * 256
+              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2 + l * hkv * c * 4)
+    assert expect <= n <= expect + 14 * 256
 
 
 def test_yarn_host_table_matches_transformers(mrsa):
