@@ -101,8 +101,8 @@ int mrsa_remote_drop_mask(const uint8_t* key_valid, int32_t* out, int64_t batch,
  * mode MRSA_WEIGHTS_AFFINE (_route_weights_torch with gate scale/offset) or
  * MRSA_WEIGHTS_SOFTMAX (route_weights).
  * workspace: at least mrsa_route_topk_workspace_size() bytes of device memory
- * (the fp32 max-pooled keys [B,Lq,Hkv,C]), 16-byte aligned; MRSA_ERR_WORKSPACE
- * when missing or short.
+ * (the fp32 max-pooled keys [B,Lq,Hkv,C] and the raw scores [B,Lq,Hq,C] in the
+ * scores dtype), 16-byte aligned; MRSA_ERR_WORKSPACE when missing or short.
  * Replaces ops/topk_head_softmax.py:15 ref_softmax_topk_max_pooling and :1242
  * online_softmax_topk_head (post_softmax, non-causal), dream_dllm_hils/routing.py:52
  * route_topk_g7, and fuses dream_dllm_hils/attention.py:126 _route_weights_torch. */
@@ -118,7 +118,7 @@ int mrsa_route_topk(const void* route_q, const void* landmarks, int lmk_per_qhea
 /* Device workspace bytes of mrsa_route_topk (0 for an invalid shape).  No
  * reference counterpart: the reference materialises its scores instead. */
 size_t mrsa_route_topk_workspace_size(int64_t batch, int64_t q_len, int64_t chunks,
-                                      int64_t kv_heads);
+                                      int64_t kv_heads, int64_t groups, int scores_dtype);
 
 /* Route weights from scores [B,L,Hq,K] bf16, indices [B,L,Hkv,K] int32,
  * prior [B,C,Hkv,G] fp32, local_lse [B,L,Hq] fp32.

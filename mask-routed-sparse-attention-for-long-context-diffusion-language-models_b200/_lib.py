@@ -34,7 +34,7 @@ _SIGS = {
     "mrsa_route_topk": [_vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _vp,
                         _int, _f32, _f32, _f32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz,
                         _vp],
-    "mrsa_route_topk_workspace_size": [_i64, _i64, _i64, _i64],
+    "mrsa_route_topk_workspace_size": [_i64, _i64, _i64, _i64, _i64, _int],
     "mrsa_route_weights": [_vp, _vp, _vp, _vp, _vp, _vp, _int, _f32, _f32, _f32,
                            _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_local_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _i64, _f32,

@@ -38,7 +38,7 @@ LayerPlan plan(const mrsa_route_layer_args* a) {
   p.scores = take(B * L * Hq * K * 2);
   p.remote_w = take(B * L * Hq * K * 2);
   p.local_w = take(B * L * Hq * 2);
-  p.route_keys = take(B * L * Hkv * C * 4);
+  p.route_keys = take(mrsa_route_topk_workspace_size(B, L, C, Hkv, Hq / Hkv, MRSA_BF16));
   p.total = off;
   return p;
 }
@@ -105,7 +105,8 @@ extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* wo
   rc = mrsa_route_topk(route_q, lmk, 1, local_lse, prior, nullptr, chunk_ok, a->local_window, 0,
                        indices, scores, MRSA_BF16, remote_w, local_w, MRSA_WEIGHTS_AFFINE,
                        a->temperature, a->gate_scale, a->gate_offset, B, L, C, Hkv, G, D,
-                       a->topk, route_keys, static_cast<size_t>(B * L * Hkv * C * 4), stream);
+                       a->topk, route_keys, mrsa_route_topk_workspace_size(B, L, C, Hkv, G, MRSA_BF16),
+                       stream);
   if (rc) return rc;
   return mrsa_selected_attention(q, k, a->v, a->key_valid, remote_w, indices, local_out, local_w,
                                  a->out, sm_scale, 1, B, L, L, Hkv, G, D, a->topk, mrsa::kChunk,

@@ -58,7 +58,8 @@ struct RouteArgs {
   const int32_t* drop;
   const uint8_t* chunk_ok;
   int64_t window, q_offset;
-  float* keys;              // workspace [B, Lq, Hkv, C]
+  float* keys;              // workspace: keys [B, Lq, Hkv, C] fp32
+  void* raw;                // workspace: raw scaled scores [B, Lq, Hq, C] (scores dtype)
   int32_t* indices;
   void* scores;
   int scores_f32;
@@ -332,9 +333,41 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
         uint32_t s[32];
         if (!(ok = read_tile(j, s, bias))) break;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x = __uint_as_float(s[i]) * scale + bias[i];
-          key[i] = fmaxf(key[i], x - Tg);
+        for (int i = 0; i < 32; ++i) s[i] = __float_as_uint(__uint_as_float(s[i]) * scale);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) key[i] = fmaxf(key[i], (__uint_as_float(s[i]) + bias[i]) - Tg);
+        // the raw scaled scores of every (head, chunk): the selection kernel gathers its slots from here
+        if (row_ok) {
+          const int c0 = t * RN + cb;
+          const int64_t o = (((int64_t)b * a.Lq + rowq) * Hq + hk * G + g) * C + c0;
+          if (a.scores_f32) {
+            float* dst = static_cast<float*>(a.raw) + o;
+            if (c0 + 32 <= C && (C & 3) == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(dst + i) = make_float4(__uint_as_float(s[i]), __uint_as_float(s[i + 1]),
+                                                                  __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (c0 + i < C) dst[i] = __uint_as_float(s[i]);
+            }
+          } else {
+            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.raw) + o;
+            if (c0 + 32 <= C && (C & 7) == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8)
+                *reinterpret_cast<uint4*>(dst + i) = make_uint4(
+                    pack_bf16x2(__uint_as_float(s[i]), __uint_as_float(s[i + 1])),
+                    pack_bf16x2(__uint_as_float(s[i + 2]), __uint_as_float(s[i + 3])),
+                    pack_bf16x2(__uint_as_float(s[i + 4]), __uint_as_float(s[i + 5])),
+                    pack_bf16x2(__uint_as_float(s[i + 6]), __uint_as_float(s[i + 7])));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (c0 + i < C) dst[i] = f2bf(__uint_as_float(s[i]));
+            }
+          }
         }
       }
       if (!ok || !row_ok) continue;
@@ -426,9 +459,11 @@ __device__ __forceinline__ void route_weights_row(float r, bool valid, float loc
 }
 
 constexpr int SEL_WARPS = 8;
-constexpr int SEL_CPL = kMaxChunks / 32;   // keys per lane at most
 
 // One warp per (query, KV head): top-K of the row's keys, raw scores, weights.
+// CPL = keys per lane (C <= 32 * CPL), a compile-time bound so the keys stay in
+// registers.
+template <int CPL>
 __global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs a) {
   __shared__ int sel_s[SEL_WARPS][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -436,15 +471,14 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs 
   const int64_t row = static_cast<int64_t>(blockIdx.x) * SEL_WARPS + warp;
   if (row >= a.Lq) return;
   const int C = a.C, G = a.G, K = a.K, Hq = a.Hkv * a.G;
-  const int cpl = (C + 31) / 32;
   const float* krow = a.keys + (((int64_t)b * a.Lq + row) * a.Hkv + hk) * C;
-  uint32_t u[SEL_CPL];
+  uint32_t u[CPL];
   const uint32_t neg_inf_ord = f2ord(-INFINITY);
   int nf = 0;
 #pragma unroll
-  for (int i = 0; i < SEL_CPL; ++i) {
+  for (int i = 0; i < CPL; ++i) {
     const int c = i * 32 + lane;
-    u[i] = (i < cpl && c < C) ? f2ord(krow[c]) : 0u;
+    u[i] = c < C ? f2ord(krow[c]) : 0u;
     nf += u[i] > neg_inf_ord;
   }
   nf = __reduce_add_sync(0xffffffffu, nf);
@@ -456,20 +490,20 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs 
       const uint32_t cand = thr | (1u << bit);
       int cnt = 0;
 #pragma unroll
-      for (int i = 0; i < SEL_CPL; ++i) cnt += (i < cpl) & (u[i] >= cand);
+      for (int i = 0; i < CPL; ++i) cnt += u[i] >= cand;
       cnt = __reduce_add_sync(0xffffffffu, cnt);
       if (cnt >= keff) thr = cand;
     }
   }
   int ngt = 0;
 #pragma unroll
-  for (int i = 0; i < SEL_CPL; ++i) ngt += (i < cpl) & (u[i] > thr);
+  for (int i = 0; i < CPL; ++i) ngt += u[i] > thr;
   ngt = keff > 0 ? __reduce_add_sync(0xffffffffu, ngt) : 0;
   int need_eq = keff - ngt, taken = 0;
   // ascending chunk order; ties at the threshold: lowest chunk ids first
 #pragma unroll
-  for (int i = 0; i < SEL_CPL; ++i) {
-    if (i >= cpl || keff == 0) break;
+  for (int i = 0; i < CPL; ++i) {
+    if (keff == 0) break;
     const int c = i * 32 + lane;
     const bool in = c < C;
     const bool gt = in && u[i] > thr;
@@ -485,30 +519,15 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs 
   __syncwarp();
   const int csel = lane < keff ? sel_s[warp][lane] : -1;
   if (lane < K) a.indices[(((int64_t)b * a.Lq + row) * a.Hkv + hk) * K + lane] = csel;
-  // raw scores of the selection (lane = slot) and route weights, head by head
+  // raw scores of the selection (lane = slot), gathered from the key kernel's
+  // full score rows, and the route weights, head by head
   for (int g = 0; g < G; ++g) {
     const int hq = hk * G + g;
+    const int64_t srow = (((int64_t)b * a.Lq + row) * Hq + hq) * C;
     float raw = -INFINITY;
-    if (csel >= 0) {
-      const __nv_bfloat16* qp = a.rq + (((int64_t)b * a.Lq + row) * Hq + hq) * D;
-      const __nv_bfloat16* lp = a.lmk + (((int64_t)b * C + csel) * a.Hkv + hk) * (int64_t)(a.lmk_per_qhead ? G * D : D) +
-                                (a.lmk_per_qhead ? g * D : 0);
-      float acc = 0.f;
-#pragma unroll 4
-      for (int p = 0; p < D / 8; ++p) {
-        const uint4 qv = *reinterpret_cast<const uint4*>(qp + p * 8);
-        const uint4 lv = *reinterpret_cast<const uint4*>(lp + p * 8);
-        const uint32_t* qw = reinterpret_cast<const uint32_t*>(&qv);
-        const uint32_t* lw = reinterpret_cast<const uint32_t*>(&lv);
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const float2 x = unpack_bf16x2(qw[w]), y = unpack_bf16x2(lw[w]);
-          acc = fmaf(x.x, y.x, acc);
-          acc = fmaf(x.y, y.y, acc);
-        }
-      }
-      raw = acc * a.sm_scale;
-    }
+    if (csel >= 0)
+      raw = a.scores_f32 ? static_cast<const float*>(a.raw)[srow + csel]
+                         : bf2f(static_cast<const __nv_bfloat16*>(a.raw)[srow + csel]);
     const int64_t o = (((int64_t)b * a.Lq + row) * Hq + hq) * K + lane;
     if (lane < K) {
       if (a.scores_f32) static_cast<float*>(a.scores)[o] = raw;
@@ -575,10 +594,19 @@ bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
 
 }  // namespace
 
+namespace {
+size_t keys_bytes(int64_t batch, int64_t q_len, int64_t chunks, int64_t kv_heads) {
+  return (static_cast<size_t>(batch * q_len * kv_heads * chunks) * sizeof(float) + 255) / 256 * 256;
+}
+}  // namespace
+
 extern "C" size_t mrsa_route_topk_workspace_size(int64_t batch, int64_t q_len, int64_t chunks,
-                                                 int64_t kv_heads) {
-  if (batch < 1 || q_len < 0 || chunks < 1 || kv_heads < 1) return 0;
-  return static_cast<size_t>(batch * q_len * kv_heads * chunks) * sizeof(float);
+                                                 int64_t kv_heads, int64_t groups, int scores_dtype) {
+  if (batch < 1 || q_len < 0 || chunks < 1 || kv_heads < 1 || groups < 1) return 0;
+  if (scores_dtype != MRSA_BF16 && scores_dtype != MRSA_F32) return 0;
+  const size_t raw = static_cast<size_t>(batch * q_len * kv_heads * groups * chunks) *
+                     (scores_dtype == MRSA_F32 ? 4 : 2);
+  return keys_bytes(batch, q_len, chunks, kv_heads) + raw;
 }
 
 extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int lmk_per_qhead,
@@ -604,7 +632,8 @@ extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int l
       (reinterpret_cast<uintptr_t>(workspace) & 15u))
     return MRSA_ERR_ALIGN;
   if (q_len == 0) return MRSA_OK;
-  if (workspace == nullptr || workspace_bytes < mrsa_route_topk_workspace_size(batch, q_len, chunks, kv_heads))
+  if (workspace == nullptr ||
+      workspace_bytes < mrsa_route_topk_workspace_size(batch, q_len, chunks, kv_heads, groups, scores_dtype))
     return MRSA_ERR_WORKSPACE;
   RouteArgs a;
   a.rq = static_cast<const __nv_bfloat16*>(route_q);
@@ -617,6 +646,7 @@ extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int l
   a.window = window;
   a.q_offset = q_offset;
   a.keys = static_cast<float*>(workspace);
+  a.raw = static_cast<char*>(workspace) + keys_bytes(batch, q_len, chunks, kv_heads);
   a.indices = indices;
   a.scores = scores_out;
   a.scores_f32 = scores_dtype == MRSA_F32;
@@ -659,7 +689,10 @@ extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int l
   MRSA_CHECK_LAUNCH();
   const int64_t sblocks = (q_len + SEL_WARPS - 1) / SEL_WARPS;
   dim3 sgrid(static_cast<unsigned>(sblocks), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
-  route_select_kernel<<<sgrid, SEL_WARPS * 32, 0, st>>>(a);
+  if (chunks <= 256) route_select_kernel<8><<<sgrid, SEL_WARPS * 32, 0, st>>>(a);
+  else if (chunks <= 512) route_select_kernel<16><<<sgrid, SEL_WARPS * 32, 0, st>>>(a);
+  else if (chunks <= 1024) route_select_kernel<32><<<sgrid, SEL_WARPS * 32, 0, st>>>(a);
+  else route_select_kernel<64><<<sgrid, SEL_WARPS * 32, 0, st>>>(a);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
 }

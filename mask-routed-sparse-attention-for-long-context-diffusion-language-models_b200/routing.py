@@ -81,7 +81,8 @@ def _route(q5: torch.Tensor, k_lmks: torch.Tensor, lse: torch.Tensor, topk: int,
         mode, temp, gs, go = weights
         rw = torch.empty(b, l, hkv * g, topk, device=dev, dtype=torch.bfloat16)
         lw = torch.empty(b, l, hkv * g, device=dev, dtype=torch.bfloat16)
-    ws_bytes = _lib.load().mrsa_route_topk_workspace_size(b, l, s, hkv)
+    sdt = _lib.F32 if scores_dtype == torch.float32 else _lib.BF16
+    ws_bytes = _lib.load().mrsa_route_topk_workspace_size(b, l, s, hkv, g, sdt)
     ws = torch.empty(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
     _lib.call("mrsa_route_topk", _lib.ptr(q), _lib.ptr(lm), per_q, _lib.ptr(lse_f), _lib.ptr(bias_f),
               _lib.ptr(drop), _lib.ptr(chunk_ok), int(window), int(q_offset), _lib.ptr(idx),

@@ -64,10 +64,13 @@ def test_bad_arguments_return_codes_without_device(mrsa):
     args3[15] = 0.0
     assert lib.mrsa_route_topk(*args3, 32, dummy, 1 << 30, None) == -5
     # the keys workspace: B*Lq*Hkv*C fp32, refused when missing or short
-    assert lib.mrsa_route_topk_workspace_size(1, 64, 4, 4) == 64 * 4 * 4 * 4
-    assert lib.mrsa_route_topk_workspace_size(0, 64, 4, 4) == 0
+    # keys fp32 [B,Lq,Hkv,C] (256-byte rounded) + raw scores [B,Lq,Hq,C] in the scores dtype
+    n = lib.mrsa_route_topk_workspace_size(1, 64, 4, 4, 7, 0)
+    assert n == 64 * 4 * 4 * 4 + 64 * 28 * 4 * 2
+    assert lib.mrsa_route_topk_workspace_size(1, 64, 4, 4, 7, 1) == 64 * 4 * 4 * 4 + 64 * 28 * 4 * 4
+    assert lib.mrsa_route_topk_workspace_size(0, 64, 4, 4, 7, 0) == 0
     assert lib.mrsa_route_topk(*args, 32, None, 0, None) == -6
-    assert lib.mrsa_route_topk(*args, 32, dummy, 64 * 4 * 4 * 4 - 1, None) == -6
+    assert lib.mrsa_route_topk(*args, 32, dummy, n - 1, None) == -6
     # selected attention: chunk must be 64, kv_len a multiple of it
     assert lib.mrsa_selected_attention(dummy, dummy, dummy, None, dummy, dummy, None, None, dummy, 0.1, 1,
                                        1, 64, 100, 4, 7, 128, 32, 64, None) == -2
@@ -88,7 +91,8 @@ def test_route_layer_workspace_size_formula(mrsa):
     n = lib.mrsa_route_layer_workspace_size(C.byref(a))
     l, hq, hkv, d, k, c = 16384, 28, 4, 128, 32, 256
     expect = (3 * l * hq * d * 2 + l * hkv * d * 2 + c * hq * d * 2 + 2 * c * hq * 4 + c
-              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2 + l * hkv * c * 4)
+              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2 + l * hkv * c * 4
+              + l * hq * c * 2)
     assert expect <= n <= expect + 14 * 256
 
 
