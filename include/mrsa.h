@@ -159,7 +159,7 @@ int mrsa_selected_attention(const void* q, const void* k, const void* v, const u
 /* Bit mask of device-side failures recorded since the last clear: bit 0 = a
  * selected-attention CTA gave up waiting on one of its internal barriers (its
  * output rows are then incomplete); bit 1 = a routing key CTA did (its keys,
- * hence its selections, are then incomplete).  Synchronises the current device; with
+ * hence its selections, are then incomplete); bit 2 = a local-window CTA did.  Synchronises the current device; with
  * clear != 0 also resets the mask.  Negative on a CUDA error.  Replaces the
  * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
 int mrsa_device_error_flags(int clear);

@@ -1,0 +1,412 @@
+// Bidirectional banded GQA attention with natural-log LSE on the tcgen05
+// tensor cores (local branch of the route layer, window W+63 with
+// landmark/invalid K,V zeroed; SWA layers, window 1280).  Semantics of
+// dream_dllm_hils/local_attention.py:35-107: zeroed keys keep logit 0 in the
+// softmax and add no value; keys with |i-j| > window are out.
+//
+// One CTA owns 16 queries of one KV head.  Its MMA tile has 128 rows, row
+// 8*qi + g = (query qi, head g of the group; rows g >= G are padding), so each
+// 64-key K/V tile is read once for all heads of the group.  Per key tile t:
+//   S[128 x 64]  = Q . K_t^T               (UMMA M=128, N=64,  K=128, TMEM)
+//   P            = exp2(S*scale*log2e - m)  (one thread per row, online max)
+//   O[128 x 128] += P . V_t                (UMMA M=128, N=128, K=64, TMEM)
+// P goes through shared memory as bf16 hi + lo parts (two MMAs per k-step),
+// keeping ~16 significant bits.  O is rescaled in TMEM when a row's running
+// max grows, between the P.V of tile t-1 and that of tile t.
+// Warps 0-3: softmax and epilogue (warp w = TMEM lanes 32w..32w+31 = rows);
+// warp 4: TMA (Q once, then K, V per tile, 3 stages) and the per-tile key
+// validity mask; warp 5: MMA issue (converged, elect.sync).  Every mbarrier
+// wait is bounded and unwinds through a shared abort flag.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+using namespace mrsa;
+
+namespace {
+
+constexpr int LQ = 16;            // queries per CTA
+constexpr int LR = 128;           // MMA rows = LQ x 8 head rows
+constexpr int LN = 64;            // keys per tile
+constexpr int LST = 3;            // K/V stages
+constexpr int D = kHeadDim;
+constexpr int L_THREADS = 192;    // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr int L_W_LOAD = 4, L_W_MMA = 5;
+constexpr uint32_t kOCol = 128;   // O accumulator columns [128, 256); S buffers at 0 and 64
+
+struct __align__(1024) LocalSmem {
+  unsigned char q[LQ][2048];          // per query: [half][8 head rows][64 dims], 128-byte swizzled
+  unsigned char k[LST][16384];        // [half][64 keys][64 dims]
+  unsigned char v[LST][16384];        // same, read as the MN-major B operand of P.V
+  unsigned char ph[2][16384];         // P hi [128 rows][64 keys]
+  unsigned char pl[2][16384];         // P lo
+  unsigned long long kmask[LST];      // bit j: key j of the stage's tile is usable (not zeroed)
+  uint64_t qfull, kvfull[LST], kvfree[LST], sdone[2], pready[2], pvdone[2], drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(LocalSmem) + 1024 <= 232448, "local attention shared memory over budget");
+
+struct LocalArgs {
+  const uint8_t* key_valid;
+  __nv_bfloat16* out;
+  float* lse;
+  int64_t window, Lq, Lk, q_offset;
+  int skip_inert, chunk, Hq, Hkv, G;
+  float sm_scale;
+};
+
+__device__ int g_local_error;
+
+__device__ __forceinline__ int swz_off(int row, int piece) { return row * 128 + ((piece ^ (row & 7)) << 4); }
+
+__global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, LocalArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  LocalSmem& sm = *reinterpret_cast<LocalSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int G = a.G;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * LQ;
+  const int64_t rows_q = (a.Lq - q0) < LQ ? (a.Lq - q0) : LQ;
+  int64_t j_lo = a.q_offset + q0 - a.window, j_hi = a.q_offset + q0 + rows_q - 1 + a.window;
+  if (j_lo < 0) j_lo = 0;
+  if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
+  const int t_lo = static_cast<int>(j_lo / LN);
+  const int NTL = j_hi >= j_lo ? static_cast<int>(j_hi / LN) - t_lo + 1 : 0;
+
+  if (tid == 0) {
+    tc::mbar_init(tc::smem_addr(&sm.qfull), 1);
+    for (int s = 0; s < LST; ++s) {
+      tc::mbar_init(tc::smem_addr(&sm.kvfull[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.kvfree[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(tc::smem_addr(&sm.sdone[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.pready[s]), 4);
+      tc::mbar_init(tc::smem_addr(&sm.pvdone[s]), 1);
+    }
+    tc::mbar_init(tc::smem_addr(&sm.drain), 1);
+    sm.abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tc::smem_addr(&sm.tmem_base), 256);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = sm.tmem_base;
+
+  if (warp == L_W_LOAD) {
+    // ============================ TMA + key masks =============================
+    const uint32_t qb = tc::smem_addr(&sm.qfull);
+    if (lane == 0) {
+      tc::prefetch_tensormap(&tm_q);
+      tc::prefetch_tensormap(&tm_k);
+      tc::prefetch_tensormap(&tm_v);
+      tc::mbar_arrive_expect_tx(qb, LQ * 2048u);
+      tc::tma_load_4d(tc::smem_addr(&sm.q[0][0]), &tm_q, 0, hk * G, 0, static_cast<int>(b * a.Lq + q0), qb);
+    }
+    int t = 0;
+    for (; t < NTL; ++t) {
+      const int st = t % LST;
+      if (t >= LST && !tc::wait_bounded_warp(tc::smem_addr(&sm.kvfree[st]), ((t / LST) - 1) & 1, abort_flag)) break;
+      const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
+      // usable keys of the tile: inside the sequence, valid, and not a landmark slot when skip_inert
+      uint32_t mk[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t j = j0 + 32 * h + lane;
+        bool ok = j < a.Lk;
+        if (ok && a.key_valid != nullptr) ok = a.key_valid[b * a.Lk + j] != 0;
+        if (ok && a.skip_inert) ok = ((j + 1) % a.chunk) != 0;
+        mk[h] = __ballot_sync(0xffffffffu, ok);
+      }
+      if (lane == 0) {
+        sm.kmask[st] = static_cast<unsigned long long>(mk[0]) | (static_cast<unsigned long long>(mk[1]) << 32);
+        const uint32_t kb = tc::smem_addr(&sm.kvfull[st]);
+        tc::mbar_arrive_expect_tx(kb, 2u * 16384u);
+        tc::tma_load_4d(tc::smem_addr(sm.k[st]), &tm_k, 0, static_cast<int>(b * a.Lk + j0), 0, hk, kb);
+        tc::tma_load_4d(tc::smem_addr(sm.v[st]), &tm_v, 0, static_cast<int>(b * a.Lk + j0), 0, hk, kb);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      tc::mbar_wait(qb, 0);
+      for (int tt = t - LST < 0 ? 0 : t - LST; tt < t; ++tt)
+        tc::mbar_wait(tc::smem_addr(&sm.kvfull[tt % LST]), (tt / LST) & 1);
+    }
+    __syncwarp();
+  } else if (warp == L_W_MMA) {
+    // ============================ MMA issue (converged warp) ==================
+    constexpr uint32_t id_s = tc::idesc_bf16_f32(128, LN, 0, 0);
+    constexpr uint32_t id_o = tc::idesc_bf16_f32(128, D, 0, 1);
+    const uint64_t dq = tc::smem_desc_sw128(tc::smem_addr(&sm.q[0][0]), 16, 2048);
+    const uint64_t dk0 = tc::smem_desc_sw128(tc::smem_addr(sm.k[0]), 16, 1024);
+    const uint64_t dv0 = tc::smem_desc_sw128(tc::smem_addr(sm.v[0]), 8192, 1024);
+    const uint64_t dh0 = tc::smem_desc_sw128(tc::smem_addr(sm.ph[0]), 16, 1024);
+    const uint64_t dl0 = tc::smem_desc_sw128(tc::smem_addr(sm.pl[0]), 16, 1024);
+    auto issue_s = [&](int t) -> bool {
+      const int st = t % LST;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st]), (t / LST) & 1, abort_flag)) return false;
+      tc::fence_after_sync();
+      const uint64_t db = tc::desc_adv(dk0, st * 16384);
+      const uint32_t dS = tbase + LN * (t & 1);
+      if (tc::elect_one()) {
+        tc::mma_bf16<false>(dS, dq, db, id_s);
+#pragma unroll
+        for (int kk = 1; kk < 8; ++kk)
+          tc::mma_bf16<true>(dS, tc::desc_adv(dq, (kk >> 2) * 1024 + (kk & 3) * 32),
+                             tc::desc_adv(db, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
+        tc::mma_commit(tc::smem_addr(&sm.sdone[t & 1]));
+      }
+      __syncwarp();
+      return true;
+    };
+    bool ok = tc::wait_bounded_warp(tc::smem_addr(&sm.qfull), 0, abort_flag);
+    for (int t = 0; ok && t < NTL && t < 2; ++t) ok = issue_s(t);
+    for (int t = 0; ok && t < NTL; ++t) {
+      const int st = t % LST, p2 = t & 1;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.pready[p2]), (t >> 1) & 1, abort_flag)) break;
+      tc::fence_after_sync();
+      const uint64_t dv = tc::desc_adv(dv0, st * 16384), dh = tc::desc_adv(dh0, p2 * 16384),
+                     dl = tc::desc_adv(dl0, p2 * 16384);
+      if (tc::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+        tc::mma_commit(tc::smem_addr(&sm.pvdone[p2]));
+        tc::mma_commit(tc::smem_addr(&sm.kvfree[st]));
+      }
+      __syncwarp();
+      if (t + 2 < NTL) ok = issue_s(t + 2);
+    }
+    if (tc::elect_one()) {
+      tc::mma_commit(tc::smem_addr(&sm.drain));
+      tc::mbar_wait(tc::smem_addr(&sm.drain), 0);
+    }
+    __syncwarp();
+  } else {
+    // ============================ softmax + epilogue (warps 0-3) ==============
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int r = warp * 32 + lane;                  // MMA row = TMEM lane
+    const int qi = r >> 3, g = r & 7;
+    const int64_t pos = a.q_offset + q0 + qi;
+    const float sl2 = a.sm_scale * kLog2e;
+    // zero O (this warp's lanes)
+    {
+      uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int c = 0; c < D; c += 8) tc::tmem_st8(tbase + lane_off + kOCol + c, z);
+      tc::tmem_wait_st();
+    }
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int t = 0; t < NTL; ++t) {
+      const int st = t % LST, p2 = t & 1;
+      const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st]), (t / LST) & 1, abort_flag))) break;
+      const unsigned long long km = sm.kmask[st];
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.sdone[p2]), (t >> 1) & 1, abort_flag))) break;
+      tc::fence_after_sync();
+      uint32_t x[64];
+      tc::tmem_ld16(tbase + lane_off + LN * p2 + 0, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
+      tc::tmem_ld16(tbase + lane_off + LN * p2 + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
+      tc::tmem_ld16(tbase + lane_off + LN * p2 + 32, *reinterpret_cast<uint32_t(*)[16]>(&x[32]));
+      tc::tmem_ld16(tbase + lane_off + LN * p2 + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
+      tc::tmem_wait_ld();
+      // band mask (out -> -inf), zeroed keys -> logit 0, scaled to the log2 domain
+      // in-band columns [dlo, dhi]: |pos - j| <= window and j < Lk (keys past the end are out)
+      const int64_t dlo = pos - a.window - j0;
+      const int64_t dhi = (pos + a.window < a.Lk - 1 ? pos + a.window : a.Lk - 1) - j0;
+      float mx = m_run;
+#pragma unroll
+      for (int c = 0; c < LN; ++c) {
+        const bool in = c >= dlo && c <= dhi;
+        const float s = ((km >> c) & 1ull) ? __uint_as_float(x[c]) * sl2 : 0.f;
+        const float v = in ? s : -INFINITY;
+        x[c] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      const float base = mx == -INFINITY ? 0.f : mx;
+      const float corr = fast_exp2(m_run - base);     // 0 when m_run = -inf
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < LN; ++c) {
+        const float e = fast_exp2(__uint_as_float(x[c]) - base);
+        s4[c & 3] += e;
+        x[c] = __float_as_uint(((km >> c) & 1ull) ? e : 0.f);   // zeroed keys: counted, no value
+      }
+      l_run = l_run * corr + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+      const bool grow = mx > m_run && m_run != -INFINITY;
+      m_run = mx;
+      uint32_t hi[32], lo[32];
+#pragma unroll
+      for (int h = 0; h < 32; ++h) {
+        const float p0 = __uint_as_float(x[2 * h]), p1 = __uint_as_float(x[2 * h + 1]);
+        hi[h] = pack_bf16x2(p0, p1);
+        lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+      }
+      // P.V of tile t-1 must have completed: P buffer t&1 (last used by t-2) is free
+      // and O holds every earlier tile before it is rescaled
+      if (t >= 1 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[(t - 1) & 1]), ((t - 1) >> 1) & 1, abort_flag))) break;
+      tc::fence_after_sync();
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        *reinterpret_cast<uint4*>(sm.ph[p2] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
+        *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
+      }
+      if (__any_sync(0xffffffffu, grow)) {
+        const float c = grow ? corr : 1.f;
+#pragma unroll
+        for (int cc = 0; cc < D; cc += 32) {
+          uint32_t o[32];
+          tc::tmem_ld16(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+          tc::tmem_ld16(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * c);
+          tc::tmem_st8(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[8]>(&o[0]));
+          tc::tmem_st8(tbase + lane_off + kOCol + cc + 8, *reinterpret_cast<uint32_t(*)[8]>(&o[8]));
+          tc::tmem_st8(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[8]>(&o[16]));
+          tc::tmem_st8(tbase + lane_off + kOCol + cc + 24, *reinterpret_cast<uint32_t(*)[8]>(&o[24]));
+        }
+        tc::tmem_wait_st();
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.pready[p2]));
+    }
+    // ---- epilogue: O / l, bf16 rows, natural-log LSE
+    if (ok && NTL > 0)
+      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[(NTL - 1) & 1]), ((NTL - 1) >> 1) & 1, abort_flag);
+    tc::fence_after_sync();
+    if (__all_sync(0xffffffffu, ok) && !__any_sync(0xffffffffu, *abort_flag != 0)) {
+      const bool row_ok = g < G && qi < rows_q;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const int64_t orow = ((b * a.Lq + q0 + qi) * a.Hq + hk * G + g);
+#pragma unroll
+      for (int cc = 0; cc < D; cc += 32) {
+        uint32_t o[32];
+        tc::tmem_ld16(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+        tc::tmem_ld16(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+        tc::tmem_wait_ld();
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(a.out + orow * D + cc);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                                pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+        }
+      }
+      if (row_ok && a.lse != nullptr)
+        a.lse[orow] = l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (tid == 0 && sm.abort_flag) atomicOr(&g_local_error, 1);
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, 256);
+  }
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+              const cuuint32_t* box) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr) return false;
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
+                  strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" int mrsa_local_attention(const void* q, const void* k, const void* v,
+                                    const uint8_t* key_valid, void* out, float* lse,
+                                    int64_t window, int skip_inert, int64_t chunk, float sm_scale,
+                                    int64_t batch, int64_t q_len, int64_t kv_len, int64_t q_offset,
+                                    int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                    mrsa_stream_t stream) {
+  if (!q || !k || !v || !out) return MRSA_ERR_NULL;
+  if (head_dim != D || kv_heads < 1 || q_heads < kv_heads || q_heads % kv_heads || q_heads / kv_heads > 8 ||
+      batch < 1 || q_len < 0 || kv_len < 1 || q_offset < 0 || q_heads > 65535 || batch > 65535 ||
+      batch * q_len * q_heads > 0x7fffffffLL || batch * kv_len > 0x7fffffffLL)
+    return MRSA_ERR_SHAPE;
+  if (window < 0 || (skip_inert && chunk <= 0)) return MRSA_ERR_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return MRSA_ERR_ALIGN;
+  if (q_len == 0) return MRSA_OK;
+  // Q [B*Lq][Hq][128] as (dim-in-half, head row, half, query): one box = 8 head rows x 16 queries
+  // K, V [B*Lk][Hkv][128] as (dim-in-half, key, half, kv head): one box = 64 keys
+  CUtensorMap tm_q, tm_k, tm_v;
+  const cuuint64_t q_dims[4] = {64, static_cast<cuuint64_t>(q_heads), 2, static_cast<cuuint64_t>(batch * q_len)};
+  const cuuint64_t q_str[3] = {256, 128, static_cast<cuuint64_t>(q_heads * D * 2)};
+  const cuuint32_t q_box[4] = {64, 8, 2, LQ};
+  const cuuint64_t kv_dims[4] = {64, static_cast<cuuint64_t>(batch * kv_len), 2, static_cast<cuuint64_t>(kv_heads)};
+  const cuuint64_t kv_str[3] = {static_cast<cuuint64_t>(kv_heads * D * 2), 128, 256};
+  const cuuint32_t kv_box[4] = {64, LN, 2, 1};
+  if (!make_map(&tm_q, q, 4, q_dims, q_str, q_box) || !make_map(&tm_k, k, 4, kv_dims, kv_str, kv_box) ||
+      !make_map(&tm_v, v, 4, kv_dims, kv_str, kv_box))
+    return MRSA_ERR_LAUNCH;
+  LocalArgs a;
+  a.key_valid = key_valid;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.lse = lse;
+  a.window = window;
+  a.Lq = q_len;
+  a.Lk = kv_len;
+  a.q_offset = q_offset;
+  a.skip_inert = skip_inert;
+  a.chunk = static_cast<int>(chunk > 0 ? chunk : 1);
+  a.Hq = static_cast<int>(q_heads);
+  a.Hkv = static_cast<int>(kv_heads);
+  a.G = static_cast<int>(q_heads / kv_heads);
+  a.sm_scale = sm_scale;
+  const size_t smem = sizeof(LocalSmem) + 1024;
+  if (cudaFuncSetAttribute(local_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return MRSA_ERR_LAUNCH;
+  const int64_t blocks = (q_len + LQ - 1) / LQ;
+  if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
+  dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
+  local_tc_kernel<<<grid, L_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_q, tm_k, tm_v, a);
+  MRSA_CHECK_LAUNCH();
+  return MRSA_OK;
+}
+
+namespace mrsa {
+int local_error_flags(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_local_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_local_error, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+}  // namespace mrsa

@@ -700,7 +700,7 @@ extern "C" int mrsa_device_error_flags(int clear) {
     const int z = 0;
     if (cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int)) != cudaSuccess) return MRSA_ERR_LAUNCH;
   }
-  const int r = mrsa::route_error_flags(clear);
-  if (r < 0) return MRSA_ERR_LAUNCH;
-  return (v ? 1 : 0) | (r ? 2 : 0);
+  const int r = mrsa::route_error_flags(clear), l = mrsa::local_error_flags(clear);
+  if (r < 0 || l < 0) return MRSA_ERR_LAUNCH;
+  return (v ? 1 : 0) | (r ? 2 : 0) | (l ? 4 : 0);
 }
