@@ -11,8 +11,9 @@
 //   P            = exp2(S*scale*log2e - m)  (one thread per row, online max)
 //   O[128 x 128] += P . V_t                (UMMA M=128, N=128, K=64, TMEM)
 // P goes through shared memory as bf16 hi + lo parts (two MMAs per k-step),
-// keeping ~16 significant bits.  O is rescaled in TMEM when a row's running
-// max grows, between the P.V of tile t-1 and that of tile t.
+// keeping ~16 significant bits.  Each row keeps a reference max that moves
+// (rescaling O in TMEM between the P.V of tile t-1 and that of tile t) only
+// when a tile max exceeds it by more than 2^8.
 // Warps 0-3: softmax and epilogue (warp w = TMEM lanes 32w..32w+31 = rows);
 // warp 4: TMA (Q once, then K, V per tile, 3 stages) and the per-tile key
 // validity mask; warp 5: MMA issue (converged, elect.sync).  Every mbarrier
@@ -30,7 +31,6 @@ using namespace mrsa;
 namespace {
 
 constexpr int LQ = 16;            // queries per CTA
-constexpr int LR = 128;           // MMA rows = LQ x 8 head rows
 constexpr int LN = 64;            // keys per tile
 constexpr int LST = 3;            // K/V stages
 constexpr int D = kHeadDim;
@@ -180,8 +180,11 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       const uint64_t dv = tc::desc_adv(dv0, st * 16384), dh = tc::desc_adv(dh0, p2 * 16384),
                      dl = tc::desc_adv(dl0, p2 * 16384);
       if (tc::elect_one()) {
+        // the first tile's P.V overwrites O (TMEM is not zeroed)
+        if (t == 0) tc::mma_bf16<false>(tbase + kOCol, dh, dv, id_o);
+        else tc::mma_bf16<true>(tbase + kOCol, dh, dv, id_o);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+        for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
         tc::mma_commit(tc::smem_addr(&sm.pvdone[p2]));
@@ -202,13 +205,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     const int qi = r >> 3, g = r & 7;
     const int64_t pos = a.q_offset + q0 + qi;
     const float sl2 = a.sm_scale * kLog2e;
-    // zero O (this warp's lanes)
-    {
-      uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int c = 0; c < D; c += 8) tc::tmem_st8(tbase + lane_off + kOCol + c, z);
-      tc::tmem_wait_st();
-    }
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, o_scale = 1.f;
     bool ok = true;
     for (int t = 0; t < NTL; ++t) {
       const int st = t % LST, p2 = t & 1;
@@ -223,31 +220,65 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       tc::tmem_ld16(tbase + lane_off + LN * p2 + 32, *reinterpret_cast<uint32_t(*)[16]>(&x[32]));
       tc::tmem_ld16(tbase + lane_off + LN * p2 + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
       tc::tmem_wait_ld();
-      // band mask (out -> -inf), zeroed keys -> logit 0, scaled to the log2 domain
-      // in-band columns [dlo, dhi]: |pos - j| <= window and j < Lk (keys past the end are out)
+      // Zeroed keys (invalid, or landmark slots) keep logit 0: their raw score is
+      // replaced by 0.  The mask is per tile, so this branch is warp-uniform; with
+      // landmark skipping on 64-aligned tiles only the last column is zeroed.
+      if (km != ~0ull) {
+        if (km == (~0ull >> 1)) {
+          x[LN - 1] = 0u;
+        } else {
+#pragma unroll
+          for (int c = 0; c < LN; ++c)
+            if (!((km >> c) & 1ull)) x[c] = 0u;
+        }
+      }
+      // band |pos - j| <= window and j < Lk: in-band columns [dlo, dhi] of this tile;
+      // columns outside are -inf (only the first and last tiles of a row have any)
       const int64_t dlo = pos - a.window - j0;
       const int64_t dhi = (pos + a.window < a.Lk - 1 ? pos + a.window : a.Lk - 1) - j0;
-      float mx = m_run;
+      if (dlo > 0 || dhi < LN - 1) {
+        const int lo32 = dlo < 0 ? 0 : (dlo > LN ? LN : static_cast<int>(dlo));
+        const int hi32 = dhi < -1 ? -1 : (dhi > LN - 1 ? LN - 1 : static_cast<int>(dhi));
 #pragma unroll
-      for (int c = 0; c < LN; ++c) {
-        const bool in = c >= dlo && c <= dhi;
-        const float s = ((km >> c) & 1ull) ? __uint_as_float(x[c]) * sl2 : 0.f;
-        const float v = in ? s : -INFINITY;
-        x[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < LN; ++c)
+          if (c < lo32 || c > hi32) x[c] = __float_as_uint(-INFINITY);
       }
-      const float base = mx == -INFINITY ? 0.f : mx;
-      const float corr = fast_exp2(m_run - base);     // 0 when m_run = -inf
+      // tile max of the raw scores (sl2 > 0, so it is the max of the scaled ones)
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < LN; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(x[c]));
+      const float tmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+      // Lazy rescaling: the row keeps a reference max m_run and moves it (scaling
+      // O and l) only when a tile max exceeds it by more than 2^8.  Until then
+      // p = 2^(s - m_run) may exceed 1, which the fp32 accumulators and the hi/lo
+      // split absorb; O / l and the LSE are the same in exact arithmetic.
+      bool rescale = false;
+      if (tmax > m_run + 8.f) {
+        const float corr = m_run == -INFINITY ? 0.f : fast_exp2(m_run - tmax);
+        rescale = m_run != -INFINITY;
+        l_run *= corr;
+        o_scale = corr;
+        m_run = tmax;
+      }
+      const float nbase = m_run == -INFINITY ? 0.f : -m_run;
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < LN; ++c) {
-        const float e = fast_exp2(__uint_as_float(x[c]) - base);
+        const float e = fast_exp2(fmaf(__uint_as_float(x[c]), sl2, nbase));   // -inf -> 0
         s4[c & 3] += e;
-        x[c] = __float_as_uint(((km >> c) & 1ull) ? e : 0.f);   // zeroed keys: counted, no value
+        x[c] = __float_as_uint(e);
       }
-      l_run = l_run * corr + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
-      const bool grow = mx > m_run && m_run != -INFINITY;
-      m_run = mx;
+      l_run += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      // zeroed keys are counted in l but add no value
+      if (km != ~0ull) {
+        if (km == (~0ull >> 1)) {
+          x[LN - 1] = 0u;
+        } else {
+#pragma unroll
+          for (int c = 0; c < LN; ++c)
+            if (!((km >> c) & 1ull)) x[c] = 0u;
+        }
+      }
       uint32_t hi[32], lo[32];
 #pragma unroll
       for (int h = 0; h < 32; ++h) {
@@ -255,17 +286,18 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         hi[h] = pack_bf16x2(p0, p1);
         lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
       }
-      // P.V of tile t-1 must have completed: P buffer t&1 (last used by t-2) is free
-      // and O holds every earlier tile before it is rescaled
-      if (t >= 1 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[(t - 1) & 1]), ((t - 1) >> 1) & 1, abort_flag))) break;
-      tc::fence_after_sync();
+      // P buffer t&1 was last read by the P.V of tile t-2
+      if (t >= 2 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[p2]), ((t - 2) >> 1) & 1, abort_flag))) break;
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
         *reinterpret_cast<uint4*>(sm.ph[p2] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
         *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
       }
-      if (__any_sync(0xffffffffu, grow)) {
-        const float c = grow ? corr : 1.f;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O must hold every earlier tile before it is scaled: wait for the P.V of tile t-1
+        if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[(t - 1) & 1]), ((t - 1) >> 1) & 1, abort_flag))) break;
+        tc::fence_after_sync();
+        const float c = rescale ? o_scale : 1.f;
 #pragma unroll
         for (int cc = 0; cc < D; cc += 32) {
           uint32_t o[32];
