@@ -395,7 +395,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     for (int it = 0; ok && it < n_items; ++it) {
       const int sv = it % NV, bf = it % NBUF, p2 = it & 1;
       const int nxt = it + NBUF - 1;
-      const int np = ((8 * sm.ring[it % RING].n + 15) / 16) * 16;
+      // ring entry it was written before its K/Q tiles were requested, and S(it) waited
+      // on those; clamped so the MMA shape is always valid
+      const int np = ((8 * min(max(sm.ring[it % RING].n, 1), OWN) + 15) / 16) * 16;
       // fast path: the four phases this step needs are usually complete already;
       // test them with independent non-blocking tests and one vote
       bool rdy = tc::mbar_test(su32(&sm.bar_pready[p2]), (it >> 1) & 1) &
