@@ -260,12 +260,13 @@ def main():
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
     clk = ClockSampler(local) if rank == 0 else None
     if clk:
         clk.start()
         time.sleep(0.3)
+    # every rank enters the timed region together (after rank 0's sampler is up)
+    if dist:
+        dist.barrier()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
