@@ -18,7 +18,7 @@
 //   O^T[:, 8q..8q+7] += O_part^T[:, 8j..8j+7]           (TMEM read-modify-write)
 // For these small shapes the tensor pipe retires about one MMA instruction per
 // 44 cycles (its shared-memory operand reads), so an item costs 16 MMAs and the
-// rest of the work runs beside them in a pipeline three items deep:
+// rest of the work runs beside them:
 //   warps 0-3   accumulate: the read-modify-write of every item, in order,
 //               one quadrant of output dims each;
 //   warps 4-11  softmax, two groups of four taking alternate items; each S row
@@ -27,13 +27,15 @@
 //               (one 4-D box) and each owner's 8 query rows (3-D box); its
 //               stages are released when the item's S MMAs complete;
 //   warp 13     V loader: TMA of the V tile, stages released after P.V;
-//   warp 14     MMA issue: the warp stays converged and one elected lane
-//               issues (about a third cheaper than issuing from a lone lane);
+//   warps 14-15 MMA issue, S and P.V respectively: each warp stays converged
+//               and one elected lane issues (about a third cheaper than
+//               issuing from a lone lane);
 //   warps 0-11  finally, the epilogue: bf16 rounding, the fused local-branch
 //               merge and the stores, three warps per TMEM quadrant.
-// TMEM: accumulators in columns 0-255, then four 64-column buffers; item i's S
-// lands in buffer i%4 and its P.V partial overwrites the same columns once the
-// softmax has read them, so S can run three items ahead of P.V.
+// TMEM: accumulators in columns 0-255, two 64-column S buffers and two 64-column
+// partial buffers.  An S buffer is released as soon as the item's softmax has
+// loaded it and a partial buffer as soon as the accumulate warps have read it,
+// so neither cycle waits on the other.
 // Owner j of an item goes to S row slot 2*(j%4) + j/4, so the first four
 // owners land in four different TMEM quadrants and four softmax warps share
 // the rows.  Every mbarrier wait is bounded and a shared abort flag unwinds all
@@ -55,13 +57,12 @@ constexpr int GMAX = 8;           // head rows per query in the MMA tile
 constexpr int OWN = 8;            // owners per work item (64 S rows)
 constexpr int NKQ = 3;            // K/Q load stages (released after S)
 constexpr int NV = 3;             // V load stages (released after P.V)
-constexpr int NBUF = 4;           // TMEM S/partial buffers; S runs NBUF-1 items ahead
 constexpr int RING = 16;          // item-ring entries
 constexpr int D = kHeadDim, S = kChunk, KMAX = 32;
-constexpr int NTHREADS = 480;
-constexpr int W_SMX = 4, W_LOADKQ = 12, W_LOADV = 13, W_MMA = 14;
+constexpr int NTHREADS = 512;
+constexpr int W_SMX = 4, W_LOADKQ = 12, W_LOADV = 13, W_MMA = 14;   // MMA warps 14 (S) and 15 (P.V)
 constexpr int kAccCols = QB * GMAX;          // 256
-constexpr int kBufCol = 256;                 // buffer b at columns 256 + 64 b
+constexpr int kSCol = 256, kPCol = 384;      // S buffers at 256 / 320, partial buffers at 384 / 448
 
 struct Item {
   int n;                          // owners
@@ -81,8 +82,8 @@ struct __align__(1024) TcSmem {
   int2 ulist[QB * KMAX];          // per union chunk: (chunk, owner-query mask)
   Item ring[RING];
   uint64_t bar_kqfull[NKQ], bar_kqfree[NKQ], bar_vfull[NV], bar_vfree[NV];
-  uint64_t bar_sdone[NBUF], bar_pvdone[NBUF], bar_partfree[NBUF], bar_pready[2];
-  uint64_t bar_ring[RING], bar_mma_drain;
+  uint64_t bar_sdone[2], bar_sfree[2], bar_pready[2], bar_pvdone[2], bar_partfree[2];
+  uint64_t bar_ring[RING], bar_mma_drain[2];
   uint32_t tmem_base;
   int nu, n_items, abort_flag;
 };
@@ -189,14 +190,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       tc::mbar_init(su32(&sm.bar_vfull[s]), 1);
       tc::mbar_init(su32(&sm.bar_vfree[s]), 1);
     }
-    for (int s = 0; s < NBUF; ++s) {
+    for (int s = 0; s < 2; ++s) {
       tc::mbar_init(su32(&sm.bar_sdone[s]), 1);
+      tc::mbar_init(su32(&sm.bar_sfree[s]), 4);
       tc::mbar_init(su32(&sm.bar_pvdone[s]), 1);
       tc::mbar_init(su32(&sm.bar_partfree[s]), 4);
     }
     for (int s = 0; s < 2; ++s) tc::mbar_init(su32(&sm.bar_pready[s]), 4);
     for (int r = 0; r < RING; ++r) tc::mbar_init(su32(&sm.bar_ring[r]), 1);
-    tc::mbar_init(su32(&sm.bar_mma_drain), 1);
+    for (int s = 0; s < 2; ++s) tc::mbar_init(su32(&sm.bar_mma_drain[s]), 1);
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -356,81 +358,77 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         tc::mbar_wait(su32(&sm.bar_vfull[it % NV]), (it / NV) & 1);
     }
     __syncwarp();
-  } else if (warp == W_MMA) {
-    // ============================ MMA issue (converged warp) =================
-    // Per step: P.V of item it and S of item it+3 go out in one elected batch
-    // after all four of their waits, so the warp passes one fence and one
-    // convergence point per item.
-    constexpr uint32_t id_s = tc::idesc_bf16_f32(64, 64, 0, 0);
+  } else if (warp >= W_MMA) {
+    // ============================ MMA issue (two converged warps) ============
+    // Warp 14 issues the S MMAs, warp 15 the P.V MMAs.  S(i) lands in S buffer
+    // i%2, free once the softmax of item i-2 has loaded it; P.V(i) lands in
+    // partial buffer i%2, free once the accumulate warps have read item i-2's.
+    // Each warp waits only for its own operands; every hand-off between them
+    // goes through an mbarrier.
+    const bool s_role = warp == W_MMA;
     const uint64_t dq0 = tc::smem_desc_sw128(su32(sm.at[0]), 16, 2048);
     const uint64_t dk0 = tc::smem_desc_sw128(su32(sm.kt[0]), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(su32(sm.vt[0]), 8192, 1024);
     const uint64_t dh0 = tc::smem_desc_sw128(su32(sm.ph[0]), 16, 1024);
     const uint64_t dl0 = tc::smem_desc_sw128(su32(sm.pl[0]), 16, 1024);
-    auto s_mmas = [&](int it) {
-      const int st = it % NKQ, bf = it % NBUF;
-      const uint64_t da = adv(dq0, st * 16384), db = adv(dk0, st * 16384);
-      const uint32_t dS = tbase + kBufCol + 64 * bf;
-      tc::mma_bf16<false>(dS, da, db, id_s);
+    if (s_role) {
+      constexpr uint32_t id_s = tc::idesc_bf16_f32(64, 64, 0, 0);
+      for (int it = 0; it < n_items; ++it) {
+        const int st = it % NKQ, s2 = it & 1;
+        bool rdy = tc::mbar_test(su32(&sm.bar_kqfull[st]), (it / NKQ) & 1);
+        if (it >= 2) rdy &= tc::mbar_test(su32(&sm.bar_sfree[s2]), ((it >> 1) - 1) & 1);
+        if (!__all_sync(0xffffffffu, rdy)) {
+          if (!wait_bar_warp(sm, &sm.bar_kqfull[st], (it / NKQ) & 1)) break;
+          if (it >= 2 && !wait_bar_warp(sm, &sm.bar_sfree[s2], ((it >> 1) - 1) & 1)) break;
+        }
+        tc::fence_after_sync();
+        const uint64_t da = adv(dq0, st * 16384), db = adv(dk0, st * 16384);
+        const uint32_t dS = tbase + kSCol + 64 * s2;
+        if (elect_one()) {
+          tc::mma_bf16<false>(dS, da, db, id_s);
 #pragma unroll
-      for (int kk = 1; kk < 8; ++kk)
-        tc::mma_bf16<true>(dS, adv(da, (kk >> 2) * 1024 + (kk & 3) * 32), adv(db, (kk >> 2) * 8192 + (kk & 3) * 32),
-                           id_s);
-      tc::mma_commit(su32(&sm.bar_sdone[bf]));
-      tc::mma_commit(su32(&sm.bar_kqfree[st]));
-    };
-    // S of item it is ready to go: its K/Q tiles landed and its buffer's previous partial was read
-    auto s_ready = [&](int it) -> bool {
-      if (!wait_bar_warp(sm, &sm.bar_kqfull[it % NKQ], (it / NKQ) & 1)) return false;
-      return it < NBUF || wait_bar_warp(sm, &sm.bar_partfree[it % NBUF], ((it / NBUF) - 1) & 1);
-    };
-    bool ok = true;
-    for (int it = 0; ok && it < n_items && it < NBUF - 1; ++it) {
-      ok = s_ready(it);
-      if (!ok) break;
-      tc::fence_after_sync();
-      if (elect_one()) s_mmas(it);
-      __syncwarp();
-    }
-    for (int it = 0; ok && it < n_items; ++it) {
-      const int sv = it % NV, bf = it % NBUF, p2 = it & 1;
-      const int nxt = it + NBUF - 1;
-      // ring entry it was written before its K/Q tiles were requested, and S(it) waited
-      // on those; clamped so the MMA shape is always valid
-      const int np = ((8 * min(max(sm.ring[it % RING].n, 1), OWN) + 15) / 16) * 16;
-      // fast path: the four phases this step needs are usually complete already;
-      // test them with independent non-blocking tests and one vote
-      bool rdy = tc::mbar_test(su32(&sm.bar_pready[p2]), (it >> 1) & 1) &
-                 tc::mbar_test(su32(&sm.bar_vfull[sv]), (it / NV) & 1);
-      if (nxt < n_items) {
-        rdy &= tc::mbar_test(su32(&sm.bar_kqfull[nxt % NKQ]), (nxt / NKQ) & 1);
-        if (nxt >= NBUF) rdy &= tc::mbar_test(su32(&sm.bar_partfree[nxt % NBUF]), ((nxt / NBUF) - 1) & 1);
+          for (int kk = 1; kk < 8; ++kk)
+            tc::mma_bf16<true>(dS, adv(da, (kk >> 2) * 1024 + (kk & 3) * 32),
+                               adv(db, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
+          tc::mma_commit(su32(&sm.bar_sdone[s2]));
+          tc::mma_commit(su32(&sm.bar_kqfree[st]));
+        }
+        __syncwarp();
       }
-      if (!__all_sync(0xffffffffu, rdy)) {
-        if (!wait_bar_warp(sm, &sm.bar_pready[p2], (it >> 1) & 1)) break;
-        if (!wait_bar_warp(sm, &sm.bar_vfull[sv], (it / NV) & 1)) break;
-        if (nxt < n_items && !s_ready(nxt)) break;
-      }
-      tc::fence_after_sync();
-      const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
-      const uint64_t dv = adv(dv0, sv * 16384), dh = adv(dh0, p2 * 8192), dl = adv(dl0, p2 * 8192);
-      const uint32_t dP = tbase + kBufCol + 64 * bf;
-      if (elect_one()) {
-        tc::mma_bf16<false>(dP, dv, dh, id_o);
+    } else {
+      for (int it = 0; it < n_items; ++it) {
+        const int sv = it % NV, p2 = it & 1;
+        bool rdy = tc::mbar_test(su32(&sm.bar_pready[p2]), (it >> 1) & 1) &
+                   tc::mbar_test(su32(&sm.bar_vfull[sv]), (it / NV) & 1);
+        if (it >= 2) rdy &= tc::mbar_test(su32(&sm.bar_partfree[p2]), ((it >> 1) - 1) & 1);
+        if (!__all_sync(0xffffffffu, rdy)) {
+          if (!wait_bar_warp(sm, &sm.bar_pready[p2], (it >> 1) & 1)) break;
+          if (!wait_bar_warp(sm, &sm.bar_vfull[sv], (it / NV) & 1)) break;
+          if (it >= 2 && !wait_bar_warp(sm, &sm.bar_partfree[p2], ((it >> 1) - 1) & 1)) break;
+        }
+        tc::fence_after_sync();
+        // the owner count is read only now: the item's softmax has consumed its ring
+        // entry (pready), so it is written; clamped so the MMA shape is always valid
+        const int np = ((8 * min(max(sm.ring[it % RING].n, 1), OWN) + 15) / 16) * 16;
+        const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
+        const uint64_t dv = adv(dv0, sv * 16384), dh = adv(dh0, p2 * 8192), dl = adv(dl0, p2 * 8192);
+        const uint32_t dP = tbase + kPCol + 64 * p2;
+        if (elect_one()) {
+          tc::mma_bf16<false>(dP, dv, dh, id_o);
 #pragma unroll
-        for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dh, kk * 32), id_o);
+          for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dh, kk * 32), id_o);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
-        tc::mma_commit(su32(&sm.bar_pvdone[bf]));
-        tc::mma_commit(su32(&sm.bar_vfree[sv]));
-        if (nxt < n_items) s_mmas(nxt);
+          for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
+          tc::mma_commit(su32(&sm.bar_pvdone[p2]));
+          tc::mma_commit(su32(&sm.bar_vfree[sv]));
+        }
+        __syncwarp();
       }
-      __syncwarp();
     }
     // every MMA issued by this warp has completed once this phase lands
     if (elect_one()) {
-      tc::mma_commit(su32(&sm.bar_mma_drain));
-      tc::mbar_wait(su32(&sm.bar_mma_drain), 0);
+      tc::mma_commit(su32(&sm.bar_mma_drain[s_role ? 0 : 1]));
+      tc::mbar_wait(su32(&sm.bar_mma_drain[s_role ? 0 : 1]), 0);
     }
     __syncwarp();
   } else if (warp >= W_SMX) {
@@ -441,7 +439,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     const int jrow = t < 8 ? q : q + 4;      // owner (compact index) of this thread's row
     const int g = t & 7;
     for (int it = grp; it < n_items; it += 2) {
-      const int bf = it % NBUF, p2 = it & 1, r = it % RING;
+      const int p2 = it & 1, r = it % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
       const int n = sm.ring[r].n;
       const bool row_on = jrow < n;
@@ -452,16 +450,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         const unsigned long long vm = sm.vmask[sm.ring[r].u];
         km = static_cast<uint32_t>(hf ? (vm >> 32) : vm);
       }
-      if (!wait_bar_warp(sm, &sm.bar_sdone[bf], (it / NBUF) & 1)) break;
+      if (!wait_bar_warp(sm, &sm.bar_sdone[p2], (it >> 1) & 1)) break;
       tc::fence_after_sync();
       uint32_t x[32];
       if (q < n) {                           // warp-uniform: this quadrant holds rows
-        tc::tmem_ld_16x32bx2_x32(tbase + lane_off + kBufCol + 64 * bf, x);
+        tc::tmem_ld_16x32bx2_x32(tbase + lane_off + kSCol + 64 * p2, x);
         tc::tmem_wait_ld();
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) x[c] = 0u;
       }
+      // the S buffer is free once every warp of the group has loaded its rows
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_sfree[p2]));
       // masked keys -> -inf; the common case (every key usable but possibly the
       // last of the chunk) takes one select instead of 32
       if (__all_sync(0xffffffffu, (km | 0x80000000u) == 0xFFFFFFFFu)) {
@@ -496,7 +498,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
       }
       // the P buffer is free once the P.V of item it-2 has completed
-      if (it >= 2 && !wait_bar_warp(sm, &sm.bar_pvdone[(it - 2) % NBUF], ((it - 2) / NBUF) & 1)) break;
+      if (it >= 2 && !wait_bar_warp(sm, &sm.bar_pvdone[p2], ((it - 2) >> 1) & 1)) break;
       if (row_on) {
         const int row = 8 * jrow + g;
 #pragma unroll
@@ -516,13 +518,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     // ============================ accumulate (warps 0-3) =====================
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     for (int it = 0; it < n_items; ++it) {
-      const int bf = it % NBUF, r = it % RING;
+      const int p2 = it & 1, r = it % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
       const int n = sm.ring[r].n;
       int oq[OWN];
 #pragma unroll
       for (int j = 0; j < OWN; ++j) oq[j] = sm.ring[r].oq[j];
-      if (!wait_bar_warp(sm, &sm.bar_pvdone[bf], (it / NBUF) & 1)) break;
+      if (!wait_bar_warp(sm, &sm.bar_pvdone[p2], (it >> 1) & 1)) break;
       tc::fence_after_sync();
       tc::tmem_wait_st();                    // previous item's accumulator stores have landed
 #pragma unroll
@@ -532,7 +534,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (j0 + j < n) {
-            tc::tmem_ld8(tbase + lane_off + kBufCol + 64 * bf + 8 * (j0 + j), pv[j]);
+            tc::tmem_ld8(tbase + lane_off + kPCol + 64 * p2 + 8 * (j0 + j), pv[j]);
             tc::tmem_ld8(tbase + lane_off + 8 * oq[j0 + j], acc[j]);
           }
         }
@@ -540,7 +542,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         if (j0 + 4 >= n) {                   // last partial columns read: release the buffer
           tc::fence_before_sync();
           __syncwarp();
-          if (lane == 0) tc::mbar_arrive(su32(&sm.bar_partfree[bf]));
+          if (lane == 0) tc::mbar_arrive(su32(&sm.bar_partfree[p2]));
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
