@@ -23,13 +23,16 @@
 //               one quadrant of output dims each;
 //   warps 4-11  softmax, two groups of four taking alternate items; each S row
 //               is read by two threads (32 columns each) with 16x32bx2 loads;
-//   warp 12     K/Q loader: owner lists into an item ring, TMA of the K tile
-//               (one 4-D box) and each owner's 8 query rows (3-D box); its
-//               stages are released when the item's S MMAs complete;
-//   warp 13     V loader: TMA of the V tile, stages released after P.V;
+//   warps 12-13 K/Q loaders, taking alternate items: owner lists into an item
+//               ring, TMA of the K tile (one 4-D box) and each owner's 8 query
+//               rows (3-D box); stages are released when the item's S MMAs
+//               complete.  One warp issuing every item's 1 + n copies set
+//               the item rate (about 1700 cycles an item), so two share it;
 //   warps 14-15 MMA issue, S and P.V respectively: each warp stays converged
 //               and one elected lane issues (about a third cheaper than
-//               issuing from a lone lane);
+//               issuing from a lone lane).  The P.V warp also requests the V
+//               tiles: before P.V(i) it waits for P.V(i-1) to complete (its
+//               stage is then free) and asks for item i-1+NV's tile;
 //   warps 0-11  finally, the epilogue: bf16 rounding, the fused local-branch
 //               merge and the stores, three warps per TMEM quadrant.
 // TMEM: accumulators in columns 0-255, two 64-column S buffers and two 64-column
@@ -60,13 +63,14 @@ constexpr int NV = 3;             // V load stages (released after P.V)
 constexpr int RING = 16;          // item-ring entries
 constexpr int D = kHeadDim, S = kChunk, KMAX = 32;
 constexpr int NTHREADS = 512;
-constexpr int W_SMX = 4, W_LOADKQ = 12, W_LOADV = 13, W_MMA = 14;   // MMA warps 14 (S) and 15 (P.V)
+constexpr int W_SMX = 4, W_LOADKQ = 12, W_LOADKQ2 = 13, W_MMA = 14;   // MMA warps 14 (S) and 15 (P.V)
 constexpr int kAccCols = QB * GMAX;          // 256
 constexpr int kSCol = 256, kPCol = 384;      // S buffers at 256 / 320, partial buffers at 384 / 448
 
 struct Item {
   int n;                          // owners
-  int u;                          // union index (chunk, key mask)
+  int u;                          // union index (key mask)
+  int c;                          // chunk
   uint8_t oq[OWN];                // owner query (CTA-local), compact order
   uint8_t slot[OWN];              // owner's slot in its chunk list (route weight)
 };
@@ -81,9 +85,10 @@ struct __align__(1024) TcSmem {
   unsigned long long vmask[QB * KMAX];   // per union chunk: bit s = key s usable
   int2 ulist[QB * KMAX];          // per union chunk: (chunk, owner-query mask)
   Item ring[RING];
-  uint64_t bar_kqfull[NKQ], bar_kqfree[NKQ], bar_vfull[NV], bar_vfree[NV];
+  uint64_t bar_kqfull[NKQ], bar_kqfree[NKQ], bar_vfull[NV];
   uint64_t bar_sdone[2], bar_sfree[2], bar_pready[2], bar_pvdone[2], bar_partfree[2];
   uint64_t bar_ring[RING], bar_mma_drain[2];
+  int kq_last[2][NKQ];            // per K/Q loader: last item it issued into each stage
   uint32_t tmem_base;
   int nu, n_items, abort_flag;
 };
@@ -160,11 +165,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   int (*idx)[KMAX + 1] = reinterpret_cast<int (*)[KMAX + 1]>(&sm.at[1][0]);
 
   // ---------------- set-up: chunk lists, weights, union of chunks ----------
-  if (warp == W_LOADKQ && lane == 0) {
+  if ((warp == W_LOADKQ || warp == W_LOADKQ2) && lane == 0) {
     tc::prefetch_tensormap(&tm_k);
     tc::prefetch_tensormap(&tm_q);
   }
-  if (warp == W_LOADV && lane == 0) tc::prefetch_tensormap(&tm_v);
+  if (warp == W_MMA + 1 && lane == 0) tc::prefetch_tensormap(&tm_v);
   for (int e = tid; e < C; e += NTHREADS) ownmask[e] = 0u;
   for (int e = tid; e < QB * KMAX; e += NTHREADS) {
     const int qi = e / KMAX, kk = e % KMAX;
@@ -186,10 +191,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       tc::mbar_init(su32(&sm.bar_kqfull[s]), 1);
       tc::mbar_init(su32(&sm.bar_kqfree[s]), 1);
     }
-    for (int s = 0; s < NV; ++s) {
-      tc::mbar_init(su32(&sm.bar_vfull[s]), 1);
-      tc::mbar_init(su32(&sm.bar_vfree[s]), 1);
-    }
+    for (int s = 0; s < NV; ++s) tc::mbar_init(su32(&sm.bar_vfull[s]), 1);
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(su32(&sm.bar_sdone[s]), 1);
       tc::mbar_init(su32(&sm.bar_sfree[s]), 4);
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     for (int r = 0; r < RING; ++r) tc::mbar_init(su32(&sm.bar_ring[r]), 1);
     for (int s = 0; s < 2; ++s) tc::mbar_init(su32(&sm.bar_mma_drain[s]), 1);
     sm.abort_flag = 0;
+    for (int s = 0; s < NKQ; ++s) sm.kq_last[0][s] = sm.kq_last[1][s] = -1;
     tc::fence_mbar_init();
   }
   if (warp == 0) {
@@ -278,12 +281,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   const int n_items = sm.n_items;
   const float sl2 = a.sm_scale * kLog2e;
 
-  if (warp == W_LOADKQ) {
-    // ============================ K/Q loader =================================
+  if (warp == W_LOADKQ || warp == W_LOADKQ2) {
+    // ============================ K/Q loaders ================================
+    // Both warps walk the same item sequence; warp 12 issues the even items,
+    // warp 13 the odd ones.
+    const int par = warp == W_LOADKQ ? 0 : 1;
     int myc[KMAX];                           // this lane's (query's) chunk list
 #pragma unroll
     for (int kk = 0; kk < KMAX; ++kk) myc[kk] = idx[lane][kk];
     tc::fence_proxy_async();                 // these reads precede TMA writes to the same area
+    const uint32_t below = (1u << lane) - 1u;
     int item = 0;
     bool ok = true;
     for (int u = 0; ok && u < sm.nu; ++u) {
@@ -294,68 +301,55 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
 #pragma unroll
       for (int kk = KMAX - 1; kk >= 0; --kk) my_slot = myc[kk] == c ? kk : my_slot;
       while (owners) {
-        const int st = item % NKQ, r = item % RING;
-        // the item's owner list goes into the ring before the stage is free
-        int n = 0;
-        uint32_t grp = 0;
-        for (uint32_t m = owners; m && n < OWN; m &= m - 1, ++n) grp |= m & (~m + 1);
+        // the next (up to) OWN owners, in query order
+        const int j = __popc(owners & below);
+        const bool mine = ((owners >> lane) & 1u) && j < OWN;
+        const uint32_t grp = __ballot_sync(0xffffffffu, mine);
         owners &= ~grp;
-        const bool mine = (grp >> lane) & 1u;
-        const int j = __popc(grp & ((1u << lane) - 1u));
-        if (mine) {
-          sm.ring[r].oq[j] = static_cast<uint8_t>(lane);
-          sm.ring[r].slot[j] = static_cast<uint8_t>(my_slot);
-        }
-        if (lane == 0) {
-          sm.ring[r].n = n;
-          sm.ring[r].u = u;
-        }
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(su32(&sm.bar_ring[r]));
-        if (item >= NKQ && !wait_bar_warp(sm, &sm.bar_kqfree[st], ((item / NKQ) - 1) & 1)) {
-          ok = false;
-          break;
-        }
-        const uint32_t bar = su32(&sm.bar_kqfull[st]);
-        if (lane == 0) {
-          tc::mbar_arrive_expect_tx(bar, 16384u + static_cast<uint32_t>(n) * 2048u);
-          tc::tma_load_4d(su32(sm.kt[st]), &tm_k, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(c) * S), 0,
-                          hk, bar);
-        }
-        __syncwarp();
-        if (mine) {
-          const int slot = 2 * (j & 3) + (j >> 2);
-          const int qy = static_cast<int>((b * a.Lq + q0 + lane) * Hq + hk * G);
-          tc::tma_load_3d(su32(sm.at[st] + slot * 2048), &tm_q, 0, qy, 0, bar);
+        if ((item & 1) == par) {
+          const int st = item % NKQ, r = item % RING, n = __popc(grp);
+          // the item's owner list goes into the ring before the stage is free
+          if (mine) {
+            sm.ring[r].oq[j] = static_cast<uint8_t>(lane);
+            sm.ring[r].slot[j] = static_cast<uint8_t>(my_slot);
+          }
+          if (lane == 0) {
+            sm.ring[r].n = n;
+            sm.ring[r].u = u;
+            sm.ring[r].c = c;
+          }
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(su32(&sm.bar_ring[r]));
+          if (item >= NKQ && !wait_bar_warp(sm, &sm.bar_kqfree[st], ((item / NKQ) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = su32(&sm.bar_kqfull[st]);
+          if (lane == 0) {
+            tc::mbar_arrive_expect_tx(bar, 16384u + static_cast<uint32_t>(n) * 2048u);
+            tc::tma_load_4d(su32(sm.kt[st]), &tm_k, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(c) * S), 0,
+                            hk, bar);
+          }
+          __syncwarp();
+          if (mine) {
+            const int slot = 2 * (j & 3) + (j >> 2);
+            const int qy = static_cast<int>((b * a.Lq + q0 + lane) * Hq + hk * G);
+            tc::tma_load_3d(su32(sm.at[st] + slot * 2048), &tm_q, 0, qy, 0, bar);
+          }
+          if (lane == 0) sm.kq_last[par][st] = item;
         }
         ++item;
       }
     }
-    // wait (bounded, even after an abort) for this CTA's copies in flight
+    // Wait (bounded, even after an abort) for this CTA's copies in flight.  A
+    // stage is reused only after the S MMAs of its previous item completed, so
+    // only the last item issued into each stage (by either warp) can be in flight.
+    asm volatile("bar.sync 2, 64;\n" ::: "memory");
     if (lane == 0) {
-      for (int it = item - NKQ < 0 ? 0 : item - NKQ; it < item; ++it)
-        tc::mbar_wait(su32(&sm.bar_kqfull[it % NKQ]), (it / NKQ) & 1);
-    }
-    __syncwarp();
-  } else if (warp == W_LOADV) {
-    // ============================ V loader ===================================
-    int item = 0;
-    for (; item < n_items; ++item) {
-      const int st = item % NV, r = item % RING;
-      if (!wait_bar_warp(sm, &sm.bar_ring[r], (item / RING) & 1)) break;
-      if (item >= NV && !wait_bar_warp(sm, &sm.bar_vfree[st], ((item / NV) - 1) & 1)) break;
-      if (lane == 0) {
-        const int c = sm.ulist[sm.ring[r].u].x;
-        const uint32_t bar = su32(&sm.bar_vfull[st]);
-        tc::mbar_arrive_expect_tx(bar, 16384u);
-        tc::tma_load_4d(su32(sm.vt[st]), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(c) * S), 0,
-                        hk, bar);
+      for (int s2 = 0; s2 < NKQ; ++s2) {
+        const int it = max(sm.kq_last[0][s2], sm.kq_last[1][s2]);
+        if (it >= 0 && (it & 1) == par) tc::mbar_wait(su32(&sm.bar_kqfull[s2]), (it / NKQ) & 1);
       }
-      __syncwarp();
-    }
-    if (lane == 0) {
-      for (int it = item - NV < 0 ? 0 : item - NV; it < item; ++it)
-        tc::mbar_wait(su32(&sm.bar_vfull[it % NV]), (it / NV) & 1);
     }
     __syncwarp();
   } else if (warp >= W_MMA) {
@@ -396,8 +390,35 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         __syncwarp();
       }
     } else {
-      for (int it = 0; it < n_items; ++it) {
+      // V tile of item `v` into stage v % NV; the ring entry names the chunk
+      auto load_v = [&](int v) -> bool {
+        const int r = v % RING;
+        if (!wait_bar_warp(sm, &sm.bar_ring[r], (v / RING) & 1)) return false;
+        if (elect_one()) {
+          const uint32_t bar = su32(&sm.bar_vfull[v % NV]);
+          tc::mbar_arrive_expect_tx(bar, 16384u);
+          tc::tma_load_4d(su32(sm.vt[v % NV]), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(sm.ring[r].c) * S),
+                          0, hk, bar);
+        }
+        __syncwarp();
+        return true;
+      };
+      int vq = 0;                            // V tiles requested so far
+      bool ok = true;
+      for (; vq < NV && vq < n_items; ++vq)
+        if (!load_v(vq)) {
+          ok = false;
+          break;
+        }
+      int it = 0;
+      for (; ok && it < n_items; ++it) {
         const int sv = it % NV, p2 = it & 1;
+        // P.V(it-1) completing frees its V stage for item it-1+NV
+        if (it >= 1 && vq < n_items) {
+          if (!wait_bar_warp(sm, &sm.bar_pvdone[(it - 1) & 1], ((it - 1) >> 1) & 1)) break;
+          if (!load_v(vq)) break;
+          ++vq;
+        }
         bool rdy = tc::mbar_test(su32(&sm.bar_pready[p2]), (it >> 1) & 1) &
                    tc::mbar_test(su32(&sm.bar_vfull[sv]), (it / NV) & 1);
         if (it >= 2) rdy &= tc::mbar_test(su32(&sm.bar_partfree[p2]), ((it >> 1) - 1) & 1);
@@ -420,10 +441,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
           tc::mma_commit(su32(&sm.bar_pvdone[p2]));
-          tc::mma_commit(su32(&sm.bar_vfree[sv]));
         }
         __syncwarp();
       }
+      // (bounded) wait for V copies still in flight after an abort: items it ..
+      // vq-1 were requested and not yet known to have landed
+      if (lane == 0)
+        for (int v = it; v < vq; ++v) tc::mbar_wait(su32(&sm.bar_vfull[v % NV]), (v / NV) & 1);
+      __syncwarp();
     }
     // every MMA issued by this warp has completed once this phase lands
     if (elect_one()) {
