@@ -483,16 +483,41 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs 
   }
   nf = __reduce_add_sync(0xffffffffu, nf);
   const int keff = nf < K ? nf : K;
-  // radix search for the largest threshold with at least keff keys >= it
+  // radix search for the largest threshold with at least keff keys >= it.
+  // The threshold is one of the finite keys, so the high bits that all finite
+  // keys share are its bits from the start; and the search may stop once
+  // exactly keff keys are >= the threshold so far: those keys are the top
+  // keff, and the selection below takes every one of them (no tie to break).
   uint32_t thr = 0;
   if (keff > 0) {
-    for (int bit = 31; bit >= 0; --bit) {
+    uint32_t orv = 0u, andv = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i)
+      if (u[i] > neg_inf_ord) {
+        orv |= u[i];
+        andv &= u[i];
+      }
+    orv = __reduce_or_sync(0xffffffffu, orv);
+    andv = __reduce_and_sync(0xffffffffu, andv);
+    const uint32_t diff = orv ^ andv;
+    int top = 31;
+    if (diff == 0u) {
+      thr = andv;                        // every finite key is the same value
+      top = -1;
+    } else {
+      top = 31 - __clz(diff);
+      thr = top == 31 ? 0u : (andv & ~((2u << top) - 1u));
+    }
+    for (int bit = top; bit >= 0; --bit) {
       const uint32_t cand = thr | (1u << bit);
       int cnt = 0;
 #pragma unroll
       for (int i = 0; i < CPL; ++i) cnt += u[i] >= cand;
       cnt = __reduce_add_sync(0xffffffffu, cnt);
-      if (cnt >= keff) thr = cand;
+      if (cnt >= keff) {
+        thr = cand;
+        if (cnt == keff) break;
+      }
     }
   }
   int ngt = 0;

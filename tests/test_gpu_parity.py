@@ -113,6 +113,37 @@ def test_route_topk_g7_matches_reference_golden(mrsa, dev):
     assert torch.equal(srt, srt.sort(-1).values)
 
 
+@pytest.mark.parametrize("c", [600, 2000])
+@pytest.mark.parametrize("tiers", [False, True])
+def test_route_ties_take_lowest_chunk_ids(mrsa, dev, c, tiers):
+    """Keys equal at the top-K boundary: the lowest chunk ids win.  Zero
+    landmarks make every key a function of its chunk's bias alone, so chunks
+    with equal bias tie exactly (on the GPU and in the oracle); with tiers the
+    boundary falls inside the lowest tier, without them every key ties."""
+    gen = torch.Generator().manual_seed(c + tiers)
+    b, l, hkv, g, d, topk = 1, 96, 2, 7, 128, 32
+    q = torch.randn(b, l, hkv * g, d, generator=gen).bfloat16()
+    lmk = torch.zeros(b, c, hkv, g, d).bfloat16()
+    lse = torch.randn(b, l, hkv, g, generator=gen)
+    bias = torch.zeros(b, c, hkv, g)
+    if tiers:
+        perm = torch.randperm(c, generator=gen)
+        bias[:, perm[:5]] = 2.0
+        bias[:, perm[5:25]] = 1.0
+    drop = (torch.rand(b, l, c, generator=gen) < 0.2).int()
+    idx, _ = mrsa.route_topk_g7(q.to(dev), lmk.to(dev), lse.to(dev), bias.to(dev), drop.to(dev),
+                                topk, 64, 512, training=False)
+    key = orc.route_keys(q, lmk, lse, bias, drop)                      # [b, l, hkv, c]
+    ids = torch.arange(c, dtype=torch.float64)
+    # order by key descending, then chunk id ascending; dropped chunks never
+    order = (key.double() * (4 * c) - ids).argsort(dim=-1, descending=True)
+    top = order[..., :topk]
+    top = torch.where(torch.gather(key, -1, top).isfinite(), top, torch.full_like(top, 1 << 30))
+    want = top.sort(-1).values
+    want = torch.where(want == (1 << 30), torch.full_like(want, -1), want)
+    assert torch.equal(idx.cpu(), want)
+
+
 def test_ref_softmax_topk_dropin_shared_landmarks(mrsa, dev):
     """per-KV-head (GQA-shared) landmarks, fp32 scores, no bias"""
     gen = torch.Generator().manual_seed(8)
