@@ -20,7 +20,11 @@
 // 44 cycles (its shared-memory operand reads), so an item costs 16 MMAs and the
 // rest of the work runs beside them:
 //   warps 0-3   accumulate: the read-modify-write of every item, in order,
-//               one quadrant of output dims each;
+//               one quadrant of output dims each.  Warps 1-3 also request the
+//               V tiles, warp w for stage w-1: once it has accumulated item i
+//               (so P.V(i) has completed and freed stage i % 3) it asks for
+//               item i+3's tile.  One request per warp every third item keeps
+//               them off every other role's per-item path;
 //   warps 4-11  softmax, two groups of four taking alternate items; each S row
 //               is read by two threads (32 columns each) with 16x32bx2 loads;
 //   warps 12-13 K/Q loaders, taking alternate items: owner lists into an item
@@ -30,9 +34,7 @@
 //               the item rate (about 1700 cycles an item), so two share it;
 //   warps 14-15 MMA issue, S and P.V respectively: each warp stays converged
 //               and one elected lane issues (about a third cheaper than
-//               issuing from a lone lane).  The P.V warp also requests the V
-//               tiles: before P.V(i) it waits for P.V(i-1) to complete (its
-//               stage is then free) and asks for item i-1+NV's tile;
+//               issuing from a lone lane);
 //   warps 0-11  finally, the epilogue: bf16 rounding, the fused local-branch
 //               merge and the stores, three warps per TMEM quadrant.
 // TMEM: accumulators in columns 0-255, two 64-column S buffers and two 64-column
@@ -169,7 +171,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     tc::prefetch_tensormap(&tm_k);
     tc::prefetch_tensormap(&tm_q);
   }
-  if (warp == W_MMA + 1 && lane == 0) tc::prefetch_tensormap(&tm_v);
+  if (warp >= 1 && warp <= NV && lane == 0) tc::prefetch_tensormap(&tm_v);
   for (int e = tid; e < C; e += NTHREADS) ownmask[e] = 0u;
   for (int e = tid; e < QB * KMAX; e += NTHREADS) {
     const int qi = e / KMAX, kk = e % KMAX;
@@ -390,35 +392,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         __syncwarp();
       }
     } else {
-      // V tile of item `v` into stage v % NV; the ring entry names the chunk
-      auto load_v = [&](int v) -> bool {
-        const int r = v % RING;
-        if (!wait_bar_warp(sm, &sm.bar_ring[r], (v / RING) & 1)) return false;
-        if (elect_one()) {
-          const uint32_t bar = su32(&sm.bar_vfull[v % NV]);
-          tc::mbar_arrive_expect_tx(bar, 16384u);
-          tc::tma_load_4d(su32(sm.vt[v % NV]), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(sm.ring[r].c) * S),
-                          0, hk, bar);
-        }
-        __syncwarp();
-        return true;
-      };
-      int vq = 0;                            // V tiles requested so far
-      bool ok = true;
-      for (; vq < NV && vq < n_items; ++vq)
-        if (!load_v(vq)) {
-          ok = false;
-          break;
-        }
-      int it = 0;
-      for (; ok && it < n_items; ++it) {
+      for (int it = 0; it < n_items; ++it) {
         const int sv = it % NV, p2 = it & 1;
-        // P.V(it-1) completing frees its V stage for item it-1+NV
-        if (it >= 1 && vq < n_items) {
-          if (!wait_bar_warp(sm, &sm.bar_pvdone[(it - 1) & 1], ((it - 1) >> 1) & 1)) break;
-          if (!load_v(vq)) break;
-          ++vq;
-        }
         bool rdy = tc::mbar_test(su32(&sm.bar_pready[p2]), (it >> 1) & 1) &
                    tc::mbar_test(su32(&sm.bar_vfull[sv]), (it / NV) & 1);
         if (it >= 2) rdy &= tc::mbar_test(su32(&sm.bar_partfree[p2]), ((it >> 1) - 1) & 1);
@@ -444,11 +419,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         }
         __syncwarp();
       }
-      // (bounded) wait for V copies still in flight after an abort: items it ..
-      // vq-1 were requested and not yet known to have landed
-      if (lane == 0)
-        for (int v = it; v < vq; ++v) tc::mbar_wait(su32(&sm.bar_vfull[v % NV]), (v / NV) & 1);
-      __syncwarp();
     }
     // every MMA issued by this warp has completed once this phase lands
     if (elect_one()) {
@@ -542,7 +512,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   } else {
     // ============================ accumulate (warps 0-3) =====================
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    for (int it = 0; it < n_items; ++it) {
+    // V tile of item `v` into stage v % NV (warp v % NV + 1); the ring entry names the chunk
+    auto load_v = [&](int v) -> bool {
+      const int r = v % RING;
+      if (!wait_bar_warp(sm, &sm.bar_ring[r], (v / RING) & 1)) return false;
+      if (elect_one()) {
+        const uint32_t bar = su32(&sm.bar_vfull[v % NV]);
+        tc::mbar_arrive_expect_tx(bar, 16384u);
+        tc::tma_load_4d(su32(sm.vt[v % NV]), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(sm.ring[r].c) * S),
+                        0, hk, bar);
+      }
+      __syncwarp();
+      return true;
+    };
+    const int vst = warp - 1;                // this warp's V stage (warps 1-3)
+    int vlast = -1;                          // last item whose V tile this warp requested
+    bool ok = true;
+    if (vst >= 0 && vst < n_items) {
+      ok = load_v(vst);
+      if (ok) vlast = vst;
+    }
+    for (int it = 0; ok && it < n_items; ++it) {
       const int p2 = it & 1, r = it % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
       const int n = sm.ring[r].n;
@@ -579,8 +569,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
           }
         }
       }
+      // P.V(it) has completed: stage it % NV takes item it+NV's tile
+      if (vst == it % NV && it + NV < n_items) {
+        if (!load_v(it + NV)) break;
+        vlast = it + NV;
+      }
     }
     tc::tmem_wait_st();
+    // (bounded) wait for this warp's last V copy, in flight after an abort; only
+    // this warp loads its stage, so the phase it waits for is unambiguous
+    if (vlast >= 0 && lane == 0) tc::mbar_wait(su32(&sm.bar_vfull[vst]), (vlast / NV) & 1);
+    __syncwarp();
   }
 
   if (warp < W_LOADKQ) {
