@@ -590,6 +590,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     tc::fence_before_sync();
     asm volatile("bar.sync 1, 384;\n" ::: "memory");
     tc::fence_after_sync();
+    // The local branch of this CTA's rows (G contiguous rows of D values per
+    // query) is staged in the idle K/Q staging area first: every K/Q copy and
+    // S MMA has completed once the last item is accumulated.  Sixteen-byte
+    // loads, all issued before any is used, instead of one two-byte load per
+    // (query, head, dim) that each waited out its own memory latency.
+    __nv_bfloat16* lsm = reinterpret_cast<__nv_bfloat16*>(&sm.kt[0][0]);   // [QB][G][D]
+    __nv_bfloat16* lwsm = lsm + QB * GMAX * D;                              // [QB][G]
+    static_assert(QB * GMAX * (D + 1) * 2 <= 2 * NKQ * 16384, "local-branch staging over the K/Q area");
+    const bool fused = a.local_out != nullptr;
+    if (fused && !__any_sync(0xffffffffu, aborted(sm))) {
+      constexpr int kEpiThreads = 384;
+      constexpr int LMAX = (QB * GMAX * D * 2 / 16 + kEpiThreads - 1) / kEpiThreads;
+      const int per_q = G * (D * 2 / 16);    // 16-byte pieces of one query's rows
+      uint4 v[LMAX];
+#pragma unroll
+      for (int i = 0; i < LMAX; ++i) {
+        const int k = tid + kEpiThreads * i, q = k / per_q;
+        v[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (q < QB && q0 + q < a.Lq)
+          v[i] = __ldg(reinterpret_cast<const uint4*>(a.local_out + ((b * a.Lq + q0 + q) * Hq + hk * G) * D) + k % per_q);
+      }
+      __nv_bfloat16 wv = f2bf(0.f);
+      if (tid < QB * G && q0 + tid / G < a.Lq) wv = a.local_w[(b * a.Lq + q0 + tid / G) * Hq + hk * G + tid % G];
+#pragma unroll
+      for (int i = 0; i < LMAX; ++i) {
+        const int k = tid + kEpiThreads * i;
+        if (k < QB * per_q) reinterpret_cast<uint4*>(lsm)[k] = v[i];
+      }
+      if (tid < QB * G) lwsm[tid] = wv;
+    }
+    asm volatile("bar.sync 1, 384;\n" ::: "memory");
     if (!__any_sync(0xffffffffu, aborted(sm))) {
       constexpr int EB = 4;
       const int qd = warp & 3, part = warp >> 2;
@@ -600,15 +631,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         float lw[EB][GMAX], lo[EB][GMAX];
 #pragma unroll
         for (int j = 0; j < EB; ++j) {
-          const int64_t rowq = q0 + q1 + j;
 #pragma unroll
           for (int gg = 0; gg < GMAX; ++gg) {
             lw[j][gg] = 0.f;
             lo[j][gg] = 0.f;
-            if (a.local_out != nullptr && gg < G && rowq < a.Lq) {
-              const int64_t hrow = (b * a.Lq + rowq) * Hq + hk * G + gg;
-              lw[j][gg] = bf2f(a.local_w[hrow]);
-              lo[j][gg] = bf2f(a.local_out[hrow * D + d]);
+            if (fused && gg < G) {
+              lw[j][gg] = bf2f(lwsm[(q1 + j) * G + gg]);
+              lo[j][gg] = bf2f(lsm[((q1 + j) * G + gg) * D + d]);
             }
           }
           tc::tmem_ld8(tbase + lane_off + 8 * (q1 + j), acc[j]);
