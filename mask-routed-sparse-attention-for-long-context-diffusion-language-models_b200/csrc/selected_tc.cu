@@ -173,20 +173,69 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   }
   if (warp >= 1 && warp <= NV && lane == 0) tc::prefetch_tensormap(&tm_v);
   for (int e = tid; e < C; e += NTHREADS) ownmask[e] = 0u;
-  for (int e = tid; e < QB * KMAX; e += NTHREADS) {
-    const int qi = e / KMAX, kk = e % KMAX;
-    int c = -1;
-    if (kk < K && q0 + qi < a.Lq) {
-      c = a.indices[((b * a.Lq + q0 + qi) * a.Hkv + hk) * K + kk];
-      if (c >= C) c = -1;
+  // Chunk lists and route weights.  Each query's list (K ints) and weights
+  // (G x K bf16) are contiguous, so where K allows it they are read as 16-byte
+  // pieces, every load issued before any is used; the scalar loops serve the
+  // other cases.  Slots kk >= K, heads g >= G and queries past Lq read as
+  // "no chunk" / weight 0.
+  const bool vec_i = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.indices) & 15u) == 0;
+  const bool vec_w = (K & 7) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15u) == 0;
+  if (vec_i) {
+    const int per_q = K >> 2, qi = tid / per_q, piece = tid % per_q;
+    int4 v = make_int4(-1, -1, -1, -1);
+    if (tid < QB * per_q && q0 + qi < a.Lq)
+      v = __ldg(reinterpret_cast<const int4*>(a.indices + ((b * a.Lq + q0 + qi) * a.Hkv + hk) * K) + piece);
+    for (int e = tid; e < QB * KMAX; e += NTHREADS)
+      if (e % KMAX >= K) idx[e / KMAX][e % KMAX] = -1;
+    if (tid < QB * per_q) {
+      const int cv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) idx[qi][4 * piece + i] = (cv[i] < 0 || cv[i] >= C) ? -1 : cv[i];
     }
-    idx[qi][kk] = c < 0 ? -1 : c;
+  } else {
+    for (int e = tid; e < QB * KMAX; e += NTHREADS) {
+      const int qi = e / KMAX, kk = e % KMAX;
+      int c = -1;
+      if (kk < K && q0 + qi < a.Lq) {
+        c = a.indices[((b * a.Lq + q0 + qi) * a.Hkv + hk) * K + kk];
+        if (c >= C) c = -1;
+      }
+      idx[qi][kk] = c < 0 ? -1 : c;
+    }
   }
-  for (int e = tid; e < QB * GMAX * KMAX; e += NTHREADS) {
-    const int qi = e / (GMAX * KMAX), g = (e / KMAX) % GMAX, kk = e % KMAX;
-    float wv = 0.f;
-    if (g < G && kk < K && q0 + qi < a.Lq) wv = bf2f(a.w[((b * a.Lq + q0 + qi) * Hq + hk * G + g) * K + kk]);
-    sm.w[qi][g][kk] = wv;
+  if (vec_w) {
+    constexpr int WP = (QB * GMAX * KMAX / 8 + NTHREADS - 1) / NTHREADS;
+    const int per_q = G * K / 8;
+    uint4 wv[WP];
+#pragma unroll
+    for (int i = 0; i < WP; ++i) {
+      const int k = tid + NTHREADS * i, qi = k / per_q;
+      wv[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (qi < QB && q0 + qi < a.Lq)
+        wv[i] = __ldg(reinterpret_cast<const uint4*>(a.w + ((b * a.Lq + q0 + qi) * Hq + hk * G) * K) + k % per_q);
+    }
+    for (int e = tid; e < QB * GMAX * KMAX; e += NTHREADS) {
+      const int g = (e / KMAX) % GMAX, kk = e % KMAX;
+      if (g >= G || kk >= K) sm.w[e / (GMAX * KMAX)][g][kk] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < WP; ++i) {
+      const int k = tid + NTHREADS * i, qi = k / per_q;
+      if (qi >= QB) continue;
+      const uint32_t wd[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int e = (k % per_q) * 8 + t, g = e / K, kk = e % K;
+        sm.w[qi][g][kk] = __uint_as_float((t & 1) ? (wd[t >> 1] & 0xffff0000u) : (wd[t >> 1] << 16));
+      }
+    }
+  } else {
+    for (int e = tid; e < QB * GMAX * KMAX; e += NTHREADS) {
+      const int qi = e / (GMAX * KMAX), g = (e / KMAX) % GMAX, kk = e % KMAX;
+      float wv = 0.f;
+      if (g < G && kk < K && q0 + qi < a.Lq) wv = bf2f(a.w[((b * a.Lq + q0 + qi) * Hq + hk * G + g) * K + kk]);
+      sm.w[qi][g][kk] = wv;
+    }
   }
   if (tid == 0) {
     for (int s = 0; s < NKQ; ++s) {
