@@ -60,6 +60,13 @@ def stage_bytes(l: int):
             "qcal": l * HIDDEN * 2 + 2 * l * HQ * D * 2}
 
 
+# DRAM bytes (read + write) of one launch of the dominant kernel, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum) of this bench's own
+# single-GPU workload; kept under profiles/ with the command that produced it.
+# Keyed by (kernel, query rows per GPU, total keys); other workloads report null.
+MEASURED_TRAFFIC = {("selected_attention", 16384, 16384): 332016128 + 101256704}
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -328,7 +335,9 @@ def main():
         if dom in ("selected_attention", "local_attention", "route"):
             ach = flops[dom] / (stages[dom] * 1e-3) / 1e12
             roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tflops,
-                    "unit": "TFLOP/s", "frac": ach / tflops, "traffic": None,
+                    "unit": "TFLOP/s", "frac": ach / tflops,
+                    "traffic": MEASURED_TRAFFIC.get((dom, lq, l_total)),
+                    "traffic_unit": "bytes per launch (ncu DRAM read + write)",
                     "peak_kind": f"{peak_kind} bf16 burst"}
         else:
             ach = byts[dom] / (stages[dom] * 1e-3) / 1e9
