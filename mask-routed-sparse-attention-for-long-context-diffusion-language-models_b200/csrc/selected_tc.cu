@@ -341,6 +341,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
 #pragma unroll
     for (int kk = 0; kk < KMAX; ++kk) myc[kk] = idx[lane][kk];
     tc::fence_proxy_async();                 // these reads precede TMA writes to the same area
+    // the chunk lists live in a K/Q stage that the first items overwrite: both
+    // loaders have read them before either issues a copy
+    asm volatile("bar.sync 2, 64;\n" ::: "memory");
     const uint32_t below = (1u << lane) - 1u;
     int item = 0;
     bool ok = true;
@@ -348,9 +351,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       const int2 ue = sm.ulist[u];
       const int c = ue.x;
       uint32_t owners = static_cast<uint32_t>(ue.y);
-      int my_slot = 0;
-#pragma unroll
-      for (int kk = KMAX - 1; kk >= 0; --kk) my_slot = myc[kk] == c ? kk : my_slot;
+      int my_slot = -1;                      // this lane's slot of chunk c, found on first use
       while (owners) {
         // the next (up to) OWN owners, in query order
         const int j = __popc(owners & below);
@@ -359,6 +360,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         owners &= ~grp;
         if ((item & 1) == par) {
           const int st = item % NKQ, r = item % RING, n = __popc(grp);
+          if (my_slot < 0) {                 // only for chunks that carry one of this warp's items
+            my_slot = 0;
+#pragma unroll
+            for (int kk = KMAX - 1; kk >= 0; --kk) my_slot = myc[kk] == c ? kk : my_slot;
+          }
           // the item's owner list goes into the ring before the stage is free
           if (mine) {
             sm.ring[r].oq[j] = static_cast<uint8_t>(lane);
