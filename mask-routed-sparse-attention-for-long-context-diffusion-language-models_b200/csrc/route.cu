@@ -19,8 +19,12 @@
 //   folds each S tile into an online log-sum-exp per (query, head), giving T;
 //   pass 2 walks tiles then heads and keeps max_g (x - T_g) in registers, applies
 //   the drop rule and writes the fp32 keys [B, Lq, Hkv, C] to the workspace.
-//   Warps 0-7 read TMEM (two threads per S row, 32 columns each, via
-//   tcgen05.ld.16x32bx2), warp 8 issues the TMA copies, warp 9 the MMAs.
+//   Warps 0-15 read TMEM (four threads per S row, 16 columns each, via
+//   tcgen05.ld.16x32bx2), warp 16 issues the TMA copies and fills the bias
+//   ring, warp 17 the MMAs.  Every role runs at a few cycles per instruction,
+//   so each keeps its per-tile instruction count small: the job order is a
+//   table built once, the bias of a tile is fetched two tiles ahead from a
+//   per-lane base pointer, and the readers split each row four ways.
 // route_select_kernel: one warp per (query, KV head) holds that row's keys in
 //   registers, finds the K-th largest with a 32-step radix search over
 //   order-preserving integer keys, emits the indices in ascending chunk order
@@ -45,8 +49,10 @@ constexpr int RN = 128;           // chunks per landmark tile (UMMA N)
 constexpr int RBUF = 4;           // TMEM S buffers of RN columns
 constexpr int RMAXST = 4;         // landmark stages (chosen at launch from the shared-memory budget)
 constexpr int RGMAX = 8;
-constexpr int R_THREADS = 320;    // warps 0-7 TMEM readers, 8 TMA, 9 MMA
-constexpr int R_W_LOAD = 8, R_W_MMA = 9;
+constexpr int R_THREADS = 576;    // warps 0-15 TMEM readers, 16 TMA, 17 MMA
+constexpr int R_W_LOAD = 16, R_W_MMA = 17;
+constexpr int RC = 16;            // tile columns per reader thread
+constexpr int RMAXJ = 2 * RGMAX * (kMaxChunks / RN);   // jobs of one CTA at most
 constexpr int kSmemLimit = 232448;
 
 struct RouteArgs {
@@ -87,7 +93,8 @@ struct RouteMisc {
   uint32_t tmem_base;
   int abort_flag;
   float T[RQ][RGMAX];              // T per (query, head), natural log
-  float part[2][RQ][RGMAX][2];     // pass-1 partials (max, sum) per column half, log2 domain
+  float part[2][4][RQ][2];         // pass-1 partials (max, sum) per column quarter, log2 domain; two heads
+  uint16_t job[RMAXJ];             // job j -> (tile << 8) | head
   uint8_t chunk_ok[kMaxChunks];
 };
 
@@ -123,6 +130,11 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
   const int J = 2 * G * NT;
 
   for (int c = tid; c < C; c += R_THREADS) ms.chunk_ok[c] = a.chunk_ok ? a.chunk_ok[(int64_t)b * C + c] : 1;
+  for (int jj = tid; jj < J; jj += R_THREADS) {
+    int g, t;
+    job_coords(jj, G, NT, g, t);
+    ms.job[jj] = static_cast<uint16_t>((t << 8) | g);
+  }
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
       tc::mbar_init(tc::smem_addr(&ms.lfull[s]), 1);
@@ -130,11 +142,11 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
     }
     for (int s = 0; s < RBUF; ++s) {
       tc::mbar_init(tc::smem_addr(&ms.sdone[s]), 1);
-      tc::mbar_init(tc::smem_addr(&ms.sfree[s]), 8);
+      tc::mbar_init(tc::smem_addr(&ms.sfree[s]), 16);
     }
     for (int s = 0; s < RBR; ++s) {
       tc::mbar_init(tc::smem_addr(&ms.bfull[s]), 1);
-      tc::mbar_init(tc::smem_addr(&ms.bfree[s]), 8);
+      tc::mbar_init(tc::smem_addr(&ms.bfree[s]), 16);
     }
     tc::mbar_init(tc::smem_addr(&ms.qfull), 1);
     tc::mbar_init(tc::smem_addr(&ms.mma_drain), 1);
@@ -161,29 +173,41 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
         tc::tma_load_4d(tc::smem_addr(qt + g * 16384), &tm_q, 0, static_cast<int>(b * a.Lq + q0), 0, hk * G + g, qb);
     }
     __syncwarp();
+    // this lane's share of a tile's bias: chunks t*RN + 32k + lane of head g
+    const float* bias_lane = a.bias != nullptr ? a.bias + ((int64_t)b * C + lane) * Hq + hk * G : nullptr;
+    auto load_bias = [&](int jj, float (&bv)[RN / 32]) {
+      const int jc = jj < J ? ms.job[jj] : 0, g = jc & 0xff, t = jc >> 8;
+#pragma unroll
+      for (int k = 0; k < RN / 32; ++k) {
+        const int c = t * RN + 32 * k + lane;
+        bv[k] = (jj < J && bias_lane != nullptr && c < C) ? bias_lane[(t * RN + 32 * k) * Hq + g] : 0.f;
+      }
+    };
+    float b0[RN / 32], b1[RN / 32];
+    load_bias(0, b0);
+    load_bias(1, b1);
     int j = 0;
     for (; j < J; ++j) {
       const int st = j % NST, bs = j % RBR;
       if (j >= NST && !tc::wait_bounded_warp(tc::smem_addr(&ms.lfree[st]), ((j / NST) - 1) & 1, abort_flag)) break;
-      int g, t;
-      job_coords(j, G, NT, g, t);
+      const int jc = ms.job[j], g = jc & 0xff, t = jc >> 8;
       if (lane == 0) {
         const uint32_t lb = tc::smem_addr(&ms.lfull[st]);
         tc::mbar_arrive_expect_tx(lb, 32768u);
         tc::tma_load_5d(tc::smem_addr(lt + st * 32768), &tm_l, 0, b * C + t * RN, 0, a.lmk_per_qhead ? g : 0, hk, lb);
       }
-      // bias[c, hq] of the job's 128 chunks (stride Hq in memory) into its ring slot
-      float bv[RN / 32];
-#pragma unroll
-      for (int k = 0; k < RN / 32; ++k) {
-        const int c = t * RN + 32 * k + lane;
-        bv[k] = (a.bias != nullptr && c < C) ? a.bias[((int64_t)b * C + c) * Hq + hk * G + g] : 0.f;
-      }
+      float b2[RN / 32];
+      load_bias(j + 2, b2);
       if (j >= RBR && !tc::wait_bounded_warp(tc::smem_addr(&ms.bfree[bs]), ((j / RBR) - 1) & 1, abort_flag)) break;
 #pragma unroll
-      for (int k = 0; k < RN / 32; ++k) ms.bias[bs][32 * k + lane] = bv[k];
+      for (int k = 0; k < RN / 32; ++k) ms.bias[bs][32 * k + lane] = b0[k];
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(tc::smem_addr(&ms.bfull[bs]));
+#pragma unroll
+      for (int k = 0; k < RN / 32; ++k) {
+        b0[k] = b1[k];
+        b1[k] = b2[k];
+      }
     }
     // wait (bounded, even after an abort) for the copies in flight
     if (lane == 0) {
@@ -202,8 +226,7 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
       if (!tc::wait_bounded_warp(tc::smem_addr(&ms.lfull[st]), (j / NST) & 1, abort_flag)) break;
       if (j >= RBUF && !tc::wait_bounded_warp(tc::smem_addr(&ms.sfree[bf]), ((j / RBUF) - 1) & 1, abort_flag)) break;
       tc::fence_after_sync();
-      int g, t;
-      job_coords(j, G, NT, g, t);
+      const int g = ms.job[j] & 0xff;
       const uint64_t da = tc::desc_adv(dq0, g * 16384), db = tc::desc_adv(dl0, st * 32768);
       const uint32_t dS = tbase + RN * bf;
       if (tc::elect_one()) {
@@ -223,28 +246,28 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
     }
     __syncwarp();
   } else {
-    // ============================ TMEM readers (warps 0-7) ====================
+    // ============================ TMEM readers (warps 0-15) ===================
     // M=64 layout: S row r sits in lane (r % 16) of TMEM quadrant r / 16.  Warp
-    // w reads quadrant w % 4, tile columns [64 (w / 4), +64): lanes 0-15 the
-    // first 32 of those, lanes 16-31 the next 32.
-    const int qd = warp & 3, ch = warp >> 2;
+    // w reads quadrant w % 4, tile columns [32 (w / 4), +32): lanes 0-15 the
+    // first 16 of those, lanes 16-31 the next 16 (tcgen05.ld.16x32bx2.x16).
+    const int qd = warp & 3, cq = warp >> 2;
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
     const int r = 16 * qd + (lane & 15);
-    const int cb = 64 * ch + 32 * (lane >> 4);              // first tile column of this thread
+    const int cb = 32 * cq + 16 * (lane >> 4);              // first tile column of this thread
     const int64_t rowq = q0 + r;
     const bool row_ok = rowq < a.Lq;
     const float scale = a.sm_scale;
     bool ok = true;
     int j = 0;
     // S tile of job jj into s, this thread's bias values into bias; both slots released
-    auto read_tile = [&](int jj, uint32_t (&s)[32], float (&bias)[32]) -> bool {
+    auto read_tile = [&](int jj, uint32_t (&s)[RC], float (&bias)[RC]) -> bool {
       const int bf = jj % RBUF, bs = jj % RBR;
       if (!tc::wait_bounded_warp(tc::smem_addr(&ms.bfull[bs]), (jj / RBR) & 1, abort_flag)) return false;
       if (!tc::wait_bounded_warp(tc::smem_addr(&ms.sdone[bf]), (jj / RBUF) & 1, abort_flag)) return false;
       tc::fence_after_sync();
-      tc::tmem_ld_16x32bx2_x32(tbase + lane_off + RN * bf + 64 * ch, s);
+      tc::tmem_ld_16x32bx2_x16(tbase + lane_off + RN * bf + 32 * cq, s);
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
+      for (int i = 0; i < RC; i += 4) {
         const float4 v = *reinterpret_cast<const float4*>(&ms.bias[bs][cb + i]);
         bias[i] = v.x;
         bias[i + 1] = v.y;
@@ -261,15 +284,15 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
       return true;
     };
     // ---- pass 1: online log-sum-exp (log2 domain) per (query, head)
-    for (int g = 0; ok && g < G; ++g) {
+    for (int g = 0; g < G; ++g) {
       float m = -INFINITY, l = 0.f;
-      for (int t = 0; t < NT; ++t, ++j) {
-        float bias[32];
-        uint32_t s[32];
+      for (int t = 0; ok && t < NT; ++t, ++j) {
+        float bias[RC];
+        uint32_t s[RC];
         if (!(ok = read_tile(j, s, bias))) break;
-        float y[32], mb = -INFINITY;
+        float y[RC], mb = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < RC; ++i) {
           const int c = t * RN + cb + i;
           const float x = __uint_as_float(s[i]) * scale + bias[i];
           y[i] = c < C ? x * kLog2e : -INFINITY;
@@ -282,36 +305,39 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
         if (m != -INFINITY) {
           float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s4[i & 3] += fast_exp2(y[i] - m);
+          for (int i = 0; i < RC; ++i) s4[i & 3] += fast_exp2(y[i] - m);
           l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
         }
       }
-      if (!ok) break;
-      // combine the two column quarters held by this warp (lanes t, t+16)
+      // combine the two column halves held by this warp (lanes t, t+16); the
+      // four column quarters of a row meet in shared memory (two buffers: head
+      // g+2 rewrites one only after the barrier of head g+1)
       const float mo = __shfl_xor_sync(0xffffffffu, m, 16), lo = __shfl_xor_sync(0xffffffffu, l, 16);
       const float mn = fmaxf(m, mo);
       l = (mn == -INFINITY) ? 0.f : l * fast_exp2(m - mn) + lo * fast_exp2(mo - mn);
       m = mn;
       if (lane < 16) {
-        ms.part[ch][r][g][0] = m;
-        ms.part[ch][r][g][1] = l;
+        ms.part[g & 1][cq][r][0] = m;
+        ms.part[g & 1][cq][r][1] = l;
       }
-    }
-    // both column halves of a row meet in shared memory
-    asm volatile("bar.sync 1, 256;\n" ::: "memory");
-    if (ok && ch == 0 && lane < 16) {
-      for (int g = 0; g < G; ++g) {
-        const float m1 = ms.part[0][r][g][0], l1 = ms.part[0][r][g][1];
-        const float m2 = ms.part[1][r][g][0], l2 = ms.part[1][r][g][1];
-        const float mn = fmaxf(m1, m2);
-        const float lsum = (mn == -INFINITY) ? 0.f : l1 * fast_exp2(m1 - mn) + l2 * fast_exp2(m2 - mn);
-        const float lse = lsum > 0.f ? (mn + __log2f(lsum)) * kLn2 : -INFINITY;
+      // every reader reaches this barrier once per head, aborted or not
+      asm volatile("bar.sync 1, 512;\n" ::: "memory");
+      if (ok && cq == 0 && lane < 16) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mx = fmaxf(mx, ms.part[g & 1][k][r][0]);
+        float lsum = 0.f;
+        if (mx != -INFINITY) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) lsum += ms.part[g & 1][k][r][1] * fast_exp2(ms.part[g & 1][k][r][0] - mx);
+        }
+        const float lse = lsum > 0.f ? (mx + __log2f(lsum)) * kLn2 : -INFINITY;
         const float loc = row_ok ? a.local_lse[((int64_t)b * a.Lq + rowq) * Hq + hk * G + g] : 0.f;
-        const float mx = fmaxf(loc, lse), mnv = fminf(loc, lse);
-        ms.T[r][g] = (mx == -INFINITY) ? -INFINITY : mx + log1pf(expf(mnv - mx));
+        const float hi = fmaxf(loc, lse), lo2 = fminf(loc, lse);
+        ms.T[r][g] = (hi == -INFINITY) ? -INFINITY : hi + log1pf(expf(lo2 - hi));
       }
     }
-    asm volatile("bar.sync 1, 256;\n" ::: "memory");
+    asm volatile("bar.sync 1, 512;\n" ::: "memory");
     // ---- pass 2: keys = max_g (x - T_g), the drop rule, fp32 keys to the workspace
     int64_t clo = 1, chi = 0;                 // dropped chunk window [clo, chi] of this row
     if (a.drop == nullptr && a.window >= 0) {
@@ -324,47 +350,48 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
     }
     float* krow = a.keys + (((int64_t)b * a.Lq + rowq) * a.Hkv + hk) * C;
     for (int t = 0; ok && t < NT; ++t) {
-      float key[32];
+      float key[RC];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) key[i] = -INFINITY;
+      for (int i = 0; i < RC; ++i) key[i] = -INFINITY;
       for (int g = 0; g < G; ++g, ++j) {
         const float Tg = ms.T[r][g];
-        float bias[32];
-        uint32_t s[32];
+        float bias[RC];
+        uint32_t s[RC];
         if (!(ok = read_tile(j, s, bias))) break;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = __float_as_uint(__uint_as_float(s[i]) * scale);
+        for (int i = 0; i < RC; ++i) s[i] = __float_as_uint(__uint_as_float(s[i]) * scale);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) key[i] = fmaxf(key[i], (__uint_as_float(s[i]) + bias[i]) - Tg);
+        for (int i = 0; i < RC; ++i) key[i] = fmaxf(key[i], (__uint_as_float(s[i]) + bias[i]) - Tg);
         // the raw scaled scores of every (head, chunk): the selection kernel gathers its slots from here
         if (row_ok) {
           const int c0 = t * RN + cb;
           const int64_t o = (((int64_t)b * a.Lq + rowq) * Hq + hk * G + g) * C + c0;
+          // whole 32-byte sectors per store where C allows (each thread's 16
+          // columns start on a multiple of 16): half-sector stores from 16 rows
+          // per instruction kept the L1 busy
           if (a.scores_f32) {
             float* dst = static_cast<float*>(a.raw) + o;
-            if (c0 + 32 <= C && (C & 3) == 0) {
+            if (c0 + RC <= C && (C & 15) == 0) {
 #pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(dst + i) = make_float4(__uint_as_float(s[i]), __uint_as_float(s[i + 1]),
-                                                                  __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
+              for (int i = 0; i < RC; i += 8) {
+                const uint32_t v8[8] = {s[i], s[i + 1], s[i + 2], s[i + 3], s[i + 4], s[i + 5], s[i + 6], s[i + 7]};
+                st_global_v8(dst + i, v8);
+              }
             } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
+              for (int i = 0; i < RC; ++i)
                 if (c0 + i < C) dst[i] = __uint_as_float(s[i]);
             }
           } else {
             __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.raw) + o;
-            if (c0 + 32 <= C && (C & 7) == 0) {
+            if (c0 + RC <= C && (C & 15) == 0) {
+              uint32_t v8[8];
 #pragma unroll
-              for (int i = 0; i < 32; i += 8)
-                *reinterpret_cast<uint4*>(dst + i) = make_uint4(
-                    pack_bf16x2(__uint_as_float(s[i]), __uint_as_float(s[i + 1])),
-                    pack_bf16x2(__uint_as_float(s[i + 2]), __uint_as_float(s[i + 3])),
-                    pack_bf16x2(__uint_as_float(s[i + 4]), __uint_as_float(s[i + 5])),
-                    pack_bf16x2(__uint_as_float(s[i + 6]), __uint_as_float(s[i + 7])));
+              for (int i = 0; i < 8; ++i) v8[i] = pack_bf16x2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1]));
+              st_global_v8(dst, v8);
             } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
+              for (int i = 0; i < RC; ++i)
                 if (c0 + i < C) dst[i] = f2bf(__uint_as_float(s[i]));
             }
           }
@@ -376,28 +403,32 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
       if (a.drop != nullptr) {
         const int32_t* dr = a.drop + ((int64_t)b * a.Lq + rowq) * C;
 #pragma unroll 8
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < RC; ++i) {
           const int c = t * RN + cb + i;
           if (c < C && dr[c] != 0) dm |= 1u << i;
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < RC; ++i) {
           const int c = t * RN + cb + i;
           if (c < C && (ms.chunk_ok[c] == 0 || (c >= clo && c <= chi))) dm |= 1u << i;
         }
       }
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
+      for (int i = 0; i < RC; ++i)
         if ((dm >> i) & 1u) key[i] = -INFINITY;
       const int c0 = t * RN + cb;
-      if (c0 + 32 <= C && (C & 3) == 0) {
+      if (c0 + RC <= C && (C & 15) == 0) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(krow + c0 + i) = make_float4(key[i], key[i + 1], key[i + 2], key[i + 3]);
+        for (int i = 0; i < RC; i += 8) {
+          const uint32_t v8[8] = {__float_as_uint(key[i]), __float_as_uint(key[i + 1]), __float_as_uint(key[i + 2]),
+                                  __float_as_uint(key[i + 3]), __float_as_uint(key[i + 4]), __float_as_uint(key[i + 5]),
+                                  __float_as_uint(key[i + 6]), __float_as_uint(key[i + 7])};
+          st_global_v8(krow + c0 + i, v8);
+        }
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
+        for (int i = 0; i < RC; ++i)
           if (c0 + i < C) krow[c0 + i] = key[i];
       }
     }
