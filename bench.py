@@ -294,28 +294,52 @@ def main():
     value = l_total / (ms_step / 1e3)
 
     # ---- e2e through the public API with pinned host buffers ---------------
+    # Pipelined as a serving loop would run it: step i's inputs go up on one
+    # copy stream while step i-1 computes, and its output comes back on a
+    # second copy stream while step i+1 computes (two buffer slots, events
+    # keep a slot's inputs until its compute has read them and its output until
+    # it has been read back).  Every step's own copies are inside the timed
+    # region: it starts before the first upload and ends after the last readback.
     host = [t.cpu().pin_memory() for t in x]
-    dev_in = [torch.empty_like(t) for t in x]
-    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    dev_in = [[torch.empty_like(t) for t in x] for _ in range(2)]
+    dev_out = [torch.empty_like(out) for _ in range(2)]
+    host_out = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host)
-    d2h = host_out.numel() * host_out.element_size()
+    d2h = host_out[0].numel() * host_out[0].element_size()
+    s_up, s_comp, s_down = (torch.cuda.Stream(dev) for _ in range(3))
+    up_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    down_done = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        for d_, h_ in zip(dev_in, host):
-            d_.copy_(h_, non_blocking=True)
-        runner(*dev_in, out=out)
-        host_out.copy_(out, non_blocking=True)
+    def e2e_step(i):
+        sl = i & 1
+        with torch.cuda.stream(s_up):
+            if i >= 2:
+                s_up.wait_event(comp_done[sl])        # step i-2 has read these inputs
+            for d_, h_ in zip(dev_in[sl], host):
+                d_.copy_(h_, non_blocking=True)
+            up_done[sl].record(s_up)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(up_done[sl])
+            if i >= 2:
+                s_comp.wait_event(down_done[sl])      # step i-2's output has been read back
+            runner(*dev_in[sl], out=dev_out[sl])
+            comp_done[sl].record(s_comp)
+        with torch.cuda.stream(s_down):
+            s_down.wait_event(comp_done[sl])
+            host_out[sl].copy_(dev_out[sl], non_blocking=True)
+            down_done[sl].record(s_down)
 
-    for _ in range(2):
-        e2e_step()
+    for i in range(3):
+        e2e_step(i)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     e2 = max(3, args.steps // 2)
-    e0.record(stream)
-    for _ in range(e2):
-        e2e_step()
-    e1.record(stream)
+    e0.record(s_up)
+    for i in range(e2):
+        e2e_step(i)
+    e1.record(s_down)
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1)
     if dist:
@@ -357,7 +381,8 @@ def main():
                 "gpu_launches": args.steps * 6,
                 "clocks": clocks,
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
-                        "d2h_bytes_per_step": d2h * world, "steps": e2}}
+                        "d2h_bytes_per_step": d2h * world, "steps": e2,
+                        "pipelining": "step i's upload and readback overlap the compute of steps i-1 and i+1"}}
         if world == 1 and not args.no_cpu_baseline:
             rate, info = cpu_route_layer_rate(l_total, 32, 160)
             line["cpu_baseline"] = {
