@@ -156,10 +156,28 @@ int mrsa_selected_attention(const void* q, const void* k, const void* v, const u
                             int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk,
                             mrsa_stream_t stream);
 
+/* mrsa_selected_attention with V given in fp16 ([B,Lk,Hkv,D] fp16, every
+ * other argument as above).  P then travels as one fp16 tile (11 significant
+ * bits) instead of bf16 hi + lo, which halves the P.V work.  No counterpart in the reference: the fused
+ * layer uses it after mrsa_convert_bf16_to_f16 on V. */
+int mrsa_selected_attention_f16v(const void* q, const void* k, const void* v_f16, const uint8_t* key_valid,
+                                 const void* weights, const int32_t* indices, const void* local_out,
+                                 const void* local_w, void* out, float sm_scale, int mask_last_token,
+                                 int64_t batch, int64_t q_len, int64_t kv_len, int64_t kv_heads,
+                                 int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk,
+                                 mrsa_stream_t stream);
+
+/* n bf16 values (n a multiple of 8, 16-byte aligned buffers) to fp16, round to
+ * nearest; values beyond +-65504 (infinities too) saturate and set bit 3 of
+ * mrsa_device_error_flags.  No counterpart in the reference (V preparation
+ * for mrsa_selected_attention_f16v). */
+int mrsa_convert_bf16_to_f16(const void* in, void* out, int64_t n, mrsa_stream_t stream);
+
 /* Bit mask of device-side failures recorded since the last clear: bit 0 = a
  * selected-attention CTA gave up waiting on one of its internal barriers (its
  * output rows are then incomplete); bit 1 = a routing key CTA did (its keys,
- * hence its selections, are then incomplete); bit 2 = a local-window CTA did.  Synchronises the current device; with
+ * hence its selections, are then incomplete); bit 2 = a local-window CTA did;
+ * bit 3 = mrsa_convert_bf16_to_f16 saturated a value.  Synchronises the current device; with
  * clear != 0 also resets the mask.  Negative on a CUDA error.  Replaces the
  * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
 int mrsa_device_error_flags(int clear);

@@ -17,7 +17,7 @@ from .route_weights import route_weights, route_weights_torch
 from .routing import (online_softmax_topk_head, ref_softmax_topk_max_pooling, remote_drop_mask,
                       route_topk_fused, route_topk_g7)
 from .selected_attention import (HiLS_block_M_head, fuse_hils_outputs, selected_attention,
-                                 selected_attention_g7, selected_attention_g7_cached)
+                                 selected_attention_g7, selected_attention_g7_cached, to_f16)
 
 __all__ = [
     "RouteLayer", "RouteLayerConfig", "swa_layer_forward", "chunk_attn_pool_gqa",
@@ -26,7 +26,7 @@ __all__ = [
     "route_weights_torch", "online_softmax_topk_head", "ref_softmax_topk_max_pooling",
     "remote_drop_mask", "route_topk_fused", "route_topk_g7", "HiLS_block_M_head",
     "fuse_hils_outputs", "selected_attention", "selected_attention_g7",
-    "selected_attention_g7_cached", "load_library",
+    "selected_attention_g7_cached", "to_f16", "load_library",
 ]
 
 

@@ -41,6 +41,9 @@ _SIGS = {
                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_selected_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _int,
                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_selected_attention_f16v": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _int,
+                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_convert_bf16_to_f16": [_vp, _vp, _i64, _vp],
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_device_error_flags": [_int],
     "mrsa_route_layer_workspace_size": [_vp],

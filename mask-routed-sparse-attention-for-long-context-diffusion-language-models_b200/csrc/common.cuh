@@ -123,6 +123,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // Device error flags of the routing and local-window kernels; -1 when unreadable.
 int route_error_flags(int clear);
 int local_error_flags(int clear);
+int convert_error_flags(int clear);
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

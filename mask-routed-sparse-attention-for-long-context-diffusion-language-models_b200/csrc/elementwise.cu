@@ -124,9 +124,47 @@ __global__ void fuse_kernel(const __nv_bfloat16* __restrict__ remote,
   }
 }
 
+// Set when mrsa_convert_bf16_to_f16 saturated a value beyond the fp16 range
+// (infinities included); read and cleared through mrsa_device_error_flags() (bit 3).
+__device__ int g_conv_error;
+
+// bf16 -> fp16, eight values per thread; values beyond +-65504 saturate.
+__global__ void __launch_bounds__(256) bf16_to_f16_kernel(const uint4* __restrict__ in, uint4* __restrict__ out,
+                                                          int64_t n8) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const uint4 v = in[i];
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+  bool sat = false;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float f0 = __uint_as_float(w[k] << 16), f1 = __uint_as_float(w[k] & 0xffff0000u);
+    const bool s0 = fabsf(f0) > 65504.f, s1 = fabsf(f1) > 65504.f;   // infinities included
+    if (s0) f0 = copysignf(65504.f, f0);
+    if (s1) f1 = copysignf(65504.f, f1);
+    sat |= s0 | s1;
+    o[k] = pack_f16x2(f0, f1);
+  }
+  out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  if (sat) atomicOr(&g_conv_error, 1);
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+namespace mrsa {
+int convert_error_flags(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_conv_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_conv_error, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+}  // namespace mrsa
 
 extern "C" {
 
@@ -144,6 +182,19 @@ const char* mrsa_strerror(int code) {
 }
 
 int mrsa_abi_version(void) { return 2; }
+
+int mrsa_convert_bf16_to_f16(const void* in, void* out, int64_t n, mrsa_stream_t stream) {
+  if (!in || !out) return MRSA_ERR_NULL;
+  if (n < 0 || n % 8) return MRSA_ERR_SHAPE;
+  if (!aligned16(in) || !aligned16(out)) return MRSA_ERR_ALIGN;
+  if (n == 0) return MRSA_OK;
+  const int64_t n8 = n / 8, blocks = (n8 + 255) / 256;
+  if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
+  bf16_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(in), static_cast<uint4*>(out), n8);
+  MRSA_CHECK_LAUNCH();
+  return MRSA_OK;
+}
 
 int mrsa_yarn_inv_freq(int dim, double base, double factor, int orig_max_pos, double beta_fast,
                        double beta_slow, int truncate, float* inv_freq_out,

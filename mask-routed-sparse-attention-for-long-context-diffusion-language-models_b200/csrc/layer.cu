@@ -38,7 +38,11 @@ LayerPlan plan(const mrsa_route_layer_args* a) {
   p.scores = take(B * L * Hq * K * 2);
   p.remote_w = take(B * L * Hq * K * 2);
   p.local_w = take(B * L * Hq * 2);
-  p.route_keys = take(mrsa_route_topk_workspace_size(B, L, C, Hkv, Hq / Hkv, MRSA_BF16));
+  // the routing keys and raw scores are dead once routing is done; fp16 V
+  // (for the selected-attention kernel, which runs after it) reuses the piece
+  const size_t route_bytes = mrsa_route_topk_workspace_size(B, L, C, Hkv, Hq / Hkv, MRSA_BF16);
+  const size_t v16_bytes = B * L * Hkv * D * 2;
+  p.route_keys = take(route_bytes > v16_bytes ? route_bytes : v16_bytes);
   p.total = off;
   return p;
 }
@@ -108,7 +112,12 @@ extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* wo
                        a->topk, route_keys, mrsa_route_topk_workspace_size(B, L, C, Hkv, G, MRSA_BF16),
                        stream);
   if (rc) return rc;
-  return mrsa_selected_attention(q, k, a->v, a->key_valid, remote_w, indices, local_out, local_w,
+  // V in fp16 (in the routing workspace, free by now): P.V then takes one fp16
+  // P tile instead of bf16 hi + lo
+  void* v16 = route_keys;
+  rc = mrsa_convert_bf16_to_f16(a->v, v16, B * L * Hkv * D, stream);
+  if (rc != MRSA_OK) return rc;
+  return mrsa_selected_attention_f16v(q, k, v16, a->key_valid, remote_w, indices, local_out, local_w,
                                  a->out, sm_scale, 1, B, L, L, Hkv, G, D, a->topk, mrsa::kChunk,
                                  stream);
 }

@@ -61,7 +61,7 @@ constexpr int QB = 32;            // queries per CTA (== warp size: one loader l
 constexpr int GMAX = 8;           // head rows per query in the MMA tile
 constexpr int OWN = 8;            // owners per work item (64 S rows)
 constexpr int NKQ = 3;            // K/Q load stages (released after S)
-constexpr int NV = 3;             // V load stages (released after P.V)
+constexpr int NVMAX = 4;          // V load stages: 3 with bf16 hi + lo P, 4 with fp16 P (stage 3 in the lo area)
 constexpr int RING = 16;          // item-ring entries
 constexpr int D = kHeadDim, S = kChunk, KMAX = 32;
 constexpr int NTHREADS = 512;
@@ -80,14 +80,17 @@ struct Item {
 struct __align__(1024) TcSmem {
   unsigned char kt[NKQ][16384];   // K tile: [half][64 keys][64 dims], 128-byte swizzled
   unsigned char at[NKQ][16384];   // owner Q rows: 8 slots x [half][8 rows][64 dims]
-  unsigned char vt[NV][16384];    // V tile, K's layout, read as V^T (MN-major)
-  unsigned char ph[2][8192];      // P hi: [64 rows x 64 keys], row 8j+g = owner j head g
-  unsigned char pl[2][8192];      // P lo
+  unsigned char vt[3][16384];     // V tiles, K's layout, read as V^T (MN-major)
+  union {                         // directly after the V tiles, so stage 3 continues them
+    unsigned char pl[2][8192];    // bf16 P: the lo part
+    unsigned char vt3[16384];     // fp16 P: V stage 3
+  };
+  unsigned char ph[2][8192];      // P (bf16 hi, or fp16): [64 rows x 64 keys], row 8j+g = owner j head g
   float w[QB][GMAX][KMAX];        // route weights; a chunk's repeats summed into its first slot
   unsigned long long vmask[QB * KMAX];   // per union chunk: bit s = key s usable
   int2 ulist[QB * KMAX];          // per union chunk: (chunk, owner-query mask)
   Item ring[RING];
-  uint64_t bar_kqfull[NKQ], bar_kqfree[NKQ], bar_vfull[NV];
+  uint64_t bar_kqfull[NKQ], bar_kqfree[NKQ], bar_vfull[NVMAX];
   uint64_t bar_sdone[2], bar_sfree[2], bar_pready[2], bar_pvdone[2], bar_partfree[2];
   uint64_t bar_ring[RING], bar_mma_drain[2];
   int kq_last[2][NKQ];            // per K/Q loader: last item it issued into each stage
@@ -96,6 +99,7 @@ struct __align__(1024) TcSmem {
 };
 // one CTA per SM: the tile set plus 1 KB of alignment slack fits the 227 KB opt-in limit
 static_assert(sizeof(TcSmem) + 1024 <= 232448, "selected-attention shared memory over budget");
+static_assert(offsetof(TcSmem, vt3) == offsetof(TcSmem, vt) + 3 * 16384, "V stage 3 must follow stages 0-2");
 
 struct TcArgs {
   const __nv_bfloat16* w;
@@ -152,6 +156,9 @@ __device__ __forceinline__ bool elect_one() {
 // UMMA descriptor start-address field advance for a byte offset.
 __device__ __forceinline__ uint64_t adv(uint64_t desc, uint32_t bytes) { return desc + (bytes >> 4); }
 
+// kF16: V arrives in fp16 and P is one fp16 tile, one P.V MMA per k-step and
+// four V stages; otherwise V is bf16 and P is split into bf16 hi + lo.
+template <bool kF16>
 __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
     const __grid_constant__ CUtensorMap tm_q, TcArgs a) {
@@ -161,6 +168,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   const int hk = blockIdx.y, b = blockIdx.z;
   const int64_t q0 = static_cast<int64_t>(blockIdx.x) * QB;
   const int G = a.G, K = a.K, C = a.C, Hq = a.Hkv * a.G;
+  constexpr int NV = kF16 ? 4 : 3;
+  unsigned char* const vbase = &sm.vt[0][0];           // V stage st at vbase + st * 16384
   // set-up tables live in the Q staging area, which is idle until the loader starts:
   // per-chunk owner masks, and the chunk lists (read once more by the loader)
   uint32_t* ownmask = reinterpret_cast<uint32_t*>(&sm.at[0][0]);
@@ -171,7 +180,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     tc::prefetch_tensormap(&tm_k);
     tc::prefetch_tensormap(&tm_q);
   }
-  if (warp >= 1 && warp <= NV && lane == 0) tc::prefetch_tensormap(&tm_v);
+  if (warp >= (kF16 ? 0 : 1) && warp < 4 && lane == 0) tc::prefetch_tensormap(&tm_v);
   for (int e = tid; e < C; e += NTHREADS) ownmask[e] = 0u;
   // Chunk lists and route weights.  Each query's list (K ints) and weights
   // (G x K bf16) are contiguous, so where K allows it they are read as 16-byte
@@ -419,7 +428,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     const bool s_role = warp == W_MMA;
     const uint64_t dq0 = tc::smem_desc_sw128(su32(sm.at[0]), 16, 2048);
     const uint64_t dk0 = tc::smem_desc_sw128(su32(sm.kt[0]), 16, 1024);
-    const uint64_t dv0 = tc::smem_desc_sw128(su32(sm.vt[0]), 8192, 1024);
+    const uint64_t dv0 = tc::smem_desc_sw128(su32(vbase), 8192, 1024);
     const uint64_t dh0 = tc::smem_desc_sw128(su32(sm.ph[0]), 16, 1024);
     const uint64_t dl0 = tc::smem_desc_sw128(su32(sm.pl[0]), 16, 1024);
     if (s_role) {
@@ -461,15 +470,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         // the owner count is read only now: the item's softmax has consumed its ring
         // entry (pready), so it is written; clamped so the MMA shape is always valid
         const int np = ((8 * min(max(sm.ring[it % RING].n, 1), OWN) + 15) / 16) * 16;
-        const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0);
+        // kind::f16 with fp16 A and B: the bf16 format bits cleared
+        const uint32_t id_o = tc::idesc_bf16_f32(128, np, 1, 0) & (kF16 ? ~((1u << 7) | (1u << 10)) : ~0u);
         const uint64_t dv = adv(dv0, sv * 16384), dh = adv(dh0, p2 * 8192), dl = adv(dl0, p2 * 8192);
         const uint32_t dP = tbase + kPCol + 64 * p2;
         if (elect_one()) {
           tc::mma_bf16<false>(dP, dv, dh, id_o);
 #pragma unroll
           for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dh, kk * 32), id_o);
+          if constexpr (!kF16) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
+            for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(dP, adv(dv, kk * 2048), adv(dl, kk * 32), id_o);
+          }
           tc::mma_commit(su32(&sm.bar_pvdone[p2]));
         }
         __syncwarp();
@@ -538,14 +550,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       }
       float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+      // P = route weight x softmax: as bf16 hi + lo, or as one fp16 tile (11
+      // significant bits; values small enough to be fp16 subnormals carry an
+      // absolute error below 2^-25, far under the bf16 output's resolution)
       const float f = sum > 0.f ? __fdividef(w, sum) : 0.f;
       uint32_t hi[16], lo[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
         const float p0 = __uint_as_float(x[2 * h]) * f;
         const float p1 = __uint_as_float(x[2 * h + 1]) * f;
-        hi[h] = pack_bf16x2(p0, p1);
-        lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+        if constexpr (kF16) {
+          hi[h] = pack_f16x2(p0, p1);
+        } else {
+          hi[h] = pack_bf16x2(p0, p1);
+          lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+        }
       }
       // the P buffer is free once the P.V of item it-2 has completed
       if (it >= 2 && !wait_bar_warp(sm, &sm.bar_pvdone[p2], ((it - 2) >> 1) & 1)) break;
@@ -555,8 +574,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         for (int p = 0; p < 4; ++p) {
           *reinterpret_cast<uint4*>(sm.ph[p2] + swz_off(row, 4 * hf + p)) =
               make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
-          *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(row, 4 * hf + p)) =
-              make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
+          if constexpr (!kF16)
+            *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(row, 4 * hf + p)) =
+                make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
         }
       }
       tc::fence_proxy_async();
@@ -567,20 +587,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
   } else {
     // ============================ accumulate (warps 0-3) =====================
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    // V tile of item `v` into stage v % NV (warp v % NV + 1); the ring entry names the chunk
+    // V tile of item `v` into stage v % NV (warp v % NV, +1 with three stages); the ring entry names the chunk
     auto load_v = [&](int v) -> bool {
       const int r = v % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (v / RING) & 1)) return false;
       if (elect_one()) {
         const uint32_t bar = su32(&sm.bar_vfull[v % NV]);
         tc::mbar_arrive_expect_tx(bar, 16384u);
-        tc::tma_load_4d(su32(sm.vt[v % NV]), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(sm.ring[r].c) * S),
+        tc::tma_load_4d(su32(vbase + (v % NV) * 16384), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(sm.ring[r].c) * S),
                         0, hk, bar);
       }
       __syncwarp();
       return true;
     };
-    const int vst = warp - 1;                // this warp's V stage (warps 1-3)
+    const int vst = kF16 ? warp : warp - 1;  // this warp's V stage (warps 0-3, or 1-3 with three stages)
     int vlast = -1;                          // last item whose V tile this warp requested
     bool ok = true;
     if (vst >= 0 && vst < n_items) {
@@ -729,7 +749,7 @@ std::once_flag g_encode_once;
 
 // bf16 tensor map with 128-byte swizzle over `rank` dims (innermost first).
 bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
-              const cuuint32_t* box) {
+              const cuuint32_t* box, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -739,21 +759,20 @@ bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
   });
   if (g_encode == nullptr) return false;
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
+  return g_encode(m, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
                   strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
 
-extern "C" int mrsa_selected_attention(const void* q, const void* k, const void* v,
-                                       const uint8_t* key_valid, const void* weights,
-                                       const int32_t* indices, const void* local_out,
-                                       const void* local_w, void* out, float sm_scale,
-                                       int mask_last_token, int64_t batch, int64_t q_len,
-                                       int64_t kv_len, int64_t kv_heads, int64_t groups,
-                                       int64_t head_dim, int64_t topk, int64_t chunk,
-                                       mrsa_stream_t stream) {
+namespace {
+
+template <bool kF16>
+int selected_launch(const void* q, const void* k, const void* v, const uint8_t* key_valid, const void* weights,
+                    const int32_t* indices, const void* local_out, const void* local_w, void* out, float sm_scale,
+                    int mask_last_token, int64_t batch, int64_t q_len, int64_t kv_len, int64_t kv_heads,
+                    int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk, mrsa_stream_t stream) {
   if (!q || !k || !v || !weights || !indices || !out) return MRSA_ERR_NULL;
   if ((local_out == nullptr) != (local_w == nullptr)) return MRSA_ERR_NULL;
   if (head_dim != D || chunk != S || groups < 1 || groups > GMAX || kv_heads < 1 || batch < 1 ||
@@ -774,7 +793,9 @@ extern "C" int mrsa_selected_attention(const void* q, const void* k, const void*
   const cuuint64_t q_dims[3] = {64, static_cast<cuuint64_t>(batch * q_len * kv_heads * groups), 2};
   const cuuint64_t q_str[2] = {256, 128};
   const cuuint32_t q_box[3] = {64, 8, 2};
-  if (!make_map(&tm_k, k, 4, kv_dims, kv_str, kv_box) || !make_map(&tm_v, v, 4, kv_dims, kv_str, kv_box) ||
+  if (!make_map(&tm_k, k, 4, kv_dims, kv_str, kv_box) ||
+      !make_map(&tm_v, v, 4, kv_dims, kv_str, kv_box,
+                kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) ||
       !make_map(&tm_q, q, 3, q_dims, q_str, q_box))
     return MRSA_ERR_LAUNCH;
   TcArgs a;
@@ -793,16 +814,44 @@ extern "C" int mrsa_selected_attention(const void* q, const void* k, const void*
   a.K = static_cast<int>(topk);
   a.C = static_cast<int>(kv_len / S);
   const size_t smem = sizeof(TcSmem) + 1024;
-  if (cudaFuncSetAttribute(selected_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(selected_tc_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return MRSA_ERR_LAUNCH;
   const int64_t blocks = (q_len + QB - 1) / QB;
   if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(kv_heads),
             static_cast<unsigned>(batch));
-  selected_tc_kernel<<<grid, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_k, tm_v, tm_q, a);
+  selected_tc_kernel<kF16><<<grid, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_k, tm_v, tm_q, a);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
+}
+
+}  // namespace
+
+extern "C" int mrsa_selected_attention(const void* q, const void* k, const void* v,
+                                       const uint8_t* key_valid, const void* weights,
+                                       const int32_t* indices, const void* local_out,
+                                       const void* local_w, void* out, float sm_scale,
+                                       int mask_last_token, int64_t batch, int64_t q_len,
+                                       int64_t kv_len, int64_t kv_heads, int64_t groups,
+                                       int64_t head_dim, int64_t topk, int64_t chunk,
+                                       mrsa_stream_t stream) {
+  return selected_launch<false>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+                                mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
+                                stream);
+}
+
+extern "C" int mrsa_selected_attention_f16v(const void* q, const void* k, const void* v_f16,
+                                            const uint8_t* key_valid, const void* weights,
+                                            const int32_t* indices, const void* local_out,
+                                            const void* local_w, void* out, float sm_scale,
+                                            int mask_last_token, int64_t batch, int64_t q_len,
+                                            int64_t kv_len, int64_t kv_heads, int64_t groups,
+                                            int64_t head_dim, int64_t topk, int64_t chunk,
+                                            mrsa_stream_t stream) {
+  return selected_launch<true>(q, k, v_f16, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+                               mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
+                               stream);
 }
 
 extern "C" int mrsa_device_error_flags(int clear) {
@@ -812,7 +861,8 @@ extern "C" int mrsa_device_error_flags(int clear) {
     const int z = 0;
     if (cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int)) != cudaSuccess) return MRSA_ERR_LAUNCH;
   }
-  const int r = mrsa::route_error_flags(clear), l = mrsa::local_error_flags(clear);
-  if (r < 0 || l < 0) return MRSA_ERR_LAUNCH;
-  return (v ? 1 : 0) | (r ? 2 : 0) | (l ? 4 : 0);
+  const int r = mrsa::route_error_flags(clear), l = mrsa::local_error_flags(clear),
+            cv = mrsa::convert_error_flags(clear);
+  if (r < 0 || l < 0 || cv < 0) return MRSA_ERR_LAUNCH;
+  return (v ? 1 : 0) | (r ? 2 : 0) | (l ? 4 : 0) | (cv ? 8 : 0);
 }

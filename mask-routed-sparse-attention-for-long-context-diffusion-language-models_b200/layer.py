@@ -21,7 +21,7 @@ from .chunk_pool import chunk_attn_pool_gqa  # noqa: F401  (re-export for caller
 from .local_attention import window_attention
 from .rope_fp32 import yarn_inv_freq, yarn_rope_qk
 from .routing import route_topk_fused
-from .selected_attention import selected_attention
+from .selected_attention import selected_attention, to_f16
 
 
 @dataclass
@@ -200,12 +200,13 @@ class RouteLayer:
                                                gate_scale=self.gate_scale,
                                                gate_offset=self.gate_offset)
         mark(5)
-        selected_attention(q, k, v, rw, idx, key_valid, chunk=c.chunk, local_out=local_out,
+        v16 = to_f16(v)                      # as the fused layer: fp16 V, one fp16 P tile
+        selected_attention(q, k, v16, rw, idx, key_valid, chunk=c.chunk, local_out=local_out,
                            local_weight=lw, out=out)
         mark(6)
         if events is not None:
             return None
-        remote = selected_attention(q, k, v, rw, idx, key_valid, chunk=c.chunk)
+        remote = selected_attention(q, k, v16, rw, idx, key_valid, chunk=c.chunk)
         return {"q": q, "k": k, "route_q": route_q, "local_out": local_out, "local_lse": local_lse,
                 "lmk": lmk, "entropy": ent, "prior_bias": prior, "chunk_ok": chunk_ok,
                 "indices": idx, "scores": scores, "remote_weights": rw, "local_weight": lw,

@@ -21,7 +21,11 @@ def selected_attention(q, k, v, weights, indices, key_valid=None, *, chunk: int 
                        local_out=None, local_weight=None, mask_last_token=True, sm_scale=None,
                        out=None):
     """``out = sum_k w_k softmax_chunk(q.K_k/sqrt(D)) V_k`` (bf16), fused with
-    ``+ local_weight * local_out`` when those are given."""
+    ``+ local_weight * local_out`` when those are given.
+
+    ``v`` in bf16 runs the exact-P kernel (P as bf16 hi + lo); ``v`` in fp16
+    (see :func:`to_f16`) runs the fp16-P kernel, which does half the P.V work
+    and keeps P to 11 significant bits."""
     b, lq, hq, d = q.shape
     lk, hkv = k.shape[1], k.shape[2]
     topk = indices.shape[-1]
@@ -35,10 +39,25 @@ def selected_attention(q, k, v, weights, indices, key_valid=None, *, chunk: int 
     if out is None:
         out = torch.empty_like(q)
     scale = float(d) ** -0.5 if sm_scale is None else float(sm_scale)
-    _lib.call("mrsa_selected_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
+    if v.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"v must be bf16 or fp16, got {v.dtype}")
+    entry = "mrsa_selected_attention_f16v" if v.dtype == torch.float16 else "mrsa_selected_attention"
+    _lib.call(entry, _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
               _lib.ptr(w), _lib.ptr(idx), _lib.ptr(lo), _lib.ptr(lw), _lib.ptr(out), scale,
               int(bool(mask_last_token)), b, lq, lk, hkv, hq // hkv, d, topk, int(chunk),
               _lib.stream_of(q))
+    return out
+
+
+def to_f16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 -> fp16 on the GPU (round to nearest; values beyond +-65504,
+    infinities included, saturate and set bit 3 of the device error flags)."""
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"expected bf16, got {x.dtype}")
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    _lib.call("mrsa_convert_bf16_to_f16", _lib.ptr(x), _lib.ptr(out), x.numel(), _lib.stream_of(x))
     return out
 
 

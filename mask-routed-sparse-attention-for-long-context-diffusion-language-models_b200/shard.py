@@ -31,7 +31,7 @@ from .layer import RouteLayer
 from .local_attention import window_attention
 from .rope_fp32 import yarn_rope_qk
 from .routing import route_topk_fused
-from .selected_attention import selected_attention
+from .selected_attention import selected_attention, to_f16
 
 
 def gather_rows(out: torch.Tensor, inp: torch.Tensor, group=None, async_op: bool = False):
@@ -92,7 +92,8 @@ class KernelOps:
         return idx, rw, lw
 
     def selected(self, q, k_all, v_all, rw, idx, valid_all, local_out, local_w, out):
-        return selected_attention(q, k_all, v_all, rw, idx, valid_all, chunk=self.cfg.chunk,
+        # fp16 V for the selected kernel, as the single-device layer does
+        return selected_attention(q, k_all, to_f16(v_all), rw, idx, valid_all, chunk=self.cfg.chunk,
                                   local_out=local_out, local_weight=local_w, out=out)
 
 

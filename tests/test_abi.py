@@ -83,16 +83,18 @@ def test_bad_arguments_return_codes_without_device(mrsa):
     assert lib.mrsa_route_layer_forward(C.byref(a), None, 0, None) == -1
 
 
-def test_route_layer_workspace_size_formula(mrsa):
+@pytest.mark.parametrize("l", [16384, 512])
+def test_route_layer_workspace_size_formula(mrsa, l):
     lib = mrsa._lib.load()
     a = mrsa._lib.RouteLayerArgs()
-    a.batch, a.seq_len, a.q_heads, a.kv_heads, a.head_dim = 1, 16384, 28, 4, 128
+    a.batch, a.seq_len, a.q_heads, a.kv_heads, a.head_dim = 1, l, 28, 4, 128
     a.hidden_size, a.rank, a.topk, a.local_window = 3584, 64, 32, 256
     n = lib.mrsa_route_layer_workspace_size(C.byref(a))
-    l, hq, hkv, d, k, c = 16384, 28, 4, 128, 32, 256
+    hq, hkv, d, k, c = 28, 4, 128, 32, l // 64
+    # the routing keys + raw scores piece is reused for fp16 V after routing
+    route_or_v16 = max(l * hkv * c * 4 + l * hq * c * 2, l * hkv * d * 2)
     expect = (3 * l * hq * d * 2 + l * hkv * d * 2 + c * hq * d * 2 + 2 * c * hq * 4 + c
-              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2 + l * hkv * c * 4
-              + l * hq * c * 2)
+              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2 + route_or_v16)
     assert expect <= n <= expect + 14 * 256
 
 

@@ -218,8 +218,9 @@ def test_selected_with_invalid_keys_matches_oracle(mrsa, dev):
     assert torch.equal(out[:, 0].cpu(), torch.zeros_like(out[:, 0].cpu()))
 
 
+@pytest.mark.parametrize("vdt", ["bf16", "f16"])
 @pytest.mark.parametrize("g,topk,lq", [(7, 32, 1000), (8, 13, 777), (3, 32, 96)])
-def test_selected_random_routing_duplicates_ragged(mrsa, dev, g, topk, lq):
+def test_selected_random_routing_duplicates_ragged(mrsa, dev, g, topk, lq, vdt):
     """random chunk lists with empty (-1) and repeated slots, a query length that
     is not a multiple of the 32-query block, batch 2, several group sizes; the
     oracle (``hils_torch_ref`` semantics) counts a repeated chunk once per slot"""
@@ -235,13 +236,15 @@ def test_selected_random_routing_duplicates_ragged(mrsa, dev, g, topk, lq):
     idx[:, ::7, :, -1] = idx[:, ::7, :, 0]
     w = torch.rand(b, lq, hkv * g, topk, generator=gen).bfloat16()
     valid = torch.rand(b, lk, generator=gen) > 0.05
-    out = mrsa.selected_attention(q.to(dev), k.to(dev), v.to(dev), w.to(dev), idx.to(dev), valid.to(dev))
+    vd = v.to(dev) if vdt == "bf16" else mrsa.to_f16(v.to(dev))   # fp16 V: the one-tile fp16 P kernel
+    out = mrsa.selected_attention(q.to(dev), k.to(dev), vd, w.to(dev), idx.to(dev), valid.to(dev))
     rows = torch.unique(torch.cat([torch.arange(0, lq, 37), torch.tensor([lq - 1, 0, 5, 35])]))
     ref = orc.selected_attention(q[:, rows], k, v, w[:, rows], idx[:, rows], valid, 64, block=16)
     close_bf16(out[:, rows.to(dev)], ref)
 
 
-def test_selected_all_queries_same_chunks(mrsa, dev):
+@pytest.mark.parametrize("vdt", ["bf16", "f16"])
+def test_selected_all_queries_same_chunks(mrsa, dev, vdt):
     """every query of a block selects the same chunks: items of 8 owners, 4 per chunk"""
     gen = torch.Generator().manual_seed(5)
     lq, lk, hkv, g, d, topk = 256, 4096, 4, 7, 128, 32
@@ -250,10 +253,32 @@ def test_selected_all_queries_same_chunks(mrsa, dev):
     v = torch.randn(1, lk, hkv, d, generator=gen).bfloat16()
     idx = (torch.arange(topk, dtype=torch.int32) * 2).expand(1, lq, hkv, -1).contiguous()
     w = torch.randn(1, lq, hkv * g, topk, generator=gen).softmax(-1).bfloat16()
-    out = mrsa.selected_attention(q.to(dev), k.to(dev), v.to(dev), w.to(dev), idx.to(dev))
+    vd = v.to(dev) if vdt == "bf16" else mrsa.to_f16(v.to(dev))
+    local = torch.randn(1, lq, hkv * g, d, generator=gen).bfloat16()
+    lw = torch.rand(1, lq, hkv * g, generator=gen).bfloat16()
+    out = mrsa.selected_attention(q.to(dev), k.to(dev), vd, w.to(dev), idx.to(dev),
+                                  local_out=local.to(dev), local_weight=lw.to(dev))
     rows = torch.tensor([0, 31, 32, 100, 255])
     ref = orc.selected_attention(q[:, rows], k, v, w[:, rows], idx[:, rows], None, 64, block=8)
+    ref = orc.fuse_outputs(ref, local[:, rows], lw[:, rows])
     close_bf16(out[:, rows.to(dev)], ref)
+
+
+def test_convert_bf16_to_f16_exact_and_saturating(mrsa, dev):
+    """in-range values convert with round-to-nearest; |x| > 65504 (and
+    infinities) saturate to +-65504 and raise bit 3 of the device flags"""
+    lib = mrsa._lib.load()
+    gen = torch.Generator().manual_seed(16)
+    x = (torch.randn(4096, generator=gen) * 300).bfloat16()
+    x[:8] = torch.tensor([70000., -70000., 65504., -65504., 1e-6, 0., float("inf"), 3e-8]).bfloat16()
+    lib.mrsa_device_error_flags(1)
+    y = mrsa.to_f16(x.to(dev)).cpu()
+    want = x.float().clamp(-65504., 65504.).half()
+    assert torch.equal(y, want)
+    assert lib.mrsa_device_error_flags(1) & 8
+    y2 = mrsa.to_f16(x[8:].to(dev)).cpu()                 # nothing out of range
+    assert torch.equal(y2, x[8:].float().half())
+    assert lib.mrsa_device_error_flags(1) & 8 == 0
 
 
 @pytest.mark.parametrize("window,skip", [(256, True), (1280, False), (40, True)])
