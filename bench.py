@@ -36,6 +36,9 @@ sys.path.insert(0, ROOT)
 L_PER_GPU = 16384
 HQ, HKV, D, HIDDEN, RANK, TOPK, CHUNK, WLOC = 28, 4, 128, 3584, 64, 32, 64, 256
 METRIC = "MRSA route-layer fwd tokens/s (bf16)"
+# this repository's kernels per forward: RoPE, V to fp16, local window, Q-Cal,
+# landmark pool, routing keys, top-K selection, selected attention
+LAUNCHES_PER_STEP = 8
 
 
 def algorithmic(l_local: int, l_total: int):
@@ -378,7 +381,7 @@ def main():
                            "global_batch": 1, "seq_len": l_total, "parallelism": f"seq{world}",
                            "l2": "inputs larger than L2 (267 MB per 16k tokens)"},
                 "roofline": roof, "stage_ms": stages,
-                "gpu_launches": args.steps * 6,
+                "gpu_launches": args.steps * LAUNCHES_PER_STEP,
                 "clocks": clocks,
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
                         "d2h_bytes_per_step": d2h * world, "steps": e2,

@@ -142,6 +142,16 @@ int mrsa_local_attention(const void* q, const void* k, const void* v, const uint
                          int64_t q_offset, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                          mrsa_stream_t stream);
 
+/* mrsa_local_attention with V given in fp16 ([B,Lk,Hkv,D] fp16): P then
+ * travels as one fp16 tile instead of bf16 hi + lo (half the P.V work).  No
+ * counterpart in the reference: the fused layer uses it after
+ * mrsa_convert_bf16_to_f16 on V. */
+int mrsa_local_attention_f16v(const void* q, const void* k, const void* v_f16, const uint8_t* key_valid,
+                              void* out, float* lse, int64_t window, int skip_inert, int64_t chunk,
+                              float sm_scale, int64_t batch, int64_t q_len, int64_t kv_len,
+                              int64_t q_offset, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                              mrsa_stream_t stream);
+
 /* Weighted per-chunk-softmax attention over the selected chunks, optionally
  * fused with the local branch: out = bf16(bf16(remote) + local_w*local) when
  * local_out and local_w are given, else bf16(remote).

@@ -11,7 +11,7 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct LayerPlan {
-  size_t q, k, route_q, lmk, entropy, prior, chunk_ok, local_out, local_lse, indices, scores,
+  size_t q, k, v16, route_q, lmk, entropy, prior, chunk_ok, local_out, local_lse, indices, scores,
       remote_w, local_w, route_keys, total;
 };
 
@@ -27,6 +27,7 @@ LayerPlan plan(const mrsa_route_layer_args* a) {
   };
   p.q = take(B * L * Hq * D * 2);
   p.k = take(B * L * Hkv * D * 2);
+  p.v16 = take(B * L * Hkv * D * 2);        // V in fp16 for the local and selected kernels
   p.route_q = take(B * L * Hq * D * 2);
   p.lmk = take(B * C * Hq * D * 2);
   p.entropy = take(B * C * Hq * 4);
@@ -38,11 +39,7 @@ LayerPlan plan(const mrsa_route_layer_args* a) {
   p.scores = take(B * L * Hq * K * 2);
   p.remote_w = take(B * L * Hq * K * 2);
   p.local_w = take(B * L * Hq * 2);
-  // the routing keys and raw scores are dead once routing is done; fp16 V
-  // (for the selected-attention kernel, which runs after it) reuses the piece
-  const size_t route_bytes = mrsa_route_topk_workspace_size(B, L, C, Hkv, Hq / Hkv, MRSA_BF16);
-  const size_t v16_bytes = B * L * Hkv * D * 2;
-  p.route_keys = take(route_bytes > v16_bytes ? route_bytes : v16_bytes);
+  p.route_keys = take(mrsa_route_topk_workspace_size(B, L, C, Hkv, Hq / Hkv, MRSA_BF16));
   p.total = off;
   return p;
 }
@@ -74,6 +71,7 @@ extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* wo
   char* ws = static_cast<char*>(workspace);
   void* q = ws + p.q;
   void* k = ws + p.k;
+  void* v16 = ws + p.v16;
   void* route_q = ws + p.route_q;
   void* lmk = ws + p.lmk;
   float* entropy = reinterpret_cast<float*>(ws + p.entropy);
@@ -94,7 +92,11 @@ extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* wo
   rc = mrsa_rope(a->q_pre, q, Hq, a->k_pre, k, Hkv, a->position_ids, a->inv_freq,
                  a->attention_factor, nullptr, nullptr, MRSA_F32, B, L, D, stream);
   if (rc) return rc;
-  rc = mrsa_local_attention(q, k, a->v, a->key_valid, local_out, local_lse,
+  // V in fp16: both attention kernels then carry P as one fp16 tile instead
+  // of bf16 hi + lo
+  rc = mrsa_convert_bf16_to_f16(a->v, v16, B * L * Hkv * D, stream);
+  if (rc) return rc;
+  rc = mrsa_local_attention_f16v(q, k, v16, a->key_valid, local_out, local_lse,
                             a->local_window + mrsa::kChunk - 1, 1, mrsa::kChunk, sm_scale, B, L, L,
                             0, Hq, Hkv, D, stream);
   if (rc) return rc;
@@ -112,11 +114,6 @@ extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* wo
                        a->topk, route_keys, mrsa_route_topk_workspace_size(B, L, C, Hkv, G, MRSA_BF16),
                        stream);
   if (rc) return rc;
-  // V in fp16 (in the routing workspace, free by now): P.V then takes one fp16
-  // P tile instead of bf16 hi + lo
-  void* v16 = route_keys;
-  rc = mrsa_convert_bf16_to_f16(a->v, v16, B * L * Hkv * D, stream);
-  if (rc != MRSA_OK) return rc;
   return mrsa_selected_attention_f16v(q, k, v16, a->key_valid, remote_w, indices, local_out, local_w,
                                  a->out, sm_scale, 1, B, L, L, Hkv, G, D, a->topk, mrsa::kChunk,
                                  stream);

@@ -64,6 +64,9 @@ __device__ int g_local_error;
 
 __device__ __forceinline__ int swz_off(int row, int piece) { return row * 128 + ((piece ^ (row & 7)) << 4); }
 
+// kF16: V arrives in fp16 and P (values up to 2^8 under the lazy rescale) is
+// one fp16 tile, one P.V MMA per k-step; otherwise P is bf16 hi + lo.
+template <bool kF16>
 __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, LocalArgs a) {
@@ -148,7 +151,8 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   } else if (warp == L_W_MMA) {
     // ============================ MMA issue (converged warp) ==================
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, LN, 0, 0);
-    constexpr uint32_t id_o = tc::idesc_bf16_f32(128, D, 0, 1);
+    // kind::f16 with fp16 A and B: the bf16 format bits cleared
+    constexpr uint32_t id_o = tc::idesc_bf16_f32(128, D, 0, 1) & (kF16 ? ~((1u << 7) | (1u << 10)) : ~0u);
     const uint64_t dq = tc::smem_desc_sw128(tc::smem_addr(&sm.q[0][0]), 16, 2048);
     const uint64_t dk0 = tc::smem_desc_sw128(tc::smem_addr(sm.k[0]), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(tc::smem_addr(sm.v[0]), 8192, 1024);
@@ -185,8 +189,11 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         else tc::mma_bf16<true>(tbase + kOCol, dh, dv, id_o);
 #pragma unroll
         for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+        if constexpr (!kF16) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+          for (int kk = 0; kk < 4; ++kk)
+            tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+        }
         tc::mma_commit(tc::smem_addr(&sm.pvdone[p2]));
         tc::mma_commit(tc::smem_addr(&sm.kvfree[st]));
       }
@@ -283,15 +290,20 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
 #pragma unroll
       for (int h = 0; h < 32; ++h) {
         const float p0 = __uint_as_float(x[2 * h]), p1 = __uint_as_float(x[2 * h + 1]);
-        hi[h] = pack_bf16x2(p0, p1);
-        lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+        if constexpr (kF16) {
+          hi[h] = pack_f16x2(p0, p1);
+        } else {
+          hi[h] = pack_bf16x2(p0, p1);
+          lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+        }
       }
       // P buffer t&1 was last read by the P.V of tile t-2
       if (t >= 2 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[p2]), ((t - 2) >> 1) & 1, abort_flag))) break;
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
         *reinterpret_cast<uint4*>(sm.ph[p2] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
-        *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
+        if constexpr (!kF16)
+          *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
       }
       if (__any_sync(0xffffffffu, rescale)) {
         // O must hold every earlier tile before it is scaled: wait for the P.V of tile t-1
@@ -362,7 +374,7 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
 bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
-              const cuuint32_t* box) {
+              const cuuint32_t* box, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -372,19 +384,16 @@ bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
   });
   if (g_encode == nullptr) return false;
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
+  return g_encode(m, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), dims,
                   strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
-
-extern "C" int mrsa_local_attention(const void* q, const void* k, const void* v,
-                                    const uint8_t* key_valid, void* out, float* lse,
-                                    int64_t window, int skip_inert, int64_t chunk, float sm_scale,
-                                    int64_t batch, int64_t q_len, int64_t kv_len, int64_t q_offset,
-                                    int64_t q_heads, int64_t kv_heads, int64_t head_dim,
-                                    mrsa_stream_t stream) {
+template <bool kF16>
+int local_launch(const void* q, const void* k, const void* v, const uint8_t* key_valid, void* out, float* lse,
+                 int64_t window, int skip_inert, int64_t chunk, float sm_scale, int64_t batch, int64_t q_len,
+                 int64_t kv_len, int64_t q_offset, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                 mrsa_stream_t stream) {
   if (!q || !k || !v || !out) return MRSA_ERR_NULL;
   if (head_dim != D || kv_heads < 1 || q_heads < kv_heads || q_heads % kv_heads || q_heads / kv_heads > 8 ||
       batch < 1 || q_len < 0 || kv_len < 1 || q_offset < 0 || q_heads > 65535 || batch > 65535 ||
@@ -403,7 +412,8 @@ extern "C" int mrsa_local_attention(const void* q, const void* k, const void* v,
   const cuuint64_t kv_str[3] = {static_cast<cuuint64_t>(kv_heads * D * 2), 128, 256};
   const cuuint32_t kv_box[4] = {64, LN, 2, 1};
   if (!make_map(&tm_q, q, 4, q_dims, q_str, q_box) || !make_map(&tm_k, k, 4, kv_dims, kv_str, kv_box) ||
-      !make_map(&tm_v, v, 4, kv_dims, kv_str, kv_box))
+      !make_map(&tm_v, v, 4, kv_dims, kv_str, kv_box,
+                kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16))
     return MRSA_ERR_LAUNCH;
   LocalArgs a;
   a.key_valid = key_valid;
@@ -420,15 +430,37 @@ extern "C" int mrsa_local_attention(const void* q, const void* k, const void* v,
   a.G = static_cast<int>(q_heads / kv_heads);
   a.sm_scale = sm_scale;
   const size_t smem = sizeof(LocalSmem) + 1024;
-  if (cudaFuncSetAttribute(local_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(local_tc_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return MRSA_ERR_LAUNCH;
   const int64_t blocks = (q_len + LQ - 1) / LQ;
   if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
-  local_tc_kernel<<<grid, L_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_q, tm_k, tm_v, a);
+  local_tc_kernel<kF16><<<grid, L_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_q, tm_k, tm_v, a);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
+}
+
+}  // namespace
+
+extern "C" int mrsa_local_attention(const void* q, const void* k, const void* v,
+                                    const uint8_t* key_valid, void* out, float* lse,
+                                    int64_t window, int skip_inert, int64_t chunk, float sm_scale,
+                                    int64_t batch, int64_t q_len, int64_t kv_len, int64_t q_offset,
+                                    int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                    mrsa_stream_t stream) {
+  return local_launch<false>(q, k, v, key_valid, out, lse, window, skip_inert, chunk, sm_scale, batch, q_len,
+                             kv_len, q_offset, q_heads, kv_heads, head_dim, stream);
+}
+
+extern "C" int mrsa_local_attention_f16v(const void* q, const void* k, const void* v_f16,
+                                         const uint8_t* key_valid, void* out, float* lse,
+                                         int64_t window, int skip_inert, int64_t chunk, float sm_scale,
+                                         int64_t batch, int64_t q_len, int64_t kv_len, int64_t q_offset,
+                                         int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                         mrsa_stream_t stream) {
+  return local_launch<true>(q, k, v_f16, key_valid, out, lse, window, skip_inert, chunk, sm_scale, batch, q_len,
+                            kv_len, q_offset, q_heads, kv_heads, head_dim, stream);
 }
 
 namespace mrsa {

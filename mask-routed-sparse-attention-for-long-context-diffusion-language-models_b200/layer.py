@@ -180,7 +180,8 @@ class RouteLayer:
         mark(0)
         q, k = yarn_rope_qk(q_pre, k_pre, position_ids, self.inv_freq, self.attention_factor)
         mark(1)
-        window_attention(q, k, v, key_valid, c.local_window + c.chunk - 1, skip_inert=True,
+        v16 = to_f16(v)                      # as the fused layer: fp16 V, one fp16 P tile
+        window_attention(q, k, v16, key_valid, c.local_window + c.chunk - 1, skip_inert=True,
                          chunk=c.chunk, out=local_out, lse=local_lse)
         mark(2)
         _lib.call("mrsa_qcal_route_query", _lib.ptr(hidden), _lib.ptr(q), _lib.ptr(self.w_in),
@@ -200,7 +201,6 @@ class RouteLayer:
                                                gate_scale=self.gate_scale,
                                                gate_offset=self.gate_offset)
         mark(5)
-        v16 = to_f16(v)                      # as the fused layer: fp16 V, one fp16 P tile
         selected_attention(q, k, v16, rw, idx, key_valid, chunk=c.chunk, local_out=local_out,
                            local_weight=lw, out=out)
         mark(6)

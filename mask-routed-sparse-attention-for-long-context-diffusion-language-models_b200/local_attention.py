@@ -34,7 +34,8 @@ def _validate_layout(q, k, v, key_valid) -> None:
 def window_attention(q, k, v, key_valid, window: int, *, skip_inert: bool, chunk: int = 64,
                      q_offset: int = 0, out=None, lse=None, need_lse: bool = True):
     """Banded attention of query rows at global positions ``q_offset..`` over
-    the full key range of ``k``/``v``; ``window`` is the effective flash window."""
+    the full key range of ``k``/``v``; ``window`` is the effective flash window.
+    ``v`` in fp16 runs the one-tile fp16 P kernel, bf16 the hi + lo one."""
     b, lq, hq, d = q.shape
     lk, hkv = k.shape[1], k.shape[2]
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
@@ -43,7 +44,10 @@ def window_attention(q, k, v, key_valid, window: int, *, skip_inert: bool, chunk
         out = torch.empty_like(q)
     if lse is None and need_lse:
         lse = torch.empty(b, lq, hq, device=q.device, dtype=torch.float32)
-    _lib.call("mrsa_local_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
+    if v.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"v must be bf16 or fp16, got {v.dtype}")
+    entry = "mrsa_local_attention_f16v" if v.dtype == torch.float16 else "mrsa_local_attention"
+    _lib.call(entry, _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
               _lib.ptr(out), _lib.ptr(lse), int(window), int(bool(skip_inert)), int(chunk),
               float(d) ** -0.5, b, lq, lk, int(q_offset), hq, hkv, d, _lib.stream_of(q))
     return out, lse

@@ -6,7 +6,8 @@ Rank ``r`` of ``N`` owns the contiguous tokens ``[r*L/N, (r+1)*L/N)`` (whole
 exchange step per layer suffices:
 
 1. RoPE on the local q/k (cos/sin from global position ids);
-2. all-gather K, V and key validity (NCCL over NVLink) -- issued
+2. all-gather K, V (in fp16, the form both attention kernels take) and key
+   validity (NCCL over NVLink) -- issued
    asynchronously, it runs while this rank computes its Q-Cal routing
    queries and landmark pool;
 3. all-gather the landmarks, prior and chunk validity (small);
@@ -47,11 +48,15 @@ def gather_rows(out: torch.Tensor, inp: torch.Tensor, group=None, async_op: bool
 class KernelOps:
     """The compute stages of a sharded route layer on the B200 kernels."""
 
-    launches_per_step = 6   # rope, qcal, pool, local, route, selected (own kernels)
+    launches_per_step = 8   # rope, V to fp16, qcal, pool, local, route keys + selection, selected
 
     def __init__(self, layer: RouteLayer):
         self.layer = layer
         self.cfg = layer.cfg
+
+    def attention_v(self, v):
+        """V as the attention kernels take it: fp16 (P then travels as one fp16 tile)."""
+        return to_f16(v)
 
     def rope(self, q_pre, k_pre, position_ids, k_out):
         lay = self.layer
@@ -92,8 +97,7 @@ class KernelOps:
         return idx, rw, lw
 
     def selected(self, q, k_all, v_all, rw, idx, valid_all, local_out, local_w, out):
-        # fp16 V for the selected kernel, as the single-device layer does
-        return selected_attention(q, k_all, to_f16(v_all), rw, idx, valid_all, chunk=self.cfg.chunk,
+        return selected_attention(q, k_all, v_all, rw, idx, valid_all, chunk=self.cfg.chunk,
                                   local_out=local_out, local_weight=local_w, out=out)
 
 
@@ -141,12 +145,13 @@ class ShardedRouteLayer:
 
         # 1. RoPE straight into this rank's slot of the gathered K buffer
         k_full = self._buf("k", (n, ls, hkv, d), torch.bfloat16, dev)
-        v_full = self._buf("v", (n, ls, hkv, d), torch.bfloat16, dev)
+        v_att = ops.attention_v(v)           # gathered in the form the attention stages take
+        v_full = self._buf("v", (n, ls, hkv, d), v_att.dtype, dev)
         kv_full = self._buf("kv", (n, ls), torch.bool, dev)
         q = ops.rope(q_pre, k_pre, position_ids, k_full[r].view(1, ls, hkv, d))
         # 2. K/V/validity all-gather, overlapped with Q-Cal + pool below
         h_k = gather_rows(k_full, k_full[r], self.group, async_op=True)
-        h_v = gather_rows(v_full, v, self.group, async_op=True)
+        h_v = gather_rows(v_full, v_att, self.group, async_op=True)
         h_m = gather_rows(kv_full, kv_local, self.group, async_op=True)
 
         route_q = ops.qcal(hidden, q, position_ids, self._buf("route_q", (1, ls, hq, d), torch.bfloat16, dev))

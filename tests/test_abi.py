@@ -91,11 +91,12 @@ def test_route_layer_workspace_size_formula(mrsa, l):
     a.hidden_size, a.rank, a.topk, a.local_window = 3584, 64, 32, 256
     n = lib.mrsa_route_layer_workspace_size(C.byref(a))
     hq, hkv, d, k, c = 28, 4, 128, 32, l // 64
-    # the routing keys + raw scores piece is reused for fp16 V after routing
-    route_or_v16 = max(l * hkv * c * 4 + l * hq * c * 2, l * hkv * d * 2)
-    expect = (3 * l * hq * d * 2 + l * hkv * d * 2 + c * hq * d * 2 + 2 * c * hq * 4 + c
-              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2 + route_or_v16)
-    assert expect <= n <= expect + 14 * 256
+    # q, route_q, local_out; k and its fp16 V; landmarks, prior, entropy, validity;
+    # local LSE, indices, scores + remote weights, local weight; routing keys + raw scores
+    expect = (3 * l * hq * d * 2 + 2 * l * hkv * d * 2 + c * hq * d * 2 + 2 * c * hq * 4 + c
+              + l * hq * 4 + l * hkv * k * 4 + 2 * l * hq * k * 2 + l * hq * 2
+              + l * hkv * c * 4 + l * hq * c * 2)
+    assert expect <= n <= expect + 15 * 256
 
 
 def test_yarn_host_table_matches_transformers(mrsa):

@@ -283,6 +283,16 @@ def test_convert_bf16_to_f16_exact_and_saturating(mrsa, dev):
 
 @pytest.mark.parametrize("window,skip", [(256, True), (1280, False), (40, True)])
 def test_local_attention_matches_oracle(mrsa, dev, window, skip):
+    _local_case(mrsa, dev, window, skip, f16v=False)
+
+
+@pytest.mark.parametrize("window,skip", [(256, True), (1280, False)])
+def test_local_attention_f16v_matches_oracle(mrsa, dev, window, skip):
+    """V in fp16: P as one fp16 tile (11 significant bits) instead of bf16 hi + lo"""
+    _local_case(mrsa, dev, window, skip, f16v=True)
+
+
+def _local_case(mrsa, dev, window, skip, f16v):
     gen = torch.Generator().manual_seed(window)
     b, l, hq, hkv, d = 2, 2048 + 64, 28, 4, 128
     q = (torch.randn(b, l, hq, d, generator=gen)).bfloat16()
@@ -290,8 +300,13 @@ def test_local_attention_matches_oracle(mrsa, dev, window, skip):
     v = torch.randn(b, l, hkv, d, generator=gen).bfloat16()
     valid = torch.rand(b, l, generator=gen) > 0.05
     valid[1, 1900:] = False
-    o, lse = mrsa.bidir_local_attention(q.to(dev), k.to(dev), v.to(dev), valid.to(dev), window, 64,
-                                        skip_inert_slots=skip)
+    if f16v:
+        eff = window + 63 if skip else window    # bidir_local_attention's effective window
+        o, lse = mrsa.window_attention(q.to(dev), k.to(dev), mrsa.to_f16(v.to(dev)), valid.to(dev), eff,
+                                       skip_inert=skip, chunk=64)
+    else:
+        o, lse = mrsa.bidir_local_attention(q.to(dev), k.to(dev), v.to(dev), valid.to(dev), window, 64,
+                                            skip_inert_slots=skip)
     sl = slice(1024, 1536)
     ro, rl = orc._local_rows(q, k, v, valid, window, 64, skip, sl)
     close_bf16(o[:, sl], ro)

@@ -30,6 +30,9 @@ class OracleOps:
         self.inv_freq, self.af = orc.yarn_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.yarn_factor,
                                                    cfg.yarn_orig_max_pos)
 
+    def attention_v(self, v):
+        return v
+
     def _cs(self, pos):
         return orc.rope_cos_sin(pos, self.inv_freq, self.af)
 
