@@ -17,12 +17,13 @@ constexpr int TM = 64;      // tokens per CTA
 constexpr int RANK = 64;    // Q-Cal rank
 constexpr int TK = 64;      // hidden slice per pipeline stage
 constexpr int NT = 128;     // threads (4 warps x 16 token rows)
+constexpr int P1ST = 4;     // phase-1 stages: h streams from HBM with three tiles in flight
 
 struct QcalSmem {
   union {
     struct {
-      __nv_bfloat16 h[2][TM * TK];     // 16 KB
-      __nv_bfloat16 w[2][RANK * TK];   // 16 KB
+      __nv_bfloat16 h[P1ST][TM * TK];  // 32 KB
+      __nv_bfloat16 w[P1ST][RANK * TK];  // 32 KB
     } p1;
     struct {
       __nv_bfloat16 wo[2][kHeadDim * RANK];  // 32 KB
@@ -88,17 +89,22 @@ __global__ void __launch_bounds__(NT) qcal_kernel(
     for (int i = 0; i < 4; ++i) acc1[n][i] = 0.f;
 
   const int ktiles = hidden / TK;
-  load_p1(0, 0);
+  for (int s0 = 0; s0 < P1ST - 1 && s0 < ktiles; ++s0) load_p1(s0, s0 * TK);
   for (int kt = 0; kt < ktiles; ++kt) {
-    if (kt + 1 < ktiles) {
-      load_p1((kt + 1) & 1, (kt + 1) * TK);
+    // tile kt has landed once at most min(P1ST - 1, tiles after it) groups are pending
+    if (kt + P1ST - 1 < ktiles) {
+      load_p1((kt + P1ST - 1) % P1ST, (kt + P1ST - 1) * TK);
+      cp_async_wait<P1ST - 1>();
+    } else if (ktiles - 1 - kt >= 2) {
+      cp_async_wait<2>();
+    } else if (ktiles - 1 - kt == 1) {
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const __nv_bfloat16* hs = sm.u.p1.h[kt & 1];
-    const __nv_bfloat16* ws = sm.u.p1.w[kt & 1];
+    const __nv_bfloat16* hs = sm.u.p1.h[kt % P1ST];
+    const __nv_bfloat16* ws = sm.u.p1.w[kt % P1ST];
 #pragma unroll
     for (int ks = 0; ks < TK / 16; ++ks) {
       uint32_t a[4];
