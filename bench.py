@@ -67,7 +67,7 @@ def stage_bytes(l: int):
 # capture (dram__bytes_read.sum + dram__bytes_write.sum) of this bench's own
 # single-GPU workload; kept under profiles/ with the command that produced it.
 # Keyed by (kernel, query rows per GPU, total keys); other workloads report null.
-MEASURED_TRAFFIC = {("selected_attention", 16384, 16384): 332016128 + 101256704}
+MEASURED_TRAFFIC = {("selected_attention", 16384, 16384): 331471360 + 99500288}
 
 
 def load_peaks():
