@@ -152,6 +152,20 @@ int mrsa_local_attention_f16v(const void* q, const void* k, const void* v_f16, c
                               int64_t q_offset, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                               mrsa_stream_t stream);
 
+/* Causal chunk-expanded window attention: query row i sits at absolute
+ * position p = kv_start + (kv_len - q_len) + i and sees keys j (absolute
+ * kv_start + j) in [start, p], start = p - window + 1, rounded down to a
+ * multiple of chunk when expand_to_chunk; with mask_lmk the landmark slots
+ * ((kv_start + j + 1) % chunk == 0) are excluded from the softmax.  Writes
+ * out [B,Lq,Hq,D] bf16 and lse [B,Lq,Hq] fp32 natural log (or NULL); rows
+ * without a visible key give 0 and -inf.  q_len <= kv_len, sm_scale > 0.
+ * Replaces ops/flex_attn_tilelang.py:1261 flex_attn_tl (forward). */
+int mrsa_flex_attention(const void* q, const void* k, const void* v, void* out, float* lse,
+                        int64_t window, int64_t chunk, int mask_lmk, int expand_to_chunk,
+                        int64_t kv_start, float sm_scale, int64_t batch, int64_t q_len,
+                        int64_t kv_len, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                        mrsa_stream_t stream);
+
 /* Weighted per-chunk-softmax attention over the selected chunks, optionally
  * fused with the local branch: out = bf16(bf16(remote) + local_w*local) when
  * local_out and local_w are given, else bf16(remote).
@@ -176,6 +190,36 @@ int mrsa_selected_attention_f16v(const void* q, const void* k, const void* v_f16
                                  int64_t batch, int64_t q_len, int64_t kv_len, int64_t kv_heads,
                                  int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk,
                                  mrsa_stream_t stream);
+
+/* Candidate token scores [B,Lq,Hkv,K,S] fp32: for chunk c = indices[b,l,h,i]
+ * and slot s, max over the G = q_heads/kv_heads heads of the group of
+ * q_g . k[c*S+s] * sm_scale; -inf when c < 0 (or c >= kv_len/S), s == S-1 or
+ * key_valid (uint8 [B,Lk], NULL = all valid) is 0.  q [B,Lq,Hq,D], k
+ * [B,Lk,Hkv,D] bf16, indices [B,Lq,Hkv,K] int32; S >= 16, kv_len % S == 0,
+ * G <= 16.  Replaces ops/hils_token_score_gqa_tilelang.py:174
+ * candidate_token_scores_gqa. */
+int mrsa_candidate_token_scores(const void* q, const void* k, const int32_t* indices,
+                                const uint8_t* key_valid, float* scores, float sm_scale,
+                                int64_t batch, int64_t q_len, int64_t kv_len, int64_t q_heads,
+                                int64_t kv_heads, int64_t head_dim, int64_t selected, int64_t chunk,
+                                mrsa_stream_t stream);
+
+/* Exact selected-token GQA attention: query row (b,l) attends the tokens
+ * indices[b,l,t] (int32, clamped to [0, kv_len)) whose valid[b,l,t] (uint8)
+ * is nonzero; fp32 softmax of q.k*sm_scale, probabilities rounded to bf16,
+ * fp32 P.V; rows without a valid token are 0.  q [B,Lq,Hq,D], k/v
+ * [B,Lk,Hkv,D] bf16, out like q; G <= 16 and the kernel's shared memory
+ * (mrsa_selected_token_attention_smem) at most 227 KB.
+ * Replaces ops/dsa_selected_attention_tilelang.py:593
+ * selected_token_attention_tilelang (forward). */
+int mrsa_selected_token_attention(const void* q, const void* k, const void* v, const int32_t* indices,
+                                  const uint8_t* valid, void* out, float sm_scale, int64_t batch,
+                                  int64_t q_len, int64_t kv_len, int64_t q_heads, int64_t kv_heads,
+                                  int64_t head_dim, int64_t topk, mrsa_stream_t stream);
+
+/* Dynamic shared memory bytes mrsa_selected_token_attention needs for
+ * `groups` heads per KV head and `topk` tokens per row (0 if out of range). */
+size_t mrsa_selected_token_attention_smem(int64_t groups, int64_t topk);
 
 /* n bf16 values (n a multiple of 8, 16-byte aligned buffers) to fp16, round to
  * nearest; values beyond +-65504 (infinities too) saturate and set bit 3 of

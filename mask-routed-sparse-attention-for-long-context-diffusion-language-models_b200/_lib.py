@@ -45,6 +45,13 @@ _SIGS = {
                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_selected_attention_f16v": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _int,
                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_flex_attention": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _i64, _f32,
+                            _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_candidate_token_scores": [_vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64, _i64,
+                                    _i64, _i64, _vp],
+    "mrsa_selected_token_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64,
+                                      _i64, _i64, _vp],
+    "mrsa_selected_token_attention_smem": [_i64, _i64],
     "mrsa_convert_bf16_to_f16": [_vp, _vp, _i64, _vp],
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_device_error_flags": [_int],
@@ -53,7 +60,7 @@ _SIGS = {
     "mrsa_route_layer_forward_noalloc": [_vp, _vp],
 }
 _RESTYPE = {"mrsa_strerror": C.c_char_p, "mrsa_route_layer_workspace_size": _sz,
-            "mrsa_route_topk_workspace_size": _sz}
+            "mrsa_route_topk_workspace_size": _sz, "mrsa_selected_token_attention_smem": _sz}
 
 EXPORTED = tuple(_SIGS)
 

@@ -181,7 +181,7 @@ const char* mrsa_strerror(int code) {
   }
 }
 
-int mrsa_abi_version(void) { return 2; }
+int mrsa_abi_version(void) { return 3; }
 
 int mrsa_convert_bf16_to_f16(const void* in, void* out, int64_t n, mrsa_stream_t stream) {
   if (!in || !out) return MRSA_ERR_NULL;

@@ -18,6 +18,12 @@
 // warp 4: TMA (Q once, then K, V per tile, 3 stages) and the per-tile key
 // validity mask; warp 5: MMA issue (converged, elect.sync).  Every mbarrier
 // wait is bounded and unwinds through a shared abort flag.
+//
+// The same kernel also runs the causal chunk-expanded window of
+// ops/flex_attn_tilelang.py:26-276 (flex_attn_tl): a row at absolute position
+// p sees keys j in [start, p] with start = p - W + 1, rounded down to a chunk
+// boundary when expanding, and masked keys (landmark slots, mask_lmk) are
+// excluded from the softmax instead of zeroed.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,9 +62,31 @@ struct LocalArgs {
   __nv_bfloat16* out;
   float* lse;
   int64_t window, Lq, Lk, q_offset;
+  int64_t shift;        // absolute position of key 0 (landmark test, chunk rounding)
   int skip_inert, chunk, Hq, Hkv, G;
+  int causal;           // 0: |i-j| <= window;  1: flex_attn_tl's causal window
+  int expand;           // causal: round the left edge down to a chunk boundary
+  int exclude;          // masked keys leave the softmax (-inf) instead of keeping logit 0
   float sm_scale;
 };
+
+__device__ __host__ __forceinline__ int64_t floor_div(int64_t x, int64_t d) {
+  return x >= 0 ? x / d : -((-x + d - 1) / d);
+}
+
+// Key range [lo, hi] (key indices, before clipping to the sequence) of the row
+// at key-index position pos.
+__device__ __forceinline__ void row_band(const LocalArgs& a, int64_t pos, int64_t& lo, int64_t& hi) {
+  if (a.causal) {
+    int64_t start = pos + a.shift - a.window + 1;
+    if (a.expand) start = floor_div(start, a.chunk) * a.chunk;
+    lo = start - a.shift;
+    hi = pos;
+  } else {
+    lo = pos - a.window;
+    hi = pos + a.window;
+  }
+}
 
 __device__ int g_local_error;
 
@@ -78,7 +106,9 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   const int G = a.G;
   const int64_t q0 = static_cast<int64_t>(blockIdx.x) * LQ;
   const int64_t rows_q = (a.Lq - q0) < LQ ? (a.Lq - q0) : LQ;
-  int64_t j_lo = a.q_offset + q0 - a.window, j_hi = a.q_offset + q0 + rows_q - 1 + a.window;
+  int64_t j_lo, j_hi, unused;
+  row_band(a, a.q_offset + q0, j_lo, unused);
+  row_band(a, a.q_offset + q0 + rows_q - 1, unused, j_hi);
   if (j_lo < 0) j_lo = 0;
   if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
   const int t_lo = static_cast<int>(j_lo / LN);
@@ -130,7 +160,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         const int64_t j = j0 + 32 * h + lane;
         bool ok = j < a.Lk;
         if (ok && a.key_valid != nullptr) ok = a.key_valid[b * a.Lk + j] != 0;
-        if (ok && a.skip_inert) ok = ((j + 1) % a.chunk) != 0;
+        if (ok && a.skip_inert) ok = ((j + a.shift + 1) % a.chunk) != 0;
         mk[h] = __ballot_sync(0xffffffffu, ok);
       }
       if (lane == 0) {
@@ -213,6 +243,10 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     const int64_t pos = a.q_offset + q0 + qi;
     const float sl2 = a.sm_scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f, o_scale = 1.f;
+    int64_t band_lo, band_hi;
+    row_band(a, pos, band_lo, band_hi);
+    if (band_hi > a.Lk - 1) band_hi = a.Lk - 1;
+    const uint32_t fill = a.exclude ? __float_as_uint(-INFINITY) : 0u;
     bool ok = true;
     for (int t = 0; t < NTL; ++t) {
       const int st = t % LST, p2 = t & 1;
@@ -228,21 +262,23 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       tc::tmem_ld16(tbase + lane_off + LN * p2 + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
       tc::tmem_wait_ld();
       // Zeroed keys (invalid, or landmark slots) keep logit 0: their raw score is
-      // replaced by 0.  The mask is per tile, so this branch is warp-uniform; with
-      // landmark skipping on 64-aligned tiles only the last column is zeroed.
+      // replaced by 0 (excluded keys: -inf).  The mask is per tile, so this branch
+      // is warp-uniform; with landmark skipping on 64-aligned tiles only the last
+      // column is masked.
       if (km != ~0ull) {
         if (km == (~0ull >> 1)) {
-          x[LN - 1] = 0u;
+          x[LN - 1] = fill;
         } else {
 #pragma unroll
           for (int c = 0; c < LN; ++c)
-            if (!((km >> c) & 1ull)) x[c] = 0u;
+            if (!((km >> c) & 1ull)) x[c] = fill;
         }
       }
-      // band |pos - j| <= window and j < Lk: in-band columns [dlo, dhi] of this tile;
-      // columns outside are -inf (only the first and last tiles of a row have any)
-      const int64_t dlo = pos - a.window - j0;
-      const int64_t dhi = (pos + a.window < a.Lk - 1 ? pos + a.window : a.Lk - 1) - j0;
+      // the row's band [band_lo, band_hi] (clipped to j < Lk): in-band columns
+      // [dlo, dhi] of this tile; columns outside are -inf (only the first and
+      // last tiles of a row have any)
+      const int64_t dlo = band_lo - j0;
+      const int64_t dhi = band_hi - j0;
       if (dlo > 0 || dhi < LN - 1) {
         const int lo32 = dlo < 0 ? 0 : (dlo > LN ? LN : static_cast<int>(dlo));
         const int hi32 = dhi < -1 ? -1 : (dhi > LN - 1 ? LN - 1 : static_cast<int>(dhi));
@@ -389,17 +425,24 @@ bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+struct Band {
+  int causal = 0, expand = 0, exclude = 0;
+  int64_t shift = 0;
+};
+
 template <bool kF16>
 int local_launch(const void* q, const void* k, const void* v, const uint8_t* key_valid, void* out, float* lse,
                  int64_t window, int skip_inert, int64_t chunk, float sm_scale, int64_t batch, int64_t q_len,
                  int64_t kv_len, int64_t q_offset, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
-                 mrsa_stream_t stream) {
+                 mrsa_stream_t stream, Band band = Band()) {
   if (!q || !k || !v || !out) return MRSA_ERR_NULL;
   if (head_dim != D || kv_heads < 1 || q_heads < kv_heads || q_heads % kv_heads || q_heads / kv_heads > 8 ||
       batch < 1 || q_len < 0 || kv_len < 1 || q_offset < 0 || q_heads > 65535 || batch > 65535 ||
       batch * q_len * q_heads > 0x7fffffffLL || batch * kv_len > 0x7fffffffLL)
     return MRSA_ERR_SHAPE;
-  if (window < 0 || (skip_inert && chunk <= 0)) return MRSA_ERR_ARG;
+  if (window < 0 || ((skip_inert || band.expand) && chunk <= 0) || band.shift < 0 ||
+      !(sm_scale > 0.f) || window > (int64_t(1) << 40) || band.shift > (int64_t(1) << 40))
+    return MRSA_ERR_ARG;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return MRSA_ERR_ALIGN;
   if (q_len == 0) return MRSA_OK;
   // Q [B*Lq][Hq][128] as (dim-in-half, head row, half, query): one box = 8 head rows x 16 queries
@@ -425,6 +468,10 @@ int local_launch(const void* q, const void* k, const void* v, const uint8_t* key
   a.q_offset = q_offset;
   a.skip_inert = skip_inert;
   a.chunk = static_cast<int>(chunk > 0 ? chunk : 1);
+  a.shift = band.shift;
+  a.causal = band.causal;
+  a.expand = band.expand;
+  a.exclude = band.exclude;
   a.Hq = static_cast<int>(q_heads);
   a.Hkv = static_cast<int>(kv_heads);
   a.G = static_cast<int>(q_heads / kv_heads);
@@ -461,6 +508,22 @@ extern "C" int mrsa_local_attention_f16v(const void* q, const void* k, const voi
                                          mrsa_stream_t stream) {
   return local_launch<true>(q, k, v_f16, key_valid, out, lse, window, skip_inert, chunk, sm_scale, batch, q_len,
                             kv_len, q_offset, q_heads, kv_heads, head_dim, stream);
+}
+
+extern "C" int mrsa_flex_attention(const void* q, const void* k, const void* v, void* out, float* lse,
+                                   int64_t window, int64_t chunk, int mask_lmk, int expand_to_chunk,
+                                   int64_t kv_start, float sm_scale, int64_t batch, int64_t q_len,
+                                   int64_t kv_len, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                   mrsa_stream_t stream) {
+  if (q_len > kv_len) return MRSA_ERR_SHAPE;
+  if (chunk <= 0 || chunk > 0x7fffffffLL) return MRSA_ERR_ARG;
+  Band band;
+  band.causal = 1;
+  band.expand = expand_to_chunk != 0;
+  band.exclude = 1;
+  band.shift = kv_start;
+  return local_launch<false>(q, k, v, nullptr, out, lse, window, mask_lmk != 0, chunk, sm_scale, batch, q_len,
+                             kv_len, kv_len - q_len, q_heads, kv_heads, head_dim, stream, band);
 }
 
 namespace mrsa {

@@ -16,7 +16,7 @@ import importlib
 import sys
 
 from . import chunk_pool, local_attention, rope_fp32, routing  # noqa: F401  (load submodules)
-from . import route_weights as _rw, selected_attention as _sel  # noqa: F401
+from . import route_weights as _rw, selected_attention as _sel, token_ops  # noqa: F401
 
 # the package re-exports functions named like two of its modules; take the modules
 route_weights = sys.modules[__package__ + ".route_weights"]
@@ -41,6 +41,10 @@ PATCHES = {
     ("dream_dllm_hils.routing", "online_softmax_topk_head"): routing.online_softmax_topk_head,
     ("dream_dllm_hils.routing", "ref_softmax_topk_max_pooling"): routing.ref_softmax_topk_max_pooling,
     ("dream_dllm_hils.attention", "_route_weights_torch"): route_weights.route_weights_torch,
+    ("ops.flex_attn_tilelang", "flex_attn_tl"): local_attention.flex_attn_tl,
+    ("ops.hils_token_score_gqa_tilelang", "candidate_token_scores_gqa"): token_ops.candidate_token_scores_gqa,
+    ("ops.dsa_selected_attention_tilelang", "selected_token_attention_tilelang"):
+        token_ops.selected_token_attention_tilelang,
 }
 
 _ORIGINALS: dict = {}

@@ -67,3 +67,46 @@ def bidir_local_attention(q, k, v, key_valid, window: int, chunk_size: int, allo
                          "do not pass a dense L×L allowed_mask")
     eff = window + chunk_size - 1 if skip_inert_slots else window
     return window_attention(q, k, v, key_valid, eff, skip_inert=skip_inert_slots, chunk=chunk_size)
+
+
+def flex_attn_tl(q, k, v, window_size: int, chunk_size: int, training: bool = True, mask_lmk: bool = True,
+                 expand_to_chunk: bool = True, sm_scale: float = None, kv_start: int = 0):
+    """Causal chunk-expanded window attention of ``ops/flex_attn_tilelang.py:1261``
+    (forward): query row i (absolute position ``kv_start + Lk - Lq + i``) sees
+    keys j with ``start <= j <= i``, ``start = i - W + 1`` (rounded down to a
+    chunk boundary with ``expand_to_chunk``); with ``mask_lmk`` the landmark
+    slots ``(j + 1) % chunk_size == 0`` are excluded.  Returns
+    ``(o [B,Lq,Hq,D] bf16, lse [B,Lq,Hq] natural log)``; rows without a
+    visible key give 0 and ``-inf``."""
+    if training and int(kv_start) != 0:
+        raise ValueError("flex_attn_tl only supports non-zero kv_start in inference (training=False)")
+    if q.device.type != "cuda":
+        raise ValueError("flex_attn_tl requires CUDA tensors")
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("q, k, and v must have (B, L, H, D) layout")
+    if q.dtype != torch.bfloat16 or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("flex_attn_tl requires BF16 q, k, and v")
+    b, lq, hq, d = q.shape
+    lk, hkv = k.shape[1], k.shape[2]
+    if k.shape[0] != b or v.shape[:3] != k.shape[:3] or k.shape[-1] != d:
+        raise ValueError(f"q/k/v shape mismatch: {tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+    if v.shape[-1] != d or d != 128:
+        raise ValueError("the B200 kernel supports D_qk = D_v = 128")
+    if hq % hkv or hq // hkv > 8:
+        raise ValueError("the B200 kernel supports query groups of at most 8 heads")
+    if lq > lk:
+        raise ValueError(f"q_len={lq} must not exceed kv_len={lk}")
+    if chunk_size <= 0 or window_size < 0 or kv_start < 0:
+        raise ValueError(f"invalid window/chunk: W={window_size}, S={chunk_size}, kv_start={kv_start}")
+    scale = float(d) ** -0.5 if sm_scale is None else float(sm_scale)
+    if not scale > 0.0:
+        raise ValueError("the B200 kernel requires sm_scale > 0")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty(b, lq, hq, device=q.device, dtype=torch.float32)
+    if out.numel() == 0:
+        return out, lse
+    _lib.call("mrsa_flex_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(lse),
+              int(window_size), int(chunk_size), int(bool(mask_lmk)), int(bool(expand_to_chunk)),
+              int(kv_start), scale, b, lq, lk, hq, hkv, d, _lib.stream_of(q))
+    return out, lse

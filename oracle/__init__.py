@@ -11,3 +11,4 @@ fixtures under ``tests/golden/`` (see ``tests/golden/make_golden.py``).
 """
 
 from .route_layer import *  # noqa: F401,F403
+from . import token_ops  # noqa: F401

@@ -18,6 +18,10 @@ outputs of the reference's OWN functions, imported from the checkout:
 * ``local_mask.pt`` ``dream_dllm_hils/local_attention.py:35-64`` K/V masking + window
 * ``layer.pt``     a whole route layer composed from the functions above (the
   flash-attn local branch, GPU-only in the reference, comes from the oracle)
+* ``token_scores.pt`` ``dream_dllm_hils/token_refinement.py:10 candidate_token_scores_reference``
+* ``dsa.pt``       ``dream_dllm_hils/dsa_attention.py:498 selected_token_attention_reference``
+* ``flex.pt``      ``ops/flex_attn_tilelang.py:1355 _torch_ref_flex_attn`` (torch
+  flex_attention with the reference's mask; its block mask is built on the CPU)
 
 The fixtures are consumed by ``tests/test_oracle_golden.py`` (CPU) and by the
 GPU parity tests; nothing at test time reads the reference checkout.
@@ -228,6 +232,78 @@ def gen_layer():
                        "out": out})
 
 
+def gen_token_scores():
+    from dream_dllm_hils.token_refinement import candidate_token_scores_reference
+
+    g = torch.Generator().manual_seed(41)
+    b, lq, lk, hkv, gg, d, sel, s = 1, 12, 512, 2, 7, 32, 5, 64
+    q = torch.randn(b, lq, hkv * gg, d, generator=g).bfloat16()
+    k = torch.randn(b, lk, hkv, d, generator=g).bfloat16()
+    c = lk // s
+    idx = torch.randint(0, c, (b, lq, hkv, sel), generator=g).to(torch.int32)
+    idx[:, 3, 1, 2] = -1
+    idx[:, 4, 0] = -1
+    valid = torch.ones(b, lk, dtype=torch.bool)
+    valid[:, 70:90] = False
+    out = candidate_token_scores_reference(q, k, idx, valid, s)
+    _save("token_scores.pt", {"q": q, "k": k, "indices": idx, "key_valid": valid, "chunk": s,
+                              "out": out})
+
+
+def gen_dsa():
+    from dream_dllm_hils.dsa_attention import selected_token_attention_reference
+
+    g = torch.Generator().manual_seed(23)
+    b, lq, lk, hkv, gg, d, topk = 1, 9, 256, 2, 7, 32, 101
+    q = torch.randn(b, lq, hkv * gg, d, generator=g).bfloat16()
+    k = torch.randn(b, lk, hkv, d, generator=g).bfloat16()
+    v = torch.randn(b, lk, hkv, d, generator=g).bfloat16()
+    idx = torch.randint(-3, lk + 3, (b, lq, topk), generator=g)
+    valid = torch.rand(b, lq, topk, generator=g) > 0.2
+    valid[:, 0] = False
+    out = selected_token_attention_reference(q, k, v, idx, valid)
+    _save("dsa.pt", {"q": q, "k": k, "v": v, "indices": idx, "valid": valid, "out": out})
+
+
+FLEX_CASES = [
+    # (name, q_len, kv_len, window, chunk, mask_lmk, expand_to_chunk)
+    ("lmk_expand", 192, 192, 48, 32, True, True),
+    ("no_flags", 192, 192, 48, 32, False, False),
+    ("lmk_only", 192, 192, 48, 32, True, False),
+    ("expand_only", 192, 192, 48, 32, False, True),
+    ("prefill_part", 40, 192, 48, 32, True, True),
+    ("decode_q1", 1, 192, 100, 32, True, False),
+    ("chunk65", 150, 150, 100, 65, True, True),
+    ("window_ge_seq", 64, 64, 512, 32, True, True),
+]
+
+
+def gen_flex():
+    import functools
+
+    import torch.nn.attention.flex_attention as fa
+    from ops.flex_attn_tilelang import _torch_ref_flex_attn
+
+    # the reference builds its block mask on the default CUDA device; build it on the CPU
+    orig = fa.create_block_mask
+    fa.create_block_mask = functools.partial(orig, device="cpu")
+    try:
+        cases = []
+        for i, (name, lq, lk, w, c, lmk, exp) in enumerate(FLEX_CASES):
+            g = torch.Generator().manual_seed(100 + i)
+            hq, hkv, d = 4, 2, 32
+            q = (torch.randn(1, lq, hq, d, generator=g) * 0.5).bfloat16()
+            k = (torch.randn(1, lk, hkv, d, generator=g) * 0.5).bfloat16()
+            v = (torch.randn(1, lk, hkv, d, generator=g) * 0.5).bfloat16()
+            o, lse = _torch_ref_flex_attn(q.float(), k.float(), v.float(), w, c, lmk, exp)
+            cases.append({"name": name, "window": w, "chunk": c, "mask_lmk": lmk, "expand": exp,
+                          "q": q, "k": k, "v": v, "o": o.transpose(1, 2).contiguous(),
+                          "lse": lse.transpose(1, 2).contiguous()})
+    finally:
+        fa.create_block_mask = orig
+    _save("flex.pt", {"cases": cases})
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gen_yarn()
@@ -239,4 +315,7 @@ if __name__ == "__main__":
     gen_qcal()
     gen_local_mask()
     gen_layer()
+    gen_token_scores()
+    gen_dsa()
+    gen_flex()
     print("done")

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(mrsa):
 
 def test_strerror_and_version(mrsa):
     lib = mrsa._lib.load()
-    assert lib.mrsa_abi_version() == 2
+    assert lib.mrsa_abi_version() == 3
     assert lib.mrsa_strerror(0) == b"ok"
     assert b"NULL" in lib.mrsa_strerror(-1)
     assert lib.mrsa_strerror(-99) == b"unknown error"
@@ -127,3 +127,29 @@ def test_ops_raise_without_cuda_tensors(mrsa):
         mrsa.chunk_attn_pool_gqa(torch.zeros(1, 1, 4, 7, 128, dtype=torch.bfloat16),
                                  torch.zeros(1, 1, 64, 4, 128, dtype=torch.bfloat16),
                                  torch.ones(1, 1, 64, dtype=torch.bool))
+
+
+def test_token_ops_and_flex_reject_bad_arguments(mrsa):
+    lib = mrsa._lib.load()
+    d = C.c_void_p(4096)
+    # flex: q_len > kv_len is a shape error, chunk <= 0 and sm_scale <= 0 argument errors
+    assert lib.mrsa_flex_attention(d, d, d, d, None, 64, 64, 1, 1, 0, 0.1, 1, 65, 64, 8, 2, 128, None) == -2
+    assert lib.mrsa_flex_attention(d, d, d, d, None, 64, 0, 1, 1, 0, 0.1, 1, 64, 64, 8, 2, 128, None) == -5
+    assert lib.mrsa_flex_attention(d, d, d, d, None, 64, 64, 1, 1, 0, 0.0, 1, 64, 64, 8, 2, 128, None) == -5
+    assert lib.mrsa_flex_attention(d, d, d, d, None, 64, 64, 1, 1, -1, 0.1, 1, 64, 64, 8, 2, 128, None) == -5
+    assert lib.mrsa_flex_attention(None, d, d, d, None, 64, 64, 1, 1, 0, 0.1, 1, 64, 64, 8, 2, 128, None) == -1
+    # token scores: chunk < 16, kv_len not a multiple of chunk, head_dim != 128, groups > 16
+    ts = [d, d, d, None, d, 0.1, 1, 4]
+    assert lib.mrsa_candidate_token_scores(*ts, 256, 28, 4, 128, 2, 8, None) == -2
+    assert lib.mrsa_candidate_token_scores(*ts, 250, 28, 4, 128, 2, 64, None) == -2
+    assert lib.mrsa_candidate_token_scores(*ts, 256, 28, 4, 64, 2, 64, None) == -2
+    assert lib.mrsa_candidate_token_scores(*ts, 256, 34, 2, 128, 2, 64, None) == -2
+    assert lib.mrsa_candidate_token_scores(C.c_void_p(4100), d, d, None, d, 0.1, 1, 4, 256, 28, 4, 128, 2, 64,
+                                           None) == -3
+    # selected-token attention: NULL valid, groups > 16, shared memory beyond 227 KB
+    assert lib.mrsa_selected_token_attention(d, d, d, d, None, d, 0.1, 1, 4, 256, 28, 4, 128, 8, None) == -1
+    assert lib.mrsa_selected_token_attention(d, d, d, d, d, d, 0.1, 1, 4, 256, 34, 2, 128, 8, None) == -2
+    assert lib.mrsa_selected_token_attention(d, d, d, d, d, d, 0.1, 1, 4, 256, 28, 4, 128, 20000, None) == -2
+    assert lib.mrsa_selected_token_attention_smem(7, 2560) == 7 * 512 + 7 * 2560 * 4 + 2560 * 4 + 4 * 7 * 512
+    assert lib.mrsa_selected_token_attention_smem(7, 101) == 7 * 512 + 7 * 104 * 4 + 104 * 4 + 4 * 7 * 512
+    assert lib.mrsa_selected_token_attention_smem(17, 64) == 0

@@ -169,3 +169,49 @@ def test_topk_set_agreement_flags_real_differences():
     worst = key.topk(32, -1, largest=False).indices.sort(-1).values
     viol, exact = orc.topk_set_agreement(key, top, worst, 32)
     assert viol > 0 and exact == 0.0
+
+
+def test_candidate_token_scores_match_reference():
+    from oracle import token_ops as tok
+
+    g = load_golden("token_scores.pt")
+    out = tok.candidate_token_scores(g["q"], g["k"], g["indices"], g["key_valid"], g["chunk"])
+    ref = g["out"]
+    assert torch.equal(torch.isinf(out), torch.isinf(ref))
+    fin = torch.isfinite(ref)
+    torch.testing.assert_close(out[fin], ref[fin], atol=1e-5, rtol=1e-5)
+    assert torch.isinf(out[:, 4, 0]).all() and torch.isinf(out[..., -1]).all()
+
+
+def test_selected_token_attention_matches_reference():
+    from oracle import token_ops as tok
+
+    g = load_golden("dsa.pt")
+    out = tok.selected_token_attention(g["q"], g["k"], g["v"], g["indices"], g["valid"])
+    # both round P to bf16 and the output to bf16; the einsum order may differ by one bf16 ulp
+    torch.testing.assert_close(out.float(), g["out"].float(), atol=1e-2, rtol=1e-2)
+    assert (out.float() - g["out"].float()).abs().mean() < 1e-4
+    assert torch.count_nonzero(out[:, 0]) == 0
+
+
+def test_flex_window_matches_torch_flex_attention():
+    from oracle import token_ops as tok
+
+    for case in load_golden("flex.pt")["cases"]:
+        o, lse = tok.flex_window_attention(case["q"], case["k"], case["v"], case["window"], case["chunk"],
+                                           case["mask_lmk"], case["expand"])
+        torch.testing.assert_close(o, case["o"], atol=2e-5, rtol=1e-4, msg=case["name"])
+        fin = torch.isfinite(case["lse"])
+        assert torch.equal(fin, torch.isfinite(lse)), case["name"]
+        torch.testing.assert_close(lse[fin], case["lse"][fin], atol=2e-5, rtol=1e-5, msg=case["name"])
+
+
+def test_flex_mask_kv_start_is_a_shift():
+    """With a truncated cache (kv_start > 0) the mask equals the full-prefix
+    mask restricted to the kept keys (absolute positions throughout)."""
+    from oracle import token_ops as tok
+
+    full = tok.flex_window_mask(8, 200, 70, 32, True, True, 0)
+    part = tok.flex_window_mask(8, 136, 70, 32, True, True, 64)
+    assert torch.equal(full[:, 64:], part)
+    assert not full[:, :64].any()
