@@ -152,6 +152,18 @@ int mrsa_local_attention_f16v(const void* q, const void* k, const void* v_f16, c
                               int64_t q_offset, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                               mrsa_stream_t stream);
 
+/* mrsa_local_attention for query rows at arbitrary positions of the K/V
+ * cache: row i sits at query_positions[i] (int64 [q_len], shared by the batch,
+ * each in [0, kv_len)) and attends keys j with |query_positions[i] - j| <=
+ * window, with the same zeroed-key rules.  Replaces
+ * dream_dllm_hils/local_attention.py:147 cached_local_attention (the
+ * Fast-dLLM cached decode step). */
+int mrsa_local_attention_positions(const void* q, const void* k, const void* v, const uint8_t* key_valid,
+                                   const int64_t* query_positions, void* out, float* lse, int64_t window,
+                                   int skip_inert, int64_t chunk, float sm_scale, int64_t batch,
+                                   int64_t q_len, int64_t kv_len, int64_t q_heads, int64_t kv_heads,
+                                   int64_t head_dim, mrsa_stream_t stream);
+
 /* Causal chunk-expanded window attention: query row i sits at absolute
  * position p = kv_start + (kv_len - q_len) + i and sees keys j (absolute
  * kv_start + j) in [start, p], start = p - window + 1, rounded down to a

@@ -11,7 +11,8 @@ library is missing.
 from . import _lib
 from .chunk_pool import chunk_attn_pool_gqa
 from .layer import RouteLayer, RouteLayerConfig, swa_layer_forward
-from .local_attention import bidir_local_attention, flex_attn_tl, window_attention
+from .local_attention import (bidir_local_attention, cached_local_attention, flex_attn_tl,
+                              window_attention)
 from .rope_fp32 import rope_rotary_pos_emb, single_tensor_rope_autograd, yarn_inv_freq, yarn_rope_qk
 from .route_weights import route_weights, route_weights_torch
 from .routing import (online_softmax_topk_head, ref_softmax_topk_max_pooling, remote_drop_mask,
@@ -22,7 +23,7 @@ from .token_ops import candidate_token_scores_gqa, selected_token_attention_tile
 
 __all__ = [
     "RouteLayer", "RouteLayerConfig", "swa_layer_forward", "chunk_attn_pool_gqa",
-    "bidir_local_attention", "window_attention", "rope_rotary_pos_emb",
+    "bidir_local_attention", "cached_local_attention", "window_attention", "rope_rotary_pos_emb",
     "single_tensor_rope_autograd", "yarn_inv_freq", "yarn_rope_qk", "route_weights",
     "route_weights_torch", "online_softmax_topk_head", "ref_softmax_topk_max_pooling",
     "remote_drop_mask", "route_topk_fused", "route_topk_g7", "HiLS_block_M_head",

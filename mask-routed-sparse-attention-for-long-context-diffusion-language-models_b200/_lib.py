@@ -45,6 +45,8 @@ _SIGS = {
                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_selected_attention_f16v": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _int,
                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_local_attention_positions": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _i64, _f32,
+                                       _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_flex_attention": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _i64, _f32,
                             _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_candidate_token_scores": [_vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64, _i64,

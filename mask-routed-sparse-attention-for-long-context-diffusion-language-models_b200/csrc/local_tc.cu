@@ -59,6 +59,7 @@ static_assert(sizeof(LocalSmem) + 1024 <= 232448, "local attention shared memory
 
 struct LocalArgs {
   const uint8_t* key_valid;
+  const int64_t* qpos;  // per query row position (NULL: q_offset + row)
   __nv_bfloat16* out;
   float* lse;
   int64_t window, Lq, Lk, q_offset;
@@ -106,9 +107,21 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   const int G = a.G;
   const int64_t q0 = static_cast<int64_t>(blockIdx.x) * LQ;
   const int64_t rows_q = (a.Lq - q0) < LQ ? (a.Lq - q0) : LQ;
+  // positions of the CTA's first and last rows (the band is monotone in the
+  // position); with explicit row positions, their minimum and maximum
+  int64_t p_min = a.q_offset + q0, p_max = a.q_offset + q0 + rows_q - 1;
+  if (a.qpos != nullptr) {
+    p_min = a.qpos[q0];
+    p_max = p_min;
+    for (int i = 1; i < rows_q; ++i) {
+      const int64_t p = a.qpos[q0 + i];
+      p_min = p < p_min ? p : p_min;
+      p_max = p > p_max ? p : p_max;
+    }
+  }
   int64_t j_lo, j_hi, unused;
-  row_band(a, a.q_offset + q0, j_lo, unused);
-  row_band(a, a.q_offset + q0 + rows_q - 1, unused, j_hi);
+  row_band(a, p_min, j_lo, unused);
+  row_band(a, p_max, unused, j_hi);
   if (j_lo < 0) j_lo = 0;
   if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
   const int t_lo = static_cast<int>(j_lo / LN);
@@ -240,7 +253,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
     const int r = warp * 32 + lane;                  // MMA row = TMEM lane
     const int qi = r >> 3, g = r & 7;
-    const int64_t pos = a.q_offset + q0 + qi;
+    const int64_t pos = a.qpos != nullptr ? a.qpos[q0 + (qi < rows_q ? qi : rows_q - 1)] : a.q_offset + q0 + qi;
     const float sl2 = a.sm_scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f, o_scale = 1.f;
     int64_t band_lo, band_hi;
@@ -428,6 +441,7 @@ bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
 struct Band {
   int causal = 0, expand = 0, exclude = 0;
   int64_t shift = 0;
+  const int64_t* qpos = nullptr;
 };
 
 template <bool kF16>
@@ -460,6 +474,7 @@ int local_launch(const void* q, const void* k, const void* v, const uint8_t* key
     return MRSA_ERR_LAUNCH;
   LocalArgs a;
   a.key_valid = key_valid;
+  a.qpos = band.qpos;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.lse = lse;
   a.window = window;
@@ -508,6 +523,19 @@ extern "C" int mrsa_local_attention_f16v(const void* q, const void* k, const voi
                                          mrsa_stream_t stream) {
   return local_launch<true>(q, k, v_f16, key_valid, out, lse, window, skip_inert, chunk, sm_scale, batch, q_len,
                             kv_len, q_offset, q_heads, kv_heads, head_dim, stream);
+}
+
+extern "C" int mrsa_local_attention_positions(const void* q, const void* k, const void* v,
+                                              const uint8_t* key_valid, const int64_t* query_positions,
+                                              void* out, float* lse, int64_t window, int skip_inert,
+                                              int64_t chunk, float sm_scale, int64_t batch, int64_t q_len,
+                                              int64_t kv_len, int64_t q_heads, int64_t kv_heads,
+                                              int64_t head_dim, mrsa_stream_t stream) {
+  if (query_positions == nullptr && q_len > 0) return MRSA_ERR_NULL;
+  Band band;
+  band.qpos = query_positions;
+  return local_launch<false>(q, k, v, key_valid, out, lse, window, skip_inert, chunk, sm_scale, batch, q_len,
+                             kv_len, 0, q_heads, kv_heads, head_dim, stream, band);
 }
 
 extern "C" int mrsa_flex_attention(const void* q, const void* k, const void* v, void* out, float* lse,

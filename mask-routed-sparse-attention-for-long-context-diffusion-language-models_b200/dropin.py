@@ -41,6 +41,13 @@ PATCHES = {
     ("dream_dllm_hils.routing", "online_softmax_topk_head"): routing.online_softmax_topk_head,
     ("dream_dllm_hils.routing", "ref_softmax_topk_max_pooling"): routing.ref_softmax_topk_max_pooling,
     ("dream_dllm_hils.attention", "_route_weights_torch"): route_weights.route_weights_torch,
+    ("dream_dllm_hils.local_attention", "cached_local_attention"): local_attention.cached_local_attention,
+    # dream_dllm_hils/fastdllm_attention.py:16-21 binds these at import
+    ("dream_dllm_hils.fastdllm_attention", "cached_local_attention"): local_attention.cached_local_attention,
+    ("dream_dllm_hils.fastdllm_attention", "remote_drop_mask"): routing.remote_drop_mask,
+    ("dream_dllm_hils.fastdllm_attention", "route_topk_g7"): routing.route_topk_g7,
+    ("dream_dllm_hils.fastdllm_attention", "selected_attention_g7_cached"):
+        selected_attention.selected_attention_g7_cached,
     ("ops.flex_attn_tilelang", "flex_attn_tl"): local_attention.flex_attn_tl,
     ("ops.hils_token_score_gqa_tilelang", "candidate_token_scores_gqa"): token_ops.candidate_token_scores_gqa,
     ("ops.dsa_selected_attention_tilelang", "selected_token_attention_tilelang"):

@@ -69,6 +69,42 @@ def bidir_local_attention(q, k, v, key_valid, window: int, chunk_size: int, allo
     return window_attention(q, k, v, key_valid, eff, skip_inert=skip_inert_slots, chunk=chunk_size)
 
 
+def cached_local_attention(q, k, v, key_valid, query_positions, window: int, chunk_size: int,
+                           skip_inert_slots: bool = False):
+    """Fast-dLLM query rows at ``query_positions`` against a windowed K/V cache
+    (``dream_dllm_hils/local_attention.py:147``): each row attends the cache
+    keys within the same window as :func:`bidir_local_attention` around its own
+    position.  Returns ``(o [B, Lq, Hq, D] bf16, lse [B, Lq, Hq])``."""
+    _validate_layout(q, k, v, key_valid)
+    batch, query_len, h_q, dim = q.shape
+    seq_len = k.shape[1]
+    # mirrors dream_dllm_hils/local_attention.py:158-181
+    if query_positions.shape != (query_len,):
+        raise ValueError(f"query_positions must have shape {(query_len,)}, "
+                         f"got {tuple(query_positions.shape)}")
+    if query_positions.device != q.device or query_positions.dtype != torch.long:
+        raise ValueError("query_positions must be CUDA torch.long")
+    if query_len == 0:
+        return q.new_empty((batch, 0, h_q, dim)), q.new_empty((batch, 0, h_q), dtype=torch.float32)
+    if torch.unique(query_positions).numel() != query_len:
+        raise ValueError("query_positions must be unique")
+    if bool(((query_positions < 0) | (query_positions >= seq_len)).any()):
+        raise ValueError("query_positions must be in cache range")
+    if window < 0 or chunk_size <= 0 or seq_len % chunk_size:
+        raise ValueError(f"invalid window/chunk layout: L={seq_len}, W={window}, S={chunk_size}")
+    eff = window + chunk_size - 1 if skip_inert_slots else window
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    kv = key_valid.to(device=q.device, dtype=torch.bool).contiguous()
+    pos = query_positions.contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty(batch, query_len, h_q, device=q.device, dtype=torch.float32)
+    _lib.call("mrsa_local_attention_positions", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
+              _lib.ptr(pos), _lib.ptr(out), _lib.ptr(lse), int(eff), int(bool(skip_inert_slots)),
+              int(chunk_size), float(dim) ** -0.5, batch, query_len, seq_len, h_q, k.shape[2], dim,
+              _lib.stream_of(q))
+    return out, lse
+
+
 def flex_attn_tl(q, k, v, window_size: int, chunk_size: int, training: bool = True, mask_lmk: bool = True,
                  expand_to_chunk: bool = True, sm_scale: float = None, kv_start: int = 0):
     """Causal chunk-expanded window attention of ``ops/flex_attn_tilelang.py:1261``

@@ -153,3 +153,12 @@ def test_token_ops_and_flex_reject_bad_arguments(mrsa):
     assert lib.mrsa_selected_token_attention_smem(7, 2560) == 7 * 512 + 7 * 2560 * 4 + 2560 * 4 + 4 * 7 * 512
     assert lib.mrsa_selected_token_attention_smem(7, 101) == 7 * 512 + 7 * 104 * 4 + 104 * 4 + 4 * 7 * 512
     assert lib.mrsa_selected_token_attention_smem(17, 64) == 0
+
+
+def test_local_attention_positions_needs_positions(mrsa):
+    lib = mrsa._lib.load()
+    d = C.c_void_p(4096)
+    assert lib.mrsa_local_attention_positions(d, d, d, None, None, d, None, 256, 1, 64, 0.1, 1, 4, 256, 28, 4,
+                                              128, None) == -1
+    assert lib.mrsa_local_attention_positions(d, d, d, None, d, d, None, 256, 1, 64, 0.1, 1, 4, 256, 28, 4,
+                                              64, None) == -2

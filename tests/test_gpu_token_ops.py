@@ -1,7 +1,9 @@
 """GPU parity of the ops off the route layer's live path -- the causal flex
-window (``flex_attn_tl``), candidate token scores and selected-token (DSA)
-attention -- against the CPU oracle, which ``test_oracle_golden.py`` pins to
-the reference's own torch functions.
+window (``flex_attn_tl``), the cached (Fast-dLLM) local rows, candidate token
+scores and selected-token (DSA) attention -- against the CPU oracle, which
+``test_oracle_golden.py`` pins to the reference's own torch functions (the
+cached local rows follow the local-window oracle, unpinned like the
+flash-attn local branch).
 
 Tolerances: bf16 attention outputs max-abs <= 2e-2 and mean-rel <= 1e-3 (as
 for the route layer), plus the reference tests' own bars where they state
@@ -92,6 +94,47 @@ def test_flex_attn_tl_rejects_reference_errors(mrsa, dev):
         mrsa.flex_attn_tl(q.float(), k, k, 32, 64)
     with pytest.raises(ValueError):
         mrsa.flex_attn_tl(torch.zeros(1, 65, 8, 128, dtype=torch.bfloat16, device=dev), k, k, 32, 64)
+
+
+# ------------------------------------------------ cached (Fast-dLLM) local rows
+@pytest.mark.parametrize("positions", [
+    list(range(512, 544)),                                   # one decode block
+    [1023, 5, 700, 64, 63, 300, 301, 999, 0, 511, 128, 127, 640, 641, 642, 900, 17],   # scattered, unsorted
+])
+@pytest.mark.parametrize("window,skip", [(256, True), (1280, False)])
+def test_cached_local_attention_matches_oracle(mrsa, dev, positions, window, skip):
+    from oracle import route_layer as orc
+
+    g = torch.Generator().manual_seed(len(positions) + window)
+    b, l, hq, hkv, d = 2, 1024, 28, 4, 128
+    pos = torch.tensor(positions, dtype=torch.long)
+    q = torch.randn(b, len(positions), hq, d, generator=g).bfloat16()
+    k = torch.randn(b, l, hkv, d, generator=g).bfloat16()
+    v = torch.randn(b, l, hkv, d, generator=g).bfloat16()
+    valid = torch.rand(b, l, generator=g) > 0.05
+    valid[1, 900:] = False
+    o, lse = mrsa.cached_local_attention(q.to(dev), k.to(dev), v.to(dev), valid.to(dev), pos.to(dev),
+                                         window, 64, skip_inert_slots=skip)
+    # the reference places the rows at their positions and runs the full window
+    # (dream_dllm_hils/local_attention.py:183-197)
+    q_full = torch.zeros(b, l, hq, d, dtype=torch.bfloat16)
+    q_full[:, pos] = q
+    ro, rl = orc.local_attention(q_full, k, v, valid, window, 64, skip)
+    close_bf16(o, ro[:, pos])
+    torch.testing.assert_close(lse.cpu(), rl[:, pos], atol=2e-4, rtol=1e-5)
+
+
+def test_cached_local_attention_rejects_reference_errors(mrsa, dev):
+    q = torch.zeros(1, 3, 28, 128, dtype=torch.bfloat16, device=dev)
+    k = torch.zeros(1, 256, 4, 128, dtype=torch.bfloat16, device=dev)
+    valid = torch.ones(1, 256, dtype=torch.bool, device=dev)
+    with pytest.raises(ValueError, match="unique"):
+        mrsa.cached_local_attention(q, k, k, valid, torch.tensor([1, 1, 2], device=dev), 256, 64)
+    with pytest.raises(ValueError, match="cache range"):
+        mrsa.cached_local_attention(q, k, k, valid, torch.tensor([1, 2, 256], device=dev), 256, 64)
+    with pytest.raises(ValueError, match="torch.long"):
+        mrsa.cached_local_attention(q, k, k, valid, torch.tensor([1, 2, 3], device=dev, dtype=torch.int32),
+                                    256, 64)
 
 
 # ------------------------------------------------------ candidate token scores
