@@ -233,6 +233,21 @@ int mrsa_selected_token_attention(const void* q, const void* k, const void* v, c
  * `groups` heads per KV head and `topk` tokens per row (0 if out of range). */
 size_t mrsa_selected_token_attention_smem(int64_t groups, int64_t topk);
 
+/* mrsa_selected_attention (v_f16 = 0) or mrsa_selected_attention_f16v
+ * (v_f16 != 0) with token refinement: token_keep [B,Lq,Hkv,K,chunk] int8
+ * (16-byte aligned) drops key s of slot k for query l and KV head h where it
+ * is 0, on top of the key-validity and landmark masks; a chunk whose keys are
+ * all dropped contributes nothing.  A chunk listed twice by one query uses
+ * the keep row of its first slot.  Replaces the token_keep argument of
+ * ops/hils_fwd_bwd_head.py:1113 HiLS_block_M_head (kernel :453-507) and
+ * dream_dllm_hils/routing.py:305 selected_attention_g7. */
+int mrsa_selected_attention_keep(const void* q, const void* k, const void* v, const uint8_t* key_valid,
+                                 const void* weights, const int32_t* indices, const int8_t* token_keep,
+                                 const void* local_out, const void* local_w, void* out, float sm_scale,
+                                 int mask_last_token, int v_f16, int64_t batch, int64_t q_len,
+                                 int64_t kv_len, int64_t kv_heads, int64_t groups, int64_t head_dim,
+                                 int64_t topk, int64_t chunk, mrsa_stream_t stream);
+
 /* n bf16 values (n a multiple of 8, 16-byte aligned buffers) to fp16, round to
  * nearest; values beyond +-65504 (infinities too) saturate and set bit 3 of
  * mrsa_device_error_flags.  No counterpart in the reference (V preparation

@@ -54,6 +54,8 @@ _SIGS = {
     "mrsa_selected_token_attention": [_vp, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64,
                                       _i64, _i64, _vp],
     "mrsa_selected_token_attention_smem": [_i64, _i64],
+    "mrsa_selected_attention_keep": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _int, _int,
+                                     _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_convert_bf16_to_f16": [_vp, _vp, _i64, _vp],
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_device_error_flags": [_int],

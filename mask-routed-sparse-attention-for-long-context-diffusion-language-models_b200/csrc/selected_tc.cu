@@ -105,6 +105,7 @@ struct TcArgs {
   const __nv_bfloat16* w;
   const int32_t* indices;
   const uint8_t* key_valid;
+  const int8_t* token_keep;       // [B, Lq, Hkv, K, 64] (token refinement), or NULL
   const __nv_bfloat16 *local_out, *local_w;
   __nv_bfloat16* out;
   float sm_scale;
@@ -507,63 +508,83 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       const bool row_on = jrow < n;
       float w = 0.f;
       uint32_t km = 0xFFFFFFFFu;             // rows without an owner are computed and dropped
+      uint4 keep[2];                         // token refinement: this row's 32 keep bytes
       if (row_on) {
-        if (g < G) w = sm.w[sm.ring[r].oq[jrow]][g][sm.ring[r].slot[jrow]];
+        const int oqj = sm.ring[r].oq[jrow], slot = sm.ring[r].slot[jrow];
+        if (g < G) w = sm.w[oqj][g][slot];
         const unsigned long long vm = sm.vmask[sm.ring[r].u];
         km = static_cast<uint32_t>(hf ? (vm >> 32) : vm);
+        if (a.token_keep != nullptr) {       // issued before the S wait, used after it
+          const uint4* kp = reinterpret_cast<const uint4*>(
+              a.token_keep + (((b * a.Lq + q0 + oqj) * a.Hkv + hk) * K + slot) * S + 32 * hf);
+          keep[0] = __ldg(kp);
+          keep[1] = __ldg(kp + 1);
+        }
       }
       if (!wait_bar_warp(sm, &sm.bar_sdone[p2], (it >> 1) & 1)) break;
+      if (row_on && a.token_keep != nullptr) {
+        const uint32_t wd[8] = {keep[0].x, keep[0].y, keep[0].z, keep[0].w,
+                                keep[1].x, keep[1].y, keep[1].z, keep[1].w};
+        uint32_t kb = 0u;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) kb |= static_cast<uint32_t>(((wd[i >> 2] >> (8 * (i & 3))) & 0xFFu) != 0u) << i;
+        km &= kb;
+      }
       tc::fence_after_sync();
+      // Quadrant q holds the rows of owners q and q+4: with fewer than q+1
+      // owners (most items when the chunks are many and each is picked by
+      // one or two of the block's queries) the warp has no row to compute and
+      // keeps only its hand-offs, which frees issue slots for the other roles.
+      const bool quad_on = q < n;            // warp-uniform
       uint32_t x[32];
-      if (q < n) {                           // warp-uniform: this quadrant holds rows
+      if (quad_on) {
         tc::tmem_ld_16x32bx2_x32(tbase + lane_off + kSCol + 64 * p2, x);
         tc::tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) x[c] = 0u;
       }
       // the S buffer is free once every warp of the group has loaded its rows
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(su32(&sm.bar_sfree[p2]));
-      // masked keys -> -inf; the common case (every key usable but possibly the
-      // last of the chunk) takes one select instead of 32
-      if (__all_sync(0xffffffffu, (km | 0x80000000u) == 0xFFFFFFFFu)) {
-        if (!(km >> 31)) x[31] = __float_as_uint(-INFINITY);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (!((km >> c) & 1u)) x[c] = __float_as_uint(-INFINITY);
-      }
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(x[c]));
-      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float nb = mx == -INFINITY ? 0.f : -mx * sl2;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float e = fast_exp2(fmaf(__uint_as_float(x[c]), sl2, nb));   // masked keys: 2^-inf = 0
-        x[c] = __float_as_uint(e);
-        sum4[c & 3] += e;
-      }
-      float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-      // P = route weight x softmax: as bf16 hi + lo, or as one fp16 tile (11
-      // significant bits; values small enough to be fp16 subnormals carry an
-      // absolute error below 2^-25, far under the bf16 output's resolution)
-      const float f = sum > 0.f ? __fdividef(w, sum) : 0.f;
       uint32_t hi[16], lo[16];
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float p0 = __uint_as_float(x[2 * h]) * f;
-        const float p1 = __uint_as_float(x[2 * h + 1]) * f;
-        if constexpr (kF16) {
-          hi[h] = pack_f16x2(p0, p1);
+      if (quad_on) {
+        // masked keys -> -inf; the common case (every key usable but possibly the
+        // last of the chunk) takes one select instead of 32
+        if (__all_sync(0xffffffffu, (km | 0x80000000u) == 0xFFFFFFFFu)) {
+          if (!(km >> 31)) x[31] = __float_as_uint(-INFINITY);
         } else {
-          hi[h] = pack_bf16x2(p0, p1);
-          lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (!((km >> c) & 1u)) x[c] = __float_as_uint(-INFINITY);
+        }
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(x[c]));
+        float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float nb = mx == -INFINITY ? 0.f : -mx * sl2;
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float e = fast_exp2(fmaf(__uint_as_float(x[c]), sl2, nb));   // masked keys: 2^-inf = 0
+          x[c] = __float_as_uint(e);
+          sum4[c & 3] += e;
+        }
+        float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        // P = route weight x softmax: as bf16 hi + lo, or as one fp16 tile (11
+        // significant bits; values small enough to be fp16 subnormals carry an
+        // absolute error below 2^-25, far under the bf16 output's resolution)
+        const float f = sum > 0.f ? __fdividef(w, sum) : 0.f;
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const float p0 = __uint_as_float(x[2 * h]) * f;
+          const float p1 = __uint_as_float(x[2 * h + 1]) * f;
+          if constexpr (kF16) {
+            hi[h] = pack_f16x2(p0, p1);
+          } else {
+            hi[h] = pack_bf16x2(p0, p1);
+            lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+          }
         }
       }
       // the P buffer is free once the P.V of item it-2 has completed
@@ -772,7 +793,8 @@ template <bool kF16>
 int selected_launch(const void* q, const void* k, const void* v, const uint8_t* key_valid, const void* weights,
                     const int32_t* indices, const void* local_out, const void* local_w, void* out, float sm_scale,
                     int mask_last_token, int64_t batch, int64_t q_len, int64_t kv_len, int64_t kv_heads,
-                    int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk, mrsa_stream_t stream) {
+                    int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk, mrsa_stream_t stream,
+                    const int8_t* token_keep = nullptr) {
   if (!q || !k || !v || !weights || !indices || !out) return MRSA_ERR_NULL;
   if ((local_out == nullptr) != (local_w == nullptr)) return MRSA_ERR_NULL;
   if (head_dim != D || chunk != S || groups < 1 || groups > GMAX || kv_heads < 1 || batch < 1 ||
@@ -781,7 +803,8 @@ int selected_launch(const void* q, const void* k, const void* v, const uint8_t* 
       batch * kv_len > 0x7fffffffLL)
     return MRSA_ERR_SHAPE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
-      (local_out && !aligned16(local_out)) || (key_valid && !aligned16(key_valid)))
+      (local_out && !aligned16(local_out)) || (key_valid && !aligned16(key_valid)) ||
+      (token_keep && !aligned16(token_keep)))
     return MRSA_ERR_ALIGN;
   if (q_len == 0) return MRSA_OK;
   // K, V: [B*Lk rows][Hkv*128] viewed as (dim-in-half, row, half, head): one box = one chunk tile.
@@ -802,6 +825,7 @@ int selected_launch(const void* q, const void* k, const void* v, const uint8_t* 
   a.w = static_cast<const __nv_bfloat16*>(weights);
   a.indices = indices;
   a.key_valid = key_valid;
+  a.token_keep = token_keep;
   a.local_out = static_cast<const __nv_bfloat16*>(local_out);
   a.local_w = static_cast<const __nv_bfloat16*>(local_w);
   a.out = static_cast<__nv_bfloat16*>(out);
@@ -852,6 +876,24 @@ extern "C" int mrsa_selected_attention_f16v(const void* q, const void* k, const 
   return selected_launch<true>(q, k, v_f16, key_valid, weights, indices, local_out, local_w, out, sm_scale,
                                mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
                                stream);
+}
+
+extern "C" int mrsa_selected_attention_keep(const void* q, const void* k, const void* v,
+                                            const uint8_t* key_valid, const void* weights,
+                                            const int32_t* indices, const int8_t* token_keep,
+                                            const void* local_out, const void* local_w, void* out,
+                                            float sm_scale, int mask_last_token, int v_f16, int64_t batch,
+                                            int64_t q_len, int64_t kv_len, int64_t kv_heads, int64_t groups,
+                                            int64_t head_dim, int64_t topk, int64_t chunk,
+                                            mrsa_stream_t stream) {
+  if (token_keep == nullptr) return MRSA_ERR_NULL;
+  if (v_f16)
+    return selected_launch<true>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+                                 mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
+                                 stream, token_keep);
+  return selected_launch<false>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+                                mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
+                                stream, token_keep);
 }
 
 extern "C" int mrsa_device_error_flags(int clear) {

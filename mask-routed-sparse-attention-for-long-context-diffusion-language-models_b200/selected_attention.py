@@ -19,13 +19,17 @@ _LOGICAL_G = 7
 
 def selected_attention(q, k, v, weights, indices, key_valid=None, *, chunk: int = 64,
                        local_out=None, local_weight=None, mask_last_token=True, sm_scale=None,
-                       out=None):
+                       out=None, token_keep=None):
     """``out = sum_k w_k softmax_chunk(q.K_k/sqrt(D)) V_k`` (bf16), fused with
     ``+ local_weight * local_out`` when those are given.
 
     ``v`` in bf16 runs the exact-P kernel (P as bf16 hi + lo); ``v`` in fp16
     (see :func:`to_f16`) runs the fp16-P kernel, which does half the P.V work
-    and keeps P to 11 significant bits."""
+    and keeps P to 11 significant bits.  ``token_keep`` (``[B, Lq, Hkv, K,
+    chunk]``, nonzero = keep) additionally drops tokens of each selected chunk
+    per (query, KV head, slot), as token refinement does
+    (``ops/hils_fwd_bwd_head.py:453-507``); a chunk listed twice by one query
+    uses its first slot's keep row."""
     b, lq, hq, d = q.shape
     lk, hkv = k.shape[1], k.shape[2]
     topk = indices.shape[-1]
@@ -41,6 +45,16 @@ def selected_attention(q, k, v, weights, indices, key_valid=None, *, chunk: int 
     scale = float(d) ** -0.5 if sm_scale is None else float(sm_scale)
     if v.dtype not in (torch.bfloat16, torch.float16):
         raise ValueError(f"v must be bf16 or fp16, got {v.dtype}")
+    if token_keep is not None:
+        if tuple(token_keep.shape) != (b, lq, hkv, topk, chunk):
+            raise ValueError(f"token_keep must have shape {(b, lq, hkv, topk, chunk)}, "
+                             f"got {tuple(token_keep.shape)}")
+        keep = token_keep.to(device=dev, dtype=torch.int8).contiguous()
+        _lib.call("mrsa_selected_attention_keep", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
+                  _lib.ptr(w), _lib.ptr(idx), _lib.ptr(keep), _lib.ptr(lo), _lib.ptr(lw), _lib.ptr(out),
+                  scale, int(bool(mask_last_token)), int(v.dtype == torch.float16), b, lq, lk, hkv,
+                  hq // hkv, d, topk, int(chunk), _lib.stream_of(q))
+        return out
     entry = "mrsa_selected_attention_f16v" if v.dtype == torch.float16 else "mrsa_selected_attention"
     _lib.call(entry, _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv),
               _lib.ptr(w), _lib.ptr(idx), _lib.ptr(lo), _lib.ptr(lw), _lib.ptr(out), scale,
@@ -99,8 +113,13 @@ def selected_attention_g7(q, k, v, weights, indices, key_valid, chunk_size, trai
     """Selected-chunk attention with compact KV (``dream_dllm_hils/routing.py:305``)."""
     _validate_g7(q, k, v, weights, indices, key_valid, chunk_size)
     if token_keep is not None:
-        raise ValueError("token_keep (token refinement) is not supported by the B200 kernel")
-    return selected_attention(q, k, v, weights, indices, key_valid, chunk=chunk_size)
+        # mirrors dream_dllm_hils/routing.py:393-419
+        expect = (q.shape[0], q.shape[1], k.shape[2], indices.shape[-1], chunk_size)
+        if tuple(token_keep.shape) != expect:
+            raise ValueError(f"token_keep must have shape {expect}, got {tuple(token_keep.shape)}")
+        if token_keep.device != q.device:
+            raise ValueError("token_keep must share the q device")
+    return selected_attention(q, k, v, weights, indices, key_valid, chunk=chunk_size, token_keep=token_keep)
 
 
 def selected_attention_g7_cached(q, k, v, weights, indices, key_valid, chunk_size, token_keep=None):
@@ -114,13 +133,13 @@ def HiLS_block_M_head(q, k, v, weights, indices, block_size=64, sm_scale=None, b
                       key_valid=None, token_keep=None):
     """Forward of ``ops/hils_fwd_bwd_head.py:1113`` (q may carry padded heads;
     padded weights are zero)."""
-    if slope is not None or token_keep is not None:
-        raise ValueError("ALiBi slope / token_keep are not supported by the B200 kernel")
+    if slope is not None:
+        raise ValueError("ALiBi slope is not supported by the B200 kernel")
     hq, hkv = q.shape[2], k.shape[2]
     if hq % hkv or hq // hkv > 8:
         raise ValueError("the B200 kernel supports query groups of at most 8 heads")
     return selected_attention(q, k, v, weights, indices, key_valid, chunk=block_size,
-                              mask_last_token=mask_last_token, sm_scale=sm_scale)
+                              mask_last_token=mask_last_token, sm_scale=sm_scale, token_keep=token_keep)
 
 
 def fuse_hils_outputs(remote_output, local_output, local_weight):

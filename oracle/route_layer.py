@@ -407,7 +407,7 @@ def local_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, key_valid
 
 def selected_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weights: torch.Tensor,
                        indices: torch.Tensor, key_valid: torch.Tensor | None, chunk: int,
-                       block: int = 128, out_dtype=torch.bfloat16):
+                       block: int = 128, out_dtype=torch.bfloat16, token_keep: torch.Tensor | None = None):
     """Weighted per-chunk softmax attention over the selected chunks.
 
     ``hils_torch_ref`` (``ops/hils_fwd_bwd_head.py:21-93``, ``block_q=1``,
@@ -415,6 +415,9 @@ def selected_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight
     checks (``ops/hils_fwd_bwd_head.py:440-446``):
     ``out = sum_k w_k * softmax_s(q.K_{idx_k,s}/sqrt(D))_{s valid, s!=S-1} V_{idx_k,s}``.
     Slots with ``idx<0`` and chunks with no valid key contribute nothing.
+    ``token_keep`` ``[B,L,Hkv,K,S]`` (token refinement) further masks key s of
+    slot k per (query, KV head) where it is zero (``:453-507``; the weighted
+    per-chunk reference of ``unittests/test_hils_non_power_two_topk.py:122-135``).
     """
     b, l, hq, d = q.shape
     hkv = k.shape[2]
@@ -437,6 +440,8 @@ def selected_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, weight
         kg = kc[bi, safe, :, hi]                                     # [B,n,Hkv,K,S,D]
         vg = vc[bi, safe, :, hi]
         okg = ok[bi, safe]                                           # [B,n,Hkv,K,S]
+        if token_keep is not None:
+            okg = okg & (token_keep[:, s:e] != 0)
         qg = q[:, s:e].float().view(b, e - s, hkv, g, d)
         sc = torch.einsum("bnhgd,bnhksd->bnhgks", qg, kg) / math.sqrt(d)
         sc = sc.masked_fill(~okg[:, :, :, None], float("-inf"))

@@ -243,6 +243,37 @@ def test_selected_random_routing_duplicates_ragged(mrsa, dev, g, topk, lq, vdt):
     close_bf16(out[:, rows.to(dev)], ref)
 
 
+@pytest.mark.parametrize("cached", [False, True])
+@pytest.mark.parametrize("filtered", [False, True])
+def test_selected_k31_token_keep_matches_oracle(mrsa, dev, cached, filtered):
+    """unittests/test_hils_non_power_two_topk.py:95-142: K=31 (not a power of
+    two), the first query without chunks, every 97th key invalid, and with
+    ``filtered`` a random token_keep mask (token refinement)."""
+    g = torch.Generator().manual_seed(79)
+    lq, lk, hkv, gg, d, topk, size = (35 if cached else 2048), 2048, 4, 7, 128, 31, 64
+    q = torch.randn(1, lq, hkv * gg, d, generator=g).bfloat16()
+    k = torch.randn(1, lk, hkv, d, generator=g).bfloat16()
+    v = torch.randn(1, lk, hkv, d, generator=g).bfloat16()
+    idx = torch.arange(topk, dtype=torch.int32).expand(1, lq, hkv, -1).clone()
+    idx[:, 0] = -1
+    w = torch.randn(1, lq, hkv * gg, topk, generator=g).softmax(-1).bfloat16()
+    w[:, 0] = 0
+    valid = torch.ones(1, lk, dtype=torch.bool)
+    valid[:, ::97] = False
+    keep = (torch.rand(1, lq, hkv, topk, size, generator=g) > 0.4) if filtered else None
+    args = [t.to(dev) for t in (q, k, v, w, idx, valid)] + [size]
+    dkeep = None if keep is None else keep.to(dev)
+    got = (mrsa.selected_attention_g7_cached(*args, token_keep=dkeep) if cached else
+           mrsa.selected_attention_g7(*args, training=False, token_keep=dkeep))
+    assert torch.count_nonzero(got[:, 0]) == 0
+    ref = orc.selected_attention(q, k, v, w, idx, valid, size, token_keep=keep)
+    close_bf16(got, ref)
+    if filtered:   # the fp16-V kernel reads the same keep rows
+        got16 = mrsa.selected_attention(q.to(dev), k.to(dev), mrsa.to_f16(v.to(dev)), w.to(dev), idx.to(dev),
+                                        valid.to(dev), chunk=size, token_keep=dkeep)
+        close_bf16(got16, ref)
+
+
 @pytest.mark.parametrize("vdt", ["bf16", "f16"])
 def test_selected_all_queries_same_chunks(mrsa, dev, vdt):
     """every query of a block selects the same chunks: items of 8 owners, 4 per chunk"""
