@@ -159,7 +159,8 @@ __device__ __forceinline__ uint64_t adv(uint64_t desc, uint32_t bytes) { return 
 
 // kF16: V arrives in fp16 and P is one fp16 tile, one P.V MMA per k-step and
 // four V stages; otherwise V is bf16 and P is split into bf16 hi + lo.
-template <bool kF16>
+// kKeep: token refinement's keep rows (a.token_keep) mask each owner row.
+template <bool kF16, bool kKeep>
 __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
     const __grid_constant__ CUtensorMap tm_q, TcArgs a) {
@@ -508,13 +509,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       const bool row_on = jrow < n;
       float w = 0.f;
       uint32_t km = 0xFFFFFFFFu;             // rows without an owner are computed and dropped
-      uint4 keep[2];                         // token refinement: this row's 32 keep bytes
+      uint4 keep[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};   // token refinement: this row's 32 keep bytes
       if (row_on) {
         const int oqj = sm.ring[r].oq[jrow], slot = sm.ring[r].slot[jrow];
         if (g < G) w = sm.w[oqj][g][slot];
         const unsigned long long vm = sm.vmask[sm.ring[r].u];
         km = static_cast<uint32_t>(hf ? (vm >> 32) : vm);
-        if (a.token_keep != nullptr) {       // issued before the S wait, used after it
+        if constexpr (kKeep) {               // issued before the S wait, used after it
           const uint4* kp = reinterpret_cast<const uint4*>(
               a.token_keep + (((b * a.Lq + q0 + oqj) * a.Hkv + hk) * K + slot) * S + 32 * hf);
           keep[0] = __ldg(kp);
@@ -522,13 +523,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         }
       }
       if (!wait_bar_warp(sm, &sm.bar_sdone[p2], (it >> 1) & 1)) break;
-      if (row_on && a.token_keep != nullptr) {
-        const uint32_t wd[8] = {keep[0].x, keep[0].y, keep[0].z, keep[0].w,
-                                keep[1].x, keep[1].y, keep[1].z, keep[1].w};
-        uint32_t kb = 0u;
+      if constexpr (kKeep) {
+        if (row_on) {
+          const uint32_t wd[8] = {keep[0].x, keep[0].y, keep[0].z, keep[0].w,
+                                  keep[1].x, keep[1].y, keep[1].z, keep[1].w};
+          uint32_t kb = 0u;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) kb |= static_cast<uint32_t>(((wd[i >> 2] >> (8 * (i & 3))) & 0xFFu) != 0u) << i;
-        km &= kb;
+          for (int i = 0; i < 32; ++i) kb |= static_cast<uint32_t>(((wd[i >> 2] >> (8 * (i & 3))) & 0xFFu) != 0u) << i;
+          km &= kb;
+        }
       }
       tc::fence_after_sync();
       // Quadrant q holds the rows of owners q and q+4: with fewer than q+1
@@ -789,7 +792,7 @@ bool make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
 
 namespace {
 
-template <bool kF16>
+template <bool kF16, bool kKeep>
 int selected_launch(const void* q, const void* k, const void* v, const uint8_t* key_valid, const void* weights,
                     const int32_t* indices, const void* local_out, const void* local_w, void* out, float sm_scale,
                     int mask_last_token, int64_t batch, int64_t q_len, int64_t kv_len, int64_t kv_heads,
@@ -838,14 +841,15 @@ int selected_launch(const void* q, const void* k, const void* v, const uint8_t* 
   a.K = static_cast<int>(topk);
   a.C = static_cast<int>(kv_len / S);
   const size_t smem = sizeof(TcSmem) + 1024;
-  if (cudaFuncSetAttribute(selected_tc_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (kKeep != (token_keep != nullptr)) return MRSA_ERR_NULL;
+  if (cudaFuncSetAttribute(selected_tc_kernel<kF16, kKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return MRSA_ERR_LAUNCH;
   const int64_t blocks = (q_len + QB - 1) / QB;
   if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(kv_heads),
             static_cast<unsigned>(batch));
-  selected_tc_kernel<kF16><<<grid, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_k, tm_v, tm_q, a);
+  selected_tc_kernel<kF16, kKeep><<<grid, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_k, tm_v, tm_q, a);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
 }
@@ -860,7 +864,7 @@ extern "C" int mrsa_selected_attention(const void* q, const void* k, const void*
                                        int64_t kv_len, int64_t kv_heads, int64_t groups,
                                        int64_t head_dim, int64_t topk, int64_t chunk,
                                        mrsa_stream_t stream) {
-  return selected_launch<false>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+  return selected_launch<false, false>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
                                 mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
                                 stream);
 }
@@ -873,7 +877,7 @@ extern "C" int mrsa_selected_attention_f16v(const void* q, const void* k, const 
                                             int64_t kv_len, int64_t kv_heads, int64_t groups,
                                             int64_t head_dim, int64_t topk, int64_t chunk,
                                             mrsa_stream_t stream) {
-  return selected_launch<true>(q, k, v_f16, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+  return selected_launch<true, false>(q, k, v_f16, key_valid, weights, indices, local_out, local_w, out, sm_scale,
                                mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
                                stream);
 }
@@ -888,12 +892,12 @@ extern "C" int mrsa_selected_attention_keep(const void* q, const void* k, const 
                                             mrsa_stream_t stream) {
   if (token_keep == nullptr) return MRSA_ERR_NULL;
   if (v_f16)
-    return selected_launch<true>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
-                                 mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
-                                 stream, token_keep);
-  return selected_launch<false>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
-                                mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
-                                stream, token_keep);
+    return selected_launch<true, true>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+                                       mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk,
+                                       chunk, stream, token_keep);
+  return selected_launch<false, true>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
+                                      mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk,
+                                      chunk, stream, token_keep);
 }
 
 extern "C" int mrsa_device_error_flags(int clear) {
