@@ -212,6 +212,116 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def _flex_pairs(l: int, window: int, chunk: int) -> int:
+    """Visible (query, key) pairs of the causal chunk-expanded window with the
+    landmark slots masked (training layout, Lq = Lk = l)."""
+    i = torch.arange(l, dtype=torch.int64)
+    start = torch.div(i - window + 1, chunk, rounding_mode="floor").mul(chunk).clamp(min=0)
+    # landmarks (j+1) % chunk == 0 in [start, i]: floor((i+1)/chunk) - floor(start/chunk)
+    lmk = torch.div(i + 1, chunk, rounding_mode="floor") - torch.div(start, chunk, rounding_mode="floor")
+    return int((i - start + 1 - lmk).sum())
+
+
+def run_ops(args):
+    """``--op``: one JSON line per off-path op at Dream shapes (one GPU), timed
+    with CUDA events after warm-up; inputs are regenerated per op."""
+    import __graft_entry__
+
+    mrsa = __graft_entry__.load_package()
+    mrsa.load_library()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, tflops, peak_kind = load_peaks()
+    g = torch.Generator(device=dev).manual_seed(11)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, device=dev, generator=g) * scale).bfloat16()
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def emit(op, workload, ms, unit_count, unit, bound, work, l2_note):
+        if bound == "tensor":
+            ach = work / (ms * 1e-3) / 1e12
+            roof = {"bound": "tensor", "achieved": ach, "peak": tflops, "unit": "TFLOP/s",
+                    "frac": ach / tflops, "traffic": None, "peak_kind": f"{peak_kind} bf16 burst"}
+        else:
+            ach = work / (ms * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                    "traffic": None, "peak_kind": f"{peak_kind} HBM copy"}
+        print(json.dumps({"op": op, "metric": f"{op} {unit}/s", "value": unit_count / (ms * 1e-3),
+                          "unit": f"{unit}/s", "ms_per_call": ms, "higher_is_better": True,
+                          "dtype": "bf16", "data": "synthetic", "n_gpus": 1,
+                          "config": {"workload": workload, "l2": l2_note}, "roofline": roof,
+                          "gpu_launches_per_call": 1}), flush=True)
+
+    ops = ["flex", "cached_local", "token_scores", "dsa", "selected_keep"] if args.op == "all" else [args.op]
+    L = L_PER_GPU
+    for op in ops:
+        if op == "flex":
+            w = 1280
+            q, k, v = rnd(1, L, HQ, D, scale=D ** -0.5), rnd(1, L, HKV, D, scale=D ** -0.5), rnd(1, L, HKV, D)
+            ms = timed(lambda: mrsa.flex_attn_tl(q, k, v, w, CHUNK), args.steps)
+            emit(op, f"flex_attn_tl fwd B=1 L={L} 28/4 heads d=128 window {w} chunk 64, landmarks masked",
+                 ms, L, "tokens", "tensor", HQ * D * 4 * _flex_pairs(L, w, CHUNK),
+                 "inputs (q 117 MB + k/v 33 MB) near L2 size; no flush")
+        elif op == "cached_local":
+            nq = 32
+            q = rnd(1, nq, HQ, D, scale=D ** -0.5)
+            k, v = rnd(1, L, HKV, D, scale=D ** -0.5), rnd(1, L, HKV, D)
+            valid = torch.ones(1, L, dtype=torch.bool, device=dev)
+            pos = torch.arange(L // 2, L // 2 + nq, device=dev)
+            ms = timed(lambda: mrsa.cached_local_attention(q, k, v, valid, pos, WLOC, CHUNK,
+                                                           skip_inert_slots=True), args.steps)
+            wf = WLOC + CHUNK - 1
+            emit(op, f"cached_local_attention: {nq} decode rows against a {L}-token cache, window {WLOC}+63",
+                 ms, nq, "rows", "tensor", HQ * D * 4 * nq * (2 * wf + 1),
+                 "decode-sized; the window's K/V stay in L2 across calls")
+        elif op == "token_scores":
+            k_sel = TOPK
+            q, k = rnd(1, L, HQ, D, scale=D ** -0.5), rnd(1, L, HKV, D)
+            idx = torch.argsort(torch.rand(1, L, HKV, L // CHUNK, device=dev, generator=g), dim=-1)[..., :k_sel]
+            idx = idx.sort(dim=-1).values.to(torch.int32).contiguous()
+            valid = torch.ones(1, L, dtype=torch.bool, device=dev)
+            ms = timed(lambda: mrsa.candidate_token_scores_gqa(q, k, idx, valid, CHUNK), args.steps)
+            out_bytes = L * HKV * k_sel * CHUNK * 4
+            emit(op, f"candidate_token_scores_gqa Lq=Lk={L} 28/4 heads K={k_sel} chunk 64 (fp32 scores out)",
+                 ms, L, "tokens", "hbm", L * HQ * D * 2 + out_bytes + idx.numel() * 4,
+                 f"output {out_bytes >> 20} MB larger than L2")
+        elif op == "dsa":
+            lq, topk = 4096, 2560
+            q = rnd(1, lq, HQ, D, scale=D ** -0.5)
+            k, v = rnd(1, L, HKV, D), rnd(1, L, HKV, D)
+            idx = torch.randint(0, L, (1, lq, topk), device=dev, generator=g)
+            valid = torch.ones(1, lq, topk, dtype=torch.bool, device=dev)
+            ms = timed(lambda: mrsa.selected_token_attention_tilelang(q, k, v, idx, valid), args.steps)
+            emit(op, f"selected_token_attention_tilelang Lq={lq} Lk={L} 28/4 heads top-{topk} tokens",
+                 ms, lq, "tokens", "hbm", lq * HKV * topk * 2 * D * 2,
+                 "work = K and V rows gathered per (query, KV head), mostly L2 hits (k/v 33 MB)")
+        elif op == "selected_keep":
+            q, k, v = rnd(1, L, HQ, D, scale=D ** -0.5), rnd(1, L, HKV, D, scale=D ** -0.5), rnd(1, L, HKV, D)
+            c = L // CHUNK
+            idx = torch.argsort(torch.rand(1, L, HKV, c, device=dev, generator=g), dim=-1)[..., :TOPK]
+            idx = idx.sort(dim=-1).values.to(torch.int32).contiguous()
+            w = torch.softmax(torch.randn(1, L, HQ, TOPK, device=dev, generator=g), -1).bfloat16()
+            keep = torch.rand(1, L, HKV, TOPK, CHUNK, device=dev, generator=g) > 0.4
+            valid = torch.ones(1, L, dtype=torch.bool, device=dev)
+            v16 = mrsa.to_f16(v)
+            ms = timed(lambda: mrsa.selected_attention(q, k, v16, w, idx, valid, token_keep=keep), args.steps)
+            emit(op, f"selected attention with token_keep (60 % kept) L={L} 28/4 heads top-32x64, fp16 V, "
+                 "random sorted chunk lists", ms, L, "tokens", "tensor", L * HQ * TOPK * CHUNK * D * 4,
+                 "inputs larger than L2")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -223,7 +333,12 @@ def main():
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="run N untimed fused layer forwards at the bench workload and exit "
                          "(the target of the ncu captures summarised under profiles/)")
+    ap.add_argument("--op", default=None,
+                    choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "all"],
+                    help="time one off-path op (or all) instead of the route layer; one JSON line each")
     args = ap.parse_args()
+    if args.op:
+        return run_ops(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
