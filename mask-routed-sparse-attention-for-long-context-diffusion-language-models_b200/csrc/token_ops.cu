@@ -13,9 +13,11 @@
 //
 // Neither reuses a key tile across query rows (each row has its own chunk or
 // token list), so both are gathers: one CTA per (query row, KV head), the K
-// (and V) rows read straight from global memory / L2, fp32 FMAs against the
-// group's query rows held in shared memory.  Their bound is the gather (L2
-// bandwidth) and the FMA issue rate, not the tensor cores.
+// (and V) rows read straight from global memory / L2.  The scores run as
+// mma.sync m16n8k16 tiles (16 rows = the group's <= 16 heads, 8 gathered keys
+// per tile): tcgen05's smallest tile has 64 rows, of which a single query's
+// group fills 7, so the warp-level MMA is the better fit for these shapes.
+// The selected-token P.V stays on fp32 FMAs.
 #include "common.cuh"
 
 using namespace mrsa;
@@ -26,141 +28,187 @@ constexpr int D = kHeadDim;
 constexpr int TS_THREADS = 128;
 constexpr int MAXG = 16;
 
-// 8 bf16 (one 16-byte load) -> fp32
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
-}
+// ---- m16n8k16 fragments over gathered key rows ------------------------------
+// S[heads x keys] = Q[heads x 128] . K[keys x 128]^T as mma.sync m16n8k16
+// (bf16 in, fp32 accumulate): 16 A rows = the group's heads (G <= 16, the rest
+// zero), 8 keys per n-tile.  The dot product does not depend on the order of
+// the 128 dims, so dims are assigned to fragment slots such that lane (r, j)
+// = (lane / 4, lane % 4) needs dims [32j, 32j + 32) of its rows in every
+// k-step: logical k-index kk of step s is dim 32*((kk % 8) / 2) + 4*s +
+// (kk % 2) + 2*(kk / 8).  Each lane then reads one contiguous 64-byte quarter
+// of its key row (four 16-byte loads) and one of each of its query rows, and
+// the words of those quarters are the b0/b1 (a0/a2, a1/a3) registers of the
+// eight k-steps in order.
+struct QFrag {
+  uint32_t a[8][4];
+};
 
-// acc[g] += q_g[8p .. 8p+7] . kf, g < G (query rows fp32 in shared memory)
-__device__ __forceinline__ void dot8(float (&acc)[MAXG], const float (*qs)[D], int G, int p, const float (&kf)[8]) {
+__device__ __forceinline__ void load_qfrag(QFrag& f, const __nv_bfloat16* q_group, int G, int lane) {
+  const int r = lane >> 2, j = lane & 3;
 #pragma unroll
-  for (int g = 0; g < MAXG; ++g) {
-    if (g < G) {
-      const float4 q0 = *reinterpret_cast<const float4*>(&qs[g][8 * p]);
-      const float4 q1 = *reinterpret_cast<const float4*>(&qs[g][8 * p + 4]);
-      float a = acc[g];
-      a = fmaf(q0.x, kf[0], a); a = fmaf(q0.y, kf[1], a); a = fmaf(q0.z, kf[2], a); a = fmaf(q0.w, kf[3], a);
-      a = fmaf(q1.x, kf[4], a); a = fmaf(q1.y, kf[5], a); a = fmaf(q1.z, kf[6], a); a = fmaf(q1.w, kf[7], a);
-      acc[g] = a;
+  for (int half = 0; half < 2; ++half) {
+    const int row = r + 8 * half;
+    uint32_t w[16];
+    if (row < G) {
+      const uint4* p = reinterpret_cast<const uint4*>(q_group + row * D + 32 * j);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 u = __ldg(p + i);
+        w[4 * i] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = 0u;
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      f.a[s][half] = w[2 * s];          // a0 (rows 0-7) / a1 (rows 8-15)
+      f.a[s][2 + half] = w[2 * s + 1];  // a2 / a3
     }
   }
 }
 
-__device__ __forceinline__ void load_group_q(float (*qs)[D], const __nv_bfloat16* q, int G, int tid) {
-  for (int e = tid; e < G * D / 2; e += TS_THREADS) {
-    const float2 v = unpack_bf16x2(reinterpret_cast<const uint32_t*>(q)[e]);
-    qs[(2 * e) / D][(2 * e) % D] = v.x;
-    qs[(2 * e) / D][(2 * e) % D + 1] = v.y;
+// C[16 heads x 8 keys] of one n-tile whose key row (this lane's key r) is `krow`
+// (NULL: a masked key, read as zeros).
+__device__ __forceinline__ void mma_keys(float (&c)[4], const QFrag& f, const __nv_bfloat16* krow, int lane) {
+  uint32_t w[16];
+  if (krow != nullptr) {
+    const uint4* p = reinterpret_cast<const uint4*>(krow + 32 * (lane & 3));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = __ldg(p + i);
+      w[4 * i] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = 0u;
   }
+  c[0] = c[1] = c[2] = c[3] = 0.f;
+#pragma unroll
+  for (int s = 0; s < 8; ++s) mma_bf16(c, f.a[s], w[2 * s], w[2 * s + 1]);
 }
 
-// grid (Lq, Hkv, B); warp w takes selected chunks w, w+4, ...; lane takes
-// slots s0+lane and s0+32+lane of each 64-slot step.
+// grid (Lq, Hkv, B), 4 warps; warp w takes selected chunks w, w+4, ...  Per
+// chunk, n-tile nt covers slots 8nt .. 8nt+7; the max over the G head rows is
+// reduced across the eight lanes that share a column pair, and lane (r, j)
+// keeps the result of n-tile r (mod 8): slots 8r + 2j, 8r + 2j + 1 of each
+// 64-slot group, which the warp then writes as 64 contiguous floats.
 __global__ void __launch_bounds__(TS_THREADS) token_score_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
     const int32_t* __restrict__ indices, const uint8_t* __restrict__ key_valid, float* __restrict__ scores,
     float sm_scale, int64_t Lq, int64_t Lk, int Hkv, int G, int K, int S) {
-  __shared__ __align__(16) float qs[MAXG][D];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, j = lane & 3;
   const int64_t l = blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
   const int64_t C = Lk / S;
   const int64_t row = (static_cast<int64_t>(b) * Lq + l) * Hkv + h;   // (b, l, h)
-  load_group_q(qs, q + (row * G) * D, G, tid);
-  __syncthreads();
+  QFrag f;
+  load_qfrag(f, q + (row * G) * D, G, lane);
+  const int ntiles = (S + 7) / 8;
 
   for (int i = warp; i < K; i += TS_THREADS / 32) {
     const int64_t c = indices[row * K + i];
     float* out = scores + (row * K + i) * S;
     const bool chunk_ok = c >= 0 && c < C;
-    for (int s0 = 0; s0 < S; s0 += 64) {
-      const int sa = s0 + lane, sb = s0 + 32 + lane;
-      const int64_t ja = c * S + sa, jb = c * S + sb;
-      const bool oka = chunk_ok && sa < S - 1 && (key_valid == nullptr || key_valid[b * Lk + ja] != 0);
-      const bool okb = chunk_ok && sb < S - 1 && (key_valid == nullptr || key_valid[b * Lk + jb] != 0);
-      float acca[MAXG], accb[MAXG];
-#pragma unroll
-      for (int g = 0; g < MAXG; ++g) acca[g] = accb[g] = 0.f;
-      if (__any_sync(0xffffffffu, oka || okb)) {
-        const uint4* ka = reinterpret_cast<const uint4*>(k + ((b * Lk + (oka ? ja : 0)) * Hkv + h) * D);
-        const uint4* kb = reinterpret_cast<const uint4*>(k + ((b * Lk + (okb ? jb : 0)) * Hkv + h) * D);
+    for (int g0 = 0; g0 < ntiles; g0 += 8) {         // 64-slot groups
+      float keep0 = -INFINITY, keep1 = -INFINITY;
 #pragma unroll 2
-        for (int p = 0; p < D / 8; ++p) {
-          float fa[8], fb[8];
-          const uint4 ua = oka ? __ldg(ka + p) : make_uint4(0, 0, 0, 0);
-          const uint4 ub = okb ? __ldg(kb + p) : make_uint4(0, 0, 0, 0);
-          unpack8(ua, fa);
-          unpack8(ub, fb);
-          dot8(acca, qs, G, p, fa);
-          dot8(accb, qs, G, p, fb);
+      for (int t = 0; t < 8; ++t) {
+        const int nt = g0 + t;
+        if (nt >= ntiles) break;                      // warp-uniform
+        const int s_key = 8 * nt + r;                 // this lane's key (B column)
+        const __nv_bfloat16* krow = nullptr;
+        if (chunk_ok && s_key < S) krow = k + ((b * Lk + c * S + s_key) * Hkv + h) * D;
+        float acc[4];
+        mma_keys(acc, f, krow, lane);
+        // max over the head rows r (< G) and r + 8 (< G) of columns 2j, 2j+1
+        float m0 = r < G ? acc[0] : -INFINITY, m1 = r < G ? acc[1] : -INFINITY;
+        if (r + 8 < G) {
+          m0 = fmaxf(m0, acc[2]);
+          m1 = fmaxf(m1, acc[3]);
+        }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+          m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+        }
+        if (r == t) {
+          keep0 = m0;
+          keep1 = m1;
         }
       }
-      float ma = -INFINITY, mb = -INFINITY;
+      // slots 8*(g0 + r) + 2j, +1; -inf for masked slots
+      const int sa = 8 * (g0 + r) + 2 * j;
 #pragma unroll
-      for (int g = 0; g < MAXG; ++g)
-        if (g < G) {
-          ma = fmaxf(ma, acca[g]);
-          mb = fmaxf(mb, accb[g]);
+      for (int e = 0; e < 2; ++e) {
+        const int sl = sa + e;
+        if (sl < S) {
+          const bool ok = chunk_ok && sl < S - 1 && (key_valid == nullptr || key_valid[b * Lk + c * S + sl] != 0);
+          out[sl] = ok ? (e ? keep1 : keep0) * sm_scale : -INFINITY;
         }
-      if (sa < S) out[sa] = oka ? ma * sm_scale : -INFINITY;
-      if (sb < S) out[sb] = okb ? mb * sm_scale : -INFINITY;
+      }
     }
   }
 }
 
 // Shared memory of the selected-token kernel (dynamic; tp = topk rounded up
 // to a multiple of 4 so every region starts on 16 bytes):
-//   qs[G][D] f32 | prob[G][tp] f32 | tok[tp] int32 | red[4][G][D] f32
+//   prob[G][tp] f32 | tok[tp] int32 | red[4][G][D] f32
 __host__ __device__ inline int sta_pad(int topk) { return (topk + 3) & ~3; }
 __host__ __device__ inline size_t sta_smem_bytes(int G, int topk) {
   const size_t tp = static_cast<size_t>(sta_pad(topk));
-  return static_cast<size_t>(G) * D * 4 + static_cast<size_t>(G) * tp * 4 + tp * 4 +
-         static_cast<size_t>(TS_THREADS / 32) * G * D * 4;
+  return static_cast<size_t>(G) * tp * 4 + tp * 4 + static_cast<size_t>(TS_THREADS / 32) * G * D * 4;
 }
 
-// grid (Lq, Hkv, B).  Pass 1: thread per token, raw scores of the G heads.
-// Softmax: warp per head.  Pass 2: warp per token residue class, lane per 4
-// dims, fp32 accumulation of bf16(P) x V; the four warps' partial rows are
-// summed through shared memory.
+// grid (Lq, Hkv, B).  Pass 1: the raw scores of the G heads as m16n8k16
+// tiles of 8 gathered tokens (warp w takes tiles w, w+4, ...).  Softmax: warp
+// per head.  Pass 2: warp per group of eight tokens, lane per 4 dims, fp32
+// accumulation of bf16(P) x V; the four warps' partial rows are summed
+// through shared memory.
 __global__ void __launch_bounds__(TS_THREADS) selected_token_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     const int32_t* __restrict__ indices, const uint8_t* __restrict__ valid, __nv_bfloat16* __restrict__ out,
     float sm_scale, int64_t Lq, int64_t Lk, int Hkv, int G, int topk) {
   extern __shared__ __align__(16) float dyn[];
-  float (*qs)[D] = reinterpret_cast<float (*)[D]>(dyn);
   const int tp = sta_pad(topk);
-  float* prob = dyn + G * D;                     // prob[g * tp + t]
+  float* prob = dyn;                             // prob[g * tp + t]
   int32_t* tok = reinterpret_cast<int32_t*>(prob + static_cast<size_t>(G) * tp);
   float* red = reinterpret_cast<float*>(tok + tp);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t l = blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
   const int64_t qrow = static_cast<int64_t>(b) * Lq + l;                 // (b, l)
-  load_group_q(qs, q + ((qrow * Hkv + h) * G) * D, G, tid);
-  __syncthreads();
-
-  // pass 1: scores
+  // token list: clamped indices, -1 where not valid
   for (int t = tid; t < topk; t += TS_THREADS) {
     int64_t j = indices[qrow * topk + t];
     j = j < 0 ? 0 : (j > Lk - 1 ? Lk - 1 : j);
-    const bool ok = valid[qrow * topk + t] != 0;
-    tok[t] = ok ? static_cast<int32_t>(j) : -1;
-    float acc[MAXG];
+    tok[t] = valid[qrow * topk + t] != 0 ? static_cast<int32_t>(j) : -1;
+  }
+  QFrag f;
+  load_qfrag(f, q + ((qrow * Hkv + h) * G) * D, G, lane);
+  __syncthreads();
+
+  // pass 1: scores, 8 tokens per n-tile; lane (r, j) gathers token 8nt + r
+  // and gets columns 2j, 2j+1 of head rows r and r + 8
+  {
+    const int r = lane >> 2, j = lane & 3;
+    for (int nt = warp; nt * 8 < topk; nt += TS_THREADS / 32) {
+      const int tk = 8 * nt + r;
+      const int jt = tk < topk ? tok[tk] : -1;
+      const __nv_bfloat16* krow = jt >= 0 ? k + ((b * Lk + jt) * Hkv + h) * D : nullptr;
+      float acc[4];
+      mma_keys(acc, f, krow, lane);
 #pragma unroll
-    for (int g = 0; g < MAXG; ++g) acc[g] = 0.f;
-    if (ok) {
-      const uint4* kr = reinterpret_cast<const uint4*>(k + ((b * Lk + j) * Hkv + h) * D);
-#pragma unroll 2
-      for (int p = 0; p < D / 8; ++p) {
-        float f[8];
-        unpack8(__ldg(kr + p), f);
-        dot8(acc, qs, G, p, f);
+      for (int e = 0; e < 2; ++e) {
+        const int tc = 8 * nt + 2 * j + e;
+        if (tc < topk) {
+          const bool ok = tok[tc] >= 0;
+          if (r < G) prob[static_cast<size_t>(r) * tp + tc] = ok ? acc[e] * sm_scale : -INFINITY;
+          if (r + 8 < G) prob[static_cast<size_t>(r + 8) * tp + tc] = ok ? acc[2 + e] * sm_scale : -INFINITY;
+        }
       }
     }
-#pragma unroll
-    for (int g = 0; g < MAXG; ++g)
-      if (g < G) prob[static_cast<size_t>(g) * tp + t] = ok ? acc[g] * sm_scale : -INFINITY;
   }
   __syncthreads();
 
@@ -184,20 +232,32 @@ __global__ void __launch_bounds__(TS_THREADS) selected_token_kernel(
   float acc[MAXG][4];
 #pragma unroll
   for (int g = 0; g < MAXG; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
-  for (int t = warp; t < topk; t += TS_THREADS / 32) {
-    const int32_t j = tok[t];
-    if (j < 0) continue;   // warp-uniform
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(v + ((b * Lk + j) * Hkv + h) * D) + lane);
-    const float2 v01 = unpack_bf16x2(u.x), v23 = unpack_bf16x2(u.y);
+  // eight tokens per round: their V rows are all requested before any is used
+  constexpr int TB = 8;
+  for (int t0 = warp * TB; t0 < topk; t0 += TB * (TS_THREADS / 32)) {
+    uint2 u[TB];
 #pragma unroll
-    for (int g = 0; g < MAXG; ++g)
-      if (g < G) {
-        const float p = prob[static_cast<size_t>(g) * tp + t];
-        acc[g][0] = fmaf(p, v01.x, acc[g][0]);
-        acc[g][1] = fmaf(p, v01.y, acc[g][1]);
-        acc[g][2] = fmaf(p, v23.x, acc[g][2]);
-        acc[g][3] = fmaf(p, v23.y, acc[g][3]);
-      }
+    for (int e = 0; e < TB; ++e) {
+      const int t = t0 + e;
+      const int32_t j = t < topk ? tok[t] : -1;
+      u[e] = j >= 0 ? __ldg(reinterpret_cast<const uint2*>(v + ((b * Lk + j) * Hkv + h) * D) + lane)
+                    : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int e = 0; e < TB; ++e) {
+      const int t = t0 + e;
+      if (t >= topk) break;                   // warp-uniform
+      const float2 v01 = unpack_bf16x2(u[e].x), v23 = unpack_bf16x2(u[e].y);
+#pragma unroll
+      for (int g = 0; g < MAXG; ++g)
+        if (g < G) {
+          const float p = prob[static_cast<size_t>(g) * tp + t];   // 0 for invalid tokens
+          acc[g][0] = fmaf(p, v01.x, acc[g][0]);
+          acc[g][1] = fmaf(p, v01.y, acc[g][1]);
+          acc[g][2] = fmaf(p, v23.x, acc[g][2]);
+          acc[g][3] = fmaf(p, v23.y, acc[g][3]);
+        }
+    }
   }
 #pragma unroll
   for (int g = 0; g < MAXG; ++g)

@@ -150,8 +150,8 @@ def test_token_ops_and_flex_reject_bad_arguments(mrsa):
     assert lib.mrsa_selected_token_attention(d, d, d, d, None, d, 0.1, 1, 4, 256, 28, 4, 128, 8, None) == -1
     assert lib.mrsa_selected_token_attention(d, d, d, d, d, d, 0.1, 1, 4, 256, 34, 2, 128, 8, None) == -2
     assert lib.mrsa_selected_token_attention(d, d, d, d, d, d, 0.1, 1, 4, 256, 28, 4, 128, 20000, None) == -2
-    assert lib.mrsa_selected_token_attention_smem(7, 2560) == 7 * 512 + 7 * 2560 * 4 + 2560 * 4 + 4 * 7 * 512
-    assert lib.mrsa_selected_token_attention_smem(7, 101) == 7 * 512 + 7 * 104 * 4 + 104 * 4 + 4 * 7 * 512
+    assert lib.mrsa_selected_token_attention_smem(7, 2560) == 7 * 2560 * 4 + 2560 * 4 + 4 * 7 * 512
+    assert lib.mrsa_selected_token_attention_smem(7, 101) == 7 * 104 * 4 + 104 * 4 + 4 * 7 * 512
     assert lib.mrsa_selected_token_attention_smem(17, 64) == 0
 
 
