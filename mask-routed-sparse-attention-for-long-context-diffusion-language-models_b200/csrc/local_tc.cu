@@ -161,9 +161,23 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       tc::mbar_arrive_expect_tx(qb, LQ * 2048u);
       tc::tma_load_4d(tc::smem_addr(&sm.q[0][0]), &tm_q, 0, hk * G, 0, static_cast<int>(b * a.Lq + q0), qb);
     }
+    // key-validity bytes of tile tt (this lane's keys 32h + lane), requested one
+    // tile ahead so their latency is not on the copy-issue path
+    auto valid_bytes = [&](int tt, uint32_t (&vb)[2]) {
+      const int64_t jt = static_cast<int64_t>(t_lo + tt) * LN;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t j = jt + 32 * h + lane;
+        vb[h] = (a.key_valid != nullptr && tt < NTL && j < a.Lk) ? a.key_valid[b * a.Lk + j] : 1u;
+      }
+    };
+    uint32_t vb_next[2];
+    valid_bytes(0, vb_next);
     int t = 0;
     for (; t < NTL; ++t) {
       const int st = t % LST;
+      const uint32_t vb[2] = {vb_next[0], vb_next[1]};
+      valid_bytes(t + 1, vb_next);
       if (t >= LST && !tc::wait_bounded_warp(tc::smem_addr(&sm.kvfree[st]), ((t / LST) - 1) & 1, abort_flag)) break;
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
       // usable keys of the tile: inside the sequence, valid, and not a landmark slot when skip_inert
@@ -171,8 +185,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int64_t j = j0 + 32 * h + lane;
-        bool ok = j < a.Lk;
-        if (ok && a.key_valid != nullptr) ok = a.key_valid[b * a.Lk + j] != 0;
+        bool ok = j < a.Lk && vb[h] != 0u;
         if (ok && a.skip_inert) ok = ((j + a.shift + 1) % a.chunk) != 0;
         mk[h] = __ballot_sync(0xffffffffu, ok);
       }
