@@ -14,9 +14,12 @@
 // keeping ~16 significant bits.  Each row keeps a reference max that moves
 // (rescaling O in TMEM between the P.V of tile t-1 and that of tile t) only
 // when a tile max exceeds it by more than 2^8.
-// Warps 0-3: softmax and epilogue (warp w = TMEM lanes 32w..32w+31 = rows);
-// warp 4: TMA (Q once, then K, V per tile, 3 stages) and the per-tile key
-// validity mask; warp 5: MMA issue (converged, elect.sync).  Every mbarrier
+// Warps 0-7: softmax and epilogue in two groups of four (warp w = TMEM lanes
+// 32(w%4)..+31 = rows); group g takes the tiles t with t % 2 == g and keeps
+// its own running max, sum and O accumulator, so two softmax warps share each
+// scheduler; the epilogue merges the two partial softmaxes.  Warp 8: TMA (Q
+// once, then K, V per tile, 3 stages) and the per-tile key validity mask;
+// warp 9: MMA issue (converged, elect.sync).  Every mbarrier
 // wait is bounded and unwinds through a shared abort flag.
 //
 // The same kernel also runs the causal chunk-expanded window of
@@ -40,9 +43,9 @@ constexpr int LQ = 16;            // queries per CTA
 constexpr int LN = 64;            // keys per tile
 constexpr int LST = 3;            // K/V stages
 constexpr int D = kHeadDim;
-constexpr int L_THREADS = 192;    // warps 0-3 softmax, 4 TMA, 5 MMA
-constexpr int L_W_LOAD = 4, L_W_MMA = 5;
-constexpr uint32_t kOCol = 128;   // O accumulator columns [128, 256); S buffers at 0 and 64
+constexpr int L_THREADS = 320;    // warps 0-7 softmax (two groups), 8 TMA, 9 MMA
+constexpr int L_W_LOAD = 8, L_W_MMA = 9;
+constexpr uint32_t kOCol = 128;   // O accumulators of groups 0 / 1 at [128, 256) / [256, 384); S at 0 and 64
 
 struct __align__(1024) LocalSmem {
   unsigned char q[LQ][2048];          // per query: [half][8 head rows][64 dims], 128-byte swizzled
@@ -51,6 +54,7 @@ struct __align__(1024) LocalSmem {
   unsigned char ph[2][16384];         // P hi [128 rows][64 keys]
   unsigned char pl[2][16384];         // P lo
   unsigned long long kmask[LST];      // bit j: key j of the stage's tile is usable (not zeroed)
+  float part_m[2][128], part_l[2][128];   // per group and row: running max / sum for the merge
   uint64_t qfull, kvfull[LST], kvfree[LST], sdone[2], pready[2], pvdone[2], drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -143,7 +147,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     tc::fence_mbar_init();
   }
   if (warp == 0) {
-    tc::tmem_alloc(tc::smem_addr(&sm.tmem_base), 256);
+    tc::tmem_alloc(tc::smem_addr(&sm.tmem_base), 512);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -239,16 +243,17 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       tc::fence_after_sync();
       const uint64_t dv = tc::desc_adv(dv0, st * 16384), dh = tc::desc_adv(dh0, p2 * 16384),
                      dl = tc::desc_adv(dl0, p2 * 16384);
+      const uint32_t dO = tbase + kOCol + D * p2;       // group p2's accumulator
       if (tc::elect_one()) {
-        // the first tile's P.V overwrites O (TMEM is not zeroed)
-        if (t == 0) tc::mma_bf16<false>(tbase + kOCol, dh, dv, id_o);
-        else tc::mma_bf16<true>(tbase + kOCol, dh, dv, id_o);
+        // each group's first tile overwrites its O (TMEM is not zeroed)
+        if (t < 2) tc::mma_bf16<false>(dO, dh, dv, id_o);
+        else tc::mma_bf16<true>(dO, dh, dv, id_o);
 #pragma unroll
-        for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+        for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dO, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
         if constexpr (!kF16) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc::mma_bf16<true>(tbase + kOCol, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+            tc::mma_bf16<true>(dO, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
         }
         tc::mma_commit(tc::smem_addr(&sm.pvdone[p2]));
         tc::mma_commit(tc::smem_addr(&sm.kvfree[st]));
@@ -262,9 +267,11 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     }
     __syncwarp();
   } else {
-    // ============================ softmax + epilogue (warps 0-3) ==============
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const int r = warp * 32 + lane;                  // MMA row = TMEM lane
+    // ============================ softmax + epilogue (warps 0-7) ==============
+    const int grp = warp >> 2;                       // tiles t with t % 2 == grp
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t o_col = kOCol + D * grp;          // this group's O accumulator
+    const int r = (warp & 3) * 32 + lane;            // MMA row = TMEM lane
     const int qi = r >> 3, g = r & 7;
     const int64_t pos = a.qpos != nullptr ? a.qpos[q0 + (qi < rows_q ? qi : rows_q - 1)] : a.q_offset + q0 + qi;
     const float sl2 = a.sm_scale * kLog2e;
@@ -274,7 +281,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     if (band_hi > a.Lk - 1) band_hi = a.Lk - 1;
     const uint32_t fill = a.exclude ? __float_as_uint(-INFINITY) : 0u;
     bool ok = true;
-    for (int t = 0; t < NTL; ++t) {
+    for (int t = grp; t < NTL; t += 2) {
       const int st = t % LST, p2 = t & 1;
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
       if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st]), (t / LST) & 1, abort_flag))) break;
@@ -368,22 +375,23 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
           *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
       }
       if (__any_sync(0xffffffffu, rescale)) {
-        // O must hold every earlier tile before it is scaled: wait for the P.V of tile t-1
-        if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[(t - 1) & 1]), ((t - 1) >> 1) & 1, abort_flag))) break;
+        // O must hold every earlier tile of this group before it is scaled: the
+        // P.V of tile t-2, already waited for above (a rescale needs an earlier
+        // tile, so t >= 2 here)
         tc::fence_after_sync();
         const float c = rescale ? o_scale : 1.f;
 #pragma unroll
         for (int cc = 0; cc < D; cc += 32) {
           uint32_t o[32];
-          tc::tmem_ld16(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-          tc::tmem_ld16(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+          tc::tmem_ld16(tbase + lane_off + o_col + cc, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+          tc::tmem_ld16(tbase + lane_off + o_col + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * c);
-          tc::tmem_st8(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[8]>(&o[0]));
-          tc::tmem_st8(tbase + lane_off + kOCol + cc + 8, *reinterpret_cast<uint32_t(*)[8]>(&o[8]));
-          tc::tmem_st8(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[8]>(&o[16]));
-          tc::tmem_st8(tbase + lane_off + kOCol + cc + 24, *reinterpret_cast<uint32_t(*)[8]>(&o[24]));
+          tc::tmem_st8(tbase + lane_off + o_col + cc, *reinterpret_cast<uint32_t(*)[8]>(&o[0]));
+          tc::tmem_st8(tbase + lane_off + o_col + cc + 8, *reinterpret_cast<uint32_t(*)[8]>(&o[8]));
+          tc::tmem_st8(tbase + lane_off + o_col + cc + 16, *reinterpret_cast<uint32_t(*)[8]>(&o[16]));
+          tc::tmem_st8(tbase + lane_off + o_col + cc + 24, *reinterpret_cast<uint32_t(*)[8]>(&o[24]));
         }
         tc::tmem_wait_st();
       }
@@ -392,32 +400,56 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.pready[p2]));
     }
-    // ---- epilogue: O / l, bf16 rows, natural-log LSE
-    if (ok && NTL > 0)
-      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[(NTL - 1) & 1]), ((NTL - 1) >> 1) & 1, abort_flag);
+    // ---- epilogue: merge the two groups' partial softmaxes, bf16 rows, LSE
+    // (natural log).  Each group's last tile is t_last(g); a group without
+    // tiles never wrote its O, which is then left out.  The barrier puts both
+    // groups past their loops, so each waits at most one phase ahead.
+    const bool has0 = NTL > 0, has1 = NTL > 1;
+    sm.part_m[grp][r] = m_run;
+    sm.part_l[grp][r] = l_run;
+    asm volatile("bar.sync 1, 256;\n" ::: "memory");
+    if (ok && has0)
+      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[0]), ((NTL - 1 - ((NTL - 1) & 1)) >> 1) & 1, abort_flag);
+    if (ok && has1)
+      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[1]), ((NTL - 1 - (NTL & 1)) >> 1) & 1, abort_flag);
     tc::fence_after_sync();
     if (__all_sync(0xffffffffu, ok) && !__any_sync(0xffffffffu, *abort_flag != 0)) {
+      const float m0 = sm.part_m[0][r], m1 = sm.part_m[1][r];
+      const float m = fmaxf(m0, m1);
+      const float f0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
+      const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
+      const float l = sm.part_l[0][r] * f0 + sm.part_l[1][r] * f1;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float c0 = f0 * inv, c1 = f1 * inv;
       const bool row_ok = g < G && qi < rows_q;
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       const int64_t orow = ((b * a.Lq + q0 + qi) * a.Hq + hk * G + g);
+      // group 0 writes dims 0-63, group 1 dims 64-127
 #pragma unroll
-      for (int cc = 0; cc < D; cc += 32) {
-        uint32_t o[32];
-        tc::tmem_ld16(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-        tc::tmem_ld16(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+      for (int cc = grp * (D / 2); cc < (grp + 1) * (D / 2); cc += 32) {
+        uint32_t o0[32], o1[32];
+        if (has0) {
+          tc::tmem_ld16(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[16]>(&o0[0]));
+          tc::tmem_ld16(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o0[16]));
+        }
+        if (has1) {
+          tc::tmem_ld16(tbase + lane_off + kOCol + D + cc, *reinterpret_cast<uint32_t(*)[16]>(&o1[0]));
+          tc::tmem_ld16(tbase + lane_off + kOCol + D + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o1[16]));
+        }
         tc::tmem_wait_ld();
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          o[i] = (has0 ? __uint_as_float(o0[i]) * c0 : 0.f) + (has1 ? __uint_as_float(o1[i]) * c1 : 0.f);
         if (row_ok) {
           uint4* dst = reinterpret_cast<uint4*>(a.out + orow * D + cc);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
-                                pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
-                                pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
-                                pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+            dst[i] = make_uint4(pack_bf16x2(o[8 * i], o[8 * i + 1]), pack_bf16x2(o[8 * i + 2], o[8 * i + 3]),
+                                pack_bf16x2(o[8 * i + 4], o[8 * i + 5]), pack_bf16x2(o[8 * i + 6], o[8 * i + 7]));
         }
       }
-      if (row_ok && a.lse != nullptr)
-        a.lse[orow] = l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+      if (grp == 0 && row_ok && a.lse != nullptr)
+        a.lse[orow] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
     }
   }
 
@@ -426,7 +458,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   if (tid == 0 && sm.abort_flag) atomicOr(&g_local_error, 1);
   if (warp == 0) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tbase, 256);
+    tc::tmem_dealloc(tbase, 512);
   }
 }
 
