@@ -265,6 +265,21 @@ def run_ops(args):
                           "gpu_launches_per_call": 1}), flush=True)
 
     ops = ["flex", "cached_local", "token_scores", "dsa", "selected_keep"] if args.op == "all" else [args.op]
+    if "dream" in ops:
+        # the whole Dream-shaped forward, B=1, L=32768, random weights
+        from mrsa_b200.dream_forward import DreamConfig, DreamForward, landmark_inputs, model_parameters
+
+        cfg = DreamConfig()
+        model = DreamForward(cfg, seed=0, device=dev)
+        lseq = 32768
+        ids, pos, _ = landmark_inputs(1, lseq, cfg, mask_id=cfg.vocab - 1, device=dev)
+        valid = torch.ones(1, lseq, dtype=torch.bool, device=dev)
+        ms = timed(lambda: model(ids, pos, valid), max(1, args.steps))
+        emit("dream", f"Dream-7B-shaped forward B=1 L={lseq}: 28 layers (7 route, 21 SWA-1280), hidden 3584, "
+             f"FFN 18944, vocab 152064, {model_parameters(cfg) / 1e9:.2f} B random N(0,0.02) parameters, "
+             "logits out", ms, lseq, "tokens", "tensor", lseq * model.flops_per_token(lseq),
+             "weights 15 GB and activations larger than L2")
+        ops = [o for o in ops if o != "dream"]
     L = L_PER_GPU
     for op in ops:
         if op == "flex":
@@ -334,7 +349,7 @@ def main():
                     help="run N untimed fused layer forwards at the bench workload and exit "
                          "(the target of the ncu captures summarised under profiles/)")
     ap.add_argument("--op", default=None,
-                    choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "all"],
+                    choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "dream", "all"],
                     help="time one off-path op (or all) instead of the route layer; one JSON line each")
     args = ap.parse_args()
     if args.op:

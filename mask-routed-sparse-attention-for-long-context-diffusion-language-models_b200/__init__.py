@@ -10,6 +10,7 @@ library is missing.
 
 from . import _lib
 from .chunk_pool import chunk_attn_pool_gqa
+from .dream_forward import DreamConfig, DreamForward
 from .layer import RouteLayer, RouteLayerConfig, swa_layer_forward
 from .local_attention import (bidir_local_attention, cached_local_attention, flex_attn_tl,
                               window_attention)
@@ -22,7 +23,7 @@ from .selected_attention import (HiLS_block_M_head, fuse_hils_outputs, selected_
 from .token_ops import candidate_token_scores_gqa, selected_token_attention_tilelang
 
 __all__ = [
-    "RouteLayer", "RouteLayerConfig", "swa_layer_forward", "chunk_attn_pool_gqa",
+    "DreamConfig", "DreamForward", "RouteLayer", "RouteLayerConfig", "swa_layer_forward", "chunk_attn_pool_gqa",
     "bidir_local_attention", "cached_local_attention", "window_attention", "rope_rotary_pos_emb",
     "single_tensor_rope_autograd", "yarn_inv_freq", "yarn_rope_qk", "route_weights",
     "route_weights_torch", "online_softmax_topk_head", "ref_softmax_topk_max_pooling",
