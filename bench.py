@@ -249,7 +249,7 @@ def run_ops(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
-    def emit(op, workload, ms, unit_count, unit, bound, work, l2_note):
+    def emit(op, workload, ms, unit_count, unit, bound, work, l2_note, launches=1):
         if bound == "tensor":
             ach = work / (ms * 1e-3) / 1e12
             roof = {"bound": "tensor", "achieved": ach, "peak": tflops, "unit": "TFLOP/s",
@@ -262,7 +262,7 @@ def run_ops(args):
                           "unit": f"{unit}/s", "ms_per_call": ms, "higher_is_better": True,
                           "dtype": "bf16", "data": "synthetic", "n_gpus": 1,
                           "config": {"workload": workload, "l2": l2_note}, "roofline": roof,
-                          "gpu_launches_per_call": 1}), flush=True)
+                          "gpu_launches_per_call": launches}), flush=True)
 
     ops = ["flex", "cached_local", "token_scores", "dsa", "selected_keep"] if args.op == "all" else [args.op]
     if "dream" in ops:
@@ -278,7 +278,9 @@ def run_ops(args):
         emit("dream", f"Dream-7B-shaped forward B=1 L={lseq}: 28 layers (7 route, 21 SWA-1280), hidden 3584, "
              f"FFN 18944, vocab 152064, {model_parameters(cfg) / 1e9:.2f} B random N(0,0.02) parameters, "
              "logits out", ms, lseq, "tokens", "tensor", lseq * model.flops_per_token(lseq),
-             "weights 15 GB and activations larger than L2")
+             "weights 15 GB and activations larger than L2",
+             # this repository's kernels: 8 per route layer, RoPE + V to fp16 + window per SWA layer
+             launches=7 * LAUNCHES_PER_STEP + 21 * 3)
         ops = [o for o in ops if o != "dream"]
     L = L_PER_GPU
     for op in ops:
