@@ -264,7 +264,30 @@ def run_ops(args):
                           "config": {"workload": workload, "l2": l2_note}, "roofline": roof,
                           "gpu_launches_per_call": launches}), flush=True)
 
-    ops = ["flex", "cached_local", "token_scores", "dsa", "selected_keep"] if args.op == "all" else [args.op]
+    ops = (["swa", "flex", "cached_local", "token_scores", "dsa", "selected_keep"] if args.op == "all"
+           else [args.op])
+    L = L_PER_GPU
+    if "swa" in ops:
+        # one bidirectional SWA-1280 layer, B=4, L=16384 (RoPE + window attention)
+        bsz, w = 4, 1280
+        qp, kp = rnd(bsz, L, HQ, D, scale=D ** -0.5), rnd(bsz, L, HKV, D, scale=D ** -0.5)
+        v = rnd(bsz, L, HKV, D, scale=D ** -0.5)
+        i = torch.arange(L, device=dev)
+        pos = (i - i // CHUNK).expand(bsz, L).contiguous()
+        valid = torch.ones(bsz, L, dtype=torch.bool, device=dev)
+        inv, af = mrsa.yarn_inv_freq(D, 1.0e6, 8.0, 2048)
+        inv = inv.to(dev)
+
+        def swa():
+            q, k = mrsa.yarn_rope_qk(qp, kp, pos, inv, af)
+            return mrsa.window_attention(q, k, mrsa.to_f16(v), valid, w, skip_inert=False, chunk=CHUNK,
+                                         need_lse=False)
+
+        ms = timed(swa, args.steps)
+        pairs = L * (2 * w + 1) - w * (w + 1)
+        emit("swa", f"SWA layer fwd B={bsz} L={L} 28/4 heads d=128 radius {w} (RoPE + window, fp16 V)",
+             ms, bsz * L, "tokens", "tensor", bsz * HQ * D * 4 * pairs, "inputs larger than L2", launches=3)
+        ops = [o for o in ops if o != "swa"]
     if "dream" in ops:
         # the whole Dream-shaped forward, B=1, L=32768, random weights
         from mrsa_b200.dream_forward import DreamConfig, DreamForward, landmark_inputs, model_parameters
@@ -282,7 +305,6 @@ def run_ops(args):
              # this repository's kernels: 8 per route layer, RoPE + V to fp16 + window per SWA layer
              launches=7 * LAUNCHES_PER_STEP + 21 * 3)
         ops = [o for o in ops if o != "dream"]
-    L = L_PER_GPU
     for op in ops:
         if op == "flex":
             w = 1280
@@ -351,7 +373,8 @@ def main():
                     help="run N untimed fused layer forwards at the bench workload and exit "
                          "(the target of the ncu captures summarised under profiles/)")
     ap.add_argument("--op", default=None,
-                    choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "dream", "all"],
+                    choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "swa", "dream",
+                             "all"],
                     help="time one off-path op (or all) instead of the route layer; one JSON line each")
     args = ap.parse_args()
     if args.op:
