@@ -86,15 +86,9 @@ def cached_local_attention(q, k, v, key_valid, query_positions, window: int, chu
         raise ValueError("query_positions must be CUDA torch.long")
     if query_len == 0:
         return q.new_empty((batch, 0, h_q, dim)), q.new_empty((batch, 0, h_q), dtype=torch.float32)
-    # the reference's two checks with one device-to-host read: sorted
-    # neighbours equal -> duplicate (bit 0), out of range (bit 1)
-    srt = torch.sort(query_positions).values
-    bad = ((srt[1:] == srt[:-1]).any().to(torch.int32)
-           | (((srt[0] < 0) | (srt[-1] >= seq_len)).to(torch.int32) << 1))
-    bad = int(bad)
-    if bad & 1:
+    if torch.unique(query_positions).numel() != query_len:
         raise ValueError("query_positions must be unique")
-    if bad & 2:
+    if bool(((query_positions < 0) | (query_positions >= seq_len)).any()):
         raise ValueError("query_positions must be in cache range")
     if window < 0 or chunk_size <= 0 or seq_len % chunk_size:
         raise ValueError(f"invalid window/chunk layout: L={seq_len}, W={window}, S={chunk_size}")
