@@ -254,6 +254,14 @@ int mrsa_selected_attention_keep(const void* q, const void* k, const void* v, co
  * for mrsa_selected_attention_f16v). */
 int mrsa_convert_bf16_to_f16(const void* in, void* out, int64_t n, mrsa_stream_t stream);
 
+/* Self-test of the bounded in-kernel waits (failure detection without a GPU
+ * fault): one CTA whose warp 0 waits on an mbarrier nothing arrives on, with
+ * `rounds` (1..4000) bounded rounds, and whose warp 1 waits on another with
+ * the kernels' full limit.  Writes result[0] = 1 (warp 0 gave up), result[1] =
+ * 1 (the CTA's abort flag was raised), result[2] = 1 (warp 1 left through the
+ * flag) to the device ints `result[0..2]`.  No reference counterpart. */
+int mrsa_wait_selftest(int* result, int rounds, mrsa_stream_t stream);
+
 /* Bit mask of device-side failures recorded since the last clear: bit 0 = a
  * selected-attention CTA gave up waiting on one of its internal barriers (its
  * output rows are then incomplete); bit 1 = a routing key CTA did (its keys,

@@ -59,6 +59,7 @@ _SIGS = {
     "mrsa_convert_bf16_to_f16": [_vp, _vp, _i64, _vp],
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_device_error_flags": [_int],
+    "mrsa_wait_selftest": [_vp, _int, _vp],
     "mrsa_route_layer_workspace_size": [_vp],
     "mrsa_route_layer_forward": [_vp, _vp, _sz, _vp],
     "mrsa_route_layer_forward_noalloc": [_vp, _vp],

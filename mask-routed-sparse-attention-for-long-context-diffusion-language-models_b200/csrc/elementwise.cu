@@ -3,6 +3,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 using namespace mrsa;
 
@@ -286,3 +287,44 @@ int mrsa_fuse_outputs(const void* remote, const void* local, const void* local_w
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded mbarrier wait every pipelined kernel uses: warp 0
+// waits (with `rounds` rounds instead of the kernels' 4000) on a barrier
+// nothing ever arrives on, so it must give up and raise the CTA's abort flag;
+// warp 1 waits on a second such barrier with the full limit and must leave as
+// soon as it sees the flag.  result[0] = warp 0 gave up, result[1] = abort
+// flag raised, result[2] = warp 1 left through the flag.  Nothing faults or
+// hangs: both waits end, and the kernel returns.
+namespace {
+__global__ void wait_selftest_kernel(int* result, int rounds) {
+  __shared__ __align__(8) uint64_t bar[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(tc::smem_addr(&bar[0]), 1);
+    tc::mbar_init(tc::smem_addr(&bar[1]), 1);
+    abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  volatile int* af = &abort_flag;
+  if (warp == 0) {
+    const bool ok = tc::wait_bounded(tc::smem_addr(&bar[0]), 0, af, rounds);
+    if (lane == 0) result[0] = ok ? 0 : 1;
+  } else {
+    const bool ok = tc::wait_bounded(tc::smem_addr(&bar[1]), 0, af);
+    if (lane == 0) result[2] = (!ok && *af) ? 1 : 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) result[1] = abort_flag;
+}
+}  // namespace
+
+extern "C" int mrsa_wait_selftest(int* result, int rounds, mrsa_stream_t stream) {
+  if (!result) return MRSA_ERR_NULL;
+  if (rounds < 1 || rounds > 4000) return MRSA_ERR_ARG;
+  wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(result, rounds);
+  MRSA_CHECK_LAUNCH();
+  return MRSA_OK;
+}

@@ -242,9 +242,10 @@ __device__ __forceinline__ bool elect_one() {
 
 // Bounded wait that also gives up once another role of the CTA has set
 // *abort_flag; on expiry it sets the flag itself.  About 4e9 polls at most.
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             int rounds = 4000) {
   if (mbar_test(bar, parity)) return true;
-  for (int round = 0; round < 4000; ++round) {
+  for (int round = 0; round < rounds; ++round) {
     if (mbar_wait(bar, parity, 1000u)) return true;
     if (*abort_flag) return false;
   }

@@ -219,3 +219,17 @@ def test_selected_token_attention_empty_and_custom_scale(mrsa, dev):
 def test_token_ops_left_no_device_error(mrsa, dev):
     torch.cuda.synchronize()
     assert mrsa._lib.load().mrsa_device_error_flags(1) == 0
+
+
+def test_bounded_wait_gives_up_and_context_survives(mrsa, dev):
+    """Failure detection without a fault: a wait nothing ever satisfies gives up
+    after its bounded rounds, raises the CTA's abort flag, a second waiter
+    leaves through that flag, and the context keeps working afterwards."""
+    res = torch.full((3,), -1, dtype=torch.int32, device=dev)
+    mrsa._lib.call("mrsa_wait_selftest", mrsa._lib.ptr(res), 20, mrsa._lib.stream_of(res))
+    torch.cuda.synchronize()
+    assert res.tolist() == [1, 1, 1]
+    x = torch.randn(1024, device=dev).bfloat16()
+    assert torch.equal(mrsa.to_f16(x).float(), x.float())
+    with pytest.raises(ValueError):
+        mrsa._lib.call("mrsa_wait_selftest", mrsa._lib.ptr(res), 0, mrsa._lib.stream_of(res))
