@@ -129,3 +129,51 @@ def test_sharded_plan_matches_single_process_oracle():
     assert sorted(res) == list(range(WORLD))
     for rank, (equal, diff) in res.items():
         assert equal, (rank, diff)
+
+
+def _worker_lost_peer(rank, port, results):
+    """Rank 1 joins the group and leaves before the layer's first exchange;
+    rank 0 must get an error from that exchange (no hang) and report it."""
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=20))
+    if rank == 1:
+        results[rank] = "left"
+        return                      # the peer is lost between steps, with nothing in flight
+    import __graft_entry__
+
+    __graft_entry__.load_package()
+    from mrsa_b200.shard import ShardedRouteLayer
+
+    cfg = orc.MRSAConfig()
+    inp = orc.make_route_layer_inputs(1, L_TOTAL, cfg, hidden=HIDDEN, seed=SEED)
+    sl = slice(0, L_TOTAL // WORLD)
+    layer = ShardedRouteLayer(ops=OracleOps(inp, cfg))
+    try:
+        layer(inp["q_pre"][:, sl], inp["k_pre"][:, sl], inp["v"][:, sl], inp["hidden"][:, sl],
+              inp["position_ids"][:, sl], inp["key_valid"][:, sl])
+        results[rank] = "no error"
+    except Exception as exc:  # the backend's error type differs between versions
+        results[rank] = f"error: {type(exc).__name__}"
+
+
+@pytest.mark.timeout(300)
+def test_lost_rank_ends_the_exchange_with_an_error():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker_lost_peer, args=(r, port, results)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=240)
+        alive = [p.is_alive() for p in procs]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        res = dict(results)
+    assert not any(alive), "a rank did not finish: the lost peer was not detected"
+    assert res.get(1) == "left"
+    assert str(res.get(0, "")).startswith("error"), res
