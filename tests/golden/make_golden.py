@@ -22,6 +22,9 @@ outputs of the reference's OWN functions, imported from the checkout:
 * ``dsa.pt``       ``dream_dllm_hils/dsa_attention.py:498 selected_token_attention_reference``
 * ``flex.pt``      ``ops/flex_attn_tilelang.py:1355 _torch_ref_flex_attn`` (torch
   flex_attention with the reference's mask; its block mask is built on the CPU)
+* ``local_window.pt`` ``dream_dllm_hils/local_attention.py:110 bidir_local_attention``
+  run end to end, with its third-party ``flash_attn_func`` (GPU only) replaced by
+  torch ``flex_attention`` under flash-attn's window rule ``|i - j| <= W``
 
 The fixtures are consumed by ``tests/test_oracle_golden.py`` (CPU) and by the
 GPU parity tests; nothing at test time reads the reference checkout.
@@ -304,6 +307,67 @@ def gen_flex():
     _save("flex.pt", {"cases": cases})
 
 
+def _cpu_flash_attn_module():
+    """A stand-in ``flash_attn`` module for the CPU: ``flash_attn_func`` with
+    flash-attn's non-causal sliding window (keys j with |i - j| <= W) and its
+    return convention (out [B,L,H,D], lse [B,H,L]), computed by torch's
+    ``flex_attention``."""
+    import functools
+    import types
+
+    import torch.nn.attention.flex_attention as fa
+
+    def flash_attn_func(q, k, v, dropout_p=0.0, softmax_scale=None, causal=False, window_size=(-1, -1),
+                        return_softmax_lse=False):
+        assert dropout_p == 0.0 and not causal
+        wl, wr = window_size
+        lq, lk = q.shape[1], k.shape[1]
+
+        def mask_mod(b, h, qi, kj):
+            return (kj >= qi - wl) & (kj <= qi + wr)
+
+        bm = fa.create_block_mask(mask_mod, B=None, H=None, Q_LEN=lq, KV_LEN=lk, device="cpu")
+        o, lse = fa.flex_attention(q.transpose(1, 2).float(), k.transpose(1, 2).float(), v.transpose(1, 2).float(),
+                                   block_mask=bm, scale=softmax_scale, enable_gqa=True, return_lse=True)
+        return o.transpose(1, 2).to(q.dtype), lse
+
+    mod = types.ModuleType("flash_attn")
+    mod.flash_attn_func = flash_attn_func
+    _ = functools
+    return mod
+
+
+def gen_local_window():
+    import dream_dllm_hils.local_attention as la
+
+    saved = sys.modules.get("flash_attn")
+    sys.modules["flash_attn"] = _cpu_flash_attn_module()
+    # the reference's layout check demands CUDA tensors (local_attention.py:15-17);
+    # the rest of bidir_local_attention runs unchanged on the CPU
+    check = la._validate_layout
+    la._validate_layout = lambda *args: None
+    bidir_local_attention = la.bidir_local_attention
+    try:
+        cases = []
+        for i, (l, w, skip) in enumerate([(256, 40, True), (256, 40, False), (320, 100, True)]):
+            g = torch.Generator().manual_seed(200 + i)
+            hq, hkv, d = 4, 2, 32
+            q = torch.randn(1, l, hq, d, generator=g).bfloat16()
+            k = torch.randn(1, l, hkv, d, generator=g).bfloat16()
+            v = torch.randn(1, l, hkv, d, generator=g).bfloat16()
+            valid = torch.rand(1, l, generator=g) > 0.1
+            o, lse = bidir_local_attention(q, k, v, valid, w, 64, skip_inert_slots=skip)
+            cases.append({"q": q, "k": k, "v": v, "key_valid": valid, "window": w, "skip": skip,
+                          "o": o, "lse": lse})
+    finally:
+        la._validate_layout = check
+        if saved is None:
+            sys.modules.pop("flash_attn", None)
+        else:
+            sys.modules["flash_attn"] = saved
+    _save("local_window.pt", {"cases": cases})
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gen_yarn()
@@ -318,4 +382,5 @@ if __name__ == "__main__":
     gen_token_scores()
     gen_dsa()
     gen_flex()
+    gen_local_window()
     print("done")

@@ -215,3 +215,15 @@ def test_flex_mask_kv_start_is_a_shift():
     part = tok.flex_window_mask(8, 136, 70, 32, True, True, 64)
     assert torch.equal(full[:, 64:], part)
     assert not full[:, :64].any()
+
+
+def test_local_window_matches_reference_bidir_local_attention():
+    """The reference's own bidir_local_attention (masking helpers, window rule,
+    LSE layout), with its GPU-only flash-attn call replaced by torch's
+    flex_attention under flash-attn's |i - j| <= W window."""
+    for case in load_golden("local_window.pt")["cases"]:
+        o, lse = orc.local_attention(case["q"], case["k"], case["v"], case["key_valid"], case["window"], 64,
+                                     case["skip"])
+        d = (o.float() - case["o"].float()).abs()
+        assert d.max() <= 2 ** -6 and (d > 0).float().mean() < 0.02, (case["window"], case["skip"], d.max())
+        torch.testing.assert_close(lse, case["lse"], atol=2e-5, rtol=1e-5)
