@@ -359,13 +359,26 @@ def gen_local_window():
             o, lse = bidir_local_attention(q, k, v, valid, w, 64, skip_inert_slots=skip)
             cases.append({"q": q, "k": k, "v": v, "key_valid": valid, "window": w, "skip": skip,
                           "o": o, "lse": lse})
+        # the Fast-dLLM cached rows (local_attention.py:147-197) on the same helpers
+        g = torch.Generator().manual_seed(300)
+        l, hq, hkv, d = 256, 4, 2, 32
+        pos = torch.tensor([130, 3, 255, 64, 63, 200, 201, 17])
+        q = torch.randn(1, pos.numel(), hq, d, generator=g).bfloat16()
+        k = torch.randn(1, l, hkv, d, generator=g).bfloat16()
+        v = torch.randn(1, l, hkv, d, generator=g).bfloat16()
+        valid = torch.rand(1, l, generator=g) > 0.1
+        cached = []
+        for w, skip in [(40, True), (100, False)]:
+            o, lse = la.cached_local_attention(q, k, v, valid, pos, w, 64, skip_inert_slots=skip)
+            cached.append({"window": w, "skip": skip, "o": o, "lse": lse})
     finally:
         la._validate_layout = check
         if saved is None:
             sys.modules.pop("flash_attn", None)
         else:
             sys.modules["flash_attn"] = saved
-    _save("local_window.pt", {"cases": cases})
+    _save("local_window.pt", {"cases": cases, "cached": {"q": q, "k": k, "v": v, "key_valid": valid,
+                                                          "positions": pos, "runs": cached}})
 
 
 if __name__ == "__main__":

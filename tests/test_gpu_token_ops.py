@@ -1,9 +1,9 @@
 """GPU parity of the ops off the route layer's live path -- the causal flex
 window (``flex_attn_tl``), the cached (Fast-dLLM) local rows, candidate token
 scores and selected-token (DSA) attention -- against the CPU oracle, which
-``test_oracle_golden.py`` pins to the reference's own torch functions (the
-cached local rows follow the local-window oracle, unpinned like the
-flash-attn local branch).
+``test_oracle_golden.py`` pins to the reference's own functions (the cached
+local rows through ``cached_local_attention`` with a CPU stand-in for its
+flash-attn call).
 
 Tolerances: bf16 attention outputs max-abs <= 2e-2 and mean-rel <= 1e-3 (as
 for the route layer), plus the reference tests' own bars where they state

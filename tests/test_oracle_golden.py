@@ -227,3 +227,18 @@ def test_local_window_matches_reference_bidir_local_attention():
         d = (o.float() - case["o"].float()).abs()
         assert d.max() <= 2 ** -6 and (d > 0).float().mean() < 0.02, (case["window"], case["skip"], d.max())
         torch.testing.assert_close(lse, case["lse"], atol=2e-5, rtol=1e-5)
+
+
+def test_cached_rows_match_reference_cached_local_attention():
+    """dream_dllm_hils/local_attention.py:147 cached_local_attention (same
+    stand-in for flash-attn): rows at arbitrary cache positions equal the
+    full-window oracle's rows at those positions."""
+    g = load_golden("local_window.pt")["cached"]
+    pos = g["positions"]
+    q_full = torch.zeros(1, g["k"].shape[1], *g["q"].shape[2:], dtype=g["q"].dtype)
+    q_full[:, pos] = g["q"]
+    for run in g["runs"]:
+        o, lse = orc.local_attention(q_full, g["k"], g["v"], g["key_valid"], run["window"], 64, run["skip"])
+        d = (o[:, pos].float() - run["o"].float()).abs()
+        assert d.max() <= 2 ** -6, (run["window"], d.max())
+        torch.testing.assert_close(lse[:, pos], run["lse"], atol=2e-5, rtol=1e-5)
