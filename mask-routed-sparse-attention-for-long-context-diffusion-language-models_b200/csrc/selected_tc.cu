@@ -41,9 +41,11 @@
 // partial buffers.  An S buffer is released as soon as the item's softmax has
 // loaded it and a partial buffer as soon as the accumulate warps have read it,
 // so neither cycle waits on the other.
-// Owner j of an item goes to S row slot 2*(j%4) + j/4, so the first four
-// owners land in four different TMEM quadrants and four softmax warps share
-// the rows.  Every mbarrier wait is bounded and a shared abort flag unwinds all
+// Owner j of item i goes to S row slot 2*((j+rot)%4) + j/4 with rot =
+// (i/2)%4, so the first four owners land in four different TMEM quadrants and
+// four softmax warps share the rows, and a group's successive items with one
+// or two owners put them in different quadrants, whose warps then compute
+// those items side by side.  Every mbarrier wait is bounded and a shared abort flag unwinds all
 // roles; an aborted CTA waits (bounded) for its own copies and MMAs in flight.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -400,7 +402,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
           }
           __syncwarp();
           if (mine) {
-            const int slot = 2 * (j & 3) + (j >> 2);
+            const int slot = 2 * ((j + (item >> 1)) & 3) + (j >> 2);
             const int qy = static_cast<int>((b * a.Lq + q0 + lane) * Hq + hk * G);
             tc::tma_load_3d(su32(sm.at[st] + slot * 2048), &tm_q, 0, qy, 0, bar);
           }
@@ -500,12 +502,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     const int grp = (warp - W_SMX) >> 2, q = warp & 3;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int t = lane & 15, hf = lane >> 4;
-    const int jrow = t < 8 ? q : q + 4;      // owner (compact index) of this thread's row
+
     const int g = t & 7;
     for (int it = grp; it < n_items; it += 2) {
       const int p2 = it & 1, r = it % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
       const int n = sm.ring[r].n;
+      const int qo = (q - (it >> 1)) & 3;    // this quadrant holds owners qo and qo + 4
+      const int jrow = t < 8 ? qo : qo + 4;  // owner (compact index) of this thread's row
       const bool row_on = jrow < n;
       float w = 0.f;
       uint32_t km = 0xFFFFFFFFu;             // rows without an owner are computed and dropped
@@ -534,11 +538,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         }
       }
       tc::fence_after_sync();
-      // Quadrant q holds the rows of owners q and q+4: with fewer than q+1
+      // Quadrant q holds the rows of owners qo and qo+4: with fewer than qo+1
       // owners (most items when the chunks are many and each is picked by
       // one or two of the block's queries) the warp has no row to compute and
       // keeps only its hand-offs, which frees issue slots for the other roles.
-      const bool quad_on = q < n;            // warp-uniform
+      const bool quad_on = qo < n;           // warp-uniform
       uint32_t x[32];
       if (quad_on) {
         tc::tmem_ld_16x32bx2_x32(tbase + lane_off + kSCol + 64 * p2, x);
