@@ -1,4 +1,4 @@
-"""MRSA route-layer forward benchmark (BASELINE metric: route-layer fwd tokens/s, bf16).
+"""MRSA route-layer forward benchmark (headline metric: route-layer fwd tokens/s, bf16).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -6,14 +6,19 @@ N=1 runs configs[1]: B=1, L=16384 (256 chunks), 28/4 heads, d=128, Q-Cal
 hidden 3584 / rank 64, top-32 of 64-token chunks + local radius 256, YaRN-8
 fp32 RoPE, seeded N(0,1) activations (N(0,1)/sqrt(128) for q/k/v).  N>1
 (torchrun) shards one sequence of L = 16384*N tokens into contiguous query
-blocks of 16384 per GPU with NCCL all-gathers of K/V and chunk summaries
-(N=8: configs[4], L=131072), i.e. weak scaling in query rows.  A step is one
-route-layer forward from the projected q/k/v/h to the o_proj input.  Inputs
-(q 117 MB + h 117 MB + k/v 33 MB per 16k tokens) are larger than L2 (126 MB).
+blocks of 16384 per GPU (N=8: configs[4], L=131072), i.e. weak scaling in
+query rows: a halo exchange with the neighbours, an all-gather of the chunk
+summaries and an all-gather of K/V on its own communicator, hidden behind
+the local window attention and routing.  A step is one route-layer forward
+from the projected q/k/v/h to the o_proj input.  Inputs (q 117 MB + h 117 MB
++ k/v 33 MB per 16k tokens) are larger than L2 (126 MB).  Every arm draws
+the same inputs from seeded CPU generators (:func:`make_inputs`).
 
 ``--impl reference`` times the reference's PyTorch path restated on the CPU
 (``oracle/``; the reference is Python and its checkout is not on the GPU
-host) with all host threads, on rank 0 only.
+host) with all host threads, on rank 0 only: every timed step computes a
+disjoint share of the layer's query rows (the whole layer at N=1), the
+stages all rows share inside the first step.
 """
 
 from __future__ import annotations
@@ -43,7 +48,9 @@ LAUNCHES_PER_STEP = 8
 
 def algorithmic(l_local: int, l_total: int):
     """Algorithmic FLOPs of one route-layer forward over ``l_local`` query rows
-    with ``l_total`` keys (BASELINE.md section 3 formulas)."""
+    with ``l_total`` keys: selected 4*L*Hq*K*S*D (S = 64 slots, the masked
+    landmark column included), local 4*Hq*D per (query, key) pair within
+    256 + 63, routing 2*L*Hq*C*D per pass, Q-Cal 2*L*(hidden*rank + rank*Hq*D)."""
     c = l_total // CHUNK
     f_sel = l_local * HQ * TOPK * CHUNK * D * 4
     w = WLOC + CHUNK - 1
@@ -133,82 +140,144 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_inputs(l_local: int, rank: int, dev):
-    """Seeded synthetic inputs of this rank's rows (distributions of configs[0])."""
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    q = torch.randn(1, l_local, HQ, D, device=dev, generator=g).div_(math.sqrt(D)).bfloat16()
-    k = torch.randn(1, l_local, HKV, D, device=dev, generator=g).div_(math.sqrt(D)).bfloat16()
-    v = torch.randn(1, l_local, HKV, D, device=dev, generator=g).div_(math.sqrt(D)).bfloat16()
-    h = torch.randn(1, l_local, HIDDEN, device=dev, generator=g).bfloat16()
-    gw = torch.Generator(device=dev).manual_seed(7)          # weights identical on every rank
-    w_in = (torch.randn(RANK, HIDDEN, device=dev, generator=gw) * 0.02).bfloat16()
-    w_out = (torch.randn(HQ * D, RANK, device=dev, generator=gw) * 0.02).bfloat16()
-    role = (torch.randn(HIDDEN, device=dev, generator=gw) * 0.02).bfloat16()
-    i = torch.arange(rank * l_local, (rank + 1) * l_local, device=dev)
+def make_inputs(l_local: int, rank: int, seed: int = 0):
+    """Seeded synthetic inputs of rank ``rank``'s rows, on the host (bf16).
+
+    A CPU generator seeded ``seed + rank`` draws, in this order, h
+    ``[1,l,3584]`` ~ N(0,1), q ``[1,l,28,128]``, k and v ``[1,l,4,128]`` ~
+    N(0,1)/sqrt(128) (the distributions of configs[0]); a second generator
+    seeded 7 draws the weights every rank shares: Q-Cal W_in ``[64,3584]``,
+    W_out ``[3584,64]`` and the landmark role offset ``[3584]`` ~ N(0,0.02),
+    the offset added to h at landmark slots (63 mod 64).  Position ids follow
+    the landmark layout (slot i -> i - i//64); every key is valid."""
+    g = torch.Generator().manual_seed(seed + rank)
+    h = torch.randn(1, l_local, HIDDEN, generator=g)
+    q = torch.randn(1, l_local, HQ, D, generator=g).div_(math.sqrt(D)).bfloat16()
+    k = torch.randn(1, l_local, HKV, D, generator=g).div_(math.sqrt(D)).bfloat16()
+    v = torch.randn(1, l_local, HKV, D, generator=g).div_(math.sqrt(D)).bfloat16()
+    gw = torch.Generator().manual_seed(7)
+    w_in = (torch.randn(RANK, HIDDEN, generator=gw) * 0.02).bfloat16()
+    w_out = (torch.randn(HQ * D, RANK, generator=gw) * 0.02).bfloat16()
+    role = torch.randn(HIDDEN, generator=gw) * 0.02
+    i = torch.arange(rank * l_local, (rank + 1) * l_local)
     h[0, (i + 1) % CHUNK == 0] += role                        # landmark role offset
+    h = h.bfloat16()
     pos = (i - i // CHUNK).view(1, -1).contiguous()
-    valid = torch.ones(1, l_local, dtype=torch.bool, device=dev)
+    valid = torch.ones(1, l_local, dtype=torch.bool)
     return {"q_pre": q, "k_pre": k, "v": v, "hidden": h, "position_ids": pos, "key_valid": valid,
             "w_in": w_in, "w_out": w_out}
 
 
-def cpu_route_layer_rate(l_total: int, q_small: int, q_big: int):
-    """Oracle (the reference's PyTorch path on the CPU) timed on two query
-    slices; tokens/s of a whole layer from the linear model t(Q) = a + b*Q."""
-    from oracle import route_layer as orc
+def bench_config(l_total: int, lq: int, world: int):
+    """The ``config`` object of both arms' JSON lines."""
+    return {"workload": (f"route-layer fwd B=1 L={l_total} (query blocks of {lq} per GPU) "
+                         "28/4 heads d=128 top-32x64 + local-256, Q-Cal 3584->64, YaRN-8"),
+            "global_batch": 1, "seq_len": l_total, "parallelism": f"seq{world}",
+            "l2": "inputs larger than L2 (267 MB per 16k tokens)"}
 
-    torch.set_num_threads(os.cpu_count() or 1)
+
+def _oracle_inputs(parts, orc):
+    """The oracle's input dict for the whole sequence from the ranks' parts."""
+    def cat(name):
+        return torch.cat([p[name] for p in parts], dim=1)
+
+    return {"q_pre": cat("q_pre"), "k_pre": cat("k_pre"), "v": cat("v"), "hidden": cat("hidden"),
+            "position_ids": cat("position_ids"), "key_valid": cat("key_valid"),
+            "w_in": parts[0]["w_in"], "w_out": parts[0]["w_out"],
+            "norm_weight": torch.ones(D), "entropy_bias_scale": torch.ones(HQ),
+            "gate_offset": 0.0, "gate_scale": 1.0}
+
+
+def cpu_layer_sample(inp, shares, orc):
+    """The oracle route layer on the query-row ``shares`` (a list of slices,
+    one per step): the stages every row shares (RoPE of K, Q-Cal of the
+    landmark and sampled rows, landmark pool, prior) inside the first step,
+    then each share's rows.  Returns the seconds of each step."""
     cfg = orc.MRSAConfig()
-    inp = orc.make_route_layer_inputs(1, l_total, cfg, hidden=HIDDEN, seed=0)
-    mid = l_total // 2
-
-    def run(nq):
+    l = inp["q_pre"].shape[1]
+    rows = torch.zeros(l, dtype=torch.bool)
+    for sl in shares:
+        rows[sl] = True
+    rows[CHUNK - 1::CHUNK] = True
+    times, shared = [], None
+    for sl in shares:
         t0 = time.perf_counter()
-        orc.route_layer_forward(inp, cfg, keep=False, query_slice=slice(mid, mid + nq))
-        return time.perf_counter() - t0
+        if shared is None:
+            shared = orc.route_layer_shared(inp, cfg, rows=rows)
+        orc.route_layer_rows(inp, shared, cfg, sl, keep=False)
+        times.append(time.perf_counter() - t0)
+    return times
 
-    a_s, b_s = run(q_small), run(q_big)
-    slope = max((b_s - a_s) / (q_big - q_small), 1e-12)
-    fixed = max(a_s - slope * q_small, 0.0)
-    return l_total / (fixed + slope * l_total), {"fixed_s": fixed, "per_query_s": slope}
+
+def _cpu_model():
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for ln in out.splitlines():
+            if ln.startswith("Model name:"):
+                return ln.split(":", 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return None
+
+
+def _shares(l_total: int, n_queries: int, steps: int):
+    """``steps`` disjoint query-row slices of ``n_queries // steps`` rows
+    spread evenly over the sequence (with ``n_queries == l_total`` and
+    ``steps`` dividing it: the whole sequence)."""
+    per = max(1, n_queries // steps)
+    stride = l_total // steps
+    return [slice(s * stride, s * stride + per) for s in range(steps)]
 
 
 def run_reference(args, world, rank):
-    """Reference arm: the oracle port on the host cores, rank 0 only."""
+    """Reference arm: the oracle port on the host cores, rank 0 only.
+
+    Each timed step computes a disjoint share of the route layer's query rows
+    on the GPU arm's inputs: at N=1 the shares cover every row, so the timed
+    region computes the whole layer once; at N>1 (L = 16384 N) they cover
+    16384 rows spread over the sequence, which bounds the run."""
     if rank != 0:
         return
-    l_total = L_PER_GPU * world
     from oracle import route_layer as orc
 
+    lq = args.seq_per_gpu
+    l_total = lq * world
     torch.set_num_threads(os.cpu_count() or 1)
-    cfg = orc.MRSAConfig()
-    inp = orc.make_route_layer_inputs(1, l_total, cfg, hidden=HIDDEN, seed=0)
-    mid, q_step, q_small = l_total // 2, 128, 32
-
-    def run(nq):
-        t0 = time.perf_counter()
-        orc.route_layer_forward(inp, cfg, keep=False, query_slice=slice(mid, mid + nq))
-        return time.perf_counter() - t0
-
-    small = [run(q_small) for _ in range(max(1, args.warmup))]
-    steps = [run(q_step) for _ in range(args.steps)]
-    a_s, b_s = statistics.median(small), statistics.median(steps)
-    slope = max((b_s - a_s) / (q_step - q_small), 1e-12)
-    fixed = max(a_s - slope * q_small, 0.0)
-    value = l_total / (fixed + slope * l_total)
+    inp = _oracle_inputs([make_inputs(lq, r) for r in range(world)], orc)
+    n_q = l_total if world == 1 else min(l_total, L_PER_GPU)
+    for i in range(max(1, args.warmup)):                 # warm-up: small shares
+        cpu_layer_sample(inp, [slice(i * 64, i * 64 + 32)], orc)
+    shares = _shares(l_total, n_q, args.steps)
+    times = cpu_layer_sample(inp, shares, orc)
+    total = sum(times)
+    rows = sum(sl.stop - sl.start for sl in shares)
+    value = rows / total
     cores = torch.get_num_threads()
-    sample = (f"oracle route layer at L={l_total}: {q_step}-query slice per step "
-              f"({q_small}-query slices in warm-up) extrapolated to all {l_total} queries "
-              f"with t = a + b*Q (a={fixed:.3f}s, b={slope * 1e3:.3f}ms/query)")
+    sample = (f"oracle route layer at L={l_total}: {args.steps} timed steps of {rows // args.steps} disjoint "
+              f"query rows ({rows} rows{', the whole layer' if rows == l_total else ''}); the stages all rows "
+              "share (K RoPE, landmark Q-Cal, pool, prior) inside the first step")
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * l_total / value,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"route-layer fwd B=1 L={l_total} 28/4 heads d=128 top-32x64 + local-256",
-                       "global_batch": 1, "seq_len": l_total, "parallelism": "cpu"},
+            "config": bench_config(l_total, lq, world),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": sample},
+                             "sample": sample, "cpu_count": os.cpu_count(), "cpu_model": _cpu_model()},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if world == 1:
+        # configs[0]: fp32 storage, B=1, L=4096, the whole layer, median of 3 after one warm-up
+        cfg = orc.MRSAConfig()
+        inp0 = orc.make_route_layer_inputs(1, 4096, cfg, hidden=HIDDEN, seed=0, dtype=torch.float32)
+        runs = []
+        for _ in range(4):
+            t0 = time.perf_counter()
+            orc.route_layer_forward(inp0, cfg, keep=False)
+            runs.append(time.perf_counter() - t0)
+        med = statistics.median(runs[1:])
+        line["configs0"] = {"workload": "route-layer fwd, fp32 storage, B=1 L=4096 28/4 heads d=128 (oracle port)",
+                            "value": 4096 / med, "unit": "tokens/s", "ms_per_forward": 1e3 * med,
+                            "runs_s": runs[1:], "threads": cores, "cpu_count": os.cpu_count(),
+                            "cpu_model": _cpu_model()}
     print(json.dumps(line), flush=True)
 
 
@@ -400,12 +469,17 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     lq = args.seq_per_gpu
     l_total = lq * world
-    inp = make_inputs(lq, rank, dev)
-    layer = mrsa.RouteLayer(inp["w_in"], inp["w_out"])
+    host_inp = make_inputs(lq, rank)
+    inp = {n: t.to(dev) for n, t in host_inp.items()}
+    # device errors (fp16 range of V, bounded waits) are read once after the timed region
+    layer = mrsa.RouteLayer(inp["w_in"], inp["w_out"], check_errors=False)
     if world > 1:
+        import datetime
+
         from mrsa_b200.shard import ShardedRouteLayer
 
-        runner = ShardedRouteLayer(layer)
+        bulk = dist.new_group(list(range(world)), timeout=datetime.timedelta(seconds=120))
+        runner = ShardedRouteLayer(layer, bulk_group=bulk)
     else:
         runner = layer
     names = ("q_pre", "k_pre", "v", "hidden", "position_ids", "key_valid")
@@ -508,46 +582,89 @@ def main():
 
     # ---- per-kernel times, roofline of the dominant kernel -----------------
     hbm, tflops, peak_kind = load_peaks()
-    stages, roof = None, None
     if world == 1:
         stages = layer.stage_times(*x[:5], x[5], reps=5)
-        dom = max(stages, key=stages.get)
-        flops = algorithmic(lq, l_total)
-        byts = stage_bytes(lq)
-        if dom in ("selected_attention", "local_attention", "route"):
-            ach = flops[dom] / (stages[dom] * 1e-3) / 1e12
-            roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tflops,
-                    "unit": "TFLOP/s", "frac": ach / tflops,
-                    "traffic": MEASURED_TRAFFIC.get((dom, lq, l_total)),
-                    "traffic_unit": "bytes per launch (ncu DRAM read + write)",
-                    "peak_kind": f"{peak_kind} bf16 burst"}
-        else:
-            ach = byts[dom] / (stages[dom] * 1e-3) / 1e9
-            roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
-                    "frac": ach / hbm, "traffic": None, "peak_kind": f"{peak_kind} HBM copy"}
+    else:
+        stages = runner.stage_times(*x, reps=5)
+    kernel_stages = {n: v for n, v in stages.items() if not n.endswith("_wait")}
+    dom = max(kernel_stages, key=kernel_stages.get)
+    dom_ms = stages[dom]
+    if dist:                                  # the slowest rank's time for the dominant kernel
+        t = torch.tensor([dom_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dom_ms = t.item()
+    flops = algorithmic(lq, l_total)
+    byts = stage_bytes(lq)
+    if dom in ("selected_attention", "local_attention", "route"):
+        ach = flops[dom] / (dom_ms * 1e-3) / 1e12
+        roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tflops,
+                "unit": "TFLOP/s", "frac": ach / tflops,
+                "traffic": MEASURED_TRAFFIC.get((dom, lq, l_total)),
+                "traffic_unit": "bytes per launch (ncu DRAM read + write)",
+                "peak_kind": f"{peak_kind} bf16 burst"}
+    else:
+        ach = byts[dom] / (dom_ms * 1e-3) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                "frac": ach / hbm, "traffic": None, "peak_kind": f"{peak_kind} HBM copy"}
+    waits = None
+    if dist:
+        # time each rank's compute stream stalled on a transfer, max over ranks
+        w = torch.tensor([stages.get(n, 0.0) for n in ("halo_wait", "summaries_wait", "kv_wait")], device=dev)
+        dist.all_reduce(w, op=dist.ReduceOp.MAX)
+        waits = dict(zip(("halo_wait_ms", "summaries_wait_ms", "kv_wait_ms"), w.tolist()))
+
+    # ---- device error flags of everything above (fp16 range of V, bounded waits)
+    flags = int(mrsa._lib.load().mrsa_device_error_flags(1))
+
+    # ---- N>1: this rank's rows against the single-GPU layer on the whole sequence
+    parity = None
+    if dist:
+        from mrsa_b200.shard import gather_rows
+
+        full = []
+        for t in x:
+            buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=dev)
+            gather_rows(buf, t.contiguous())
+            full.append(buf.transpose(0, 1).reshape(1, world * t.shape[1], *t.shape[2:]).contiguous())
+        ref = layer(*full)
+        mine = runner(*x)
+        ok = torch.tensor([1.0 if torch.equal(mine, ref[:, rank * lq:(rank + 1) * lq]) else 0.0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        parity = {"ok": bool(ok.item() == 1.0),
+                  "check": ("every rank's output rows bit-equal to the same rows of the single-GPU fused "
+                            f"layer run on the whole L={l_total} sequence (gathered inputs)")}
+        del full, ref, mine
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic",
-                "config": {"workload": (f"route-layer fwd B=1 L={l_total} (query blocks of {lq} per GPU) "
-                                        "28/4 heads d=128 top-32x64 + local-256, Q-Cal 3584->64, YaRN-8"),
-                           "global_batch": 1, "seq_len": l_total, "parallelism": f"seq{world}",
-                           "l2": "inputs larger than L2 (267 MB per 16k tokens)"},
+                "config": bench_config(l_total, lq, world),
                 "roofline": roof, "stage_ms": stages,
                 "gpu_launches": args.steps * LAUNCHES_PER_STEP,
                 "clocks": clocks,
+                "device_error_flags": flags,
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d * world,
                         "d2h_bytes_per_step": d2h * world, "steps": e2,
                         "pipelining": "step i's upload and readback overlap the compute of steps i-1 and i+1"}}
+        if waits is not None:
+            line["exchange_wait_ms"] = waits
+        if parity is not None:
+            line["parity"] = parity
         if world == 1 and not args.no_cpu_baseline:
-            rate, info = cpu_route_layer_rate(l_total, 32, 160)
+            from oracle import route_layer as orc
+
+            torch.set_num_threads(os.cpu_count() or 1)
+            shares = _shares(l_total, min(l_total, 4096), 4)
+            t_cpu = cpu_layer_sample(_oracle_inputs([host_inp], orc), shares, orc)
+            n_rows = sum(sl.stop - sl.start for sl in shares)
             line["cpu_baseline"] = {
-                "value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-                "sample": (f"oracle route layer at L={l_total}, 32- and 160-query slices, "
-                           f"extrapolated t = a + b*Q (a={info['fixed_s']:.2f}s, "
-                           f"b={info['per_query_s'] * 1e3:.2f}ms/query)")}
+                "value": n_rows / sum(t_cpu), "unit": "tokens/s", "cores": torch.get_num_threads(),
+                "kind": "port",
+                "sample": (f"oracle route layer on this run's inputs (L={l_total}): {n_rows} query rows in "
+                           f"{len(shares)} slices spread over the sequence plus the stages all rows share, "
+                           f"{sum(t_cpu):.1f} s")}
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

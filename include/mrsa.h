@@ -13,8 +13,11 @@
  *   local_lse    [B, L, Hq]      fp32 (natural log)
  *   indices      [B, L, Hkv, K]  int32, ascending, -1 last
  *   scores / remote weights [B, L, Hq, K] bf16; local weight [B, L, Hq] bf16
- * Pointers (key_valid included) must be 16-byte aligned.  Stateless and re-entrant: any host
- * thread, any stream.
+ * Pointers (key_valid included) must be 16-byte aligned.  Entry points are
+ * stateless and re-entrant (any host thread, any stream) with two
+ * exceptions, described at their declarations: mrsa_route_layer_forward_noalloc
+ * shares one scratch area per device between calls, and the device error
+ * flags read by mrsa_device_error_flags are process-wide.
  */
 #ifndef MRSA_B200_H
 #define MRSA_B200_H
@@ -304,7 +307,11 @@ size_t mrsa_route_layer_workspace_size(const mrsa_route_layer_args* a);
 /* Whole route layer on one device: RoPE, local branch, Q-Cal, landmark pool,
  * routing + weights, selected attention fused with the local branch.
  * Replaces KernelDreamFullHiLSAttention.forward (dream_dllm_hils/attention.py:1313-1774)
- * from the projected q/k/v/h to the input of o_proj. */
+ * from the projected q/k/v/h to the input of o_proj.  The attention kernels
+ * take V in fp16 (the layer converts it once): V values beyond +-65504 (and
+ * infinities) saturate to +-65504 and set bit 3 of mrsa_device_error_flags,
+ * so a caller that cannot rule such values out reads the flags after the
+ * call. */
 int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* workspace, size_t ws_bytes,
                              mrsa_stream_t stream);
 
@@ -314,14 +321,15 @@ int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* workspace, si
 
 /* The route layer of mrsa_route_layer_forward for callers that cannot
  * allocate device memory (a plugin inside a framework that owns all device
- * allocations, a server with a fixed memory pool, code running while a stream
- * is recorded).  It has no counterpart in the reference.  Instead of a caller
+ * allocations, a server with a fixed memory pool).  It has no counterpart in
+ * the reference.  Instead of a caller
  * workspace it uses MRSA_NOALLOC_SCRATCH_BYTES of scratch inside the library
  * image: problems whose mrsa_route_layer_workspace_size exceeds that (about
  * 1200 tokens of the Dream shape) are rejected with MRSA_ERR_WORKSPACE before
  * anything runs.  Runs on the current device; its first call on a device
  * looks up the scratch address (cudaGetSymbolAddress), so make that first
- * call before any stream capture.  All calls on a device share the scratch:
+ * call before any stream capture; the address is looked up again when the
+ * device's context has changed since (after a cudaDeviceReset).  All calls on a device share the scratch:
  * calls whose GPU work overlaps race, so order them on one stream.  Nothing
  * in the scratch needs to start at zero.  Allocates and frees nothing. */
 int mrsa_route_layer_forward_noalloc(const mrsa_route_layer_args* a, mrsa_stream_t stream);

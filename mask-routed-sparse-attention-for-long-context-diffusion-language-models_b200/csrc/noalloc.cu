@@ -1,10 +1,10 @@
 // Route-layer forward for callers that cannot allocate device memory.
 //
 // Some hosts drive this library from places where cudaMalloc is off limits:
-// a plugin running inside a framework that owns every device allocation, an
-// inference server whose memory pool is fixed at start-up, or code that runs
-// while a stream is being recorded.  They still own the inputs and outputs,
-// but cannot hand over the ~27 KB-per-token workspace the fused layer needs.
+// a plugin running inside a framework that owns every device allocation, or
+// an inference server whose memory pool is fixed at start-up.  They still own
+// the inputs and outputs, but cannot hand over the ~27 KB-per-token workspace
+// the fused layer needs.
 // This entry point uses a fixed scratch area that is part of the library
 // image instead: MRSA_NOALLOC_SCRATCH_BYTES (32 MiB) of device memory that
 // every GPU which loads the library keeps until the process exits.  That is
@@ -14,6 +14,8 @@
 // call left in it.  The layer writes every intermediate before reading it, so
 // nothing has to start at zero; but two calls whose work overlaps on the GPU
 // (different streams, no ordering between them) race on it.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -23,23 +25,47 @@ namespace {
 static __device__ __align__(256) unsigned char g_scratch[MRSA_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+  CUcontext ctx;      // the context the address was looked up in
+  void* addr;
+};
+ScratchAddr g_scratch_addr[kMaxDevices] = {};
 std::mutex g_scratch_mu;
+
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+CtxGetCurrent g_ctx_get = nullptr;
+std::once_flag g_ctx_once;
 
 // Device address of g_scratch on the current device.  In host code the
 // symbol names a host-side stand-in, so the address has to come from the
-// runtime, once per device, with that device current.
+// runtime, once per device, with that device current.  It is looked up again
+// when the device's current context differs from the one it was found in
+// (a cudaDeviceReset destroys the context and the module with the scratch).
 int scratch_on_current_device(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return MRSA_ERR_LAUNCH;
   if (dev < 0 || dev >= kMaxDevices) return MRSA_ERR_ARG;
+  // CUDA 12 creates the device's primary context here if the runtime has not yet
+  if (cudaSetDevice(dev) != cudaSuccess) return MRSA_ERR_LAUNCH;
+  std::call_once(g_ctx_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get = reinterpret_cast<CtxGetCurrent>(fn);
+  });
+  if (g_ctx_get == nullptr) return MRSA_ERR_LAUNCH;
+  CUcontext ctx = nullptr;
+  if (g_ctx_get(&ctx) != CUDA_SUCCESS || ctx == nullptr) return MRSA_ERR_LAUNCH;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  ScratchAddr& e = g_scratch_addr[dev];
+  if (e.addr == nullptr || e.ctx != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) return MRSA_ERR_LAUNCH;
-    g_scratch_addr[dev] = p;
+    e.ctx = ctx;
+    e.addr = p;
   }
-  *out = g_scratch_addr[dev];
+  *out = e.addr;
   return MRSA_OK;
 }
 

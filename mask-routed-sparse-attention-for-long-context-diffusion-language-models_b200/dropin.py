@@ -55,6 +55,10 @@ PATCHES = {
 }
 
 _ORIGINALS: dict = {}
+# class attribute that keeps the reference forward of a class whose forward
+# is replaced by _fused_forward (the fused path hands every case it does not
+# implement back to it)
+_REFERENCE_FORWARD = "_mrsa_b200_reference_forward"
 
 
 def install(*, fused_layer: bool = False, strict: bool = False):
@@ -77,12 +81,22 @@ def install(*, fused_layer: bool = False, strict: bool = False):
         done.append(f"{mod_name}.{attr}")
     if fused_layer:
         mod = importlib.import_module("dream_dllm_hils.attention")
-        cls = mod.KernelDreamFullHiLSAttention
+        install_fused_forward(mod.KernelDreamFullHiLSAttention)
         _ORIGINALS.setdefault(("dream_dllm_hils.attention", "KernelDreamFullHiLSAttention.forward"),
-                              cls.forward)
-        cls.forward = _fused_forward
+                              getattr(mod.KernelDreamFullHiLSAttention, _REFERENCE_FORWARD))
         done.append("dream_dllm_hils.attention.KernelDreamFullHiLSAttention.forward")
     return done
+
+
+def install_fused_forward(cls):
+    """Replace ``cls.forward`` (the signature of
+    ``KernelDreamFullHiLSAttention.forward``, ``attention.py:1313-1324``) by
+    :func:`_fused_forward`, keeping the class's own forward for the cases the
+    fused layer does not implement."""
+    if cls.__dict__.get("forward") is _fused_forward:
+        return
+    setattr(cls, _REFERENCE_FORWARD, cls.forward)
+    cls.forward = _fused_forward
 
 
 def uninstall():
@@ -91,10 +105,130 @@ def uninstall():
         mod = importlib.import_module(mod_name)
         if "." in attr:
             cls_name, meth = attr.split(".")
-            setattr(getattr(mod, cls_name), meth, orig)
+            cls = getattr(mod, cls_name)
+            setattr(cls, meth, orig)
+            if _REFERENCE_FORWARD in cls.__dict__:
+                delattr(cls, _REFERENCE_FORWARD)
         else:
             setattr(mod, attr, orig)
     _ORIGINALS.clear()
+
+
+def fused_unsupported(self, hidden_states, attention_mask=None, position_ids=None,
+                      past_key_value=None, use_cache=False, position_embeddings=None):
+    """Why :func:`_fused_forward` cannot reproduce the reference forward of
+    ``self`` for this call (``None`` when it can).
+
+    The fused layer is the eval / prefill forward of the canonical config
+    (``attention.py:1358-1774`` with the defaults of ``:906-920``): attention
+    pooled chunk summaries with the entropy prior, landmark slots skipped in
+    the local branch, Q-Cal with RMSNorm, post-softmax routing, the affine
+    fusion gate, no token refinement, no forced or ablated routes, no hooks
+    and no prefill capture, cos/sin from the module's rotary embedding."""
+    import torch
+
+    if self.training:
+        return "training forward"
+    if use_cache or past_key_value is not None:
+        return "KV cache requested"
+    validate = getattr(self, "_validate_kernel_call", None)
+    if validate is not None:
+        reason = validate(hidden_states, attention_mask)
+        if reason is not None:
+            return str(reason)
+    if hidden_states.device.type != "cuda" or hidden_states.dtype != torch.bfloat16:
+        return "hidden states must be BF16 on a CUDA device"
+    if attention_mask is not None and not isinstance(attention_mask, str) and attention_mask.ndim != 2:
+        return "4-D allowed mask (routed through remote_drop_mask by the reference)"
+    if position_embeddings is not None:
+        return "explicit position_embeddings"
+    if position_ids is None:
+        return "no position_ids"
+    if (self.chunk_size, self.head_dim) != (64, 128):
+        return "chunk_size 64 and head_dim 128 only"
+    if self.num_heads % self.num_key_value_heads or self.num_heads // self.num_key_value_heads > 8:
+        return "query heads per KV head must be at most 8"
+    checks = (
+        (getattr(self, "skip_inert_slots", True) is not True, "skip_inert_slots=False"),
+        (str(getattr(self, "chunk_summary", "attn")) != "attn", "chunk_summary != 'attn'"),
+        (not bool(getattr(self, "entropy_prior", True)), "entropy_prior=False"),
+        (callable(getattr(self, "_lmk_keys_intervene", None)), "landmark intervention hook"),
+        (callable(getattr(self, "_lmk_summary_hook", None)), "landmark summary hook"),
+        (bool(getattr(self, "_prefill_capture", False)), "prefill cache capture"),
+        (getattr(self, "route_query_positions", None) is not None, "route_query_positions"),
+        (str(getattr(self, "route_selection_mode", "post_softmax")) != "post_softmax",
+         "route_selection_mode != 'post_softmax'"),
+        (getattr(self, "force_remote_query_mask", None) is not None, "forced remote routes"),
+        (bool(getattr(self, "force_remote_oracle_route", False)), "oracle routes"),
+        (float(getattr(self, "value_fusion_beta", 0.0) or 0.0) > 0, "value-aware fusion"),
+        (int(getattr(self, "token_budget", 0) or 0) > 0, "token refinement"),
+        (float(getattr(self, "route_residual_weight", 0.0) or 0.0) > 0, "soft route residual"),
+        (not hasattr(self, "qcal"), "no Q-Cal (route_q = q)"),
+        (getattr(self, "qcal_norm", None) is None, "Q-Cal without RMSNorm"),
+        (getattr(getattr(self, "rotary_emb", None), "inv_freq", None) is None,
+         "no rotary_emb.inv_freq"),
+    )
+    for bad, why in checks:
+        if bad:
+            return why
+    qc = self.qcal
+    try:
+        w_in, w_out = qc[0].weight, qc[1].weight
+    except (TypeError, IndexError, AttributeError):
+        return "Q-Cal is not a two-layer Sequential"
+    if len(qc) != 2 or getattr(qc[0], "bias", None) is not None or getattr(qc[1], "bias", None) is not None:
+        return "Q-Cal is not two bias-free linear layers"
+    if w_in.shape[0] != 64 or w_out.shape != (self.num_heads * self.head_dim, 64):
+        return "Q-Cal rank must be 64"
+    if w_in.shape[1] != hidden_states.shape[-1]:
+        return "Q-Cal input width differs from the hidden size"
+    return None
+
+
+def _fused_layer_for(self, device):
+    """The module's :class:`RouteLayer`, rebuilt whenever a parameter it
+    copies from changed (storage or in-place version)."""
+    import torch
+
+    from .layer import RouteLayer, RouteLayerConfig
+
+    norm = self.qcal_norm
+    rot = self.rotary_emb
+    srcs = [self.qcal[0].weight, self.qcal[1].weight, norm.weight, self.entropy_bias_scale,
+            rot.inv_freq]
+    gate_off = getattr(self, "fusion_gate_offset", None)
+    gate_scale = getattr(self, "fusion_gate_scale", None)
+    srcs += [t for t in (gate_off, gate_scale) if isinstance(t, torch.Tensor)]
+    sig = tuple((t.data_ptr(), t._version) for t in srcs) + (str(device),)
+    layer = getattr(self, "_mrsa_b200_layer", None)
+    if layer is not None and getattr(self, "_mrsa_b200_sig", None) == sig:
+        return layer
+    # topk < 32 takes the reference's route_weights kernel: a plain softmax over
+    # [routed logits, local LSE], i.e. the affine gate at scale 1, offset 0, T = 1
+    affine = self.topk >= 32
+    cfg = RouteLayerConfig(q_heads=self.num_heads, kv_heads=self.num_key_value_heads,
+                           head_dim=self.head_dim, chunk=self.chunk_size, topk=self.topk,
+                           local_window=self.local_window, rms_eps=float(norm.eps),
+                           qcal_scale=float(getattr(self, "qcal_scale", 1.0)),
+                           route_temperature=float(self.route_temperature) if affine else 1.0)
+    layer = RouteLayer(self.qcal[0].weight.detach().to(device), self.qcal[1].weight.detach().to(device),
+                       norm.weight.detach(), self.entropy_bias_scale.detach(),
+                       gate_offset=float(gate_off) if (affine and gate_off is not None) else 0.0,
+                       gate_scale=float(gate_scale) if (affine and gate_scale is not None) else 1.0,
+                       cfg=cfg)
+    layer.inv_freq = rot.inv_freq.detach().float().to(device).contiguous()
+    layer.attention_factor = float(getattr(rot, "attention_scaling", 1.0))
+    self._mrsa_b200_layer = layer
+    self._mrsa_b200_sig = sig
+    return layer
+
+
+def _reference_forward(self):
+    for klass in type(self).__mro__:
+        fwd = klass.__dict__.get(_REFERENCE_FORWARD)
+        if fwd is not None:
+            return fwd
+    raise RuntimeError("the fused route-layer forward is installed without a reference forward")
 
 
 def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_value=None,
@@ -102,37 +236,25 @@ def _fused_forward(self, hidden_states, attention_mask=None, position_ids=None, 
                    position_embeddings=None, **kwargs):
     """``KernelDreamFullHiLSAttention.forward`` (``attention.py:1313``) on
     :class:`RouteLayer`: the module's own q/k/v projections, the whole routed
-    attention in one C-ABI call, then ``o_proj``.  Eval / prefill only: the
-    reference's training-only branches are not supported."""
+    attention in one C-ABI call, then ``o_proj``.  Every call the fused layer
+    does not reproduce exactly (:func:`fused_unsupported`: training, caches,
+    4-D masks, explicit cos/sin, non-default summaries, hooks, forced routes,
+    token refinement, ...) goes to the reference forward instead, which runs
+    on the drop-in ops."""
     import torch
 
-    from .layer import RouteLayer, RouteLayerConfig
-
-    if use_cache or past_key_value is not None or self.training:
-        raise NotImplementedError("the fused B200 route layer is an eval/prefill forward")
+    why = fused_unsupported(self, hidden_states, attention_mask, position_ids, past_key_value, use_cache,
+                            position_embeddings)
+    if why is not None:
+        return _reference_forward(self)(self, hidden_states, attention_mask, position_ids, past_key_value,
+                                        output_attentions, use_cache, cache_position, position_embeddings,
+                                        **kwargs)
     bsz, q_len, _ = hidden_states.shape
     q = self.q_proj(hidden_states).view(bsz, q_len, self.num_heads, self.head_dim)
     k = self.k_proj(hidden_states).view(bsz, q_len, self.num_key_value_heads, self.head_dim)
     v = self.v_proj(hidden_states).view(bsz, q_len, self.num_key_value_heads, self.head_dim)
-    if position_ids is None:
-        position_ids = torch.arange(q_len, device=hidden_states.device).expand(bsz, q_len)
     key_valid = self._key_valid_mask(attention_mask, bsz, q_len, hidden_states.device)
-    layer = getattr(self, "_mrsa_b200_layer", None)
-    if layer is None:
-        cfg = RouteLayerConfig(q_heads=self.num_heads, kv_heads=self.num_key_value_heads,
-                               head_dim=self.head_dim, chunk=self.chunk_size, topk=self.topk,
-                               local_window=self.local_window,
-                               qcal_scale=float(getattr(self, "qcal_scale", 1.0)),
-                               route_temperature=float(self.route_temperature))
-        layer = RouteLayer(self.qcal[0].weight.detach(), self.qcal[1].weight.detach(),
-                           self.qcal_norm.weight.detach(), self.entropy_bias_scale.detach(),
-                           gate_offset=float(self.fusion_gate_offset),
-                           gate_scale=float(self.fusion_gate_scale), cfg=cfg)
-        rot = getattr(self, "rotary_emb", None)
-        if rot is not None and hasattr(rot, "inv_freq"):
-            layer.inv_freq = rot.inv_freq.detach().float().to(hidden_states.device)
-            layer.attention_factor = float(getattr(rot, "attention_scaling", 1.0))
-        self._mrsa_b200_layer = layer
-    out = layer(q.contiguous(), k.contiguous(), v.contiguous(), hidden_states.contiguous(),
-                position_ids.to(torch.long).contiguous(), key_valid)
-    return self.o_proj(out.reshape(bsz, q_len, self.hidden_size)), None, past_key_value
+    layer = _fused_layer_for(self, hidden_states.device)
+    pos = position_ids.to(device=hidden_states.device, dtype=torch.long).expand(bsz, q_len).contiguous()
+    out = layer(q.contiguous(), k.contiguous(), v.contiguous(), hidden_states.contiguous(), pos, key_valid)
+    return self.o_proj(out.reshape(bsz, q_len, self.num_heads * self.head_dim)), None, past_key_value

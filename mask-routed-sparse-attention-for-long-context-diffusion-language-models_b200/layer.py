@@ -24,6 +24,22 @@ from .routing import route_topk_fused
 from .selected_attention import selected_attention, to_f16
 
 
+def raise_device_errors():
+    """Read and clear the device error flags (synchronises with the device);
+    raise when a kernel set one: bit 3 = V outside the fp16 range (the
+    attention kernels take V in fp16; larger magnitudes saturate), bits 0-2
+    = a selected-attention, routing or window kernel gave up on a bounded
+    wait."""
+    flags = int(_lib.load().mrsa_device_error_flags(1))
+    if flags < 0:
+        raise RuntimeError(f"could not read the device error flags ({_lib.load().mrsa_strerror(flags).decode()})")
+    if flags & 8:
+        raise ValueError("V holds values beyond the fp16 range (|v| > 65504); the route layer's "
+                         "attention kernels take V in fp16")
+    if flags:
+        raise RuntimeError(f"a route-layer kernel gave up on a bounded wait (device error flags {flags:#x})")
+
+
 @dataclass
 class RouteLayerConfig:
     """Hot-path constants of the canonical config
@@ -53,8 +69,12 @@ class RouteLayer:
     (the ``fusion_gate_*`` parameters, ``attention.py:913-914``)."""
 
     def __init__(self, w_in, w_out, norm_weight=None, entropy_bias_scale=None, *, gate_offset=0.0,
-                 gate_scale=1.0, cfg: RouteLayerConfig | None = None):
+                 gate_scale=1.0, cfg: RouteLayerConfig | None = None, check_errors: bool = True):
         self.cfg = cfg or RouteLayerConfig()
+        # read the device error flags after every fused forward (one small
+        # synchronous read): V beyond the fp16 range, or a kernel that gave
+        # up on a bounded wait, then raises instead of returning inf/NaN rows
+        self.check_errors = bool(check_errors)
         dev = w_in.device
         if dev.type != "cuda":
             raise ValueError("RouteLayer weights must live on a CUDA device")
@@ -118,6 +138,8 @@ class RouteLayer:
             self._ws = torch.empty(need, dtype=torch.uint8, device=q_pre.device)
         _lib.call("mrsa_route_layer_forward", C.byref(a), C.c_void_p(self._ws.data_ptr()),
                   C.c_size_t(self._ws.numel()), _lib.stream_of(q_pre))
+        if self.check_errors:
+            raise_device_errors()
         return out
 
     __call__ = forward

@@ -48,6 +48,9 @@ __all__ = [
     "fuse_outputs",
     "make_route_layer_inputs",
     "route_layer_forward",
+    "route_layer_shared",
+    "route_layer_rows",
+    "remote_drop_mask_rows",
     "swa_layer_forward",
     "topk_set_agreement",
     "route_keys",
@@ -72,6 +75,7 @@ class MRSAConfig:
     yarn_factor: float = 8.0
     yarn_orig_max_pos: int = 2048
     rms_eps: float = 1e-6
+    qcal_scale: float = 1.0    # qcal_scale (attention.py:473-475)
     route_temperature: float = 1.0
     rope_precision: str = "fp32"
 
@@ -224,6 +228,22 @@ def remote_drop_mask(key_valid: torch.Tensor, window: int, chunk: int) -> torch.
     pos = torch.arange(l)
     real = (pos + 1) % chunk != 0
     chunk_ok = (key_valid.bool() & real[None]).view(b, c, chunk).any(-1)
+    lo = (pos - window).clamp_min(0) // chunk
+    hi = (pos + window).clamp_max(l - 1) // chunk
+    cid = torch.arange(c)
+    local = (cid[None, :] >= lo[:, None]) & (cid[None, :] <= hi[:, None])
+    return (local[None] | ~chunk_ok[:, None, :]).to(torch.int32)
+
+
+def remote_drop_mask_rows(key_valid: torch.Tensor, window: int, chunk: int, qs: slice) -> torch.Tensor:
+    """The rows ``qs`` of :func:`remote_drop_mask` (the same rule evaluated
+    for those query positions only; the whole mask is 1 GB at 131072
+    tokens)."""
+    b, l = key_valid.shape
+    c = l // chunk
+    real = (torch.arange(l) + 1) % chunk != 0
+    chunk_ok = (key_valid.bool() & real[None]).view(b, c, chunk).any(-1)
+    pos = torch.arange(l)[qs]
     lo = (pos - window).clamp_min(0) // chunk
     hi = (pos + window).clamp_max(l - 1) // chunk
     cid = torch.arange(c)
@@ -498,7 +518,8 @@ def make_route_layer_inputs(batch: int, seq_len: int, cfg: MRSAConfig = MRSAConf
 
 
 def route_layer_forward(inp: dict, cfg: MRSAConfig = MRSAConfig(), *, keep: bool = True,
-                        query_slice: slice | None = None, indices: torch.Tensor | None = None):
+                        query_slice: slice | None = None, indices: torch.Tensor | None = None,
+                        shared: dict | None = None):
     """Route-layer forward from post-projection q/k/v/h to the pre-``o_proj``
     output, in the order of ``KernelDreamFullHiLSAttention.forward``
     (``dream_dllm_hils/attention.py:1358-1774``): RoPE, local branch, Q-Cal,
@@ -508,11 +529,31 @@ def route_layer_forward(inp: dict, cfg: MRSAConfig = MRSAConfig(), *, keep: bool
     landmark pool still covers every chunk.  ``indices`` (for the sliced rows)
     replaces the oracle's own selection -- scores, weights and outputs are
     then evaluated on those chunks, which decouples near-tie selection flips
-    from the attention comparison.  Returns a dict of every intermediate
-    (``keep``) plus ``out``.
+    from the attention comparison.  ``shared`` is the result of
+    :func:`route_layer_shared` for the same inputs (computed here when not
+    given).  Returns a dict of every intermediate (``keep``) plus ``out``.
+
+    With a ``query_slice`` smaller than the sequence, the returned ``q`` and
+    ``route_q`` hold only the rows that slice needs (the slice and the
+    landmark rows; zero elsewhere): RoPE and Q-Cal are per-row maps, so the
+    rows computed are exactly those of the whole-sequence result.
     """
+    l = inp["q_pre"].shape[1]
+    qs = query_slice or slice(0, l)
+    if shared is None:
+        shared = route_layer_shared(inp, cfg, query_slice=qs)
+    return route_layer_rows(inp, shared, cfg, qs, keep=keep, indices=indices)
+
+
+def route_layer_shared(inp: dict, cfg: MRSAConfig = MRSAConfig(), *,
+                       query_slice: slice | None = None, rows: torch.Tensor | None = None):
+    """The stages every query row shares: YaRN cos/sin, RoPE of K, Q-Cal of
+    the landmark rows, landmark pool and entropy prior
+    (``dream_dllm_hils/attention.py:1358-1430``).  RoPE and Q-Cal of the query
+    rows run on ``rows`` (a bool ``[L]`` mask; default: the landmark rows plus
+    ``query_slice``, or every row) only."""
     chunk, d = cfg.chunk, cfg.head_dim
-    q_pre, k_pre, v = inp["q_pre"], inp["k_pre"], inp["v"]
+    q_pre, k_pre = inp["q_pre"], inp["k_pre"]
     b, l, hq, _ = q_pre.shape
     hkv = k_pre.shape[2]
     g = hq // hkv
@@ -520,26 +561,50 @@ def route_layer_forward(inp: dict, cfg: MRSAConfig = MRSAConfig(), *, keep: bool
     inv_freq, af = yarn_inv_freq(d, cfg.rope_theta, cfg.yarn_factor, cfg.yarn_orig_max_pos)
     cos, sin = rope_cos_sin(inp["position_ids"], inv_freq, af)
     prec = cfg.rope_precision
-    q = apply_rope(q_pre, cos, sin, prec)
     k = apply_rope(k_pre, cos, sin, prec)
-    key_valid = inp["key_valid"].bool()
-    qs = query_slice or slice(0, l)
-    # route_q is only needed for the queried rows and the landmark rows
-    rows = torch.zeros(l, dtype=torch.bool)
-    rows[qs] = True
-    rows[chunk - 1::chunk] = True
+    if rows is None:
+        rows = torch.zeros(l, dtype=torch.bool)
+        rows[query_slice or slice(0, l)] = True
+        rows[chunk - 1::chunk] = True
     ridx = rows.nonzero().squeeze(1)
-    rq_rows = qcal_route_query(inp["hidden"][:, ridx], q[:, ridx], inp["w_in"], inp["w_out"],
-                               inp["norm_weight"], cos[:, ridx], sin[:, ridx],
-                               eps=cfg.rms_eps, precision=prec)
-    route_q = torch.zeros_like(q)
-    route_q[:, ridx] = rq_rows
+    full = bool(rows.all())
+    q_rows = apply_rope(q_pre if full else q_pre[:, ridx], cos if full else cos[:, ridx],
+                        sin if full else sin[:, ridx], prec)
+    rq_rows = qcal_route_query(inp["hidden"] if full else inp["hidden"][:, ridx], q_rows,
+                               inp["w_in"], inp["w_out"], inp["norm_weight"],
+                               cos if full else cos[:, ridx], sin if full else sin[:, ridx],
+                               eps=cfg.rms_eps, scale=cfg.qcal_scale, precision=prec)
+    if full:
+        q, route_q = q_rows, rq_rows
+    else:
+        q = torch.zeros_like(q_pre)
+        q[:, ridx] = q_rows
+        route_q = torch.zeros_like(q_pre)
+        route_q[:, ridx] = rq_rows
+    key_valid = inp["key_valid"].bool()
     mu_q = route_q[:, chunk - 1::chunk].reshape(b, c, hkv, g, d)
     lmk, entropy = chunk_pool(mu_q, k.view(b, c, chunk, hkv, d), key_valid.view(b, c, chunk))
     prior = entropy * inp["entropy_bias_scale"].float().view(1, 1, hkv, g)
-    # per-query stages on the slice, with full K/V
+    return {"q": q, "k": k, "route_q": route_q, "rows": rows, "lmk": lmk, "entropy": entropy,
+            "prior_bias": prior, "cos": cos, "sin": sin, "key_valid": key_valid}
+
+
+def route_layer_rows(inp: dict, shared: dict, cfg: MRSAConfig, qs: slice, *, keep: bool = True,
+                     indices: torch.Tensor | None = None):
+    """The per-query stages of the route layer on the query rows ``qs``
+    (local branch, drop mask, routing, route weights, selected attention,
+    fusion; ``dream_dllm_hils/attention.py:1380-1774``) over the shared
+    stages of :func:`route_layer_shared`."""
+    chunk = cfg.chunk
+    v = inp["v"]
+    q, k, route_q, lmk, prior = shared["q"], shared["k"], shared["route_q"], shared["lmk"], shared["prior_bias"]
+    key_valid = shared["key_valid"]
+    b, l, hq, _ = q.shape
+    hkv = k.shape[2]
+    g = hq // hkv
+    assert bool(shared["rows"][qs].all()), "the shared stages did not compute these query rows"
     local_o, local_lse = _local_rows(q, k, v, key_valid, cfg.local_window, chunk, True, qs)
-    drop = remote_drop_mask(key_valid, cfg.local_window, chunk)[:, qs]
+    drop = remote_drop_mask_rows(key_valid, cfg.local_window, chunk, qs)
     idx, scores = route_topk_blocked(route_q[:, qs], lmk, local_lse.view(b, -1, hkv, g), prior, drop, cfg.topk)
     if indices is not None:
         idx = indices.long().cpu()
@@ -551,9 +616,10 @@ def route_layer_forward(inp: dict, cfg: MRSAConfig = MRSAConfig(), *, keep: bool
     res = {"out": out}
     if keep:
         res.update(route_key=route_keys(route_q[:, qs], lmk, local_lse.view(b, -1, hkv, g), prior, drop))
-        res.update(q=q, k=k, route_q=route_q, lmk=lmk, entropy=entropy, prior_bias=prior,
+        res.update(q=q, k=k, route_q=route_q, lmk=lmk, entropy=shared["entropy"], prior_bias=prior,
                    local_out=local_o, local_lse=local_lse, indices=idx, scores=scores,
-                   remote_weights=rw, local_weight=lw, remote_out=remote, cos=cos, sin=sin)
+                   remote_weights=rw, local_weight=lw, remote_out=remote, cos=shared["cos"],
+                   sin=shared["sin"], rows=shared["rows"])
     return res
 
 
