@@ -41,12 +41,13 @@
 // partial buffers.  An S buffer is released as soon as the item's softmax has
 // loaded it and a partial buffer as soon as the accumulate warps have read it,
 // so neither cycle waits on the other.
-// Owner j of item i goes to S row slot 2*((j+rot)%4) + j/4 with rot =
-// (i/2)%4, so the first four owners land in four different TMEM quadrants and
-// four softmax warps share the rows, and a group's successive items with one
-// or two owners put them in different quadrants, whose warps then compute
-// those items side by side.  Every mbarrier wait is bounded and a shared abort flag unwinds all
-// roles; an aborted CTA waits (bounded) for its own copies and MMAs in flight.
+// Owners fill TMEM quadrants two at a time: owner j of an item goes to S row
+// slot 2*((base + j/2) % 4) + j%2, and each softmax group's items take the
+// quadrants in turn (base advances by ceil(owners/2) per item of the group),
+// so an item with n owners keeps ceil(n/2) softmax warps busy with full rows
+// and the group's next item runs on the other warps beside it.  Every mbarrier
+// wait is bounded and a shared abort flag unwinds all roles; an aborted CTA
+// waits (bounded) for its own copies and MMAs in flight.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -77,6 +78,7 @@ struct Item {
   int c;                          // chunk
   uint8_t oq[OWN];                // owner query (CTA-local), compact order
   uint8_t slot[OWN];              // owner's slot in its chunk list (route weight)
+  int base;                       // TMEM quadrant of owners 0 and 1 (see the S row placement)
 };
 
 struct __align__(1024) TcSmem {
@@ -359,6 +361,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     asm volatile("bar.sync 2, 64;\n" ::: "memory");
     const uint32_t below = (1u << lane) - 1u;
     int item = 0;
+    int qcur = 0;                            // next S-tile quadrant of this warp's (softmax group's) items
     bool ok = true;
     for (int u = 0; ok && u < sm.nu; ++u) {
       const int2 ue = sm.ulist[u];
@@ -383,10 +386,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
             sm.ring[r].oq[j] = static_cast<uint8_t>(lane);
             sm.ring[r].slot[j] = static_cast<uint8_t>(my_slot);
           }
+          const int base = qcur;
+          qcur = (qcur + (n + 1) / 2) & 3;
           if (lane == 0) {
             sm.ring[r].n = n;
             sm.ring[r].u = u;
             sm.ring[r].c = c;
+            sm.ring[r].base = base;
           }
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(su32(&sm.bar_ring[r]));
@@ -402,7 +408,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
           }
           __syncwarp();
           if (mine) {
-            const int slot = 2 * ((j + (item >> 1)) & 3) + (j >> 2);
+            const int slot = 2 * ((base + (j >> 1)) & 3) + (j & 1);
             const int qy = static_cast<int>((b * a.Lq + q0 + lane) * Hq + hk * G);
             tc::tma_load_3d(su32(sm.at[st] + slot * 2048), &tm_q, 0, qy, 0, bar);
           }
@@ -508,8 +514,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       const int p2 = it & 1, r = it % RING;
       if (!wait_bar_warp(sm, &sm.bar_ring[r], (it / RING) & 1)) break;
       const int n = sm.ring[r].n;
-      const int qo = (q - (it >> 1)) & 3;    // this quadrant holds owners qo and qo + 4
-      const int jrow = t < 8 ? qo : qo + 4;  // owner (compact index) of this thread's row
+      const int qo = 2 * ((q - sm.ring[r].base) & 3);   // this quadrant holds owners qo and qo + 1
+      const int jrow = qo + (t >> 3);        // owner (compact index) of this thread's row
       const bool row_on = jrow < n;
       float w = 0.f;
       uint32_t km = 0xFFFFFFFFu;             // rows without an owner are computed and dropped
@@ -538,10 +544,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
         }
       }
       tc::fence_after_sync();
-      // Quadrant q holds the rows of owners qo and qo+4: with fewer than qo+1
-      // owners (most items when the chunks are many and each is picked by
-      // one or two of the block's queries) the warp has no row to compute and
-      // keeps only its hand-offs, which frees issue slots for the other roles.
+      // Quadrant q holds the rows of owners qo and qo+1: with fewer than qo+1
+      // owners the warp has no row to compute and keeps only its hand-offs,
+      // which frees issue slots for the other roles.
       const bool quad_on = qo < n;           // warp-uniform
       uint32_t x[32];
       if (quad_on) {
