@@ -221,9 +221,12 @@ def _cpu_model():
 
 
 def _shares(l_total: int, n_queries: int, steps: int):
-    """``steps`` disjoint query-row slices of ``n_queries // steps`` rows
-    spread evenly over the sequence (with ``n_queries == l_total`` and
-    ``steps`` dividing it: the whole sequence)."""
+    """``steps`` disjoint query-row slices spread evenly over the sequence,
+    ``n_queries`` rows in all (with ``n_queries == l_total``: the whole
+    sequence, the remainder rows spread one each over the first slices)."""
+    if n_queries >= l_total:
+        bounds = [l_total * s // steps for s in range(steps + 1)]
+        return [slice(bounds[s], bounds[s + 1]) for s in range(steps)]
     per = max(1, n_queries // steps)
     stride = l_total // steps
     return [slice(s * stride, s * stride + per) for s in range(steps)]
@@ -253,7 +256,7 @@ def run_reference(args, world, rank):
     rows = sum(sl.stop - sl.start for sl in shares)
     value = rows / total
     cores = torch.get_num_threads()
-    sample = (f"oracle route layer at L={l_total}: {args.steps} timed steps of {rows // args.steps} disjoint "
+    sample = (f"oracle route layer at L={l_total}: {args.steps} timed steps of ~{rows // args.steps} disjoint "
               f"query rows ({rows} rows{', the whole layer' if rows == l_total else ''}); the stages all rows "
               "share (K RoPE, landmark Q-Cal, pool, prior) inside the first step")
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,

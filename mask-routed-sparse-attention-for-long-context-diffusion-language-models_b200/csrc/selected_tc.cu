@@ -360,6 +360,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
     // loaders have read them before either issues a copy
     asm volatile("bar.sync 2, 64;\n" ::: "memory");
     const uint32_t below = (1u << lane) - 1u;
+    // A list of distinct chunks in ascending order, -1 only after them (as the
+    // routing produces it): the union walk visits this lane's chunks in slot
+    // order, so the slot of its k-th chunk is k.  Other lists search for it.
+    bool sorted_list = true;
+#pragma unroll
+    for (int kk = 0; kk + 1 < KMAX; ++kk)
+      sorted_list &= myc[kk + 1] < 0 || (myc[kk] >= 0 && myc[kk] < myc[kk + 1]);
+    int visited = 0;                         // this lane's chunks walked so far
     int item = 0;
     int qcur = 0;                            // next S-tile quadrant of this warp's (softmax group's) items
     bool ok = true;
@@ -367,7 +375,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) selected_tc_kernel(
       const int2 ue = sm.ulist[u];
       const int c = ue.x;
       uint32_t owners = static_cast<uint32_t>(ue.y);
-      int my_slot = -1;                      // this lane's slot of chunk c, found on first use
+      int my_slot = sorted_list ? visited : -1;   // -1: found on first use
+      visited += (owners >> lane) & 1u;
       while (owners) {
         // the next (up to) OWN owners, in query order
         const int j = __popc(owners & below);
