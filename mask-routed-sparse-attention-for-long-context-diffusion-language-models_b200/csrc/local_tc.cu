@@ -19,7 +19,9 @@
 // its own running max, sum and O accumulator, so two softmax warps share each
 // scheduler; the epilogue merges the two partial softmaxes.  Warp 8: TMA (Q
 // once, then K, V per tile, 3 stages) and the per-tile key validity mask;
-// warp 9: MMA issue (converged, elect.sync).  Every mbarrier
+// warps 9 and 10: MMA issue for the even and the odd tiles (converged,
+// elect.sync; one issuing thread takes about twice the tensor pipe's time per
+// MMA instruction).  Every mbarrier
 // wait is bounded and unwinds through a shared abort flag.
 //
 // The same kernel also runs the causal chunk-expanded window of
@@ -43,7 +45,7 @@ constexpr int LQ = 16;            // queries per CTA
 constexpr int LN = 64;            // keys per tile
 constexpr int LST = 3;            // K/V stages
 constexpr int D = kHeadDim;
-constexpr int L_THREADS = 320;    // warps 0-7 softmax (two groups), 8 TMA, 9 MMA
+constexpr int L_THREADS = 352;    // warps 0-7 softmax (two groups), 8 TMA, 9-10 MMA (even / odd tiles)
 constexpr int L_W_LOAD = 8, L_W_MMA = 9;
 constexpr uint32_t kOCol = 128;   // O accumulators of groups 0 / 1 at [128, 256) / [256, 384); S at 0 and 64
 
@@ -55,7 +57,10 @@ struct __align__(1024) LocalSmem {
   unsigned char pl[2][16384];         // P lo
   unsigned long long kmask[LST];      // bit j: key j of the stage's tile is usable (not zeroed)
   float part_m[2][128], part_l[2][128];   // per group and row: running max / sum for the merge
-  uint64_t qfull, kvfull[LST], kvfree[LST], sdone[2], pready[2], pvdone[2], drain;
+  // K/V stage barriers per stage and tile parity: the two parities' MMAs are
+  // issued by different warps, and a barrier's phases must belong to one
+  // waiter's tiles in order
+  uint64_t qfull, kvfull[LST][2], kvfree[LST][2], sdone[2], pready[2], pvdone[2], drain[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -130,19 +135,23 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
   const int t_lo = static_cast<int>(j_lo / LN);
   const int NTL = j_hi >= j_lo ? static_cast<int>(j_hi / LN) - t_lo + 1 : 0;
+  // phase parity of tile t on its (stage, parity) barrier: tiles of one stage
+  // and parity are 2*LST apart
+  auto kv_phase = [](int t) { return (t / (2 * LST)) & 1; };
 
   if (tid == 0) {
     tc::mbar_init(tc::smem_addr(&sm.qfull), 1);
-    for (int s = 0; s < LST; ++s) {
-      tc::mbar_init(tc::smem_addr(&sm.kvfull[s]), 1);
-      tc::mbar_init(tc::smem_addr(&sm.kvfree[s]), 1);
-    }
+    for (int s = 0; s < LST; ++s)
+      for (int p = 0; p < 2; ++p) {
+        tc::mbar_init(tc::smem_addr(&sm.kvfull[s][p]), 1);
+        tc::mbar_init(tc::smem_addr(&sm.kvfree[s][p]), 1);
+      }
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(tc::smem_addr(&sm.sdone[s]), 1);
       tc::mbar_init(tc::smem_addr(&sm.pready[s]), 4);
       tc::mbar_init(tc::smem_addr(&sm.pvdone[s]), 1);
     }
-    tc::mbar_init(tc::smem_addr(&sm.drain), 1);
+    for (int s = 0; s < 2; ++s) tc::mbar_init(tc::smem_addr(&sm.drain[s]), 1);
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -182,7 +191,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       const int st = t % LST;
       const uint32_t vb[2] = {vb_next[0], vb_next[1]};
       valid_bytes(t + 1, vb_next);
-      if (t >= LST && !tc::wait_bounded_warp(tc::smem_addr(&sm.kvfree[st]), ((t / LST) - 1) & 1, abort_flag)) break;
+      if (t >= LST && !tc::wait_bounded_warp(tc::smem_addr(&sm.kvfree[st][(t - LST) & 1]), kv_phase(t - LST), abort_flag)) break;
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
       // usable keys of the tile: inside the sequence, valid, and not a landmark slot when skip_inert
       uint32_t mk[2];
@@ -195,7 +204,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       }
       if (lane == 0) {
         sm.kmask[st] = static_cast<unsigned long long>(mk[0]) | (static_cast<unsigned long long>(mk[1]) << 32);
-        const uint32_t kb = tc::smem_addr(&sm.kvfull[st]);
+        const uint32_t kb = tc::smem_addr(&sm.kvfull[st][t & 1]);
         tc::mbar_arrive_expect_tx(kb, 2u * 16384u);
         tc::tma_load_4d(tc::smem_addr(sm.k[st]), &tm_k, 0, static_cast<int>(b * a.Lk + j0), 0, hk, kb);
         tc::tma_load_4d(tc::smem_addr(sm.v[st]), &tm_v, 0, static_cast<int>(b * a.Lk + j0), 0, hk, kb);
@@ -205,11 +214,15 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     if (lane == 0) {
       tc::mbar_wait(qb, 0);
       for (int tt = t - LST < 0 ? 0 : t - LST; tt < t; ++tt)
-        tc::mbar_wait(tc::smem_addr(&sm.kvfull[tt % LST]), (tt / LST) & 1);
+        tc::mbar_wait(tc::smem_addr(&sm.kvfull[tt % LST][tt & 1]), kv_phase(tt));
     }
     __syncwarp();
-  } else if (warp == L_W_MMA) {
-    // ============================ MMA issue (converged warp) ==================
+  } else if (warp >= L_W_MMA) {
+    // ============================ MMA issue (two converged warps) =============
+    // Warp 9 issues the MMAs of the even tiles, warp 10 those of the odd tiles
+    // (one issuing thread needs about twice the tensor pipe's time per MMA):
+    // S(t) into S buffer t%2, then per tile P.V(t) into its group's O and S(t+2).
+    const int par = warp - L_W_MMA;
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, LN, 0, 0);
     // kind::f16 with fp16 A and B: the bf16 format bits cleared
     constexpr uint32_t id_o = tc::idesc_bf16_f32(128, D, 0, 1) & (kF16 ? ~((1u << 7) | (1u << 10)) : ~0u);
@@ -220,30 +233,30 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     const uint64_t dl0 = tc::smem_desc_sw128(tc::smem_addr(sm.pl[0]), 16, 1024);
     auto issue_s = [&](int t) -> bool {
       const int st = t % LST;
-      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st]), (t / LST) & 1, abort_flag)) return false;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st][par]), kv_phase(t), abort_flag)) return false;
       tc::fence_after_sync();
       const uint64_t db = tc::desc_adv(dk0, st * 16384);
-      const uint32_t dS = tbase + LN * (t & 1);
+      const uint32_t dS = tbase + LN * par;
       if (tc::elect_one()) {
         tc::mma_bf16<false>(dS, dq, db, id_s);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
           tc::mma_bf16<true>(dS, tc::desc_adv(dq, (kk >> 2) * 1024 + (kk & 3) * 32),
                              tc::desc_adv(db, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
-        tc::mma_commit(tc::smem_addr(&sm.sdone[t & 1]));
+        tc::mma_commit(tc::smem_addr(&sm.sdone[par]));
       }
       __syncwarp();
       return true;
     };
     bool ok = tc::wait_bounded_warp(tc::smem_addr(&sm.qfull), 0, abort_flag);
-    for (int t = 0; ok && t < NTL && t < 2; ++t) ok = issue_s(t);
-    for (int t = 0; ok && t < NTL; ++t) {
-      const int st = t % LST, p2 = t & 1;
-      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.pready[p2]), (t >> 1) & 1, abort_flag)) break;
+    if (ok && par < NTL) ok = issue_s(par);
+    for (int t = par; ok && t < NTL; t += 2) {
+      const int st = t % LST;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.pready[par]), (t >> 1) & 1, abort_flag)) break;
       tc::fence_after_sync();
-      const uint64_t dv = tc::desc_adv(dv0, st * 16384), dh = tc::desc_adv(dh0, p2 * 16384),
-                     dl = tc::desc_adv(dl0, p2 * 16384);
-      const uint32_t dO = tbase + kOCol + D * p2;       // group p2's accumulator
+      const uint64_t dv = tc::desc_adv(dv0, st * 16384), dh = tc::desc_adv(dh0, par * 16384),
+                     dl = tc::desc_adv(dl0, par * 16384);
+      const uint32_t dO = tbase + kOCol + D * par;      // group par's accumulator
       if (tc::elect_one()) {
         // each group's first tile overwrites its O (TMEM is not zeroed)
         if (t < 2) tc::mma_bf16<false>(dO, dh, dv, id_o);
@@ -255,15 +268,15 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
           for (int kk = 0; kk < 4; ++kk)
             tc::mma_bf16<true>(dO, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
         }
-        tc::mma_commit(tc::smem_addr(&sm.pvdone[p2]));
-        tc::mma_commit(tc::smem_addr(&sm.kvfree[st]));
+        tc::mma_commit(tc::smem_addr(&sm.pvdone[par]));
+        tc::mma_commit(tc::smem_addr(&sm.kvfree[st][par]));
       }
       __syncwarp();
       if (t + 2 < NTL) ok = issue_s(t + 2);
     }
     if (tc::elect_one()) {
-      tc::mma_commit(tc::smem_addr(&sm.drain));
-      tc::mbar_wait(tc::smem_addr(&sm.drain), 0);
+      tc::mma_commit(tc::smem_addr(&sm.drain[par]));
+      tc::mbar_wait(tc::smem_addr(&sm.drain[par]), 0);
     }
     __syncwarp();
   } else {
@@ -284,7 +297,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     for (int t = grp; t < NTL; t += 2) {
       const int st = t % LST, p2 = t & 1;
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
-      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st]), (t / LST) & 1, abort_flag))) break;
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st][p2]), kv_phase(t), abort_flag))) break;
       const unsigned long long km = sm.kmask[st];
       if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.sdone[p2]), (t >> 1) & 1, abort_flag))) break;
       tc::fence_after_sync();
@@ -319,11 +332,16 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         for (int c = 0; c < LN; ++c)
           if (c < lo32 || c > hi32) x[c] = __float_as_uint(-INFINITY);
       }
-      // tile max of the raw scores (sl2 > 0, so it is the max of the scaled ones)
+      // tile max of the raw scores (sl2 > 0, so it is the max of the scaled
+      // ones): four chains of three-input maxima
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < LN; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(x[c]));
-      const float tmax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+      for (int c = 0; c < LN; c += 8) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          m4[k] = fmax3(m4[k], __uint_as_float(x[c + 2 * k]), __uint_as_float(x[c + 2 * k + 1]));
+      }
+      const float tmax = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
       // Lazy rescaling: the row keeps a reference max m_run and moves it (scaling
       // O and l) only when a tile max exceeds it by more than 2^8.  Until then
       // p = 2^(s - m_run) may exceed 1, which the fp32 accumulators and the hi/lo
@@ -337,14 +355,18 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         m_run = tmax;
       }
       const float nbase = m_run == -INFINITY ? 0.f : -m_run;
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+      // exponents and their sum on column pairs (paired fp32 fma and add)
+      const float2 sl2x2 = make_float2(sl2, sl2), nbx2 = make_float2(nbase, nbase);
+      float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int c = 0; c < LN; ++c) {
-        const float e = fast_exp2(fmaf(__uint_as_float(x[c]), sl2, nbase));   // -inf -> 0
-        s4[c & 3] += e;
-        x[c] = __float_as_uint(e);
+      for (int h = 0; h < LN / 2; ++h) {
+        const float2 t2 = ffma2(make_float2(__uint_as_float(x[2 * h]), __uint_as_float(x[2 * h + 1])), sl2x2, nbx2);
+        const float2 e = make_float2(fast_exp2(t2.x), fast_exp2(t2.y));   // -inf -> 0
+        s2[h & 1] = fadd2(s2[h & 1], e);
+        x[2 * h] = __float_as_uint(e.x);
+        x[2 * h + 1] = __float_as_uint(e.y);
       }
-      l_run += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      l_run += (s2[0].x + s2[1].x) + (s2[0].y + s2[1].y);
       // zeroed keys are counted in l but add no value
       if (km != ~0ull) {
         if (km == (~0ull >> 1)) {
