@@ -77,6 +77,61 @@ def stage_bytes(l: int):
 MEASURED_TRAFFIC = {("selected_attention", 16384, 16384): 331471360 + 99500288}
 
 
+def selected_items(indices: torch.Tensor, chunks: int, qb: int = 32, own: int = 8):
+    """Work items of the selected-attention kernel for these chunk lists: per
+    block of ``qb`` queries and KV head, one item per (chunk, up to ``own``
+    owner queries).  Returns (items, owner-chunk pairs)."""
+    b, l, hkv, k = indices.shape
+    nb = (l + qb - 1) // qb
+    idx = torch.full((b, nb * qb, hkv, k), -1, dtype=torch.int64, device=indices.device)
+    idx[:, :l] = indices.long()
+    idx = idx.view(b, nb, qb, hkv, k).permute(0, 1, 3, 2, 4).reshape(b * nb * hkv, qb * k)
+    # owner count per (block, head, chunk): each query counts a chunk once
+    keyed = torch.where(idx >= 0, idx, torch.full_like(idx, chunks))
+    hist = torch.zeros(idx.shape[0], chunks + 1, dtype=torch.int32, device=idx.device)
+    qid = torch.arange(qb, device=idx.device).repeat_interleave(k).expand_as(idx)
+    flat = keyed * qb + qid                              # (chunk, query) pairs, deduplicated per row
+    flat = torch.sort(flat, dim=1).values
+    first = torch.ones_like(flat, dtype=torch.bool)
+    first[:, 1:] = flat[:, 1:] != flat[:, :-1]
+    hist.scatter_add_(1, flat // qb, first.to(torch.int32))
+    hist = hist[:, :chunks]
+    items = int(((hist + own - 1) // own).sum().item())
+    return items, int(hist.sum().item())
+
+
+def gather_peak_gbs(lib, k, v, q, owners: int, items_per_cta: int, reps: int = 5):
+    """Measured L2 -> shared-memory ceiling of the selected kernel's loads:
+    ``mrsa_probe_tile_gather`` on the kernel's own K, V and query operands
+    (L2-resident), one CTA per SM loading K+V tiles and ``owners`` query boxes
+    per item and computing nothing.  GB/s, CUDA events on this stream."""
+    dev = k.device
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    stream = torch.cuda.current_stream(dev)
+    b, lk, hkv, d = k.shape
+    q_rows = q.numel() // d
+
+    def launch():
+        rc = lib.mrsa_probe_tile_gather(k.data_ptr(), v.data_ptr(), q.data_ptr(), b * lk, hkv, q_rows, owners,
+                                        items_per_cta, status.data_ptr(), stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"mrsa_probe_tile_gather: {lib.mrsa_strerror(rc).decode()}")
+
+    for _ in range(2):
+        launch()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if int(status.item()) != 0:
+        raise RuntimeError("tile-gather probe gave up on a bounded wait")
+    moved = sms * items_per_cta * (32768 + 2048 * owners) * reps
+    return moved / (e0.elapsed_time(e1) * 1e-3) / 1e9
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -360,6 +415,42 @@ def run_ops(args):
         emit("swa", f"SWA layer fwd B={bsz} L={L} 28/4 heads d=128 radius {w} (RoPE + window, fp16 V)",
              ms, bsz * L, "tokens", "tensor", bsz * HQ * D * 4 * pairs, "inputs larger than L2", launches=3)
         ops = [o for o in ops if o != "swa"]
+    if "coherent" in ops:
+        # Diagnostic, not a configs[] workload: the route layer at configs[1]'s
+        # shape with q, k and h sharing a component that varies slowly along the
+        # sequence, so neighbouring queries route to overlapping chunks (as real
+        # text does) and each gathered K/V tile serves more owner rows of a
+        # query block.
+        for mix in (0.0, 0.5, 0.8):
+            inp = {n: t.to(dev) for n, t in make_inputs(L, 0).items()}
+            if mix > 0:
+                gsm = torch.Generator(device=dev).manual_seed(21)
+                anchors = torch.randn(L // 256 + 2, HQ, D, device=dev, generator=gsm)
+                pos = torch.arange(L, device=dev, dtype=torch.float32) / 256
+                i0 = pos.floor().long()
+                fr = (pos - i0)[:, None, None]
+                smooth = (anchors[i0] * (1 - fr) + anchors[i0 + 1] * fr)[None] / math.sqrt(D)
+                qf = inp["q_pre"].float() * (1 - mix) + smooth * mix
+                inp["q_pre"] = qf.bfloat16()
+                kf = inp["k_pre"].float()
+                kf = kf * (1 - mix) + mix * smooth.view(1, L, HKV, HQ // HKV, D).mean(3)
+                inp["k_pre"] = kf.bfloat16()
+                # the Q-Cal term of the routing query comes from h: h shares a
+                # slowly varying component too, or that term stays random
+                h_anchor = torch.randn(L // 256 + 2, HIDDEN, device=dev, generator=gsm)
+                hs = h_anchor[i0] * (1 - fr[:, :, 0]) + h_anchor[i0 + 1] * fr[:, :, 0]
+                inp["hidden"] = (inp["hidden"].float() * (1 - mix) + hs[None] * mix).bfloat16()
+            layer = mrsa.RouteLayer(inp["w_in"], inp["w_out"], check_errors=False)
+            args = [inp[n] for n in ("q_pre", "k_pre", "v", "hidden", "position_ids")]
+            st = layer.stage_times(*args, inp["key_valid"], reps=5)
+            idx = layer.forward(*args, inp["key_valid"], stages=True)["indices"]
+            items, pairs = selected_items(idx, L // CHUNK)
+            ms = st["selected_attention"]
+            emit("coherent", f"diagnostic (not a configs[] workload): route layer L={L}, q, k and h mixed "
+                 f"{mix:.1f} with a component varying over 256 tokens; selected attention {items} work items, "
+                 f"{pairs / items:.2f} owner queries per item", ms, L, "tokens", "tensor",
+                 L * HQ * TOPK * CHUNK * D * 4, "inputs larger than L2")
+        ops = [o for o in ops if o != "coherent"]
     if "dream" in ops:
         # the whole Dream-shaped forward, B=1, L=32768, random weights
         from mrsa_b200.dream_forward import DreamConfig, DreamForward, landmark_inputs, model_parameters
@@ -445,7 +536,7 @@ def main():
                     help="run N untimed fused layer forwards at the bench workload and exit "
                          "(the target of the ncu captures summarised under profiles/)")
     ap.add_argument("--op", default=None,
-                    choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "swa", "dream",
+                    choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "swa", "dream", "coherent",
                              "all"],
                     help="time one off-path op (or all) instead of the route layer; one JSON line each")
     args = ap.parse_args()
@@ -609,6 +700,25 @@ def main():
         ach = byts[dom] / (dom_ms * 1e-3) / 1e9
         roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                 "frac": ach / hbm, "traffic": None, "peak_kind": f"{peak_kind} HBM copy"}
+    if dom == "selected_attention":
+        # the gather bound beside the tensor one: the K and V tiles (32 KB) of
+        # every work item and each owner's query rows (2 KB) go through L2
+        if world == 1:
+            idx = layer.forward(*x[:5], x[5], stages=True)["indices"]
+        else:
+            idx = None
+        if idx is not None:
+            items, pairs = selected_items(idx, l_total // CHUNK)
+            gbytes = items * 32768 + pairs * 2048
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            owners = max(1, round(pairs / items))
+            peak_g = gather_peak_gbs(mrsa._lib.load(), x[1], x[2], x[0], owners, -(-items // sms))
+            ach_g = gbytes / (dom_ms * 1e-3) / 1e9
+            roof["gather"] = {"bound": "l2", "bytes_per_launch": gbytes, "achieved": ach_g, "unit": "GB/s",
+                              "peak": peak_g, "frac": ach_g / peak_g, "items": items,
+                              "owners_per_item": pairs / items,
+                              "peak_kind": (f"measured in this run: mrsa_probe_tile_gather, the kernel's K/V tile "
+                                            f"and {owners} query boxes per item from L2, nothing computed")}
     waits = None
     if dist:
         # time each rank's compute stream stalled on a transfer, max over ranks

@@ -274,6 +274,18 @@ int mrsa_wait_selftest(int* result, int rounds, mrsa_stream_t stream);
  * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
 int mrsa_device_error_flags(int clear);
 
+/* Measurement helper with no reference counterpart: the L2 -> shared-memory
+ * ceiling of the selected-attention loads.  One CTA per SM loads
+ * `items_per_cta` work items, each the 64-row K and V tiles of a pseudo-random
+ * (chunk, KV head) of k, v [kv_len, kv_heads, 128] (2-byte elements) plus
+ * `owners` (0..8) 8-row boxes of q [q_rows, 128] -- the selected kernel's
+ * tensor-map boxes -- and computes nothing.  Bytes moved per launch = SMs x
+ * items_per_cta x (32768 + 2048 x owners).  Sets *status (device int) to 1 if
+ * a CTA gave up on a bounded wait. */
+int mrsa_probe_tile_gather(const void* k, const void* v, const void* q, int64_t kv_len, int64_t kv_heads,
+                           int64_t q_rows, int owners, int64_t items_per_cta, int* status,
+                           mrsa_stream_t stream);
+
 /* out = bf16(remote + local_w * local) over rows = B*L*H, each of head_dim.
  * Replaces ops/hils_bidir_output_fusion_tilelang.py:138 fuse_hils_outputs. */
 int mrsa_fuse_outputs(const void* remote, const void* local, const void* local_w, void* out,

@@ -58,6 +58,7 @@ _SIGS = {
                                      _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_convert_bf16_to_f16": [_vp, _vp, _i64, _vp],
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
+    "mrsa_probe_tile_gather": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _i64, _vp, _vp],
     "mrsa_device_error_flags": [_int],
     "mrsa_wait_selftest": [_vp, _int, _vp],
     "mrsa_route_layer_workspace_size": [_vp],

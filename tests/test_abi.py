@@ -77,6 +77,10 @@ def test_bad_arguments_return_codes_without_device(mrsa):
     # local/weight must come together
     assert lib.mrsa_selected_attention(dummy, dummy, dummy, None, dummy, dummy, dummy, None, dummy, 0.1, 1,
                                        1, 64, 128, 4, 7, 128, 32, 64, None) == -1
+    # tile-gather probe: missing status pointer, more than 8 owners, kv_len not whole chunks
+    assert lib.mrsa_probe_tile_gather(dummy, dummy, dummy, 4096, 4, 64, 4, 10, None, None) == -1
+    assert lib.mrsa_probe_tile_gather(dummy, dummy, dummy, 4096, 4, 64, 9, 10, dummy, None) == -2
+    assert lib.mrsa_probe_tile_gather(dummy, dummy, dummy, 4000, 4, 64, 4, 10, dummy, None) == -2
     # route layer: workspace checks
     a = mrsa._lib.RouteLayerArgs()
     assert lib.mrsa_route_layer_workspace_size(C.byref(a)) == 0
