@@ -451,6 +451,47 @@ def run_ops(args):
                  f"{pairs / items:.2f} owner queries per item", ms, L, "tokens", "tensor",
                  L * HQ * TOPK * CHUNK * D * 4, "inputs larger than L2")
         ops = [o for o in ops if o != "coherent"]
+    if "backward" in ops:
+        # Not a configs[] workload: the backward kernels at configs[1]'s route
+        # layer (L=16384, the layer's own routing), gradients of random cotangents.
+        inp = {n: t.to(dev) for n, t in make_inputs(L, 0).items()}
+        layer = mrsa.RouteLayer(inp["w_in"], inp["w_out"], check_errors=False)
+        args5 = [inp[n] for n in ("q_pre", "k_pre", "v", "hidden", "position_ids")]
+        st = layer.forward(*args5, inp["key_valid"], stages=True)
+        q, k, v = st["q"], st["k"], inp["v"]
+        idx, w = st["indices"], st["remote_weights"]
+        go = rnd(1, L, HQ, D)
+        valid = inp["key_valid"]
+        ms = timed(lambda: mrsa.selected_attention_backward(q, k, v, w, idx, go, valid), args.steps)
+        f_sel = L * HQ * TOPK * CHUNK * D * 4
+        emit("selected_backward", f"selected-attention backward (dQ, dK, dV, dW) at route-layer L={L}, "
+             "28/4 heads, top-32x64, the layer's own routing; work = 2.5 x the forward's FLOPs "
+             "(S recomputed, dP, dQ, dK, dV)", ms, L, "tokens", "tensor", 2.5 * f_sel, "inputs larger than L2",
+             launches=7)
+        lmk = st["lmk"]
+        gs = rnd(1, L, HQ, TOPK)
+        ms = timed(lambda: mrsa.route_scores_backward(st["route_q"], lmk, idx, gs), args.steps)
+        emit("route_scores_backward", f"routing-score backward (dq gather + d_landmarks over the inverted "
+             f"index) at L={L}", ms, L, "tokens", "hbm",
+             L * HQ * D * (2 + 4) + L * HQ * TOPK * 2 * 2 + L * HQ * D * 2 * TOPK / 8, "inputs larger than L2",
+             launches=6)
+        c = L // CHUNK
+        mu = st["route_q"][:, CHUNK - 1::CHUNK].reshape(1, c, HKV, HQ // HKV, D).contiguous()
+        kc = k.view(1, c, CHUNK, HKV, D)
+        gl = rnd(1, c, HKV, HQ // HKV, D)
+        ge = torch.randn(1, c, HKV, HQ // HKV, device=dev)
+        ms = timed(lambda: mrsa.chunk_pool_backward(mu, kc, valid.view(1, c, CHUNK), gl, ge), args.steps)
+        emit("pool_backward", f"landmark-pool backward at L={L}", ms, L, "tokens", "hbm", L * HKV * D * 2 * 2,
+             "K fits L2 (16.8 MB)", launches=1)
+        from mrsa_b200.route_weights import route_weights_backward
+        from mrsa_b200 import _lib as mlib
+
+        grw, glw = rnd(1, L, HQ, TOPK), rnd(1, L, HQ)
+        ms = timed(lambda: route_weights_backward(st["scores"], idx, st["prior_bias"], st["local_lse"], grw, glw,
+                                                  mode=mlib.WEIGHTS_AFFINE), args.steps)
+        emit("route_weights_backward", f"route-weights backward (affine gate) at L={L}", ms, L, "tokens", "hbm",
+             L * HQ * TOPK * (2 + 2 + 4) + L * HKV * TOPK * 4 + L * HQ * 12, "inputs larger than L2", launches=1)
+        ops = [o for o in ops if o != "backward"]
     if "dream" in ops:
         # the whole Dream-shaped forward, B=1, L=32768, random weights
         from mrsa_b200.dream_forward import DreamConfig, DreamForward, landmark_inputs, model_parameters
@@ -537,6 +578,7 @@ def main():
                          "(the target of the ncu captures summarised under profiles/)")
     ap.add_argument("--op", default=None,
                     choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "swa", "dream", "coherent",
+                             "backward",
                              "all"],
                     help="time one off-path op (or all) instead of the route layer; one JSON line each")
     args = ap.parse_args()

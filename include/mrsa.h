@@ -45,6 +45,10 @@ enum { MRSA_BF16 = 0, MRSA_F32 = 1 };                 /* cos/sin and score dtype
 enum { MRSA_WEIGHTS_AFFINE = 0, MRSA_WEIGHTS_SOFTMAX = 1 };
 
 const char* mrsa_strerror(int code);
+/* The CUDA error (name, message and the entry point or step that met it)
+ * behind the last MRSA_ERR_LAUNCH returned on the calling host thread; "" if
+ * none.  The string stays valid until the thread's next failing call. */
+const char* mrsa_last_error(void);
 int mrsa_abi_version(void);
 
 /* YaRN inverse frequencies [dim/2] and attention factor, host-side.
@@ -206,6 +210,83 @@ int mrsa_selected_attention_f16v(const void* q, const void* k, const void* v_f16
                                  int64_t groups, int64_t head_dim, int64_t topk, int64_t chunk,
                                  mrsa_stream_t stream);
 
+/* Backward of mrsa_selected_attention (bf16 q, k, v; no local merge, no token
+ * refinement): given grad_out [B,Lq,Hq,D] bf16 writes dq [B,Lq,Hq,D], dk and
+ * dv [B,Lk,Hkv,D] in fp32 (every element, dk/dv of unselected keys 0) and dw
+ * [B,Lq,Hq,K] bf16 (dw of slot k = sum_s P dP over its chunk; 0 for an empty
+ * slot).  The softmax gradient dS and w*P are rounded to bf16 before their
+ * GEMMs.  dK/dV are summed per chunk over an inverted chunk -> (query, slot)
+ * index in query order (no atomics: every run gives the same bits).  workspace: at least
+ * mrsa_selected_attention_backward_workspace() bytes, 16-byte aligned.
+ * Sets bit 4 of mrsa_device_error_flags if a CTA gave up on a bounded wait.
+ * Replaces the backward of ops/hils_fwd_bwd_head.py:915-1098
+ * (_hils_block_M_attention_inverse, kernel :573-910). */
+int mrsa_selected_attention_backward(const void* q, const void* k, const void* v, const uint8_t* key_valid,
+                                     const void* weights, const int32_t* indices, const void* grad_out,
+                                     float* dq, float* dk, float* dv, void* dw, float sm_scale,
+                                     int mask_last_token, int64_t batch, int64_t q_len, int64_t kv_len,
+                                     int64_t kv_heads, int64_t groups, int64_t head_dim, int64_t topk,
+                                     int64_t chunk, void* workspace, size_t ws_bytes, mrsa_stream_t stream);
+/* Workspace of mrsa_selected_attention_backward: chunk counts and offsets
+ * (B*Hkv*C int32 each), per-256-query-block chunk counts (B*Hkv*ceil(Lq/256)*C
+ * int32) and the inverted index (B*Lq*Hkv*K int32). */
+size_t mrsa_selected_attention_backward_workspace(int64_t batch, int64_t q_len, int64_t kv_len,
+                                                  int64_t kv_heads, int64_t topk);
+
+/* Backward of mrsa_chunk_pool (landmarks and entropy): mu_q [B,C,Hkv,G,D]
+ * bf16 contiguous, k [B,C*64,Hkv,D] bf16, key_valid as in the forward,
+ * grad_landmarks [B,C,Hkv,G,D] bf16 and grad_entropy [B,C,Hkv,G] fp32 (either
+ * NULL = zero) -> d_mu [B,C,Hkv,G,D] and d_k [B,C*64,Hkv,D] bf16.  The pool
+ * probabilities and entropy are recomputed; the softmax gradient is rounded to
+ * bf16 before its GEMMs, as in the reference kernel.  G <= 16, D = 128.
+ * Replaces the backward of ops/chunk_attn_pool_gqa_tilelang.py:328-393
+ * (_ChunkAttnPoolGQA, kernel _pool_gqa_bwd :183-325). */
+int mrsa_chunk_pool_backward(const void* mu_q, const void* k, const uint8_t* key_valid,
+                             const void* grad_landmarks, const float* grad_entropy, void* d_mu, void* d_k,
+                             float sm_scale, int64_t batch, int64_t chunks, int64_t kv_heads, int64_t groups,
+                             int64_t head_dim, mrsa_stream_t stream);
+
+/* Backward of mrsa_route_weights: grad_remote [B,L,Hq,K] and grad_local
+ * [B,L,Hq] bf16 -> d_scores [B,L,Hq,K] fp32 (0 on empty slots), d_prior
+ * [B,C,Hkv,G] fp32 (cleared, then summed over the slots that selected each
+ * chunk), d_local_lse [B,L,Hq] fp32 and d_gate[2] fp32 = the gradients of
+ * gate_scale and gate_offset (cleared, then summed over rows; in
+ * MRSA_WEIGHTS_SOFTMAX mode d_gate[0] = 0).  Rows whose logits are all
+ * masked get zero gradients; a row with no selected chunk adds 0 to
+ * d_gate[0] (torch autograd of the reference gives NaN there).
+ * Replaces the backward of ops/hils_bidir_route_weights_tilelang.py:190-255
+ * (_RouteWeights, kernel :97-166) and torch autograd through
+ * dream_dllm_hils/attention.py:126-227 _route_weights_torch (affine gate). */
+int mrsa_route_weights_backward(const void* scores, const int32_t* indices, const float* prior,
+                                const float* local_lse, const void* grad_remote, const void* grad_local,
+                                float* d_scores, float* d_prior, float* d_local_lse, float* d_gate,
+                                int weight_mode, float temperature, float gate_scale, float gate_offset,
+                                int64_t batch, int64_t seq_len, int64_t chunks, int64_t kv_heads,
+                                int64_t groups, int64_t topk, mrsa_stream_t stream);
+
+/* Backward of the gathered routing scores s[b,l,hq,k] = q[b,l,hq] .
+ * landmarks[b,c_k,hq] * sm_scale (c_k = indices[b,l,hq/G,k]): q [B,L,Hq,D]
+ * and landmarks [B,C,Hkv,G,D] bf16, grad_scores [B,L,Hq,K] bf16 -> d_q
+ * [B,L,Hq,D] and d_landmarks [B,C,Hkv,G,D] fp32 (every element written).
+ * d_landmarks is summed per chunk over an inverted index built in
+ * workspace (mrsa_route_scores_backward_workspace bytes, 16-byte aligned).
+ * Replaces ops/topk_head_softmax.py:1071-1122 (SoftmaxTopKMaxPooling
+ * backward, per-query-head landmarks). */
+int mrsa_route_scores_backward(const void* q, const void* landmarks, const int32_t* indices,
+                               const void* grad_scores, float* d_q, float* d_landmarks, float sm_scale,
+                               int64_t batch, int64_t q_len, int64_t chunks, int64_t kv_heads, int64_t groups,
+                               int64_t head_dim, int64_t topk, void* workspace, size_t ws_bytes,
+                               mrsa_stream_t stream);
+size_t mrsa_route_scores_backward_workspace(int64_t batch, int64_t q_len, int64_t chunks, int64_t kv_heads,
+                                            int64_t topk);
+
+/* Backward of mrsa_fuse_outputs: d_remote = bf16(g), d_local = bf16(g * w),
+ * d_local_w = bf16(sum_d g * local) over rows = B*L*H rows of head_dim.
+ * Replaces ops/hils_bidir_output_fusion_tilelang.py:38-99,117-130. */
+int mrsa_fuse_outputs_backward(const void* local, const void* local_w, const void* grad_out, void* d_remote,
+                               void* d_local, void* d_local_w, int64_t rows, int64_t head_dim,
+                               mrsa_stream_t stream);
+
 /* Candidate token scores [B,Lq,Hkv,K,S] fp32: for chunk c = indices[b,l,h,i]
  * and slot s, max over the G = q_heads/kv_heads heads of the group of
  * q_g . k[c*S+s] * sm_scale; -inf when c < 0 (or c >= kv_len/S), s == S-1 or
@@ -269,7 +350,8 @@ int mrsa_wait_selftest(int* result, int rounds, mrsa_stream_t stream);
  * selected-attention CTA gave up waiting on one of its internal barriers (its
  * output rows are then incomplete); bit 1 = a routing key CTA did (its keys,
  * hence its selections, are then incomplete); bit 2 = a local-window CTA did;
- * bit 3 = mrsa_convert_bf16_to_f16 saturated a value.  Synchronises the current device; with
+ * bit 3 = mrsa_convert_bf16_to_f16 saturated a value; bit 4 = a CTA of the
+ * selected-attention backward gave up on a wait (its gradients are then incomplete).  Synchronises the current device; with
  * clear != 0 also resets the mask.  Negative on a CUDA error.  Replaces the
  * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
 int mrsa_device_error_flags(int clear);

@@ -23,6 +23,7 @@ _vp, _i64, _f32, _int, _sz = C.c_void_p, C.c_int64, C.c_float, C.c_int, C.c_size
 # name -> argtypes (restype int unless listed in _RESTYPE)
 _SIGS = {
     "mrsa_strerror": [_int],
+    "mrsa_last_error": [],
     "mrsa_abi_version": [],
     "mrsa_yarn_inv_freq": [_int, C.c_double, C.c_double, _int, C.c_double, C.c_double, _int, _vp, _vp],
     "mrsa_rope": [_vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _f32, _vp, _vp, _int, _i64, _i64, _i64, _vp],
@@ -59,14 +60,25 @@ _SIGS = {
     "mrsa_convert_bf16_to_f16": [_vp, _vp, _i64, _vp],
     "mrsa_fuse_outputs": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_probe_tile_gather": [_vp, _vp, _vp, _i64, _i64, _i64, _int, _i64, _vp, _vp],
+    "mrsa_selected_attention_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _int,
+                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp],
+    "mrsa_selected_attention_backward_workspace": [_i64, _i64, _i64, _i64, _i64],
+    "mrsa_chunk_pool_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_route_weights_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _f32, _f32, _f32,
+                                    _i64, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_route_scores_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _f32, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                   _vp, _sz, _vp],
+    "mrsa_route_scores_backward_workspace": [_i64, _i64, _i64, _i64, _i64],
+    "mrsa_fuse_outputs_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_device_error_flags": [_int],
     "mrsa_wait_selftest": [_vp, _int, _vp],
     "mrsa_route_layer_workspace_size": [_vp],
     "mrsa_route_layer_forward": [_vp, _vp, _sz, _vp],
     "mrsa_route_layer_forward_noalloc": [_vp, _vp],
 }
-_RESTYPE = {"mrsa_strerror": C.c_char_p, "mrsa_route_layer_workspace_size": _sz,
-            "mrsa_route_topk_workspace_size": _sz, "mrsa_selected_token_attention_smem": _sz}
+_RESTYPE = {"mrsa_strerror": C.c_char_p, "mrsa_last_error": C.c_char_p, "mrsa_route_layer_workspace_size": _sz,
+            "mrsa_route_topk_workspace_size": _sz, "mrsa_selected_token_attention_smem": _sz,
+            "mrsa_selected_attention_backward_workspace": _sz, "mrsa_route_scores_backward_workspace": _sz}
 
 EXPORTED = tuple(_SIGS)
 
@@ -100,6 +112,8 @@ def check(rc: int, what: str):
     msg = load().mrsa_strerror(rc).decode()
     if rc in (ERR_SHAPE, ERR_ARG, ERR_NULL, ERR_ALIGN):
         raise ValueError(f"{what}: {msg} (code {rc})")
+    if rc == ERR_LAUNCH:
+        msg += f" [{load().mrsa_last_error().decode()}]"
     raise MRSAError(f"{what}: {msg} (code {rc})")
 
 

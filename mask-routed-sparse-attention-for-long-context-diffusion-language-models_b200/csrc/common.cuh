@@ -124,6 +124,18 @@ __device__ __forceinline__ float fast_exp2(float x) {
 int route_error_flags(int clear);
 int local_error_flags(int clear);
 int convert_error_flags(int clear);
+int bwd_error_flags(int clear);
+
+// Inverted chunk -> (query, slot) index of indices [B,Lq,Hkv,K] int32: per
+// segment (b, h, c) (flattened as (b*Hkv + h)*C + c) cnt[seg] entries from
+// pairs[off[seg]] on, each (l << 5) | slot, in (l, slot) order.  Built in
+// `workspace` (at least chunk_index_bytes() bytes); C <= 12288.
+struct ChunkIndex {
+  const int32_t *cnt, *off, *pairs;
+};
+size_t chunk_index_bytes(int64_t batch, int64_t q_len, int64_t kv_heads, int64_t topk, int64_t chunks);
+int build_chunk_index(const int32_t* indices, int64_t batch, int64_t q_len, int kv_heads, int topk, int chunks,
+                      void* workspace, cudaStream_t s, ChunkIndex* out);
 
 // ---- sm_100 paired fp32 arithmetic (one instruction for two lanes of work)
 // fma/add/mul on a register pair, each half rounded as the scalar op would be.
@@ -171,8 +183,43 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 }  // namespace mrsa
 
+namespace mrsa {
+// For the scope of an entry point: makes the primary context of the device
+// that owns `p` current on the calling thread (a thread that has made no CUDA
+// runtime call yet -- an autograd worker, say -- has none, and the tensor-map
+// encoder needs one), and restores the thread's previous device afterwards.
+class DeviceScope {
+ public:
+  explicit DeviceScope(const void* p) {
+    cudaPointerAttributes at{};
+    if (p == nullptr || cudaPointerGetAttributes(&at, p) != cudaSuccess ||
+        (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged)) {
+      (void)cudaGetLastError();
+      return;
+    }
+    if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+    if (cudaSetDevice(at.device) == cudaSuccess) dev_ = at.device;
+  }
+  ~DeviceScope() {
+    if (prev_ >= 0 && dev_ >= 0 && prev_ != dev_) (void)cudaSetDevice(prev_);
+  }
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+
+ private:
+  int prev_ = -1, dev_ = -1;
+};
+
+// Keeps, per host thread, the CUDA error behind the last MRSA_ERR_LAUNCH
+// (read through mrsa_last_error()).
+void note_cuda_error(cudaError_t e, const char* where);
+}  // namespace mrsa
+
 #define MRSA_CHECK_LAUNCH()                                   \
   do {                                                        \
     cudaError_t _e = cudaGetLastError();                      \
-    if (_e != cudaSuccess) return MRSA_ERR_LAUNCH;            \
+    if (_e != cudaSuccess) {                                  \
+      mrsa::note_cuda_error(_e, __func__);                    \
+      return MRSA_ERR_LAUNCH;                                 \
+    }                                                         \
   } while (0)

@@ -2,6 +2,8 @@
 // fusion, plus the ABI's small host helpers.
 #include <math.h>
 
+#include <cstdio>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -165,9 +167,16 @@ int convert_error_flags(int clear) {
   }
   return v;
 }
+thread_local char g_last_error[256] = "";
+
+void note_cuda_error(cudaError_t e, const char* where) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorString(e), cudaGetErrorName(e));
+}
 }  // namespace mrsa
 
 extern "C" {
+
+const char* mrsa_last_error(void) { return mrsa::g_last_error; }
 
 const char* mrsa_strerror(int code) {
   switch (code) {

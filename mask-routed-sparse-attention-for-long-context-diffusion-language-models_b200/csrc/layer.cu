@@ -61,6 +61,7 @@ extern "C" size_t mrsa_route_layer_workspace_size(const mrsa_route_layer_args* a
 extern "C" int mrsa_route_layer_forward(const mrsa_route_layer_args* a, void* workspace,
                                         size_t ws_bytes, mrsa_stream_t stream) {
   if (a == nullptr) return MRSA_ERR_NULL;
+  mrsa::DeviceScope device_scope(a->q_pre);
   if (!a->q_pre || !a->k_pre || !a->v || !a->hidden || !a->position_ids || !a->inv_freq ||
       !a->w_in || !a->w_out || !a->norm_weight || !a->out)
     return MRSA_ERR_NULL;

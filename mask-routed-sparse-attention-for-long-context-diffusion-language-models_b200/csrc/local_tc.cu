@@ -578,6 +578,7 @@ extern "C" int mrsa_local_attention(const void* q, const void* k, const void* v,
                                     int64_t batch, int64_t q_len, int64_t kv_len, int64_t q_offset,
                                     int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                     mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(q);
   return local_launch<false>(q, k, v, key_valid, out, lse, window, skip_inert, chunk, sm_scale, batch, q_len,
                              kv_len, q_offset, q_heads, kv_heads, head_dim, stream);
 }
@@ -588,6 +589,7 @@ extern "C" int mrsa_local_attention_f16v(const void* q, const void* k, const voi
                                          int64_t batch, int64_t q_len, int64_t kv_len, int64_t q_offset,
                                          int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                          mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(q);
   return local_launch<true>(q, k, v_f16, key_valid, out, lse, window, skip_inert, chunk, sm_scale, batch, q_len,
                             kv_len, q_offset, q_heads, kv_heads, head_dim, stream);
 }
@@ -598,6 +600,7 @@ extern "C" int mrsa_local_attention_positions(const void* q, const void* k, cons
                                               int64_t chunk, float sm_scale, int64_t batch, int64_t q_len,
                                               int64_t kv_len, int64_t q_heads, int64_t kv_heads,
                                               int64_t head_dim, mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(q);
   if (query_positions == nullptr && q_len > 0) return MRSA_ERR_NULL;
   Band band;
   band.qpos = query_positions;
@@ -610,6 +613,7 @@ extern "C" int mrsa_flex_attention(const void* q, const void* k, const void* v, 
                                    int64_t kv_start, float sm_scale, int64_t batch, int64_t q_len,
                                    int64_t kv_len, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                    mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(q);
   if (q_len > kv_len) return MRSA_ERR_SHAPE;
   if (chunk <= 0 || chunk > 0x7fffffffLL) return MRSA_ERR_ARG;
   Band band;

@@ -118,6 +118,7 @@ bool probe_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dim
 extern "C" int mrsa_probe_tile_gather(const void* k, const void* v, const void* q, int64_t kv_len, int64_t kv_heads,
                                       int64_t q_rows, int owners, int64_t items_per_cta, int* status,
                                       mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(k);
   if (!k || !v || !q || !status) return MRSA_ERR_NULL;
   if (kv_len < 64 || kv_len % 64 || kv_len / 64 > 0x7fffffffLL || kv_heads < 1 || kv_heads > 4096 || q_rows < 8 ||
       q_rows > 0x7fffffffLL || owners < 0 || owners > kMaxOwners || items_per_cta < 1 || items_per_cta > (1LL << 40))

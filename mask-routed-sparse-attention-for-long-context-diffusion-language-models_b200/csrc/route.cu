@@ -674,6 +674,7 @@ extern "C" int mrsa_route_topk(const void* route_q, const void* landmarks, int l
                                int64_t chunks, int64_t kv_heads, int64_t groups, int64_t head_dim,
                                int64_t topk, void* workspace, size_t workspace_bytes,
                                mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(route_q);
   if (!route_q || !landmarks || !local_lse || !indices || !scores_out) return MRSA_ERR_NULL;
   if ((remote_w == nullptr) != (local_w == nullptr)) return MRSA_ERR_NULL;
   if (head_dim != D || groups < 1 || groups > RGMAX || kv_heads < 1 || batch < 1 || q_len < 0 ||

@@ -882,6 +882,7 @@ extern "C" int mrsa_selected_attention(const void* q, const void* k, const void*
                                        int64_t kv_len, int64_t kv_heads, int64_t groups,
                                        int64_t head_dim, int64_t topk, int64_t chunk,
                                        mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(q);
   return selected_launch<false, false>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
                                 mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
                                 stream);
@@ -895,6 +896,7 @@ extern "C" int mrsa_selected_attention_f16v(const void* q, const void* k, const 
                                             int64_t kv_len, int64_t kv_heads, int64_t groups,
                                             int64_t head_dim, int64_t topk, int64_t chunk,
                                             mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(q);
   return selected_launch<true, false>(q, k, v_f16, key_valid, weights, indices, local_out, local_w, out, sm_scale,
                                mask_last_token, batch, q_len, kv_len, kv_heads, groups, head_dim, topk, chunk,
                                stream);
@@ -908,6 +910,7 @@ extern "C" int mrsa_selected_attention_keep(const void* q, const void* k, const 
                                             int64_t q_len, int64_t kv_len, int64_t kv_heads, int64_t groups,
                                             int64_t head_dim, int64_t topk, int64_t chunk,
                                             mrsa_stream_t stream) {
+  mrsa::DeviceScope device_scope(q);
   if (token_keep == nullptr) return MRSA_ERR_NULL;
   if (v_f16)
     return selected_launch<true, true>(q, k, v, key_valid, weights, indices, local_out, local_w, out, sm_scale,
@@ -926,7 +929,7 @@ extern "C" int mrsa_device_error_flags(int clear) {
     if (cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int)) != cudaSuccess) return MRSA_ERR_LAUNCH;
   }
   const int r = mrsa::route_error_flags(clear), l = mrsa::local_error_flags(clear),
-            cv = mrsa::convert_error_flags(clear);
-  if (r < 0 || l < 0 || cv < 0) return MRSA_ERR_LAUNCH;
-  return (v ? 1 : 0) | (r ? 2 : 0) | (l ? 4 : 0) | (cv ? 8 : 0);
+            cv = mrsa::convert_error_flags(clear), bw = mrsa::bwd_error_flags(clear);
+  if (r < 0 || l < 0 || cv < 0 || bw < 0) return MRSA_ERR_LAUNCH;
+  return (v ? 1 : 0) | (r ? 2 : 0) | (l ? 4 : 0) | (cv ? 8 : 0) | (bw ? 16 : 0);
 }

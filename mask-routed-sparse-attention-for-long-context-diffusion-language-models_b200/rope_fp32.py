@@ -1,7 +1,7 @@
 """fp32 YaRN RoPE on the B200 kernels.
 
 Drop-ins for ``ops/rope_tilelang_fp32.py``: ``rope_rotary_pos_emb`` (:84) and
-``single_tensor_rope_autograd`` (:173, forward only), plus the position-id
+``single_tensor_rope_autograd`` (:173, with its backward), plus the position-id
 form used by the fused layer (cos/sin computed in the kernel from the YaRN
 inverse frequencies, as Dream's rotary module computes them).
 """
@@ -69,8 +69,7 @@ def rope_rotary_pos_emb(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin
     return qo, ko
 
 
-def single_tensor_rope_autograd(x: torch.Tensor, x_cos: torch.Tensor, x_sin: torch.Tensor):
-    """Single-tensor fp32 RoPE (``ops/rope_tilelang_fp32.py:173``, forward)."""
+def _single_rope(x, x_cos, x_sin):
     _check_x(x, "x")
     cos, sin, cs_dtype = _cs(x_cos, x_sin, x)
     x = x.contiguous()
@@ -79,6 +78,29 @@ def single_tensor_rope_autograd(x: torch.Tensor, x_cos: torch.Tensor, x_sin: tor
     _lib.call("mrsa_rope", _lib.ptr(x), _lib.ptr(y), h, None, None, 0, None, None, 0.0,
               _lib.ptr(cos), _lib.ptr(sin), cs_dtype, b, l, d, _lib.stream_of(x))
     return y
+
+
+class _SingleTensorRoPE(torch.autograd.Function):
+    """``ops/rope_tilelang_fp32.py:150 SingleTensorRoPEFunction``: the
+    backward is the same rotation with -sin."""
+
+    @staticmethod
+    def forward(ctx, x, x_cos, x_sin):
+        ctx.save_for_backward(x_cos, x_sin)
+        return _single_rope(x, x_cos, x_sin)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x_cos, x_sin = ctx.saved_tensors
+        return _single_rope(dy.to(torch.bfloat16).contiguous(), x_cos, -x_sin), None, None
+
+
+def single_tensor_rope_autograd(x: torch.Tensor, x_cos: torch.Tensor, x_sin: torch.Tensor):
+    """Single-tensor fp32 RoPE (``ops/rope_tilelang_fp32.py:173``); records
+    its backward when x requires grad."""
+    if torch.is_grad_enabled() and x.requires_grad:
+        return _SingleTensorRoPE.apply(x, x_cos, x_sin)
+    return _single_rope(x, x_cos, x_sin)
 
 
 def yarn_rope_qk(q: torch.Tensor, k: torch.Tensor | None, position_ids: torch.Tensor,

@@ -1,7 +1,8 @@
 """Query -> chunk routing on the B200 kernels.
 
 Drop-ins for ``ops/topk_head_softmax.py`` (``ref_softmax_topk_max_pooling``
-:15, ``online_softmax_topk_head`` :1242), ``dream_dllm_hils/routing.py``
+:15, ``online_softmax_topk_head`` :1242 with its scores backward :1071),
+``dream_dllm_hils/routing.py``
 (``route_topk_g7`` :52) and ``dream_dllm_hils/kernel_utils.py``
 (``remote_drop_mask`` :102).  The fused route layer does not materialise the
 dense drop mask; it evaluates the same rule inline.
@@ -92,6 +93,61 @@ def _route(q5: torch.Tensor, k_lmks: torch.Tensor, lse: torch.Tensor, topk: int,
     return idx, sc, rw, lw
 
 
+def route_scores_backward(q, landmarks, indices, grad_scores, sm_scale=None):
+    """``(d_q [B,L,Hq,D], d_landmarks [B,C,Hkv,G,D])`` in fp32 for the gathered
+    routing scores ``q . lmk[c_k] * sm_scale``: the backward of
+    ``ops/topk_head_softmax.py:1005 SoftmaxTopKMaxPoolingFusedFn``
+    (``:1071-1122``) with per-query-head landmarks."""
+    b, l, hq, d = q.shape
+    _, c, hkv, g, _ = landmarks.shape
+    topk = indices.shape[-1]
+    dev = q.device
+    qq = q.to(torch.bfloat16).contiguous()
+    lm = landmarks.to(torch.bfloat16).contiguous()
+    idx = indices.to(device=dev, dtype=torch.int32).contiguous()
+    gs = grad_scores.to(torch.bfloat16).reshape(b, l, hq, topk).contiguous()
+    d_q = torch.empty(b, l, hq, d, dtype=torch.float32, device=dev)
+    d_l = torch.empty(b, c, hkv, g, d, dtype=torch.float32, device=dev)
+    scale = d ** -0.5 if sm_scale is None else float(sm_scale)
+    lib = _lib.load()
+    ws_bytes = lib.mrsa_route_scores_backward_workspace(b, l, c, hkv, topk)
+    ws = torch.empty(max(int(ws_bytes), 16), dtype=torch.uint8, device=dev)
+    _lib.call("mrsa_route_scores_backward", _lib.ptr(qq), _lib.ptr(lm), _lib.ptr(idx), _lib.ptr(gs),
+              _lib.ptr(d_q), _lib.ptr(d_l), scale, b, l, c, hkv, g, d, topk, _lib.ptr(ws), int(ws_bytes),
+              _lib.stream_of(qq))
+    return d_q, d_l
+
+
+class _RouteScores(torch.autograd.Function):
+    """Routing with the B200 backward of the gathered scores (indices carry
+    no gradient): ``ops/topk_head_softmax.py:1005-1122``."""
+
+    @staticmethod
+    def forward(ctx, q5, k_lmks, lse, drop_mask, bias, topk, scores_dtype):
+        idx, sc, _, _ = _route(q5, k_lmks, lse, topk, drop_mask, bias, scores_dtype)
+        ctx.mark_non_differentiable(idx)
+        ctx.save_for_backward(q5, k_lmks, idx)
+        return idx, sc
+
+    @staticmethod
+    def backward(ctx, grad_idx, grad_sc):
+        q5, k_lmks, idx = ctx.saved_tensors
+        b, l, hkv, g, d = q5.shape
+        s = k_lmks.shape[1]
+        per_q = k_lmks.shape[2] == hkv * g
+        lm = k_lmks.view(b, s, hkv, g, d) if per_q else k_lmks[:, :, :, None, :].expand(b, s, hkv, g, d)
+        d_q, d_l = route_scores_backward(q5.reshape(b, l, hkv * g, d), lm, idx, grad_sc)
+        d_l = d_l.reshape(b, s, hkv * g, d) if per_q else d_l.sum(3)
+        return d_q.view(q5.shape).to(q5.dtype), d_l.to(k_lmks.dtype), None, None, None, None, None
+
+
+def _route_autograd(q5, k_lmks, lse, topk, drop_mask, bias, scores_dtype):
+    if torch.is_grad_enabled() and (q5.requires_grad or k_lmks.requires_grad):
+        return _RouteScores.apply(q5, k_lmks, lse, drop_mask, bias, topk, scores_dtype)
+    idx, sc, _, _ = _route(q5, k_lmks, lse, topk, drop_mask, bias, scores_dtype)
+    return idx, sc
+
+
 def ref_softmax_topk_max_pooling(q, k_lmks, lse_swa, topk, block_size, window_size, is_causal=False,
                                  q_offset=0, drop_mask=None, bias=None, gumbel_noise=None,
                                  selection_mode="post_softmax"):
@@ -112,17 +168,17 @@ def ref_softmax_topk_max_pooling(q, k_lmks, lse_swa, topk, block_size, window_si
 def online_softmax_topk_head(q, lmks, lse_swa, topk, block_size, window_size, is_causal=True,
                              q_offset=0, is_training=True, drop_mask=None, sm_scale=None, bias=None,
                              use_gumbel=False, gumbel_noise=None, G=1):
-    """Fused routing entry (``ops/topk_head_softmax.py:1242``), forward of the
-    non-causal, Gumbel-free selection.  ``q [B,L,Hq,D]``; returns
-    ``(indices [B,L,Hkv,topk] int32, scores [B,L,Hq,topk] bf16)``."""
+    """Fused routing entry (``ops/topk_head_softmax.py:1242``): the non-causal,
+    Gumbel-free selection.  ``q [B,L,Hq,D]``; returns ``(indices
+    [B,L,Hkv,topk] int32, scores [B,L,Hq,topk] bf16)``; the scores carry the
+    B200 backward to q and lmks when those require grad."""
     if is_causal or use_gumbel or gumbel_noise is not None:
         raise ValueError("the B200 routing kernel implements non-causal, Gumbel-free routing")
     if sm_scale is not None and abs(sm_scale - q.shape[-1] ** -0.5) > 1e-12:
         raise ValueError("only sm_scale = 1/sqrt(D) is supported")
     b, l, hq, d = q.shape
     hkv = hq // G
-    idx, sc, _, _ = _route(q.view(b, l, hkv, G, d), lmks, lse_swa, topk, drop_mask, bias,
-                           torch.bfloat16)
+    idx, sc = _route_autograd(q.view(b, l, hkv, G, d), lmks, lse_swa, topk, drop_mask, bias, torch.bfloat16)
     return idx, sc
 
 
@@ -151,9 +207,9 @@ def route_topk_g7(q, lmks, local_lse, prior_bias, drop_mask, topk, chunk_size, w
         raise ValueError(f"topk must be positive, got {topk}")
     if selection_mode != "post_softmax" or (use_gumbel and training):
         raise ValueError("the B200 routing kernel implements post_softmax routing without Gumbel")
-    idx, sc, _, _ = _route(q.view(batch, seq_len, h_kv, _LOGICAL_G, dim),
-                           lmks.reshape(batch, chunks, h_q, dim), local_lse, topk, drop_mask,
-                           prior_bias, torch.bfloat16)
+    idx, sc = _route_autograd(q.view(batch, seq_len, h_kv, _LOGICAL_G, dim),
+                              lmks.reshape(batch, chunks, h_q, dim), local_lse, topk, drop_mask,
+                              prior_bias, torch.bfloat16)
     idx = idx.long()
     sc = sc.to(q.dtype)
     if return_selected_gumbel:

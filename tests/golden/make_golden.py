@@ -14,6 +14,13 @@ outputs of the reference's OWN functions, imported from the checkout:
 * ``route.pt``     ``dream_dllm_hils/routing.py:52 route_topk_g7(training=False)``
 * ``weights.pt``   ``dream_dllm_hils/attention.py:126 _route_weights_torch``
 * ``selected.pt``  ``ops/hils_fwd_bwd_head.py:21 hils_torch_ref``
+* ``selected_bwd.pt`` gradients of ``hils_torch_ref`` (torch autograd on fp32
+  leaves): the quantities of the backward kernel ``:573-910``
+* ``pool_bwd.pt``  gradients of ``_compact_pool_torch`` (autograd, fp32 leaves)
+* ``weights_bwd.pt`` gradients of ``_route_weights_torch`` (autograd, fp32
+  leaves; affine gate and the plain softmax branch)
+* ``scores_bwd.pt`` ``ops/topk_head_softmax.py:1071 SoftmaxTopKMaxPoolingFusedFn.backward``
+  run on the CPU (its torch scatter + bmm), per-query-head landmarks
 * ``qcal.pt``      ``attention.py:41-63`` RoPE / inverse RoPE + ``qcal.py:22 rms_norm``
 * ``local_mask.pt`` ``dream_dllm_hils/local_attention.py:35-64`` K/V masking + window
 * ``layer.pt``     a whole route layer composed from the functions above (the
@@ -143,6 +150,87 @@ def gen_selected():
     w = torch.softmax(torch.randn(b, lq, hkv * gg, topk, generator=g), -1).bfloat16()
     out = hils_torch_ref(q, k, v, w, idx, chunk_size=s, sm_scale=d ** -0.5, block_q=1)
     _save("selected.pt", {"q": q, "k": k, "v": v, "weights": w, "indices": idx, "out": out})
+
+
+def gen_selected_bwd():
+    from ops.hils_fwd_bwd_head import hils_torch_ref
+
+    r = torch.load(os.path.join(HERE, "selected.pt"))
+    g = torch.Generator().manual_seed(83)
+    q, k, v, w = (r[n].float().requires_grad_() for n in ("q", "k", "v", "weights"))
+    d = q.shape[-1]
+    out = hils_torch_ref(q, k, v, w, r["indices"], chunk_size=64, sm_scale=d ** -0.5, block_q=1)
+    grad_out = torch.randn(out.shape, generator=g).bfloat16()
+    dq, dk, dv, dw = torch.autograd.grad(out, (q, k, v, w), grad_out.float())
+    _save("selected_bwd.pt", {"grad_out": grad_out, "dq": dq, "dk": dk, "dv": dv, "dw": dw})
+
+
+def gen_pool_bwd():
+    from ops.chunk_attn_pool_gqa_tilelang import _compact_pool_torch
+
+    r = torch.load(os.path.join(HERE, "pool.pt"))
+    g = torch.Generator().manual_seed(17)
+    mu = r["mu_q"].float().requires_grad_()
+    k = r["k_chunked"].float().requires_grad_()
+    lmk, ent = _compact_pool_torch(mu, k, r["key_valid"], 1.0 / math.sqrt(mu.shape[-1]))
+    g_lmk = torch.randn(lmk.shape, generator=g).bfloat16()
+    g_ent = torch.randn(ent.shape, generator=g)
+    d_mu, d_k = torch.autograd.grad((lmk, ent), (mu, k), (g_lmk.float(), g_ent))
+    _save("pool_bwd.pt", {"grad_lmk": g_lmk, "grad_entropy": g_ent, "d_mu": d_mu, "d_k": d_k})
+
+
+def gen_weights_bwd():
+    from dream_dllm_hils.attention import _route_weights_torch
+
+    r = torch.load(os.path.join(HERE, "route.pt"))
+    w = torch.load(os.path.join(HERE, "weights.pt"))
+    idx = r["indices"].clone()
+    scores = r["scores"].clone()
+    # every row keeps at least one selected chunk with a finite score (autograd
+    # of the affine gate is NaN for gate_scale on a row without one)
+    empty = idx[..., 0] < 0
+    idx[..., 0] = idx[..., 0].clamp_min(0)
+    scores[..., 0] = torch.where(empty.repeat_interleave(scores.shape[2] // idx.shape[2], dim=2),
+                                 torch.zeros((), dtype=scores.dtype), scores[..., 0])
+    g = torch.Generator().manual_seed(19)
+    b, l, hq, k = scores.shape
+    g_rw = torch.randn(b, l, hq, k, generator=g).bfloat16()
+    g_lw = torch.randn(b, l, hq, generator=g).bfloat16()
+    out = {"indices": idx, "scores": scores, "grad_remote": g_rw, "grad_local": g_lw, "cases": {}}
+    for affine, temp, off, scl in ((True, 1.0, 0.3, 1.7), (True, 0.7, -0.2, 0.8), (False, 1.0, 0.0, None),
+                                   (False, 0.7, 0.4, None)):
+        sc = scores.float().requires_grad_()
+        pb = r["bias"].float().contiguous().requires_grad_()
+        ll = w["local_lse"].float().requires_grad_()
+        go = torch.tensor(off, requires_grad=True)
+        gs = torch.tensor(scl, requires_grad=True) if affine else None
+        rw, lw = _route_weights_torch(sc, idx, pb, ll, temperature=temp, gate_offset=go, gate_scale=gs)
+        loss = (rw * g_rw.float()).sum() + (lw * g_lw.float()).sum()
+        leaves = (sc, pb, ll, go) + ((gs,) if affine else ())
+        grads = torch.autograd.grad(loss, leaves)
+        out["cases"][(affine, temp, off, scl)] = grads
+    _save("weights_bwd.pt", out)
+
+
+def gen_scores_bwd():
+    from ops.topk_head_softmax import SoftmaxTopKMaxPoolingFusedFn
+
+    r = torch.load(os.path.join(HERE, "route.pt"))
+    b, l, hq, d = r["q"].shape
+    _, c, hkv, gg, _ = r["lmk"].shape
+    g = torch.Generator().manual_seed(23)
+    grad = torch.randn(b, l, hq, r["topk"], generator=g).bfloat16()
+
+    class Ctx:
+        pass
+
+    ctx = Ctx()
+    ctx.saved_tensors = (r["q"].float().view(b, l, hkv, gg, d), r["lmk"].float().reshape(b, c, hq, d),
+                         r["indices"].to(torch.int32))
+    ctx.h_kv, ctx.G, ctx.shapes, ctx.sm_scale, ctx.per_qhead_lmks = hkv, gg, (b, l, c, hkv, d), None, True
+    res = SoftmaxTopKMaxPoolingFusedFn.backward(ctx, None, grad.float().view(b, l, hkv, gg, -1))
+    _save("scores_bwd.pt", {"grad_scores": grad, "d_q": res[0].reshape(b, l, hq, d),
+                            "d_lmk": res[1].reshape(b, c, hkv, gg, d)})
 
 
 def gen_qcal():
@@ -389,6 +477,10 @@ if __name__ == "__main__":
     gen_route()
     gen_weights()
     gen_selected()
+    gen_selected_bwd()
+    gen_pool_bwd()
+    gen_weights_bwd()
+    gen_scores_bwd()
     gen_qcal()
     gen_local_mask()
     gen_layer()
