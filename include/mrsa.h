@@ -267,7 +267,7 @@ int mrsa_route_weights_backward(const void* scores, const int32_t* indices, cons
 /* Backward of the gathered routing scores s[b,l,hq,k] = q[b,l,hq] .
  * landmarks[b,c_k,hq] * sm_scale (c_k = indices[b,l,hq/G,k]): q [B,L,Hq,D]
  * and landmarks [B,C,Hkv,G,D] bf16, grad_scores [B,L,Hq,K] bf16 -> d_q
- * [B,L,Hq,D] and d_landmarks [B,C,Hkv,G,D] fp32 (every element written).
+ * [B,L,Hq,D] and d_landmarks [B,C,Hkv,G,D] fp32 (every element written); G <= 8.
  * d_landmarks is summed per chunk over an inverted index built in
  * workspace (mrsa_route_scores_backward_workspace bytes, 16-byte aligned).
  * Replaces ops/topk_head_softmax.py:1071-1122 (SoftmaxTopKMaxPooling

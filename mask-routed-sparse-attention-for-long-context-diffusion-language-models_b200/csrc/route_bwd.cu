@@ -240,37 +240,56 @@ __global__ void __launch_bounds__(256) scores_dq_kernel(const __nv_bfloat16* __r
 }
 
 // d_lmk[c, hq, :] = scale * sum over the (l, k) that selected c of g[l, hq, k] * q[l, hq, :];
-// one CTA per (chunk, KV head, batch), thread = dim, the G heads in registers.
-__global__ void __launch_bounds__(128) scores_dlmk_kernel(const __nv_bfloat16* __restrict__ q,
+// one CTA per (chunk, KV head, batch): its 8 warps take every 8th pair, lane =
+// 4 dims, the G <= 8 heads in registers; the warps' sums meet in shared memory.
+constexpr int SG = 8;
+
+__global__ void __launch_bounds__(256) scores_dlmk_kernel(const __nv_bfloat16* __restrict__ q,
                                                           const __nv_bfloat16* __restrict__ grad,
                                                           const int32_t* __restrict__ cnt,
                                                           const int32_t* __restrict__ off,
                                                           const int32_t* __restrict__ pairs, float* __restrict__ dlmk,
                                                           int64_t seq_len, int Hkv, int G, int C, int K, float scale) {
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, d = threadIdx.x;
+  __shared__ float red[8][SG][PD];
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Hq = Hkv * G;
   const int seg = (b * Hkv + h) * C + c;
   const int n = cnt[seg], o = off[seg];
-  float acc[PG];
+  float acc[SG][4];
 #pragma unroll
-  for (int g = 0; g < PG; ++g) acc[g] = 0.f;
-  for (int i = 0; i < n; ++i) {
+  for (int g = 0; g < SG; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+  for (int i = warp; i < n; i += 8) {
     const int pr = pairs[o + i];
     const int64_t l = pr >> 5;
     const int slot = pr & 31;
     const int64_t base = (static_cast<int64_t>(b) * seq_len + l) * Hq + h * G;
+    const float gl = lane < G ? bf2f(grad[(base + lane) * K + slot]) : 0.f;
+    uint2 raw[SG];
 #pragma unroll
-    for (int g = 0; g < PG; ++g) {
-      if (g >= G) break;
-      const float gs = bf2f(grad[(base + g) * K + slot]);
-      acc[g] = fmaf(gs, bf2f(q[(base + g) * PD + d]), acc[g]);
+    for (int g = 0; g < SG; ++g)
+      raw[g] = g < G ? *reinterpret_cast<const uint2*>(q + (base + g) * PD + 4 * lane) : make_uint2(0u, 0u);
+#pragma unroll
+    for (int g = 0; g < SG; ++g) {
+      const float gg = __shfl_sync(0xffffffffu, gl, g);
+      const float2 a0 = unpack_bf16x2(raw[g].x), a1 = unpack_bf16x2(raw[g].y);
+      acc[g][0] = fmaf(gg, a0.x, acc[g][0]);
+      acc[g][1] = fmaf(gg, a0.y, acc[g][1]);
+      acc[g][2] = fmaf(gg, a1.x, acc[g][2]);
+      acc[g][3] = fmaf(gg, a1.y, acc[g][3]);
     }
   }
-  const int64_t out0 = ((static_cast<int64_t>(b) * C + c) * Hkv + h) * G;
 #pragma unroll
-  for (int g = 0; g < PG; ++g) {
-    if (g >= G) break;
-    dlmk[(out0 + g) * PD + d] = acc[g] * scale;
+  for (int g = 0; g < SG; ++g)
+    *reinterpret_cast<float4*>(&red[warp][g][4 * lane]) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+  __syncthreads();
+  const int64_t out0 = ((static_cast<int64_t>(b) * C + c) * Hkv + h) * G;
+  for (int e = threadIdx.x; e < G * PD; e += 256) {
+    const int g = e / PD, d = e % PD;
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][g][d];
+    dlmk[(out0 + g) * PD + d] = t * scale;
   }
 }
 
@@ -374,10 +393,10 @@ extern "C" int mrsa_route_scores_backward(const void* q, const void* landmarks, 
                                           size_t ws_bytes, mrsa_stream_t stream) {
   mrsa::DeviceScope device_scope(q);
   if (!q || !landmarks || !indices || !grad_scores || !d_q || !d_landmarks) return MRSA_ERR_NULL;
-  if (head_dim != PD || batch < 1 || q_len < 0 || chunks < 1 || kv_heads < 1 || groups < 1 || groups > PG ||
+  if (head_dim != PD || batch < 1 || q_len < 0 || chunks < 1 || kv_heads < 1 || groups < 1 || groups > SG ||
       topk < 1 || topk > 32 || batch > 65535 || kv_heads > 65535 || chunks > 0x7fffffffLL)
     return MRSA_ERR_SHAPE;
-  if ((reinterpret_cast<uintptr_t>(landmarks) | reinterpret_cast<uintptr_t>(d_q) |
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(landmarks) | reinterpret_cast<uintptr_t>(d_q) |
        reinterpret_cast<uintptr_t>(workspace)) & 15u)
     return MRSA_ERR_ALIGN;
   const size_t need = mrsa_route_scores_backward_workspace(batch, q_len, chunks, kv_heads, topk);
@@ -397,7 +416,7 @@ extern "C" int mrsa_route_scores_backward(const void* q, const void* landmarks, 
   }
   scores_dlmk_kernel<<<dim3(static_cast<unsigned>(chunks), static_cast<unsigned>(kv_heads),
                             static_cast<unsigned>(batch)),
-                       PD, 0, s>>>(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(grad_scores),
+                       256, 0, s>>>(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(grad_scores),
                                    ix.cnt, ix.off, ix.pairs, d_landmarks, q_len, hkv, g, c, kk, sm_scale);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;

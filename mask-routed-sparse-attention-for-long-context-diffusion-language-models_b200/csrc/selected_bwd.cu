@@ -887,29 +887,34 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ 
   if (threadIdx.x == 0) off[n] = carry;
 }
 
-// One warp walks its block's queries in order; lane k places slot k.  A
-// chunk listed twice by one query takes consecutive positions in slot order.
-__global__ void __launch_bounds__(32) place_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ hist,
-                                                   const int32_t* __restrict__ off, int32_t* __restrict__ pairs,
-                                                   int64_t Lq, int Hkv, int K, int C) {
-  extern __shared__ int ctr[];
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z, nqb = gridDim.x, lane = threadIdx.x;
+// The block's chunk lists are staged in shared memory by all threads; then one
+// warp walks the queries in order, lane k placing slot k.  A chunk listed twice
+// by one query takes consecutive positions in slot order.
+__global__ void __launch_bounds__(128) place_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ hist,
+                                                    const int32_t* __restrict__ off, int32_t* __restrict__ pairs,
+                                                    int64_t Lq, int Hkv, int K, int C) {
+  extern __shared__ int place_smem[];
+  int* ctr = place_smem;                     // [C]
+  int* lists = place_smem + C;               // [QT][K]
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z, nqb = gridDim.x;
   const int64_t seg0 = (static_cast<int64_t>(b) * Hkv + h) * C;
   const int32_t* pre = hist + ((static_cast<int64_t>(b) * Hkv + h) * nqb + qb) * C;
-  for (int c = lane; c < C; c += 32) ctr[c] = off[seg0 + c] + pre[c];
-  __syncwarp();
   const int64_t l0 = static_cast<int64_t>(qb) * QT;
   const int nq = static_cast<int>(Lq - l0 < QT ? Lq - l0 : QT);
+  for (int c = threadIdx.x; c < C; c += blockDim.x) ctr[c] = off[seg0 + c] + pre[c];
+  for (int e = threadIdx.x; e < nq * K; e += blockDim.x) lists[e] = idx[((b * Lq + l0 + e / K) * Hkv + h) * K + e % K];
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
   for (int i = 0; i < nq; ++i) {
     const int64_t l = l0 + i;
-    const int c = lane < K ? idx[((b * Lq + l) * Hkv + h) * K + lane] : -1;
+    const int c = lane < K ? lists[i * K + lane] : -1;
     const bool ok = c >= 0 && c < C;
     const uint32_t act = __ballot_sync(0xffffffffu, ok);
     if (ok) {
       const uint32_t peers = __match_any_sync(act, c);
       const int rank = __popc(peers & ((1u << lane) - 1u));
-      const int pos = ctr[c] + rank;
-      pairs[pos] = static_cast<int32_t>((l << 5) | lane);
+      pairs[ctr[c] + rank] = static_cast<int32_t>((l << 5) | lane);
       __syncwarp(act);
       if (rank == 0) ctr[c] += __popc(peers);
     }
@@ -987,13 +992,26 @@ int build_chunk_index(const int32_t* indices, int64_t batch, int64_t q_len, int 
   out->off = off;
   out->pairs = pairs;
   const size_t ctr_bytes = static_cast<size_t>(chunks) * sizeof(int);
+  const size_t place_bytes = ctr_bytes + static_cast<size_t>(QT) * topk * sizeof(int);
+  if (const cudaError_t e = cudaFuncSetAttribute(place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(place_bytes));
+      e != cudaSuccess) {
+    note_cuda_error(e, "build_chunk_index: shared-memory opt-in");
+    return MRSA_ERR_LAUNCH;
+  }
+  if (const cudaError_t e = cudaFuncSetAttribute(hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(ctr_bytes));
+      e != cudaSuccess) {
+    note_cuda_error(e, "build_chunk_index: shared-memory opt-in");
+    return MRSA_ERR_LAUNCH;
+  }
   if (nqb > 0) {
     const dim3 grid(static_cast<unsigned>(nqb), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
     hist_kernel<<<grid, 256, ctr_bytes, s>>>(indices, hist, q_len, kv_heads, topk, chunks);
     colscan_kernel<<<static_cast<unsigned>((segs + 255) / 256), 256, 0, s>>>(hist, cnt, segs, static_cast<int>(nqb),
                                                                             chunks);
     scan_kernel<<<1, 1024, 0, s>>>(cnt, off, static_cast<int>(segs));
-    place_kernel<<<grid, 32, ctr_bytes, s>>>(indices, hist, off, pairs, q_len, kv_heads, topk, chunks);
+    place_kernel<<<grid, 128, place_bytes, s>>>(indices, hist, off, pairs, q_len, kv_heads, topk, chunks);
   } else {
     if (const cudaError_t e = cudaMemsetAsync(cnt, 0, segs * 4, s); e != cudaSuccess) {
       note_cuda_error(e, "build_chunk_index: clearing the chunk counts");

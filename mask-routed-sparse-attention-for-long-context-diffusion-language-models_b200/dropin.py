@@ -124,11 +124,15 @@ def fused_unsupported(self, hidden_states, attention_mask=None, position_ids=Non
     pooled chunk summaries with the entropy prior, landmark slots skipped in
     the local branch, Q-Cal with RMSNorm, post-softmax routing, the affine
     fusion gate, no token refinement, no forced or ablated routes, no hooks
-    and no prefill capture, cos/sin from the module's rotary embedding."""
+    and no prefill capture, cos/sin from the module's rotary embedding, and
+    no gradient requested."""
     import torch
 
     if self.training:
         return "training forward"
+    if torch.is_grad_enabled() and (getattr(hidden_states, "requires_grad", False) or
+                                    any(p.requires_grad for p in self.parameters())):
+        return "gradient requested (the fused layer is forward-only)"
     if use_cache or past_key_value is not None:
         return "KV cache requested"
     validate = getattr(self, "_validate_kernel_call", None)

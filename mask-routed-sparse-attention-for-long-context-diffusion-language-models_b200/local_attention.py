@@ -1,6 +1,7 @@
 """Bidirectional window attention on the B200 kernel.
 
 Drop-in for ``dream_dllm_hils/local_attention.py:110 bidir_local_attention``
+(forward only: a call that would need its gradient raises)
 (the reference hands this to third-party flash-attn with
 ``window_size=(W, W)``): keys that are invalid or, with ``skip_inert_slots``,
 landmark slots get zero K and V -- they stay in the softmax with logit 0 --
@@ -12,6 +13,13 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+
+
+def _no_backward(*tensors) -> None:
+    # the window branch has no B200 backward: refuse rather than drop the gradient
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors):
+        raise NotImplementedError("the local window attention has no backward on the B200 kernels; "
+                                  "call it under torch.no_grad() or with inputs that do not require grad")
 
 
 def _validate_layout(q, k, v, key_valid) -> None:
@@ -36,6 +44,7 @@ def window_attention(q, k, v, key_valid, window: int, *, skip_inert: bool, chunk
     """Banded attention of query rows at global positions ``q_offset..`` over
     the full key range of ``k``/``v``; ``window`` is the effective flash window.
     ``v`` in fp16 runs the one-tile fp16 P kernel, bf16 the hi + lo one."""
+    _no_backward(q, k, v)
     b, lq, hq, d = q.shape
     lk, hkv = k.shape[1], k.shape[2]
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
@@ -75,6 +84,7 @@ def cached_local_attention(q, k, v, key_valid, query_positions, window: int, chu
     (``dream_dllm_hils/local_attention.py:147``): each row attends the cache
     keys within the same window as :func:`bidir_local_attention` around its own
     position.  Returns ``(o [B, Lq, Hq, D] bf16, lse [B, Lq, Hq])``."""
+    _no_backward(q, k, v)
     _validate_layout(q, k, v, key_valid)
     batch, query_len, h_q, dim = q.shape
     seq_len = k.shape[1]
@@ -116,6 +126,7 @@ def flex_attn_tl(q, k, v, window_size: int, chunk_size: int, training: bool = Tr
     visible key give 0 and ``-inf``."""
     if training and int(kv_start) != 0:
         raise ValueError("flex_attn_tl only supports non-zero kv_start in inference (training=False)")
+    _no_backward(q, k, v)
     if q.device.type != "cuda":
         raise ValueError("flex_attn_tl requires CUDA tensors")
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:

@@ -328,3 +328,16 @@ def test_fusion_and_rope_backward(mrsa, cuda_device):
     y.backward(gy.to(dev))
     want = orc.apply_rope(gy, cos, -sin)
     torch.testing.assert_close(xd.grad.float().cpu(), want.float(), atol=1e-2, rtol=8e-3)
+
+
+def test_local_window_refuses_to_drop_a_gradient(mrsa):
+    """No B200 backward for the window branch: asking for one raises instead
+    of returning a result that silently carries no gradient."""
+    from mrsa_b200.local_attention import _no_backward
+
+    x = torch.zeros(2, requires_grad=True)
+    with pytest.raises(NotImplementedError):
+        _no_backward(x, None)
+    with torch.no_grad():
+        _no_backward(x)
+    _no_backward(torch.zeros(2))

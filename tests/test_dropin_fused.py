@@ -112,7 +112,9 @@ def test_unsupported_calls_go_to_the_reference_forward(mrsa, fused_cls):
     m = fused_cls(hidden=256).eval()
     h = FakeHidden((1, 1024, 256))
     pos = torch.arange(1024)[None]
-    assert dropin.fused_unsupported(m, h, None, pos) is None
+    assert dropin.fused_unsupported(m, h, None, pos) == "gradient requested (the fused layer is forward-only)"
+    with torch.no_grad():
+        assert dropin.fused_unsupported(m, h, None, pos) is None
     mask4 = torch.ones(1, 1, 1024, 1024, dtype=torch.bool)
     cases = {
         "4-D allowed mask": dict(attention_mask=mask4),
@@ -120,6 +122,8 @@ def test_unsupported_calls_go_to_the_reference_forward(mrsa, fused_cls):
         "KV cache requested": dict(use_cache=True),
         "no position_ids": dict(position_ids=None),
     }
+    for p in m.parameters():
+        p.requires_grad_(False)
     for why, kw in cases.items():
         args = dict(attention_mask=None, position_ids=pos)
         args.update(kw)
@@ -131,7 +135,7 @@ def test_unsupported_calls_go_to_the_reference_forward(mrsa, fused_cls):
                              ("qcal_norm", None, "Q-Cal without RMSNorm"),
                              ("route_query_positions", torch.tensor([3]), "route_query_positions"),
                              ("_prefill_capture", True, "prefill cache capture")]:
-        m2 = fused_cls(hidden=256).eval()
+        m2 = fused_cls(hidden=256).eval().requires_grad_(False)
         setattr(m2, attr, value)
         assert dropin.fused_unsupported(m2, h, None, pos) == why, attr
     m.train()
