@@ -98,6 +98,14 @@ int mrsa_chunk_pool(const void* mu_q, int64_t mu_stride_b, int64_t mu_stride_c, 
 int mrsa_remote_drop_mask(const uint8_t* key_valid, int32_t* out, int64_t batch, int64_t seq_len,
                           int64_t window, int64_t chunk, mrsa_stream_t stream);
 
+/* The rows of that mask for query rows at cache positions `positions`
+ * [q_len] int64 (each in [0, seq_len)): out [B,q_len,C] int32.  The Fast-dLLM
+ * cached step's drop mask, remote_drop_mask(...).index_select(1, positions)
+ * (dream_dllm_hils/fastdllm_attention.py:279-283), without the dense [B,L,C]. */
+int mrsa_remote_drop_mask_positions(const uint8_t* key_valid, const int64_t* positions, int32_t* out,
+                                    int64_t batch, int64_t seq_len, int64_t q_len, int64_t window, int64_t chunk,
+                                    mrsa_stream_t stream);
+
 /* Post-softmax max-pooled top-K chunk routing + optional route weights.
  * route_q [B,Lq,Hq,D] (query rows at global positions q_offset..), landmarks
  * [B,C,Hkv,G,D] (lmk_per_qhead=1) or [B,C,Hkv,D] (0), local_lse [B,Lq,Hq],

@@ -32,6 +32,7 @@ _SIGS = {
     "mrsa_chunk_pool": [_vp, _i64, _i64, _vp, _vp, _f32, _vp, _vp, _vp, _vp, _vp,
                         _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_remote_drop_mask": [_vp, _vp, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_remote_drop_mask_positions": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp],
     "mrsa_route_topk": [_vp, _vp, _int, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp, _vp,
                         _int, _f32, _f32, _f32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz,
                         _vp],

@@ -87,9 +87,12 @@ __global__ void __launch_bounds__(256) rope_kernel(
 }
 
 __global__ void drop_mask_kernel(const uint8_t* __restrict__ key_valid, int32_t* __restrict__ out,
-                                 int64_t L, int64_t C, int64_t W, int64_t S) {
-  // one CTA per (query row, batch): chunk validity recomputed per chunk column
-  const int64_t i = blockIdx.x, b = blockIdx.y;
+                                 int64_t L, int64_t C, int64_t W, int64_t S, const int64_t* __restrict__ rows,
+                                 int64_t Lq) {
+  // one CTA per (query row, batch): chunk validity recomputed per chunk column;
+  // row r sits at position rows[r] (rows == NULL: at position r, Lq == L)
+  const int64_t r = blockIdx.x, b = blockIdx.y;
+  const int64_t i = rows != nullptr ? rows[r] : r;
   const int64_t lo = (i - W > 0 ? i - W : 0) / S;
   const int64_t hi = (i + W < L - 1 ? i + W : L - 1) / S;
   for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
@@ -99,7 +102,7 @@ __global__ void drop_mask_kernel(const uint8_t* __restrict__ key_valid, int32_t*
       const uint8_t* kv = key_valid + b * L + c * S;
       for (int s = 0; s < S - 1; ++s) ok |= kv[s] != 0;
     }
-    out[(b * L + i) * C + c] = ((c >= lo && c <= hi) || !ok) ? 1 : 0;
+    out[(b * Lq + r) * C + c] = ((c >= lo && c <= hi) || !ok) ? 1 : 0;
   }
 }
 
@@ -273,7 +276,22 @@ int mrsa_remote_drop_mask(const uint8_t* key_valid, int32_t* out, int64_t batch,
   if (seq_len > 0x7fffffffLL || batch > 65535) return MRSA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(seq_len), static_cast<unsigned>(batch));
   drop_mask_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      key_valid, out, seq_len, seq_len / chunk, window, chunk);
+      key_valid, out, seq_len, seq_len / chunk, window, chunk, nullptr, seq_len);
+  MRSA_CHECK_LAUNCH();
+  return MRSA_OK;
+}
+
+int mrsa_remote_drop_mask_positions(const uint8_t* key_valid, const int64_t* positions, int32_t* out,
+                                    int64_t batch, int64_t seq_len, int64_t q_len, int64_t window, int64_t chunk,
+                                    mrsa_stream_t stream) {
+  if (!out || !positions) return MRSA_ERR_NULL;
+  if (batch <= 0 || seq_len <= 0 || q_len < 0 || chunk <= 0 || seq_len % chunk) return MRSA_ERR_SHAPE;
+  if (window < 0) return MRSA_ERR_ARG;
+  if (q_len > 0x7fffffffLL || batch > 65535) return MRSA_ERR_SHAPE;
+  if (q_len == 0) return MRSA_OK;
+  dim3 grid(static_cast<unsigned>(q_len), static_cast<unsigned>(batch));
+  drop_mask_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      key_valid, out, seq_len, seq_len / chunk, window, chunk, positions, q_len);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
 }
