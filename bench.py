@@ -451,6 +451,33 @@ def run_ops(args):
                  f"{pairs / items:.2f} owner queries per item", ms, L, "tokens", "tensor",
                  L * HQ * TOPK * CHUNK * D * 4, "inputs larger than L2")
         ops = [o for o in ops if o != "coherent"]
+    if "gemm" in ops:
+        # Not a configs[] workload: the dense layers of configs[3] (Dream-shaped
+        # forward, B=1, L=32768) on the tcgen05 GEMM, torch's cuBLAS GEMM timed
+        # beside it for reference.
+        from mrsa_b200 import dense
+
+        m = 32768
+        x = rnd(m, 3584)
+        for name, n, k, mode in (("qkv_proj", 4608, 3584, "plain"), ("o_proj", 3584, 3584, "residual"),
+                                 ("gate_up_swiglu", 2 * 18944, 3584, "swiglu"), ("down_proj", 3584, 18944, "residual"),
+                                 ("lm_head", 152064, 3584, "plain")):
+            a = x if k == 3584 else rnd(m, k)
+            w = rnd(n, k, scale=0.02)
+            if mode == "plain":
+                fn = lambda: dense.linear(a, w)
+            elif mode == "residual":
+                r = rnd(m, n)
+                fn = lambda: dense.linear_residual(a, w, r)
+            else:
+                fn = lambda: dense.swiglu(a, w)
+            reps = max(2, args.steps // (4 if n > 100000 else 1))
+            ms = timed(fn, reps)
+            ms_ref = timed(lambda: torch.matmul(a, w.t()), reps)
+            emit("gemm", f"{name}: M={m} N={n} K={k} bf16 (epilogue {mode}); torch cuBLAS matmul of the same "
+                 f"shape {ms_ref:.3f} ms ({2 * m * n * k / ms_ref / 1e9:.0f} TFLOP/s)", ms, m, "rows", "tensor",
+                 2 * m * n * k, "operands larger than L2")
+        ops = [o for o in ops if o != "gemm"]
     if "backward" in ops:
         # Not a configs[] workload: the backward kernels at configs[1]'s route
         # layer (L=16384, the layer's own routing), gradients of random cotangents.
@@ -506,8 +533,10 @@ def run_ops(args):
              f"FFN 18944, vocab 152064, {model_parameters(cfg) / 1e9:.2f} B random N(0,0.02) parameters, "
              "logits out", ms, lseq, "tokens", "tensor", lseq * model.flops_per_token(lseq),
              "weights 15 GB and activations larger than L2",
-             # this repository's kernels: 8 per route layer, RoPE + V to fp16 + window per SWA layer
-             launches=7 * LAUNCHES_PER_STEP + 21 * 3)
+             # this repository's kernels per layer: 2 RMSNorm + 3 projection GEMMs + o_proj + SwiGLU +
+             # down_proj, and the attention (8 per route layer; RoPE + V to fp16 + window per SWA
+             # layer); the final RMSNorm and lm_head
+             launches=28 * 8 + 7 * LAUNCHES_PER_STEP + 21 * 3 + 2)
         ops = [o for o in ops if o != "dream"]
     for op in ops:
         if op == "flex":
@@ -578,7 +607,7 @@ def main():
                          "(the target of the ncu captures summarised under profiles/)")
     ap.add_argument("--op", default=None,
                     choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "swa", "dream", "coherent",
-                             "backward",
+                             "backward", "gemm",
                              "all"],
                     help="time one off-path op (or all) instead of the route layer; one JSON line each")
     args = ap.parse_args()

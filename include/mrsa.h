@@ -43,6 +43,7 @@ enum {
 
 enum { MRSA_BF16 = 0, MRSA_F32 = 1 };                 /* cos/sin and score dtypes */
 enum { MRSA_WEIGHTS_AFFINE = 0, MRSA_WEIGHTS_SOFTMAX = 1 };
+enum { MRSA_GEMM_PLAIN = 0, MRSA_GEMM_SWIGLU = 1, MRSA_GEMM_RESIDUAL = 2 };   /* mrsa_gemm_bf16 epilogues */
 
 const char* mrsa_strerror(int code);
 /* The CUDA error (name, message and the entry point or step that met it)
@@ -295,6 +296,24 @@ int mrsa_fuse_outputs_backward(const void* local, const void* local_w, const voi
                                void* d_local, void* d_local_w, int64_t rows, int64_t head_dim,
                                mrsa_stream_t stream);
 
+/* Dense bf16 GEMM of the Dream-shaped forward's projections and MLP (no
+ * reference counterpart: the reference runs them in Dream's remote modeling
+ * code through torch): C = A[M,K] . B[N,K]^T with fp32 accumulation and a
+ * fused epilogue -- MRSA_GEMM_PLAIN: C[M,N] = bf16(acc + bias[N]) (bias may
+ * be NULL); MRSA_GEMM_SWIGLU: B's rows interleaved per 256-row block as
+ * [gate n0..n0+127 ; up n0..n0+127], C[M,N/2] = bf16(bf16(silu(bf16(gate))) *
+ * bf16(up)); MRSA_GEMM_RESIDUAL: C[M,N] = bf16(residual[M,N] + bf16(acc)).
+ * N % 8 == 0 (N % 256 == 0 for SwiGLU), K % 64 == 0, row-major, 16-byte
+ * aligned pointers.  Sets bit 5
+ * of mrsa_device_error_flags if a CTA gave up on a bounded wait. */
+int mrsa_gemm_bf16(const void* a, const void* b, const void* bias, const void* residual, void* c, int64_t m,
+                   int64_t n, int64_t k, int epilogue, mrsa_stream_t stream);
+
+/* Qwen2RMSNorm over rows of dim bf16 values: y = w * bf16(x * rsqrt(mean(x^2)
+ * + eps)) with fp32 statistics (dim % 8 == 0). */
+int mrsa_rms_norm(const void* x, const void* weight, void* y, int64_t rows, int64_t dim, float eps,
+                  mrsa_stream_t stream);
+
 /* Candidate token scores [B,Lq,Hkv,K,S] fp32: for chunk c = indices[b,l,h,i]
  * and slot s, max over the G = q_heads/kv_heads heads of the group of
  * q_g . k[c*S+s] * sm_scale; -inf when c < 0 (or c >= kv_len/S), s == S-1 or
@@ -359,7 +378,8 @@ int mrsa_wait_selftest(int* result, int rounds, mrsa_stream_t stream);
  * output rows are then incomplete); bit 1 = a routing key CTA did (its keys,
  * hence its selections, are then incomplete); bit 2 = a local-window CTA did;
  * bit 3 = mrsa_convert_bf16_to_f16 saturated a value; bit 4 = a CTA of the
- * selected-attention backward gave up on a wait (its gradients are then incomplete).  Synchronises the current device; with
+ * selected-attention backward gave up on a wait (its gradients are then
+ * incomplete); bit 5 = a GEMM CTA did.  Synchronises the current device; with
  * clear != 0 also resets the mask.  Negative on a CUDA error.  Replaces the
  * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
 int mrsa_device_error_flags(int clear);

@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(_HERE, "libmrsa_b200.so")
 ERR_NULL, ERR_SHAPE, ERR_ALIGN, ERR_LAUNCH, ERR_ARG, ERR_WORKSPACE = -1, -2, -3, -4, -5, -6
 BF16, F32 = 0, 1
 WEIGHTS_AFFINE, WEIGHTS_SOFTMAX = 0, 1
+GEMM_PLAIN, GEMM_SWIGLU, GEMM_RESIDUAL = 0, 1, 2
 
 _vp, _i64, _f32, _int, _sz = C.c_void_p, C.c_int64, C.c_float, C.c_int, C.c_size_t
 
@@ -71,6 +72,8 @@ _SIGS = {
                                    _vp, _sz, _vp],
     "mrsa_route_scores_backward_workspace": [_i64, _i64, _i64, _i64, _i64],
     "mrsa_fuse_outputs_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
+    "mrsa_gemm_bf16": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
+    "mrsa_rms_norm": [_vp, _vp, _vp, _i64, _i64, _f32, _vp],
     "mrsa_device_error_flags": [_int],
     "mrsa_wait_selftest": [_vp, _int, _vp],
     "mrsa_route_layer_workspace_size": [_vp],

@@ -7,10 +7,11 @@ heads of 128, vocab 152064, RMSNorm eps 1e-6, route layers at
 ``idx % 4 == 3`` as ``dream_dllm_hils/attention.py:1823-1826`` installs them,
 the other 21 layers bidirectional SWA-1280).  Around the attention it keeps
 Qwen2's decoder layer: pre-norm, q/k/v projections with bias, ``o_proj``,
-residuals, SwiGLU MLP, final norm and ``lm_head``; the projections and MLP are
-plain library GEMMs (``torch.nn.functional.linear``), every attention stage
-runs on this package's kernels (the fused route layer, or RoPE plus the
-window kernel with fp16 V).  The landmark role offset is added to the input
+residuals, SwiGLU MLP, final norm and ``lm_head``.  Every stage runs on this
+package's kernels: the projections, the MLP and ``lm_head`` on the tcgen05
+GEMM with the bias, SwiGLU and residual epilogues fused (``dense.py``),
+RMSNorm on its own kernel, and the attention on the fused route layer or on
+RoPE plus the window kernel with fp16 V.  The landmark role offset is added to the input
 embeddings at landmark slots (``train_fulltext.py:2339-2351``).  Weights are
 random N(0, 0.02) (biases zero, norm weights one): no checkpoint is available.
 """
@@ -20,8 +21,8 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
-import torch.nn.functional as F
 
+from .dense import interleave_gate_up, linear, linear_residual, rms_norm, swiglu
 from .layer import RouteLayer, RouteLayerConfig
 from .local_attention import window_attention
 from .rope_fp32 import yarn_inv_freq, yarn_rope_qk
@@ -94,8 +95,9 @@ class DreamForward:
                 "wk": w(kd, c.hidden), "bk": torch.zeros(kd, device=dev, dtype=torch.bfloat16),
                 "wv": w(kd, c.hidden), "bv": torch.zeros(kd, device=dev, dtype=torch.bfloat16),
                 "wo": w(c.hidden, qd),
-                "wg": w(c.ffn, c.hidden), "wu": w(c.ffn, c.hidden), "wd": w(c.hidden, c.ffn),
             }
+            lay["wgu"] = interleave_gate_up(w(c.ffn, c.hidden), w(c.ffn, c.hidden))
+            lay["wd"] = w(c.hidden, c.ffn)
             if c.is_route(idx):
                 lay["route"] = RouteLayer(w(c.qcal_rank, c.hidden), w(qd, c.qcal_rank), cfg=lcfg)
             self.layers.append(lay)
@@ -106,17 +108,22 @@ class DreamForward:
 
     def rms_norm(self, x, weight):
         # Qwen2RMSNorm: fp32 statistics, back to the input dtype, times the weight
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.rms_eps)
-        return weight * xf.to(x.dtype)
+        return rms_norm(x, weight, self.cfg.rms_eps)
+
+    def gate_up(self, idx):
+        """The gate and up weights ``[F, H]`` of layer ``idx`` (copies out of
+        the interleaved SwiGLU operand)."""
+        wgu, c = self.layers[idx]["wgu"], self.cfg
+        blocks = wgu.view(c.ffn // 128, 2, 128, c.hidden)
+        return blocks[:, 0].reshape(c.ffn, c.hidden), blocks[:, 1].reshape(c.ffn, c.hidden)
 
     def attention(self, idx, h, position_ids, key_valid):
         """Attention output of layer ``idx`` before ``o_proj``: ``[B, L, Hq*D]``."""
         c, lay = self.cfg, self.layers[idx]
         b, l, _ = h.shape
-        q = F.linear(h, lay["wq"], lay["bq"]).view(b, l, c.q_heads, c.head_dim)
-        k = F.linear(h, lay["wk"], lay["bk"]).view(b, l, c.kv_heads, c.head_dim)
-        v = F.linear(h, lay["wv"], lay["bv"]).view(b, l, c.kv_heads, c.head_dim)
+        q = linear(h, lay["wq"], lay["bq"]).view(b, l, c.q_heads, c.head_dim)
+        k = linear(h, lay["wk"], lay["bk"]).view(b, l, c.kv_heads, c.head_dim)
+        v = linear(h, lay["wv"], lay["bv"]).view(b, l, c.kv_heads, c.head_dim)
         if "route" in lay:
             o = lay["route"].forward(q, k, v, h, position_ids, key_valid)
         else:
@@ -128,9 +135,9 @@ class DreamForward:
     def layer(self, idx, x, position_ids, key_valid):
         lay = self.layers[idx]
         h = self.rms_norm(x, lay["in_norm"])
-        x = x + F.linear(self.attention(idx, h, position_ids, key_valid), lay["wo"])
+        x = linear_residual(self.attention(idx, h, position_ids, key_valid), lay["wo"], x)
         h = self.rms_norm(x, lay["post_norm"])
-        return x + F.linear(F.silu(F.linear(h, lay["wg"])) * F.linear(h, lay["wu"]), lay["wd"])
+        return linear_residual(swiglu(h, lay["wgu"]), lay["wd"], x)
 
     @torch.inference_mode()
     def forward(self, ids, position_ids, key_valid=None, *, logits: bool = True, return_layer_inputs=False):
@@ -144,7 +151,7 @@ class DreamForward:
             x = self.layer(idx, x, position_ids, key_valid)
         out = self.rms_norm(x, self.final_norm)
         if logits:
-            out = F.linear(out, self.lm_head)
+            out = linear(out, self.lm_head)
         return (out, inputs) if return_layer_inputs else out
 
     __call__ = forward

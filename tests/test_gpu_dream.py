@@ -21,6 +21,7 @@ pytestmark = pytest.mark.gpu
 def _oracle_layer(model, idx, x, pos, valid):
     c, lay = model.cfg, model.layers[idx]
     cpu = {k: v.cpu() for k, v in lay.items() if torch.is_tensor(v)}
+    cpu["wg"], cpu["wu"] = (w.cpu() for w in model.gate_up(idx))
 
     def norm(t, w):
         tf = t.float()
