@@ -510,6 +510,16 @@ def run_ops(args):
         ms = timed(lambda: mrsa.chunk_pool_backward(mu, kc, valid.view(1, c, CHUNK), gl, ge), args.steps)
         emit("pool_backward", f"landmark-pool backward at L={L}", ms, L, "tokens", "hbm", L * HKV * D * 2 * 2,
              "K fits L2 (16.8 MB)", launches=1)
+        # the local window's backward (route layer: effective window 319, landmark keys zeroed)
+        kv_b = valid
+        lo, llse = mrsa.window_attention(q, k, v, kv_b, WLOC + CHUNK - 1, skip_inert=True, chunk=CHUNK)
+        gl_lse = torch.randn(1, L, HQ, device=dev)
+        ms = timed(lambda: mrsa.window_attention_backward(q, k, v, kv_b, lo, llse, go, gl_lse, window=WLOC + CHUNK - 1,
+                                                          skip_inert=True), args.steps)
+        pairs_loc = sum(min(L - 1, i + WLOC + CHUNK - 1) - max(0, i - WLOC - CHUNK + 1) + 1 for i in range(L))
+        emit("local_backward", f"local-window backward (dQ, dK, dV with the LSE gradient) at route-layer L={L}, "
+             "window 319; work = 2.5 x the forward's band FLOPs", ms, L, "tokens", "tensor",
+             2.5 * HQ * D * 4 * pairs_loc, "inputs larger than L2", launches=3)
         from mrsa_b200.route_weights import route_weights_backward
         from mrsa_b200 import _lib as mlib
 

@@ -296,6 +296,26 @@ int mrsa_fuse_outputs_backward(const void* local, const void* local_w, const voi
                                void* d_local, void* d_local_w, int64_t rows, int64_t head_dim,
                                mrsa_stream_t stream);
 
+/* Backward of mrsa_local_attention (bf16 V): from the forward's inputs q
+ * [B,L,Hq,D], k, v [B,L,Hkv,D] bf16 (q and k as the forward took them), key
+ * validity, its output `out` [B,L,Hq,D] bf16 and natural-log `lse` [B,L,Hq]
+ * fp32, and grad_out [B,L,Hq,D] bf16 plus grad_lse [B,L,Hq] fp32 (NULL =
+ * zero), writes dq [B,L,Hq,D] and dk, dv [B,L,Hkv,D] in fp32 (every element;
+ * zeroed keys -- invalid, or landmark slots with skip_inert -- get 0).  The
+ * softmax gradient dS and P are rounded to bf16 before their GEMMs.
+ * `window` is the effective window (|i - j| <= window), L % 64 == 0, G <= 8.
+ * workspace: mrsa_local_attention_backward_workspace() bytes (the per-row
+ * dO.O - dlse terms).  Sets bit 6 of mrsa_device_error_flags if a CTA gave up
+ * on a bounded wait.  Replaces the backward of the flash-attn call inside
+ * dream_dllm_hils/local_attention.py:110-144 bidir_local_attention. */
+int mrsa_local_attention_backward(const void* q, const void* k, const void* v, const uint8_t* key_valid,
+                                  const void* out, const float* lse, const void* grad_out, const float* grad_lse,
+                                  float* dq, float* dk, float* dv, void* workspace, size_t ws_bytes,
+                                  int64_t window, int skip_inert, int64_t chunk, float sm_scale, int64_t batch,
+                                  int64_t seq_len, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                  mrsa_stream_t stream);
+size_t mrsa_local_attention_backward_workspace(int64_t batch, int64_t seq_len, int64_t q_heads);
+
 /* Dense bf16 GEMM of the Dream-shaped forward's projections and MLP (no
  * reference counterpart: the reference runs them in Dream's remote modeling
  * code through torch): C = A[M,K] . B[N,K]^T with fp32 accumulation and a
@@ -379,7 +399,8 @@ int mrsa_wait_selftest(int* result, int rounds, mrsa_stream_t stream);
  * hence its selections, are then incomplete); bit 2 = a local-window CTA did;
  * bit 3 = mrsa_convert_bf16_to_f16 saturated a value; bit 4 = a CTA of the
  * selected-attention backward gave up on a wait (its gradients are then
- * incomplete); bit 5 = a GEMM CTA did.  Synchronises the current device; with
+ * incomplete); bit 5 = a GEMM CTA did; bit 6 = a CTA of the local-window
+ * backward did.  Synchronises the current device; with
  * clear != 0 also resets the mask.  Negative on a CUDA error.  Replaces the
  * reference's host-side kernel-fallback reporting (dream_dllm_hils/attention.py:932-940). */
 int mrsa_device_error_flags(int clear);

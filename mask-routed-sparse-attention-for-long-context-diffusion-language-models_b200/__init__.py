@@ -13,7 +13,7 @@ from .chunk_pool import chunk_attn_pool_gqa, chunk_pool_backward
 from .dream_forward import DreamConfig, DreamForward
 from .layer import RouteLayer, RouteLayerConfig, swa_layer_forward
 from .local_attention import (bidir_local_attention, cached_local_attention, flex_attn_tl,
-                              window_attention)
+                              window_attention, window_attention_backward)
 from .rope_fp32 import rope_rotary_pos_emb, single_tensor_rope_autograd, yarn_inv_freq, yarn_rope_qk
 from .route_weights import route_weights, route_weights_backward, route_weights_torch
 from .routing import (online_softmax_topk_head, ref_softmax_topk_max_pooling, remote_drop_mask,
@@ -33,7 +33,7 @@ __all__ = [
     "selected_attention_g7",
     "selected_attention_g7_cached", "to_f16", "flex_attn_tl", "candidate_token_scores_gqa",
     "selected_token_attention_tilelang", "load_library", "chunk_pool_backward", "route_weights_backward",
-    "route_scores_backward", "fuse_outputs_backward",
+    "route_scores_backward", "fuse_outputs_backward", "window_attention_backward",
 ]
 
 

@@ -74,6 +74,9 @@ _SIGS = {
     "mrsa_fuse_outputs_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "mrsa_gemm_bf16": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp],
     "mrsa_rms_norm": [_vp, _vp, _vp, _i64, _i64, _f32, _vp],
+    "mrsa_local_attention_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64, _int,
+                                      _i64, _f32, _i64, _i64, _i64, _i64, _i64, _vp],
+    "mrsa_local_attention_backward_workspace": [_i64, _i64, _i64],
     "mrsa_device_error_flags": [_int],
     "mrsa_wait_selftest": [_vp, _int, _vp],
     "mrsa_route_layer_workspace_size": [_vp],
@@ -82,7 +85,8 @@ _SIGS = {
 }
 _RESTYPE = {"mrsa_strerror": C.c_char_p, "mrsa_last_error": C.c_char_p, "mrsa_route_layer_workspace_size": _sz,
             "mrsa_route_topk_workspace_size": _sz, "mrsa_selected_token_attention_smem": _sz,
-            "mrsa_selected_attention_backward_workspace": _sz, "mrsa_route_scores_backward_workspace": _sz}
+            "mrsa_selected_attention_backward_workspace": _sz, "mrsa_route_scores_backward_workspace": _sz,
+            "mrsa_local_attention_backward_workspace": _sz}
 
 EXPORTED = tuple(_SIGS)
 

@@ -126,6 +126,7 @@ int local_error_flags(int clear);
 int convert_error_flags(int clear);
 int bwd_error_flags(int clear);
 int gemm_error_flags(int clear);
+int local_bwd_error_flags(int clear);
 
 // Inverted chunk -> (query, slot) index of indices [B,Lq,Hkv,K] int32: per
 // segment (b, h, c) (flattened as (b*Hkv + h)*C + c) cnt[seg] entries from

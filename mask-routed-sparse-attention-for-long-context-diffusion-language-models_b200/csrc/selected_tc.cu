@@ -930,7 +930,7 @@ extern "C" int mrsa_device_error_flags(int clear) {
   }
   const int r = mrsa::route_error_flags(clear), l = mrsa::local_error_flags(clear),
             cv = mrsa::convert_error_flags(clear), bw = mrsa::bwd_error_flags(clear),
-            gm = mrsa::gemm_error_flags(clear);
-  if (r < 0 || l < 0 || cv < 0 || bw < 0 || gm < 0) return MRSA_ERR_LAUNCH;
-  return (v ? 1 : 0) | (r ? 2 : 0) | (l ? 4 : 0) | (cv ? 8 : 0) | (bw ? 16 : 0) | (gm ? 32 : 0);
+            gm = mrsa::gemm_error_flags(clear), lb = mrsa::local_bwd_error_flags(clear);
+  if (r < 0 || l < 0 || cv < 0 || bw < 0 || gm < 0 || lb < 0) return MRSA_ERR_LAUNCH;
+  return (v ? 1 : 0) | (r ? 2 : 0) | (l ? 4 : 0) | (cv ? 8 : 0) | (bw ? 16 : 0) | (gm ? 32 : 0) | (lb ? 64 : 0);
 }

@@ -1,7 +1,9 @@
 """Bidirectional window attention on the B200 kernel.
 
 Drop-in for ``dream_dllm_hils/local_attention.py:110 bidir_local_attention``
-(forward only: a call that would need its gradient raises)
+with its backward (``window_attention_backward``; flash-attn's in the
+reference); ``cached_local_attention`` and ``flex_attn_tl`` are forward-only
+and raise when a gradient would be needed
 (the reference hands this to third-party flash-attn with
 ``window_size=(W, W)``): keys that are invalid or, with ``skip_inert_slots``,
 landmark slots get zero K and V -- they stay in the softmax with logit 0 --
@@ -16,10 +18,66 @@ from . import _lib
 
 
 def _no_backward(*tensors) -> None:
-    # the window branch has no B200 backward: refuse rather than drop the gradient
-    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors):
-        raise NotImplementedError("the local window attention has no backward on the B200 kernels; "
+    # calls without a B200 backward refuse rather than drop the gradient
+    if _wants_grad(*tensors):
+        raise NotImplementedError("this window attention call has no backward on the B200 kernels; "
                                   "call it under torch.no_grad() or with inputs that do not require grad")
+
+
+def _wants_grad(*tensors) -> bool:
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
+def window_attention_backward(q, k, v, key_valid, out, lse, grad_out, grad_lse=None, *, window: int,
+                              skip_inert: bool, chunk: int = 64, sm_scale=None):
+    """``(dq, dk, dv)`` in fp32 of :func:`window_attention` (query rows = the
+    key rows, bf16 V): the backward of the flash-attn call inside
+    ``dream_dllm_hils/local_attention.py:110-144``, including the gradient
+    that reaches the LSE output (``grad_lse``, e.g. from the route weights).
+    ``window`` is the effective window; zeroed keys get zero dk / dv."""
+    b, l, hq, d = q.shape
+    hkv = k.shape[2]
+    dev = q.device
+    if v.dtype != torch.bfloat16 or q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise ValueError("the window-attention backward requires BF16 q, k and v")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    kv = None if key_valid is None else key_valid.to(device=dev, dtype=torch.bool).contiguous()
+    o = out.to(torch.bfloat16).contiguous()
+    ls = lse.to(torch.float32).contiguous()
+    go = grad_out.to(torch.bfloat16).contiguous()
+    gl = None if grad_lse is None else grad_lse.to(torch.float32).contiguous()
+    dq = torch.empty(b, l, hq, d, dtype=torch.float32, device=dev)
+    dk = torch.empty(b, l, hkv, d, dtype=torch.float32, device=dev)
+    dv = torch.empty_like(dk)
+    ws_bytes = int(_lib.load().mrsa_local_attention_backward_workspace(b, l, hq))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    scale = float(d) ** -0.5 if sm_scale is None else float(sm_scale)
+    _lib.call("mrsa_local_attention_backward", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(kv), _lib.ptr(o),
+              _lib.ptr(ls), _lib.ptr(go), _lib.ptr(gl), _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(ws),
+              ws_bytes, int(window), int(bool(skip_inert)), int(chunk), scale, b, l, hq, hkv, d, _lib.stream_of(q))
+    return dq, dk, dv
+
+
+class _WindowAttention(torch.autograd.Function):
+    """Window attention with the B200 backward (flash-attn's role in the reference)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, key_valid, window, skip_inert, chunk):
+        with torch.no_grad():
+            out, lse = _window_forward(q, k, v, key_valid, window, skip_inert=skip_inert, chunk=chunk)
+        ctx.save_for_backward(q, k, v, key_valid, out, lse)
+        ctx.cfg = (window, skip_inert, chunk)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, grad_out, grad_lse):
+        q, k, v, key_valid, out, lse = ctx.saved_tensors
+        window, skip_inert, chunk = ctx.cfg
+        if grad_out is None:
+            grad_out = torch.zeros_like(out)
+        dq, dk, dv = window_attention_backward(q, k, v, key_valid, out, lse, grad_out, grad_lse, window=window,
+                                               skip_inert=skip_inert, chunk=chunk)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None, None
 
 
 def _validate_layout(q, k, v, key_valid) -> None:
@@ -43,8 +101,20 @@ def window_attention(q, k, v, key_valid, window: int, *, skip_inert: bool, chunk
                      q_offset: int = 0, out=None, lse=None, need_lse: bool = True):
     """Banded attention of query rows at global positions ``q_offset..`` over
     the full key range of ``k``/``v``; ``window`` is the effective flash window.
-    ``v`` in fp16 runs the one-tile fp16 P kernel, bf16 the hi + lo one."""
-    _no_backward(q, k, v)
+    ``v`` in fp16 runs the one-tile fp16 P kernel, bf16 the hi + lo one.
+    When an input requires grad (query rows = key rows, bf16 V, no output
+    buffers) the call records the B200 backward."""
+    if _wants_grad(q, k, v):
+        if q_offset != 0 or q.shape[1] != k.shape[1] or out is not None or lse is not None or \
+                v.dtype != torch.bfloat16:
+            _no_backward(q, k, v)
+        return _WindowAttention.apply(q, k, v, key_valid, int(window), bool(skip_inert), int(chunk))
+    return _window_forward(q, k, v, key_valid, window, skip_inert=skip_inert, chunk=chunk, q_offset=q_offset,
+                           out=out, lse=lse, need_lse=need_lse)
+
+
+def _window_forward(q, k, v, key_valid, window: int, *, skip_inert: bool, chunk: int = 64,
+                    q_offset: int = 0, out=None, lse=None, need_lse: bool = True):
     b, lq, hq, d = q.shape
     lk, hkv = k.shape[1], k.shape[2]
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()

@@ -17,7 +17,8 @@ import math
 
 import torch
 
-__all__ = ["selected_attention_grads", "pool_grads", "route_weights_grads", "route_scores_grads", "fuse_grads"]
+__all__ = ["selected_attention_grads", "pool_grads", "route_weights_grads", "route_scores_grads", "fuse_grads",
+           "local_attention_grads", "dense_local_attention"]
 
 
 def _selected_fp32(q, k, v, w, idx, ok, chunk, scale):
@@ -194,3 +195,44 @@ def fuse_grads(local, local_weight, grad_out):
     (``ops/hils_bidir_output_fusion_tilelang.py:38-99``), fp32."""
     gf = grad_out.float()
     return gf, gf * local_weight.float()[..., None], (gf * local.float()).sum(-1)
+
+
+def local_attention_grads(q, k, v, key_valid, window: int, chunk: int, skip_inert_slots: bool, grad_out,
+                          grad_lse=None):
+    """(dq, dk, dv) in fp32: autograd of the oracle's banded attention
+    (:func:`oracle.route_layer.local_attention`, the restatement of
+    ``dream_dllm_hils/local_attention.py:35-144`` that hands the window to
+    flash-attn), including the gradient that reaches its LSE output.
+    ``window`` is the layer's window (the oracle widens it by chunk - 1 with
+    ``skip_inert_slots``)."""
+    from . import route_layer as orc
+
+    qf, kf, vf = (t.float().detach().requires_grad_() for t in (q, k, v))
+    out, lse = orc.local_attention(qf, kf, vf, key_valid, window, chunk, skip_inert_slots)
+    outs, grads = [out], [grad_out.float()]
+    if grad_lse is not None:
+        outs.append(lse)
+        grads.append(grad_lse.float())
+    return torch.autograd.grad(outs, (qf, kf, vf), grads)
+
+
+def dense_local_attention(q, k, v, key_valid, window: int, chunk: int, skip_inert_slots: bool):
+    """The same banded attention written densely over the whole [L, L] score
+    matrix (an independent formulation for pinning :func:`local_attention_grads`
+    on small inputs): keys zeroed where invalid (and at landmark slots with
+    ``skip_inert_slots``), ``|i - j| <= window (+ chunk - 1)``."""
+    b, l, hq, d = q.shape
+    g = hq // k.shape[2]
+    valid = key_valid.bool()
+    if skip_inert_slots:
+        valid = valid & ((torch.arange(l) + 1) % chunk != 0)[None]
+    w = window + chunk - 1 if skip_inert_slots else window
+    z = valid.to(k.dtype)[:, :, None, None]
+    kz = (k * z).repeat_interleave(g, dim=2)
+    vz = (v * z).repeat_interleave(g, dim=2)
+    s = torch.einsum("bihd,bjhd->bhij", q, kz) / math.sqrt(d)
+    band = (torch.arange(l)[:, None] - torch.arange(l)[None, :]).abs() <= w
+    s = s.masked_fill(~band[None, None], float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    out = torch.einsum("bhij,bjhd->bihd", torch.softmax(s, dim=-1), vz)
+    return out, lse.permute(0, 2, 1)

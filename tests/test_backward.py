@@ -330,9 +330,74 @@ def test_fusion_and_rope_backward(mrsa, cuda_device):
     torch.testing.assert_close(xd.grad.float().cpu(), want.float(), atol=1e-2, rtol=8e-3)
 
 
+def test_local_grads_oracle_matches_a_dense_formulation():
+    """The banded oracle's gradients (block-wise softmax with an LSE output)
+    equal autograd of the dense [L, L] formulation."""
+    g = torch.Generator().manual_seed(43)
+    b, l, hkv, gg, d = 1, 256, 1, 3, 128
+    q = torch.randn(b, l, hkv * gg, d, generator=g)
+    k = torch.randn(b, l, hkv, d, generator=g) / d ** 0.5
+    v = torch.randn(b, l, hkv, d, generator=g)
+    valid = torch.ones(b, l, dtype=torch.bool)
+    valid[0, 90:100] = False
+    go = torch.randn(b, l, hkv * gg, d, generator=g)
+    gl = torch.randn(b, l, hkv * gg, generator=g)
+    for window, skip in ((40, True), (70, False)):
+        got = obw.local_attention_grads(q, k, v, valid, window, 64, skip, go, gl)
+        qf, kf, vf = (t.clone().requires_grad_() for t in (q, k, v))
+        out, lse = obw.dense_local_attention(qf, kf, vf, valid, window, 64, skip)
+        want = torch.autograd.grad((out, lse), (qf, kf, vf), (go, gl))
+        for a, w_ in zip(got, want):
+            torch.testing.assert_close(a, w_, atol=2e-5, rtol=1e-4)
+
+
+def _local_case(b, l, hkv, g, seed):
+    gen = torch.Generator().manual_seed(seed)
+    q = (torch.randn(b, l, hkv * g, 128, generator=gen) / 2).bfloat16()
+    k = (torch.randn(b, l, hkv, 128, generator=gen) / 2).bfloat16()
+    v = torch.randn(b, l, hkv, 128, generator=gen).bfloat16()
+    valid = torch.ones(b, l, dtype=torch.bool)
+    valid[:, 150:190] = False
+    valid[-1, l - 100:] = False
+    go = torch.randn(b, l, hkv * g, 128, generator=gen).bfloat16()
+    gl = torch.randn(b, l, hkv * g, generator=gen)
+    return q, k, v, valid, go, gl
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("b,l,hkv,g,window,skip", [
+    (2, 1024, 2, 7, 256, True),       # the route layer's local branch (effective window 319)
+    (1, 2048, 1, 7, 1280, False),     # an SWA layer
+    (1, 512, 2, 8, 40, True),         # a full 8-head group, a short window
+])
+def test_local_window_backward_matches_oracle(mrsa, cuda_device, b, l, hkv, g, window, skip):
+    dev = cuda_device
+    q, k, v, valid, go, gl = _local_case(b, l, hkv, g, seed=l + window)
+    eff = window + 63 if skip else window
+    qd, kd, vd = (t.to(dev).requires_grad_() for t in (q, k, v))
+    out, lse = mrsa.bidir_local_attention(qd, kd, vd, valid.to(dev), window, 64, skip_inert_slots=skip)
+    torch.autograd.backward((out, lse), (go.to(dev), gl.to(dev)))
+    torch.cuda.synchronize()
+    assert mrsa._lib.load().mrsa_device_error_flags(1) == 0
+    rq, rk, rv = obw.local_attention_grads(q, k, v, valid, window, 64, skip, go, gl)
+    close_grad(qd.grad, rq, "dq")
+    close_grad(kd.grad, rk, "dk")
+    close_grad(vd.grad, rv, "dv")
+    # zeroed keys get no gradient
+    zero = ~valid
+    if skip:
+        zero = zero | ((torch.arange(l) + 1) % 64 == 0)[None]
+    assert (kd.grad.cpu()[zero] == 0).all() and (vd.grad.cpu()[zero] == 0).all()
+    # the direct call with the same inputs gives the same bits
+    dq, dk, dv = mrsa.window_attention_backward(q.to(dev), k.to(dev), v.to(dev), valid.to(dev), out.detach(),
+                                                lse.detach(), go.to(dev), gl.to(dev), window=eff, skip_inert=skip)
+    assert torch.equal(dq.bfloat16(), qd.grad) and torch.equal(dk.bfloat16(), kd.grad)
+
+
 def test_local_window_refuses_to_drop_a_gradient(mrsa):
-    """No B200 backward for the window branch: asking for one raises instead
-    of returning a result that silently carries no gradient."""
+    """Calls without a backward (cached rows, the causal flex window, output
+    buffers) raise instead of returning a result that silently carries no
+    gradient."""
     from mrsa_b200.local_attention import _no_backward
 
     x = torch.zeros(2, requires_grad=True)
