@@ -93,8 +93,9 @@ class _RouteWeights(torch.autograd.Function):
         d_sc, d_pb, d_ll, d_gs, d_go = route_weights_backward(
             scores, indices, prior_bias, local_lse, grad_rw, grad_lw, mode=mode, temperature=temperature,
             gate_scale=gs, gate_offset=go)
+        need = ctx.needs_input_grad
         return (d_sc.to(dtype), None, d_pb.to(prior_bias.dtype), d_ll.to(local_lse.dtype),
-                d_gs if has_gs else None, d_go if has_go else None, None, None)
+                d_gs if has_gs and need[4] else None, d_go if has_go and need[5] else None, None, None)
 
 
 def _wants_grad(*xs) -> bool:

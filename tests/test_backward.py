@@ -406,3 +406,73 @@ def test_local_window_refuses_to_drop_a_gradient(mrsa):
     with torch.no_grad():
         _no_backward(x)
     _no_backward(torch.zeros(2))
+
+
+@pytest.mark.gpu
+def test_route_layer_training_step_matches_oracle_autograd(mrsa, cuda_device):
+    """A whole route layer trained through the drop-ins -- RoPE, local window,
+    Q-Cal (torch, as the reference module computes it), landmark pool,
+    routing scores, affine-gate route weights, selected attention and fusion,
+    each with its B200 backward -- against fp32 autograd of the oracle's
+    composition on the kernel's own selection (routing indices carry no
+    gradient).  Gradients of q, k, v, the hidden state and the Q-Cal weights
+    within relative L2 5e-2 (bf16 roundings on every stage of the GPU side)."""
+    from oracle import route_layer as orc
+
+    dev = cuda_device
+    cfg = orc.MRSAConfig()
+    l, topk = 1024, 8
+    inp = orc.make_route_layer_inputs(1, l, cfg, hidden=3584, seed=17)
+    inp["key_valid"][0, 700:720] = False
+    pos = orc.landmark_position_ids(1, l)
+    inv, af = orc.yarn_inv_freq(128, cfg.rope_theta, cfg.yarn_factor, cfg.yarn_orig_max_pos)
+    cos, sin = orc.rope_cos_sin(pos, inv, af)
+    valid = inp["key_valid"]
+    gen = torch.Generator().manual_seed(5)
+    gout = torch.randn(1, l, 28, 128, generator=gen)
+    names = ("q_pre", "k_pre", "v", "hidden", "w_in", "w_out")
+
+    # ---- GPU: the drop-ins under autograd
+    leaves = {n: inp[n].to(dev).requires_grad_() for n in names}
+    c, s = cos.to(dev), sin.to(dev)
+    vd = valid.to(dev)
+    q = mrsa.single_tensor_rope_autograd(leaves["q_pre"], c, s)
+    k = mrsa.single_tensor_rope_autograd(leaves["k_pre"], c, s)
+    lo, lse = mrsa.bidir_local_attention(q, k, leaves["v"], vd, cfg.local_window, 64, skip_inert_slots=True)
+    t = (leaves["hidden"] @ leaves["w_in"].t())
+    delta = (t @ leaves["w_out"].t()).view(1, l, 28, 128)
+    comb = (mrsa.single_tensor_rope_autograd(q, c, -s).float() + delta.float()).bfloat16()
+    cf = comb.float()
+    normed = (cf * torch.rsqrt(cf.pow(2).mean(-1, keepdim=True) + cfg.rms_eps)).bfloat16()
+    route_q = mrsa.single_tensor_rope_autograd(normed, c, s)
+    n_chunks = l // 64
+    mu = route_q[:, 63::64].reshape(1, n_chunks, 4, 7, 128)
+    lmk, ent = mrsa.chunk_attn_pool_gqa(mu, k.view(1, n_chunks, 64, 4, 128), vd.view(1, n_chunks, 64))
+    prior = ent * 1.0
+    drop = mrsa.remote_drop_mask(vd, cfg.local_window, 64)
+    idx, sc = mrsa.route_topk_g7(route_q, lmk, lse.view(1, l, 4, 7), prior, drop, topk, 64, cfg.local_window)
+    rw, lw = mrsa.route_weights_torch(sc, idx, prior, lse, temperature=1.0, gate_offset=torch.tensor(0.3),
+                                      gate_scale=torch.tensor(1.2))
+    remote = mrsa.HiLS_block_M_head(q, k, leaves["v"], rw, idx, key_valid=vd)
+    out = mrsa.fuse_hils_outputs(remote, lo, lw)
+    (out.float() * gout.to(dev)).sum().backward()
+    torch.cuda.synchronize()
+    assert mrsa._lib.load().mrsa_device_error_flags(1) == 0
+
+    # ---- CPU: the oracle's composition in fp32 on the same selection
+    ref = {n: inp[n].float().requires_grad_() for n in names}
+    rq = orc.apply_rope(ref["q_pre"], cos, sin)
+    rk = orc.apply_rope(ref["k_pre"], cos, sin)
+    rlo, rlse = orc.local_attention(rq, rk, ref["v"], valid, cfg.local_window, 64, True)
+    rroute = orc.qcal_route_query(ref["hidden"], rq, ref["w_in"], ref["w_out"], torch.ones(128), cos, sin,
+                                  eps=cfg.rms_eps)
+    rmu = rroute[:, 63::64].reshape(1, n_chunks, 4, 7, 128)
+    rlmk, rent = orc.chunk_pool(rmu, rk.view(1, n_chunks, 64, 4, 128), valid.view(1, n_chunks, 64))
+    ridx = idx.long().cpu()
+    rsc = orc.route_scores_at(rroute, rlmk, ridx)
+    rrw, rlw = orc.route_weights_affine(rsc, ridx, rent, rlse, gate_offset=0.3, gate_scale=1.2)
+    rremote = orc.selected_attention(rq, rk, ref["v"], rrw, ridx, valid, 64, out_dtype=torch.float32)
+    rout = rremote + rlw[..., None] * rlo
+    (rout * gout).sum().backward()
+    for n in names:
+        close_grad(leaves[n].grad, ref[n].grad, n, rel_l2=5e-2, max_frac=1.0)
