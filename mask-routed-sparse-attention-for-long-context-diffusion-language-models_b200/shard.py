@@ -14,14 +14,16 @@ transfer hides behind compute:
   chunk validity of every chunk -- routing scores all C chunks.
 * **K/V** (all-gather, 235 MB received per rank at N=8, route layer only):
   the selected chunks can lie anywhere in the sequence.  It runs on its own
-  communicator, so it does not queue ahead of the two small exchanges, and
-  only selected-chunk attention waits for it.
+  communicator and is posted after the summaries, so neither Q-Cal nor the
+  two small exchanges share the GPU with it, and only selected-chunk
+  attention waits for it.
 
 Route-layer order on the compute stream: RoPE (K straight into the halo
-buffer) and V to fp16; post the halo and the K/V all-gather; Q-Cal and the
-landmark pool of this rank's chunks; post the summary all-gather; wait for
-the halo, local window attention; wait for the summaries, routing over all
-C chunks; wait for K/V, selected-chunk attention with the fused local merge.
+buffer) and V to fp16; post the halo; Q-Cal and the landmark pool of this
+rank's chunks; post the summary all-gather, then the K/V all-gather; wait
+for the halo, local window attention; wait for the summaries, routing over
+all C chunks; wait for K/V, selected-chunk attention with the fused local
+merge.
 Every kernel reads only local HBM.  The SWA layer (21 of the 28 layers,
 ``dream_dllm_hils/attention.py:1168-1220``) is RoPE, the halo exchange and
 the window attention.
@@ -272,13 +274,8 @@ class ShardedRouteLayer:
         ops.attention_v(v, out=v_own)
         m_own.copy_(key_valid.to(torch.bool))
         mark("rope")
-        # 2. post the halo and the K/V all-gather (own communicator)
+        # 2. post the halo exchange (small; the local window needs it first)
         h_halo = ex.halo((k_h, v_h, m_h), ls, h)
-        k_full = self._buf("k", (n, ls, hkv, d), torch.bfloat16, dev)
-        v_full = self._buf("v", (n, ls, hkv, d), ops.v_dtype, dev)
-        m_full = self._buf("kv", (n, ls), torch.bool, dev)
-        h_kv = _Many([ex.gather(k_full, k_own, bulk=True), ex.gather(v_full, v_own, bulk=True),
-                      ex.gather(m_full, m_own, bulk=True)])
         # 3. Q-Cal and the landmark pool of this rank's chunks, then the summaries
         route_q = ops.qcal(hidden, q, position_ids, self._buf("route_q", (1, ls, hq, d), torch.bfloat16, dev))
         mark("qcal")
@@ -291,6 +288,14 @@ class ShardedRouteLayer:
         mark("pool")
         h_sum = _Many([ex.gather(lmk_full, lmk_full[r]), ex.gather(prior_full, prior_full[r]),
                        ex.gather(ok_full, ok_full[r])])
+        # the K/V all-gather (own communicator) goes out after the summaries, so
+        # neither Q-Cal nor the summaries' gather shares the GPU with it; local
+        # attention and routing (which need no remote K/V) hide it
+        k_full = self._buf("k", (n, ls, hkv, d), torch.bfloat16, dev)
+        v_full = self._buf("v", (n, ls, hkv, d), ops.v_dtype, dev)
+        m_full = self._buf("kv", (n, ls), torch.bool, dev)
+        h_kv = _Many([ex.gather(k_full, k_own, bulk=True), ex.gather(v_full, v_own, bulk=True),
+                      ex.gather(m_full, m_own, bulk=True)])
         # 4. local window attention over [left halo | own rows | right halo]
         h_halo.wait()
         mark("halo_wait")
