@@ -10,19 +10,21 @@
 //   S[128 x 64]  = Q . K_t^T               (UMMA M=128, N=64,  K=128, TMEM)
 //   P            = exp2(S*scale*log2e - m)  (one thread per row, online max)
 //   O[128 x 128] += P . V_t                (UMMA M=128, N=128, K=64, TMEM)
-// P goes through shared memory as bf16 hi + lo parts (two MMAs per k-step),
-// keeping ~16 significant bits.  Each row keeps a reference max that moves
-// (rescaling O in TMEM between the P.V of tile t-1 and that of tile t) only
-// when a tile max exceeds it by more than 2^8.
+// P goes through shared memory: fp16 when V is fp16, else bf16 hi + lo parts
+// (two MMAs per k-step, ~16 significant bits).  Each row keeps a reference
+// max that moves (rescaling O in TMEM) only when a tile max exceeds it by more
+// than 2^8.
 // Warps 0-7: softmax and epilogue in two groups of four (warp w = TMEM lanes
 // 32(w%4)..+31 = rows); group g takes the tiles t with t % 2 == g and keeps
-// its own running max, sum and O accumulator, so two softmax warps share each
-// scheduler; the epilogue merges the two partial softmaxes.  Warp 8: TMA (Q
-// once, then K, V per tile, 3 stages) and the per-tile key validity mask;
-// warps 9 and 10: MMA issue for the even and the odd tiles (converged,
-// elect.sync; one issuing thread takes about twice the tensor pipe's time per
-// MMA instruction).  Every mbarrier
-// wait is bounded and unwinds through a shared abort flag.
+// its own running max, sum and O accumulator, merged in the epilogue.  Each
+// group has two S buffers in TMEM, so the S of its next tile is computed while
+// it works on the current one and the softmax never waits for an MMA round
+// trip; with fp16 P it also has two P buffers.  Warp 8: TMA of Q and of the K
+// tiles (4 stages) and the per-tile key validity masks; warp 11: TMA of the V
+// tiles (4 stages, released by P.V); warps 9 and 10: MMA issue for the even
+// and the odd tiles (converged, elect.sync), in the order S(t), S(t+2), then
+// per tile P.V(t), S(t+4).  Every mbarrier wait is bounded and unwinds through
+// a shared abort flag.
 //
 // The same kernel also runs the causal chunk-expanded window of
 // ops/flex_attn_tilelang.py:26-276 (flex_attn_tl): a row at absolute position
@@ -43,24 +45,22 @@ namespace {
 
 constexpr int LQ = 16;            // queries per CTA
 constexpr int LN = 64;            // keys per tile
-constexpr int LST = 3;            // K/V stages
+constexpr int NKS = 4;            // K stages (even: a stage's tiles share one parity, hence one MMA warp)
+constexpr int NVS = 4;            // V stages (even, likewise)
+constexpr int NMS = 8;            // key-mask slots
 constexpr int D = kHeadDim;
-constexpr int L_THREADS = 352;    // warps 0-7 softmax (two groups), 8 TMA, 9-10 MMA (even / odd tiles)
-constexpr int L_W_LOAD = 8, L_W_MMA = 9;
-constexpr uint32_t kOCol = 128;   // O accumulators of groups 0 / 1 at [128, 256) / [256, 384); S at 0 and 64
+constexpr int L_THREADS = 384;    // warps 0-7 softmax (two groups), 8 Q/K TMA + masks, 9-10 MMA, 11 V TMA
+constexpr int L_W_KLOAD = 8, L_W_MMA = 9, L_W_VLOAD = 11;
+constexpr uint32_t kOCol = 256;   // O of groups 0 / 1 at [256, 384) / [384, 512); S buffer i at [64 i, 64 i + 64)
 
 struct __align__(1024) LocalSmem {
   unsigned char q[LQ][2048];          // per query: [half][8 head rows][64 dims], 128-byte swizzled
-  unsigned char k[LST][16384];        // [half][64 keys][64 dims]
-  unsigned char v[LST][16384];        // same, read as the MN-major B operand of P.V
-  unsigned char ph[2][16384];         // P hi [128 rows][64 keys]
-  unsigned char pl[2][16384];         // P lo
-  unsigned long long kmask[LST];      // bit j: key j of the stage's tile is usable (not zeroed)
-  float part_m[2][128], part_l[2][128];   // per group and row: running max / sum for the merge
-  // K/V stage barriers per stage and tile parity: the two parities' MMAs are
-  // issued by different warps, and a barrier's phases must belong to one
-  // waiter's tiles in order
-  uint64_t qfull, kvfull[LST][2], kvfree[LST][2], sdone[2], pready[2], pvdone[2], drain[2];
+  unsigned char k[NKS][16384];        // [half][64 keys][64 dims]
+  unsigned char v[NVS][16384];        // same, read as the MN-major B operand of P.V
+  unsigned char p[4][16384];          // fp16 P: group g's buffers 2g, 2g+1; bf16 P: group g's hi 2g, lo 2g+1
+  unsigned long long kmask[NMS];      // bit j: key j of the tile is usable (not zeroed); slot t % NMS
+  uint64_t qfull, kfull[NKS], kfree[NKS], vfull[NVS], vfree[NVS], mfull[NMS];
+  uint64_t sfull[4], sfree[4], pready[4], pfree[4], drain[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -135,21 +135,30 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
   const int t_lo = static_cast<int>(j_lo / LN);
   const int NTL = j_hi >= j_lo ? static_cast<int>(j_hi / LN) - t_lo + 1 : 0;
-  // phase parity of tile t on its (stage, parity) barrier: tiles of one stage
-  // and parity are 2*LST apart
-  auto kv_phase = [](int t) { return (t / (2 * LST)) & 1; };
+  // P buffer of tile t (group t % 2, the group's (t / 2)-th tile) and how many
+  // times that buffer was used before: fp16 P alternates two buffers per
+  // group, bf16 hi + lo P has one pair per group
+  auto p_idx = [](int t) { return kF16 ? 2 * (t & 1) + ((t >> 1) & 1) : 2 * (t & 1); };
+  auto p_use = [](int t) { return kF16 ? (t >> 2) : (t >> 1); };
+  // S buffer of tile t: group t % 2 alternates its two buffers
+  auto s_idx = [](int t) { return 2 * (t & 1) + ((t >> 1) & 1); };
 
   if (tid == 0) {
     tc::mbar_init(tc::smem_addr(&sm.qfull), 1);
-    for (int s = 0; s < LST; ++s)
-      for (int p = 0; p < 2; ++p) {
-        tc::mbar_init(tc::smem_addr(&sm.kvfull[s][p]), 1);
-        tc::mbar_init(tc::smem_addr(&sm.kvfree[s][p]), 1);
-      }
-    for (int s = 0; s < 2; ++s) {
-      tc::mbar_init(tc::smem_addr(&sm.sdone[s]), 1);
+    for (int s = 0; s < NKS; ++s) {
+      tc::mbar_init(tc::smem_addr(&sm.kfull[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.kfree[s]), 1);
+    }
+    for (int s = 0; s < NVS; ++s) {
+      tc::mbar_init(tc::smem_addr(&sm.vfull[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.vfree[s]), 1);
+    }
+    for (int s = 0; s < NMS; ++s) tc::mbar_init(tc::smem_addr(&sm.mfull[s]), 1);
+    for (int s = 0; s < 4; ++s) {
+      tc::mbar_init(tc::smem_addr(&sm.sfull[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.sfree[s]), 4);
       tc::mbar_init(tc::smem_addr(&sm.pready[s]), 4);
-      tc::mbar_init(tc::smem_addr(&sm.pvdone[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.pfree[s]), 1);
     }
     for (int s = 0; s < 2; ++s) tc::mbar_init(tc::smem_addr(&sm.drain[s]), 1);
     sm.abort_flag = 0;
@@ -164,13 +173,12 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   tc::fence_after_sync();
   const uint32_t tbase = sm.tmem_base;
 
-  if (warp == L_W_LOAD) {
-    // ============================ TMA + key masks =============================
+  if (warp == L_W_KLOAD) {
+    // ============================ Q, K tiles + key masks ======================
     const uint32_t qb = tc::smem_addr(&sm.qfull);
     if (lane == 0) {
       tc::prefetch_tensormap(&tm_q);
       tc::prefetch_tensormap(&tm_k);
-      tc::prefetch_tensormap(&tm_v);
       tc::mbar_arrive_expect_tx(qb, LQ * 2048u);
       tc::tma_load_4d(tc::smem_addr(&sm.q[0][0]), &tm_q, 0, hk * G, 0, static_cast<int>(b * a.Lq + q0), qb);
     }
@@ -188,10 +196,12 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     valid_bytes(0, vb_next);
     int t = 0;
     for (; t < NTL; ++t) {
-      const int st = t % LST;
+      const int st = t % NKS;
       const uint32_t vb[2] = {vb_next[0], vb_next[1]};
       valid_bytes(t + 1, vb_next);
-      if (t >= LST && !tc::wait_bounded_warp(tc::smem_addr(&sm.kvfree[st][(t - LST) & 1]), kv_phase(t - LST), abort_flag)) break;
+      // stage st was last read by S(t - NKS); mask slot t % NMS by the softmax of
+      // tile t - NMS, which precedes the P.V(t - NMS) that S(t - NKS) is issued after
+      if (t >= NKS && !tc::wait_bounded_warp(tc::smem_addr(&sm.kfree[st]), ((t / NKS) - 1) & 1, abort_flag)) break;
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
       // usable keys of the tile: inside the sequence, valid, and not a landmark slot when skip_inert
       uint32_t mk[2];
@@ -203,25 +213,46 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         mk[h] = __ballot_sync(0xffffffffu, ok);
       }
       if (lane == 0) {
-        sm.kmask[st] = static_cast<unsigned long long>(mk[0]) | (static_cast<unsigned long long>(mk[1]) << 32);
-        const uint32_t kb = tc::smem_addr(&sm.kvfull[st][t & 1]);
-        tc::mbar_arrive_expect_tx(kb, 2u * 16384u);
+        sm.kmask[t % NMS] = static_cast<unsigned long long>(mk[0]) | (static_cast<unsigned long long>(mk[1]) << 32);
+        tc::mbar_arrive(tc::smem_addr(&sm.mfull[t % NMS]));
+        const uint32_t kb = tc::smem_addr(&sm.kfull[st]);
+        tc::mbar_arrive_expect_tx(kb, 16384u);
         tc::tma_load_4d(tc::smem_addr(sm.k[st]), &tm_k, 0, static_cast<int>(b * a.Lk + j0), 0, hk, kb);
-        tc::tma_load_4d(tc::smem_addr(sm.v[st]), &tm_v, 0, static_cast<int>(b * a.Lk + j0), 0, hk, kb);
       }
       __syncwarp();
     }
+    // wait (bounded, even after an abort) for the copies in flight
     if (lane == 0) {
       tc::mbar_wait(qb, 0);
-      for (int tt = t - LST < 0 ? 0 : t - LST; tt < t; ++tt)
-        tc::mbar_wait(tc::smem_addr(&sm.kvfull[tt % LST][tt & 1]), kv_phase(tt));
+      for (int tt = t - NKS < 0 ? 0 : t - NKS; tt < t; ++tt)
+        tc::mbar_wait(tc::smem_addr(&sm.kfull[tt % NKS]), (tt / NKS) & 1);
     }
+    __syncwarp();
+  } else if (warp == L_W_VLOAD) {
+    // ============================ V tiles =====================================
+    if (lane == 0) tc::prefetch_tensormap(&tm_v);
+    int t = 0;
+    for (; t < NTL; ++t) {
+      const int st = t % NVS;
+      if (t >= NVS && !tc::wait_bounded_warp(tc::smem_addr(&sm.vfree[st]), ((t / NVS) - 1) & 1, abort_flag)) break;
+      if (lane == 0) {
+        const uint32_t vb = tc::smem_addr(&sm.vfull[st]);
+        tc::mbar_arrive_expect_tx(vb, 16384u);
+        tc::tma_load_4d(tc::smem_addr(sm.v[st]), &tm_v, 0, static_cast<int>(b * a.Lk + static_cast<int64_t>(t_lo + t) * LN),
+                        0, hk, vb);
+      }
+      __syncwarp();
+    }
+    if (lane == 0)
+      for (int tt = t - NVS < 0 ? 0 : t - NVS; tt < t; ++tt)
+        tc::mbar_wait(tc::smem_addr(&sm.vfull[tt % NVS]), (tt / NVS) & 1);
     __syncwarp();
   } else if (warp >= L_W_MMA) {
     // ============================ MMA issue (two converged warps) =============
     // Warp 9 issues the MMAs of the even tiles, warp 10 those of the odd tiles
     // (one issuing thread needs about twice the tensor pipe's time per MMA):
-    // S(t) into S buffer t%2, then per tile P.V(t) into its group's O and S(t+2).
+    // S(t) and S(t+2) first, then per tile P.V(t) into its group's O and S(t+4)
+    // into the S buffer that tile t's softmax has released.
     const int par = warp - L_W_MMA;
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, LN, 0, 0);
     // kind::f16 with fp16 A and B: the bf16 format bits cleared
@@ -229,33 +260,36 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     const uint64_t dq = tc::smem_desc_sw128(tc::smem_addr(&sm.q[0][0]), 16, 2048);
     const uint64_t dk0 = tc::smem_desc_sw128(tc::smem_addr(sm.k[0]), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(tc::smem_addr(sm.v[0]), 8192, 1024);
-    const uint64_t dh0 = tc::smem_desc_sw128(tc::smem_addr(sm.ph[0]), 16, 1024);
-    const uint64_t dl0 = tc::smem_desc_sw128(tc::smem_addr(sm.pl[0]), 16, 1024);
+    const uint64_t dp0 = tc::smem_desc_sw128(tc::smem_addr(sm.p[0]), 16, 1024);
     auto issue_s = [&](int t) -> bool {
-      const int st = t % LST;
-      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st][par]), kv_phase(t), abort_flag)) return false;
+      const int st = t % NKS, sb = s_idx(t), use = t >> 2;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.kfull[st]), (t / NKS) & 1, abort_flag)) return false;
+      if (use >= 1 && !tc::wait_bounded_warp(tc::smem_addr(&sm.sfree[sb]), (use - 1) & 1, abort_flag)) return false;
       tc::fence_after_sync();
       const uint64_t db = tc::desc_adv(dk0, st * 16384);
-      const uint32_t dS = tbase + LN * par;
+      const uint32_t dS = tbase + LN * sb;
       if (tc::elect_one()) {
         tc::mma_bf16<false>(dS, dq, db, id_s);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
           tc::mma_bf16<true>(dS, tc::desc_adv(dq, (kk >> 2) * 1024 + (kk & 3) * 32),
                              tc::desc_adv(db, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
-        tc::mma_commit(tc::smem_addr(&sm.sdone[par]));
+        tc::mma_commit(tc::smem_addr(&sm.sfull[sb]));
+        tc::mma_commit(tc::smem_addr(&sm.kfree[st]));
       }
       __syncwarp();
       return true;
     };
     bool ok = tc::wait_bounded_warp(tc::smem_addr(&sm.qfull), 0, abort_flag);
     if (ok && par < NTL) ok = issue_s(par);
+    if (ok && par + 2 < NTL) ok = issue_s(par + 2);
     for (int t = par; ok && t < NTL; t += 2) {
-      const int st = t % LST;
-      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.pready[par]), (t >> 1) & 1, abort_flag)) break;
+      const int sv = t % NVS, pb = p_idx(t);
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.pready[pb]), p_use(t) & 1, abort_flag)) break;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.vfull[sv]), (t / NVS) & 1, abort_flag)) break;
       tc::fence_after_sync();
-      const uint64_t dv = tc::desc_adv(dv0, st * 16384), dh = tc::desc_adv(dh0, par * 16384),
-                     dl = tc::desc_adv(dl0, par * 16384);
+      const uint64_t dv = tc::desc_adv(dv0, sv * 16384), dh = tc::desc_adv(dp0, pb * 16384),
+                     dl = tc::desc_adv(dp0, (pb + 1) * 16384);
       const uint32_t dO = tbase + kOCol + D * par;      // group par's accumulator
       if (tc::elect_one()) {
         // each group's first tile overwrites its O (TMEM is not zeroed)
@@ -268,11 +302,11 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
           for (int kk = 0; kk < 4; ++kk)
             tc::mma_bf16<true>(dO, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
         }
-        tc::mma_commit(tc::smem_addr(&sm.pvdone[par]));
-        tc::mma_commit(tc::smem_addr(&sm.kvfree[st][par]));
+        tc::mma_commit(tc::smem_addr(&sm.pfree[pb]));
+        tc::mma_commit(tc::smem_addr(&sm.vfree[sv]));
       }
       __syncwarp();
-      if (t + 2 < NTL) ok = issue_s(t + 2);
+      if (t + 4 < NTL) ok = issue_s(t + 4);
     }
     if (tc::elect_one()) {
       tc::mma_commit(tc::smem_addr(&sm.drain[par]));
@@ -295,18 +329,22 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     const uint32_t fill = a.exclude ? __float_as_uint(-INFINITY) : 0u;
     bool ok = true;
     for (int t = grp; t < NTL; t += 2) {
-      const int st = t % LST, p2 = t & 1;
+      const int sb = s_idx(t), pb = p_idx(t), pu = p_use(t);
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
-      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.kvfull[st][p2]), kv_phase(t), abort_flag))) break;
-      const unsigned long long km = sm.kmask[st];
-      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.sdone[p2]), (t >> 1) & 1, abort_flag))) break;
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.mfull[t % NMS]), (t / NMS) & 1, abort_flag))) break;
+      const unsigned long long km = sm.kmask[t % NMS];
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.sfull[sb]), (t >> 2) & 1, abort_flag))) break;
       tc::fence_after_sync();
       uint32_t x[64];
-      tc::tmem_ld16(tbase + lane_off + LN * p2 + 0, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
-      tc::tmem_ld16(tbase + lane_off + LN * p2 + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
-      tc::tmem_ld16(tbase + lane_off + LN * p2 + 32, *reinterpret_cast<uint32_t(*)[16]>(&x[32]));
-      tc::tmem_ld16(tbase + lane_off + LN * p2 + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
+      tc::tmem_ld16(tbase + lane_off + LN * sb + 0, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
+      tc::tmem_ld16(tbase + lane_off + LN * sb + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
+      tc::tmem_ld16(tbase + lane_off + LN * sb + 32, *reinterpret_cast<uint32_t(*)[16]>(&x[32]));
+      tc::tmem_ld16(tbase + lane_off + LN * sb + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
       tc::tmem_wait_ld();
+      // the S buffer is free for S(t + 4) as soon as it is in registers
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.sfree[sb]));
       // Zeroed keys (invalid, or landmark slots) keep logit 0: their raw score is
       // replaced by 0 (excluded keys: -inf).  The mask is per tile, so this branch
       // is warp-uniform; with landmark skipping on 64-aligned tiles only the last
@@ -388,18 +426,20 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
           lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
         }
       }
-      // P buffer t&1 was last read by the P.V of tile t-2
-      if (t >= 2 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[p2]), ((t - 2) >> 1) & 1, abort_flag))) break;
+      // the P buffer's previous tile must have been read by its P.V
+      if (pu >= 1 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[pb]), (pu - 1) & 1, abort_flag))) break;
 #pragma unroll
       for (int p = 0; p < 8; ++p) {
-        *reinterpret_cast<uint4*>(sm.ph[p2] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
+        *reinterpret_cast<uint4*>(sm.p[pb] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
         if constexpr (!kF16)
-          *reinterpret_cast<uint4*>(sm.pl[p2] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
+          *reinterpret_cast<uint4*>(sm.p[pb + 1] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
       }
       if (__any_sync(0xffffffffu, rescale)) {
         // O must hold every earlier tile of this group before it is scaled: the
-        // P.V of tile t-2, already waited for above (a rescale needs an earlier
-        // tile, so t >= 2 here)
+        // P.V of tile t-2 (a rescale needs an earlier tile, so t >= 2 here); with
+        // one P buffer per group that was the wait above
+        if (kF16 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(t - 2)]), p_use(t - 2) & 1, abort_flag)))
+          break;
         tc::fence_after_sync();
         const float c = rescale ? o_scale : 1.f;
 #pragma unroll
@@ -420,27 +460,36 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       tc::fence_proxy_async();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.pready[p2]));
+      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.pready[pb]));
     }
     // ---- epilogue: merge the two groups' partial softmaxes, bf16 rows, LSE
-    // (natural log).  Each group's last tile is t_last(g); a group without
-    // tiles never wrote its O, which is then left out.  The barrier puts both
-    // groups past their loops, so each waits at most one phase ahead.
+    // (natural log).  A group without tiles never wrote its O, which is then
+    // left out.  The per-row partials go to the K stages, idle once every S is
+    // done: both groups have read all their S tiles when they pass the first
+    // barrier (before it, the other group's last S may still read them).
     const bool has0 = NTL > 0, has1 = NTL > 1;
-    sm.part_m[grp][r] = m_run;
-    sm.part_l[grp][r] = l_run;
+    float* part_m = reinterpret_cast<float*>(sm.k[0]);          // [group][row]
+    float* part_l = part_m + 2 * 128;
     asm volatile("bar.sync 1, 256;\n" ::: "memory");
-    if (ok && has0)
-      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[0]), ((NTL - 1 - ((NTL - 1) & 1)) >> 1) & 1, abort_flag);
-    if (ok && has1)
-      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pvdone[1]), ((NTL - 1 - (NTL & 1)) >> 1) & 1, abort_flag);
+    part_m[grp * 128 + r] = m_run;
+    part_l[grp * 128 + r] = l_run;
+    asm volatile("bar.sync 1, 256;\n" ::: "memory");
+    // each group's last P.V: the last even and the last odd tile
+    if (ok && has0) {
+      const int tl = (NTL - 1) - ((NTL - 1) & 1);
+      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(tl)]), p_use(tl) & 1, abort_flag);
+    }
+    if (ok && has1) {
+      const int tl = (NTL - 1) - (NTL & 1);
+      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(tl)]), p_use(tl) & 1, abort_flag);
+    }
     tc::fence_after_sync();
     if (__all_sync(0xffffffffu, ok) && !__any_sync(0xffffffffu, *abort_flag != 0)) {
-      const float m0 = sm.part_m[0][r], m1 = sm.part_m[1][r];
+      const float m0 = part_m[r], m1 = part_m[128 + r];
       const float m = fmaxf(m0, m1);
       const float f0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
       const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
-      const float l = sm.part_l[0][r] * f0 + sm.part_l[1][r] * f1;
+      const float l = part_l[r] * f0 + part_l[128 + r] * f1;
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const float c0 = f0 * inv, c1 = f1 * inv;
       const bool row_ok = g < G && qi < rows_q;
