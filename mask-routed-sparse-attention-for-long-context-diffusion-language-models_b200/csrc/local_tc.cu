@@ -4,9 +4,10 @@
 // dream_dllm_hils/local_attention.py:35-107: zeroed keys keep logit 0 in the
 // softmax and add no value; keys with |i-j| > window are out.
 //
-// One CTA owns 16 queries of one KV head.  Its MMA tile has 128 rows, row
-// 8*qi + g = (query qi, head g of the group; rows g >= G are padding), so each
-// 64-key K/V tile is read once for all heads of the group.  Per key tile t:
+// One CTA owns LQ = floor(128 / G) queries of one KV head (18 for GQA 7:1).
+// Its MMA tile has 128 rows, row G*qi + g = (query qi, head g of the group;
+// rows >= LQ*G are zero padding), so each 64-key K/V tile is read once for all
+// heads of the group.  Per key tile t:
 //   S[128 x 64]  = Q . K_t^T               (UMMA M=128, N=64,  K=128, TMEM)
 //   P            = exp2(S*scale*log2e - m)  (one thread per row, online max)
 //   O[128 x 128] += P . V_t                (UMMA M=128, N=128, K=64, TMEM)
@@ -15,7 +16,8 @@
 // max that moves (rescaling O in TMEM) only when a tile max exceeds it by more
 // than 2^8.
 // Warps 0-7: softmax and epilogue in two groups of four (warp w = TMEM lanes
-// 32(w%4)..+31 = rows); group g takes the tiles t with t % 2 == g and keeps
+// 32(w%4)..+31 = rows); group g takes every other key tile (by the tile's
+// parity counted from query row 0's tile) and keeps
 // its own running max, sum and O accumulator, merged in the epilogue.  Each
 // group has two S buffers in TMEM, so the S of its next tile is computed while
 // it works on the current one and the softmax never waits for an MMA round
@@ -43,7 +45,6 @@ using namespace mrsa;
 
 namespace {
 
-constexpr int LQ = 16;            // queries per CTA
 constexpr int LN = 64;            // keys per tile
 constexpr int NKS = 4;            // K stages (even: a stage's tiles share one parity, hence one MMA warp)
 constexpr int NVS = 4;            // V stages (even, likewise)
@@ -54,7 +55,7 @@ constexpr int L_W_KLOAD = 8, L_W_MMA = 9, L_W_VLOAD = 11;
 constexpr uint32_t kOCol = 256;   // O of groups 0 / 1 at [256, 384) / [384, 512); S buffer i at [64 i, 64 i + 64)
 
 struct __align__(1024) LocalSmem {
-  unsigned char q[LQ][2048];          // per query: [half][8 head rows][64 dims], 128-byte swizzled
+  unsigned char q[2][16384];          // [half][128 rows = (query, head)][64 dims], 128-byte swizzled
   unsigned char k[NKS][16384];        // [half][64 keys][64 dims]
   unsigned char v[NVS][16384];        // same, read as the MN-major B operand of P.V
   unsigned char p[4][16384];          // fp16 P: group g's buffers 2g, 2g+1; bf16 P: group g's hi 2g, lo 2g+1
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   volatile int* abort_flag = &sm.abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hk = blockIdx.y, b = blockIdx.z;
-  const int G = a.G;
+  const int G = a.G, LQ = 128 / G, nrows = LQ * G;
   const int64_t q0 = static_cast<int64_t>(blockIdx.x) * LQ;
   const int64_t rows_q = (a.Lq - q0) < LQ ? (a.Lq - q0) : LQ;
   // positions of the CTA's first and last rows (the band is monotone in the
@@ -135,13 +136,19 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
   const int t_lo = static_cast<int>(j_lo / LN);
   const int NTL = j_hi >= j_lo ? static_cast<int>(j_hi / LN) - t_lo + 1 : 0;
-  // P buffer of tile t (group t % 2, the group's (t / 2)-th tile) and how many
-  // times that buffer was used before: fp16 P alternates two buffers per
-  // group, bf16 hi + lo P has one pair per group
-  auto p_idx = [](int t) { return kF16 ? 2 * (t & 1) + ((t >> 1) & 1) : 2 * (t & 1); };
+  // Tile t (key tile t_lo + t) belongs to softmax group (t + e) % 2, the parity
+  // of its key tile counted from the tile of query row 0: a row's tiles then go
+  // to the same groups, in the same order, whichever rows share its CTA, so a
+  // row's result does not depend on how the rows are cut into CTAs (a query
+  // shard with a tile-aligned halo gets the bits of the whole sequence).
+  const int e = static_cast<int>((static_cast<int64_t>(t_lo) - floor_div(a.q_offset, LN)) & 1);
+  auto grp_of = [e](int t) { return (t + e) & 1; };
+  // P buffer of tile t and how many times that buffer was used before: fp16 P
+  // alternates two buffers per group, bf16 hi + lo P has one pair per group
+  auto p_idx = [grp_of](int t) { return kF16 ? 2 * grp_of(t) + ((t >> 1) & 1) : 2 * grp_of(t); };
   auto p_use = [](int t) { return kF16 ? (t >> 2) : (t >> 1); };
-  // S buffer of tile t: group t % 2 alternates its two buffers
-  auto s_idx = [](int t) { return 2 * (t & 1) + ((t >> 1) & 1); };
+  // S buffer of tile t: each group alternates its two buffers
+  auto s_idx = [grp_of](int t) { return 2 * grp_of(t) + ((t >> 1) & 1); };
 
   if (tid == 0) {
     tc::mbar_init(tc::smem_addr(&sm.qfull), 1);
@@ -164,6 +171,13 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
+  // zero the padding rows of the Q tile (the TMA box fills rows [0, nrows)),
+  // visible to the tensor core's async proxy
+  for (int i = tid; i < 2 * (128 - nrows) * 8; i += L_THREADS) {
+    const int h = i / ((128 - nrows) * 8), rem = i % ((128 - nrows) * 8);
+    *reinterpret_cast<uint4*>(sm.q[h] + (nrows + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  tc::fence_proxy_async();
   if (warp == 0) {
     tc::tmem_alloc(tc::smem_addr(&sm.tmem_base), 512);
     tc::tmem_relinquish();
@@ -179,8 +193,9 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     if (lane == 0) {
       tc::prefetch_tensormap(&tm_q);
       tc::prefetch_tensormap(&tm_k);
-      tc::mbar_arrive_expect_tx(qb, LQ * 2048u);
-      tc::tma_load_4d(tc::smem_addr(&sm.q[0][0]), &tm_q, 0, hk * G, 0, static_cast<int>(b * a.Lq + q0), qb);
+      tc::mbar_arrive_expect_tx(qb, static_cast<uint32_t>(nrows) * 256u);
+      tc::tma_load_4d(tc::smem_addr(sm.q[0]), &tm_q, 0, hk * G, 0, static_cast<int>(b * a.Lq + q0), qb);
+      tc::tma_load_4d(tc::smem_addr(sm.q[1]), &tm_q, 0, hk * G, 1, static_cast<int>(b * a.Lq + q0), qb);
     }
     // key-validity bytes of tile tt (this lane's keys 32h + lane), requested one
     // tile ahead so their latency is not on the copy-issue path
@@ -257,7 +272,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, LN, 0, 0);
     // kind::f16 with fp16 A and B: the bf16 format bits cleared
     constexpr uint32_t id_o = tc::idesc_bf16_f32(128, D, 0, 1) & (kF16 ? ~((1u << 7) | (1u << 10)) : ~0u);
-    const uint64_t dq = tc::smem_desc_sw128(tc::smem_addr(&sm.q[0][0]), 16, 2048);
+    const uint64_t dq = tc::smem_desc_sw128(tc::smem_addr(sm.q[0]), 16, 1024);
     const uint64_t dk0 = tc::smem_desc_sw128(tc::smem_addr(sm.k[0]), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(tc::smem_addr(sm.v[0]), 8192, 1024);
     const uint64_t dp0 = tc::smem_desc_sw128(tc::smem_addr(sm.p[0]), 16, 1024);
@@ -272,7 +287,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         tc::mma_bf16<false>(dS, dq, db, id_s);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
-          tc::mma_bf16<true>(dS, tc::desc_adv(dq, (kk >> 2) * 1024 + (kk & 3) * 32),
+          tc::mma_bf16<true>(dS, tc::desc_adv(dq, (kk >> 2) * 16384 + (kk & 3) * 32),
                              tc::desc_adv(db, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
         tc::mma_commit(tc::smem_addr(&sm.sfull[sb]));
         tc::mma_commit(tc::smem_addr(&sm.kfree[st]));
@@ -281,9 +296,10 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       return true;
     };
     bool ok = tc::wait_bounded_warp(tc::smem_addr(&sm.qfull), 0, abort_flag);
-    if (ok && par < NTL) ok = issue_s(par);
-    if (ok && par + 2 < NTL) ok = issue_s(par + 2);
-    for (int t = par; ok && t < NTL; t += 2) {
+    const int t0 = par ^ e;                           // this group's first tile
+    if (ok && t0 < NTL) ok = issue_s(t0);
+    if (ok && t0 + 2 < NTL) ok = issue_s(t0 + 2);
+    for (int t = t0; ok && t < NTL; t += 2) {
       const int sv = t % NVS, pb = p_idx(t);
       if (!tc::wait_bounded_warp(tc::smem_addr(&sm.pready[pb]), p_use(t) & 1, abort_flag)) break;
       if (!tc::wait_bounded_warp(tc::smem_addr(&sm.vfull[sv]), (t / NVS) & 1, abort_flag)) break;
@@ -315,11 +331,11 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     __syncwarp();
   } else {
     // ============================ softmax + epilogue (warps 0-7) ==============
-    const int grp = warp >> 2;                       // tiles t with t % 2 == grp
+    const int grp = warp >> 2;                       // tiles t with (t + e) % 2 == grp
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t o_col = kOCol + D * grp;          // this group's O accumulator
     const int r = (warp & 3) * 32 + lane;            // MMA row = TMEM lane
-    const int qi = r >> 3, g = r & 7;
+    const int qi = r / G, g = r - qi * G;
     const int64_t pos = a.qpos != nullptr ? a.qpos[q0 + (qi < rows_q ? qi : rows_q - 1)] : a.q_offset + q0 + qi;
     const float sl2 = a.sm_scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f, o_scale = 1.f;
@@ -328,7 +344,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     if (band_hi > a.Lk - 1) band_hi = a.Lk - 1;
     const uint32_t fill = a.exclude ? __float_as_uint(-INFINITY) : 0u;
     bool ok = true;
-    for (int t = grp; t < NTL; t += 2) {
+    for (int t = grp ^ e; t < NTL; t += 2) {
       const int sb = s_idx(t), pb = p_idx(t), pu = p_use(t);
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
       if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.mfull[t % NMS]), (t / NMS) & 1, abort_flag))) break;
@@ -467,20 +483,20 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     // left out.  The per-row partials go to the K stages, idle once every S is
     // done: both groups have read all their S tiles when they pass the first
     // barrier (before it, the other group's last S may still read them).
-    const bool has0 = NTL > 0, has1 = NTL > 1;
+    const bool has0 = (0 ^ e) < NTL, has1 = (1 ^ e) < NTL;
     float* part_m = reinterpret_cast<float*>(sm.k[0]);          // [group][row]
     float* part_l = part_m + 2 * 128;
     asm volatile("bar.sync 1, 256;\n" ::: "memory");
     part_m[grp * 128 + r] = m_run;
     part_l[grp * 128 + r] = l_run;
     asm volatile("bar.sync 1, 256;\n" ::: "memory");
-    // each group's last P.V: the last even and the last odd tile
+    // each group's last P.V (group g's tiles are t = g ^ e mod 2)
     if (ok && has0) {
-      const int tl = (NTL - 1) - ((NTL - 1) & 1);
+      const int tl = (NTL - 1) - (((NTL - 1) ^ e) & 1);
       ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(tl)]), p_use(tl) & 1, abort_flag);
     }
     if (ok && has1) {
-      const int tl = (NTL - 1) - (NTL & 1);
+      const int tl = (NTL - 1) - (((NTL - 1) ^ e ^ 1) & 1);
       ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(tl)]), p_use(tl) & 1, abort_flag);
     }
     tc::fence_after_sync();
@@ -492,7 +508,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       const float l = part_l[r] * f0 + part_l[128 + r] * f1;
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const float c0 = f0 * inv, c1 = f1 * inv;
-      const bool row_ok = g < G && qi < rows_q;
+      const bool row_ok = r < nrows && qi < rows_q;
       const int64_t orow = ((b * a.Lq + q0 + qi) * a.Hq + hk * G + g);
       // group 0 writes dims 0-63, group 1 dims 64-127
 #pragma unroll
@@ -575,12 +591,14 @@ int local_launch(const void* q, const void* k, const void* v, const uint8_t* key
     return MRSA_ERR_ARG;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return MRSA_ERR_ALIGN;
   if (q_len == 0) return MRSA_OK;
-  // Q [B*Lq][Hq][128] as (dim-in-half, head row, half, query): one box = 8 head rows x 16 queries
+  // Q [B*Lq][Hq][128] as (dim-in-half, head row, half, query): one box = one half of
+  // the G head rows of LQ = 128 / G queries, rows (query, head) back to back
   // K, V [B*Lk][Hkv][128] as (dim-in-half, key, half, kv head): one box = 64 keys
+  const int64_t G = q_heads / kv_heads, LQ = 128 / G;
   CUtensorMap tm_q, tm_k, tm_v;
   const cuuint64_t q_dims[4] = {64, static_cast<cuuint64_t>(q_heads), 2, static_cast<cuuint64_t>(batch * q_len)};
   const cuuint64_t q_str[3] = {256, 128, static_cast<cuuint64_t>(q_heads * D * 2)};
-  const cuuint32_t q_box[4] = {64, 8, 2, LQ};
+  const cuuint32_t q_box[4] = {64, static_cast<cuuint32_t>(G), 1, static_cast<cuuint32_t>(LQ)};
   const cuuint64_t kv_dims[4] = {64, static_cast<cuuint64_t>(batch * kv_len), 2, static_cast<cuuint64_t>(kv_heads)};
   const cuuint64_t kv_str[3] = {static_cast<cuuint64_t>(kv_heads * D * 2), 128, 256};
   const cuuint32_t kv_box[4] = {64, LN, 2, 1};
@@ -605,7 +623,7 @@ int local_launch(const void* q, const void* k, const void* v, const uint8_t* key
   a.exclude = band.exclude;
   a.Hq = static_cast<int>(q_heads);
   a.Hkv = static_cast<int>(kv_heads);
-  a.G = static_cast<int>(q_heads / kv_heads);
+  a.G = static_cast<int>(G);
   a.sm_scale = sm_scale;
   const size_t smem = sizeof(LocalSmem) + 1024;
   if (cudaFuncSetAttribute(local_tc_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
