@@ -103,6 +103,28 @@ __device__ int g_local_error;
 
 __device__ __forceinline__ int swz_off(int row, int piece) { return row * 128 + ((piece ^ (row & 7)) << 4); }
 
+// 2^y for a pair on the FMA pipe, taking load off the special-function unit:
+// Cody-Waite reduction y = n + f (n = round(y) through the 1.5 * 2^23 shift,
+// |f| <= 1/2), 2^f by a degree-4 polynomial whose coefficients were fitted
+// for this kernel by Remez exchange on [-1/2, 1/2] (relative error 2.7e-6
+// evaluated in fp32, below fp16 P's rounding), and 2^n added to the exponent
+// field.  y is clamped to >= -126, so -inf gives 2^-126 rather than 0: only
+// for tiles without masked columns, where every row's sum is >= 1.
+__device__ __forceinline__ float2 exp2_poly2(float2 y) {
+  constexpr float kShift = 12582912.0f;   // 1.5 * 2^23
+  y.x = fmaxf(y.x, -126.0f);
+  y.y = fmaxf(y.y, -126.0f);
+  const float2 r = fadd2(y, make_float2(kShift, kShift));
+  const float2 n = fadd2(r, make_float2(-kShift, -kShift));
+  const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), y);
+  float2 p = ffma2(make_float2(0.009570102f, 0.009570102f), f, make_float2(0.05591786f, 0.05591786f));
+  p = ffma2(p, f, make_float2(0.24024744f, 0.24024744f));
+  p = ffma2(p, f, make_float2(0.69312179f, 0.69312179f));
+  p = ffma2(p, f, make_float2(0.99999928f, 0.99999928f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(r.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(r.y) << 23)));
+}
+
 // kF16: V arrives in fp16 and P (values up to 2^8 under the lazy rescale) is
 // one fp16 tile, one P.V MMA per k-step; otherwise P is bf16 hi + lo.
 template <bool kF16>
@@ -344,23 +366,28 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     if (band_hi > a.Lk - 1) band_hi = a.Lk - 1;
     const uint32_t fill = a.exclude ? __float_as_uint(-INFINITY) : 0u;
     bool ok = true;
-    for (int t = grp ^ e; t < NTL; t += 2) {
+    uint32_t x[64];
+    auto load_s = [&](int tt) -> bool {
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.sfull[s_idx(tt)]), (tt >> 2) & 1, abort_flag)) return false;
+      tc::fence_after_sync();
+      const uint32_t sa = tbase + lane_off + LN * s_idx(tt);
+      tc::tmem_ld16(sa + 0, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
+      tc::tmem_ld16(sa + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
+      tc::tmem_ld16(sa + 32, *reinterpret_cast<uint32_t(*)[16]>(&x[32]));
+      tc::tmem_ld16(sa + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
+      return true;
+    };
+    if ((grp ^ e) < NTL) ok = load_s(grp ^ e);
+    for (int t = grp ^ e; ok && t < NTL; t += 2) {
       const int sb = s_idx(t), pb = p_idx(t), pu = p_use(t);
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
-      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.mfull[t % NMS]), (t / NMS) & 1, abort_flag))) break;
-      const unsigned long long km = sm.kmask[t % NMS];
-      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.sfull[sb]), (t >> 2) & 1, abort_flag))) break;
-      tc::fence_after_sync();
-      uint32_t x[64];
-      tc::tmem_ld16(tbase + lane_off + LN * sb + 0, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
-      tc::tmem_ld16(tbase + lane_off + LN * sb + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
-      tc::tmem_ld16(tbase + lane_off + LN * sb + 32, *reinterpret_cast<uint32_t(*)[16]>(&x[32]));
-      tc::tmem_ld16(tbase + lane_off + LN * sb + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
       tc::tmem_wait_ld();
       // the S buffer is free for S(t + 4) as soon as it is in registers
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.sfree[sb]));
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.mfull[t % NMS]), (t / NMS) & 1, abort_flag))) break;
+      const unsigned long long km = sm.kmask[t % NMS];
       // Zeroed keys (invalid, or landmark slots) keep logit 0: their raw score is
       // replaced by 0 (excluded keys: -inf).  The mask is per tile, so this branch
       // is warp-uniform; with landmark skipping on 64-aligned tiles only the last
@@ -412,13 +439,29 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       // exponents and their sum on column pairs (paired fp32 fma and add)
       const float2 sl2x2 = make_float2(sl2, sl2), nbx2 = make_float2(nbase, nbase);
       float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      // fp16 P on a tile with no -inf column in this row (zeroed keys hold logit
+      // 0): a third of the exponentials on the FMA pipe, the rest on the
+      // special-function unit.  The choice is the row's own (lanes differ only on
+      // the band's edge tiles), so a row's bits do not depend on which rows
+      // share its warp.
+      if (kF16 && (km == ~0ull || !a.exclude) && dlo <= 0 && dhi >= LN - 1) {
 #pragma unroll
-      for (int h = 0; h < LN / 2; ++h) {
-        const float2 t2 = ffma2(make_float2(__uint_as_float(x[2 * h]), __uint_as_float(x[2 * h + 1])), sl2x2, nbx2);
-        const float2 e = make_float2(fast_exp2(t2.x), fast_exp2(t2.y));   // -inf -> 0
-        s2[h & 1] = fadd2(s2[h & 1], e);
-        x[2 * h] = __float_as_uint(e.x);
-        x[2 * h + 1] = __float_as_uint(e.y);
+        for (int h = 0; h < LN / 2; ++h) {
+          const float2 t2 = ffma2(make_float2(__uint_as_float(x[2 * h]), __uint_as_float(x[2 * h + 1])), sl2x2, nbx2);
+          const float2 e = (h % 3 == 2) ? exp2_poly2(t2) : make_float2(fast_exp2(t2.x), fast_exp2(t2.y));
+          s2[h & 1] = fadd2(s2[h & 1], e);
+          x[2 * h] = __float_as_uint(e.x);
+          x[2 * h + 1] = __float_as_uint(e.y);
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < LN / 2; ++h) {
+          const float2 t2 = ffma2(make_float2(__uint_as_float(x[2 * h]), __uint_as_float(x[2 * h + 1])), sl2x2, nbx2);
+          const float2 e = make_float2(fast_exp2(t2.x), fast_exp2(t2.y));   // -inf -> 0
+          s2[h & 1] = fadd2(s2[h & 1], e);
+          x[2 * h] = __float_as_uint(e.x);
+          x[2 * h + 1] = __float_as_uint(e.y);
+        }
       }
       l_run += (s2[0].x + s2[1].x) + (s2[0].y + s2[1].y);
       // zeroed keys are counted in l but add no value
@@ -459,17 +502,14 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         tc::fence_after_sync();
         const float c = rescale ? o_scale : 1.f;
 #pragma unroll
-        for (int cc = 0; cc < D; cc += 32) {
-          uint32_t o[32];
-          tc::tmem_ld16(tbase + lane_off + o_col + cc, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
-          tc::tmem_ld16(tbase + lane_off + o_col + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+        for (int cc = 0; cc < D; cc += 16) {
+          uint32_t o[16];
+          tc::tmem_ld16(tbase + lane_off + o_col + cc, o);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * c);
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * c);
           tc::tmem_st8(tbase + lane_off + o_col + cc, *reinterpret_cast<uint32_t(*)[8]>(&o[0]));
           tc::tmem_st8(tbase + lane_off + o_col + cc + 8, *reinterpret_cast<uint32_t(*)[8]>(&o[8]));
-          tc::tmem_st8(tbase + lane_off + o_col + cc + 16, *reinterpret_cast<uint32_t(*)[8]>(&o[16]));
-          tc::tmem_st8(tbase + lane_off + o_col + cc + 24, *reinterpret_cast<uint32_t(*)[8]>(&o[24]));
         }
         tc::tmem_wait_st();
       }
@@ -477,7 +517,11 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.pready[pb]));
+      // the group's next S: requested here, after this tile's P is handed over
+      // (waiting for it before the P store held the P.V back)
+      if (t + 2 < NTL && !(ok = load_s(t + 2))) break;
     }
+    tc::tmem_wait_ld();   // an S load still in flight after an abort
     // ---- epilogue: merge the two groups' partial softmaxes, bf16 rows, LSE
     // (natural log).  A group without tiles never wrote its O, which is then
     // left out.  The per-row partials go to the K stages, idle once every S is
