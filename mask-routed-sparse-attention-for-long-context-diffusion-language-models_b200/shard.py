@@ -101,6 +101,12 @@ class GroupExchange:
         self.rank = dist.get_rank(group)
         self.bulk = bulk
 
+    def align(self):
+        """Barrier over the group (every rank), so a timed forward starts on all
+        ranks together and the exchange waits inside it measure transfers, not
+        how far one rank's host ran ahead of another's."""
+        dist.barrier(group=self.group)
+
     def halo(self, bufs, ls: int, h: int):
         """Post the halo exchange of the tensors ``bufs`` (each
         ``[B, rows, ...]``: this rank's ``ls`` rows after an ``h``-row left
@@ -323,8 +329,11 @@ class ShardedRouteLayer:
         time the stream stalled on a transfer)."""
         names = ("start",) + self.STAGES
         tot = {n: 0.0 for n in self.STAGES}
+        align = getattr(self.exchange, "align", None)
         for it in range(reps + 1):
             ev = {n: torch.cuda.Event(enable_timing=True) for n in names}
+            if align is not None:
+                align()
             self.forward(*args, events=ev)
             torch.cuda.synchronize()
             if it == 0:
