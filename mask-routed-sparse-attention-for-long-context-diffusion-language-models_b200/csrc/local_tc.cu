@@ -331,11 +331,18 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       const uint32_t dO = tbase + kOCol + D * par;      // group par's accumulator
       if (tc::elect_one()) {
         // each group's first tile overwrites its O (TMEM is not zeroed)
-        if (t < 2) tc::mma_bf16<false>(dO, dh, dv, id_o);
-        else tc::mma_bf16<true>(dO, dh, dv, id_o);
+        if constexpr (kF16) {
+          // P from TMEM: 16 keys (8 columns of fp16 pairs) per k-step
+          const uint32_t aP = tbase + LN * s_idx(t);
+          if (t < 2) tc::mma_f16_ts<false>(dO, aP, dv, id_o);
+          else tc::mma_f16_ts<true>(dO, aP, dv, id_o);
 #pragma unroll
-        for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dO, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
-        if constexpr (!kF16) {
+          for (int kk = 1; kk < 4; ++kk) tc::mma_f16_ts<true>(dO, aP + 8 * kk, tc::desc_adv(dv, kk * 2048), id_o);
+        } else {
+          if (t < 2) tc::mma_bf16<false>(dO, dh, dv, id_o);
+          else tc::mma_bf16<true>(dO, dh, dv, id_o);
+#pragma unroll
+          for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dO, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             tc::mma_bf16<true>(dO, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
@@ -344,6 +351,8 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         tc::mma_commit(tc::smem_addr(&sm.vfree[sv]));
       }
       __syncwarp();
+      // fp16 P lives in the S buffer that S(t + 4) overwrites: wait for its P.V
+      if (kF16 && t + 4 < NTL && !tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[pb]), p_use(t) & 1, abort_flag)) break;
       if (t + 4 < NTL) ok = issue_s(t + 4);
     }
     if (tc::elect_one()) {
@@ -485,13 +494,21 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
           lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
         }
       }
-      // the P buffer's previous tile must have been read by its P.V
-      if (pu >= 1 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[pb]), (pu - 1) & 1, abort_flag))) break;
+      if constexpr (kF16) {
+        // fp16 P over the first 32 columns of its own S buffer, the A operand of
+        // P.V straight from TMEM (the buffer's next S is issued only after this
+        // P.V has completed)
+        tc::tmem_st16(tbase + lane_off + LN * sb, &hi[0]);
+        tc::tmem_st16(tbase + lane_off + LN * sb + 16, &hi[16]);
+        tc::tmem_wait_st();
+      } else {
+        // the P buffer's previous tile must have been read by its P.V
+        if (pu >= 1 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[pb]), (pu - 1) & 1, abort_flag))) break;
 #pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        *reinterpret_cast<uint4*>(sm.p[pb] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
-        if constexpr (!kF16)
+        for (int p = 0; p < 8; ++p) {
+          *reinterpret_cast<uint4*>(sm.p[pb] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
           *reinterpret_cast<uint4*>(sm.p[pb + 1] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
+        }
       }
       if (__any_sync(0xffffffffu, rescale)) {
         // O must hold every earlier tile of this group before it is scaled: the

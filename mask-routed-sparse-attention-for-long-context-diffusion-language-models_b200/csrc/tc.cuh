@@ -58,6 +58,15 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
                "l"(b_desc), "r"(idesc), "n"(kAccumulate ? 1 : 0));
 }
 
+// D (+)= A . B with A in tensor memory (kind::f16, M rows on the lanes of
+// a_tmem, two 16-bit K elements per 32-bit column, K-major) and B in shared
+// memory.
+template <bool kAccumulate>
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, %4;\n" ::"r"(d_tmem), "r"(a_tmem),
+               "l"(b_desc), "r"(idesc), "n"(kAccumulate ? 1 : 0));
+}
+
 // Arrive on `bar` once all tcgen05.mma issued so far by this thread complete.
 __device__ __forceinline__ void mma_commit(uint32_t bar_smem) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
@@ -129,6 +138,13 @@ __device__ __forceinline__ void tmem_ld_16x32bx2_x16(uint32_t taddr, uint32_t (&
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+// 32 lanes x 16 columns: thread i of the warp writes lane (warp%4)*32 + i.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr),
