@@ -4,29 +4,31 @@
 // dream_dllm_hils/local_attention.py:35-107: zeroed keys keep logit 0 in the
 // softmax and add no value; keys with |i-j| > window are out.
 //
-// One CTA owns LQ = floor(128 / G) queries of one KV head (18 for GQA 7:1).
-// Its MMA tile has 128 rows, row G*qi + g = (query qi, head g of the group;
-// rows >= LQ*G are zero padding), so each 64-key K/V tile is read once for all
-// heads of the group.  Per key tile t:
+// One CTA owns two query tiles of LQ = floor(128 / G) queries each (18 for
+// GQA 7:1) of one KV head.  A tile's MMA rows are G*qi + g = (query qi, head
+// g of the group; rows >= LQ*G are zero padding), so each 64-key K/V tile is
+// read once for all heads of the group and both query tiles.  Per query tile
+// and key tile t:
 //   S[128 x 64]  = Q . K_t^T               (UMMA M=128, N=64,  K=128, TMEM)
 //   P            = exp2(S*scale*log2e - m)  (one thread per row, online max)
-//   O[128 x 128] += P . V_t                (UMMA M=128, N=128, K=64, TMEM)
-// P goes through shared memory: fp16 when V is fp16, else bf16 hi + lo parts
-// (two MMAs per k-step, ~16 significant bits).  Each row keeps a reference
-// max that moves (rescaling O in TMEM) only when a tile max exceeds it by more
-// than 2^8.
-// Warps 0-7: softmax and epilogue in two groups of four (warp w = TMEM lanes
-// 32(w%4)..+31 = rows); group g takes every other key tile (by the tile's
-// parity counted from query row 0's tile) and keeps
-// its own running max, sum and O accumulator, merged in the epilogue.  Each
-// group has two S buffers in TMEM, so the S of its next tile is computed while
-// it works on the current one and the softmax never waits for an MMA round
-// trip; with fp16 P it also has two P buffers.  Warp 8: TMA of Q and of the K
-// tiles (4 stages) and the per-tile key validity masks; warp 11: TMA of the V
-// tiles (4 stages, released by P.V); warps 9 and 10: MMA issue for the even
-// and the odd tiles (converged, elect.sync), in the order S(t), S(t+2), then
-// per tile P.V(t), S(t+4).  Every mbarrier wait is bounded and unwinds through
-// a shared abort flag.
+//   O[128 x 128] += P . V_t                (UMMA M=128, N=128, K=64, A = P in TMEM)
+// P (fp16 when V is fp16, else bf16 hi + lo parts, ~16 significant bits) is
+// written back over its own S buffer and read by P.V from there.  Each row keeps a
+// reference max that moves (rescaling O in TMEM) only when a tile max exceeds
+// it by more than 2^8.
+// Warps 0-3 and 4-7: the softmax and epilogue of query tiles 0 and 1 (warp w
+// = TMEM lanes 32(w%4)..+31 = rows); group g walks the key tiles of its own
+// band in order with two S buffers, so the S of its next tile is computed
+// while it works on the current one.  Warp 8: TMA of Q and of the K tiles (4
+// stages) and the per-tile key validity masks; warp 11: TMA of the V tiles
+// (4 stages); warps 9 and 10: MMA issue for groups 0 and 1 (converged,
+// elect.sync): S(first), S(first+1), then per tile P.V(t) and, once that P.V
+// has read the buffer, S(t+2) into it.  A K or V stage is released by both
+// groups (an MMA commit, or a plain arrive for a tile outside the group's
+// band).  Every mbarrier wait is bounded and unwinds through a shared abort
+// flag.  A row's tiles are its own group's, in order, whichever rows share its
+// CTA (tiles outside its band add exact zeros), so a row's result does not
+// depend on how rows are cut into CTAs.
 //
 // The same kernel also runs the causal chunk-expanded window of
 // ops/flex_attn_tilelang.py:26-276 (flex_attn_tl): a row at absolute position
@@ -46,8 +48,8 @@ using namespace mrsa;
 namespace {
 
 constexpr int LN = 64;            // keys per tile
-constexpr int NKS = 4;            // K stages (even: a stage's tiles share one parity, hence one MMA warp)
-constexpr int NVS = 4;            // V stages (even, likewise)
+constexpr int NKS = 4;            // K stages
+constexpr int NVS = 4;            // V stages
 constexpr int NMS = 8;            // key-mask slots
 constexpr int D = kHeadDim;
 constexpr int L_THREADS = 384;    // warps 0-7 softmax (two groups), 8 Q/K TMA + masks, 9-10 MMA, 11 V TMA
@@ -55,13 +57,12 @@ constexpr int L_W_KLOAD = 8, L_W_MMA = 9, L_W_VLOAD = 11;
 constexpr uint32_t kOCol = 256;   // O of groups 0 / 1 at [256, 384) / [384, 512); S buffer i at [64 i, 64 i + 64)
 
 struct __align__(1024) LocalSmem {
-  unsigned char q[2][16384];          // [half][128 rows = (query, head)][64 dims], 128-byte swizzled
+  unsigned char q[2][2][16384];       // [query tile][half][128 rows = (query, head)][64 dims], 128-byte swizzled
   unsigned char k[NKS][16384];        // [half][64 keys][64 dims]
   unsigned char v[NVS][16384];        // same, read as the MN-major B operand of P.V
-  unsigned char p[4][16384];          // fp16 P: group g's buffers 2g, 2g+1; bf16 P: group g's hi 2g, lo 2g+1
   unsigned long long kmask[NMS];      // bit j: key j of the tile is usable (not zeroed); slot t % NMS
   uint64_t qfull, kfull[NKS], kfree[NKS], vfull[NVS], vfree[NVS], mfull[NMS];
-  uint64_t sfull[4], sfree[4], pready[4], pfree[4], drain[2];
+  uint64_t sfull[4], pready[4], pfree[4], drain[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -101,8 +102,6 @@ __device__ __forceinline__ void row_band(const LocalArgs& a, int64_t pos, int64_
 
 __device__ int g_local_error;
 
-__device__ __forceinline__ int swz_off(int row, int piece) { return row * 128 + ((piece ^ (row & 7)) << 4); }
-
 // 2^y for a pair on the FMA pipe, taking load off the special-function unit:
 // Cody-Waite reduction y = n + f (n = round(y) through the 1.5 * 2^23 shift,
 // |f| <= 1/2), 2^f by a degree-4 polynomial whose coefficients were fitted
@@ -137,55 +136,73 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hk = blockIdx.y, b = blockIdx.z;
   const int G = a.G, LQ = 128 / G, nrows = LQ * G;
-  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * LQ;
-  const int64_t rows_q = (a.Lq - q0) < LQ ? (a.Lq - q0) : LQ;
-  // positions of the CTA's first and last rows (the band is monotone in the
-  // position); with explicit row positions, their minimum and maximum
-  int64_t p_min = a.q_offset + q0, p_max = a.q_offset + q0 + rows_q - 1;
-  if (a.qpos != nullptr) {
-    p_min = a.qpos[q0];
-    p_max = p_min;
-    for (int i = 1; i < rows_q; ++i) {
-      const int64_t p = a.qpos[q0 + i];
-      p_min = p < p_min ? p : p_min;
-      p_max = p > p_max ? p : p_max;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * 2 * LQ;   // query tile g starts at q0 + g LQ
+  // key tiles of each query tile's band (absolute tile indices; empty: lo > hi)
+  int64_t tile_lo[2], tile_hi[2];
+#pragma unroll
+  for (int qt = 0; qt < 2; ++qt) {
+    const int64_t r0 = q0 + qt * LQ;
+    const int64_t nr = (a.Lq - r0) < LQ ? (a.Lq - r0) : LQ;
+    tile_lo[qt] = 1;
+    tile_hi[qt] = 0;
+    if (nr <= 0) continue;
+    // positions of the tile's first and last rows (the band is monotone in the
+    // position); with explicit row positions, their minimum and maximum
+    int64_t p_min = a.q_offset + r0, p_max = a.q_offset + r0 + nr - 1;
+    if (a.qpos != nullptr) {
+      p_min = a.qpos[r0];
+      p_max = p_min;
+      for (int i = 1; i < nr; ++i) {
+        const int64_t p = a.qpos[r0 + i];
+        p_min = p < p_min ? p : p_min;
+        p_max = p > p_max ? p : p_max;
+      }
+    }
+    int64_t j_lo, j_hi, unused;
+    row_band(a, p_min, j_lo, unused);
+    row_band(a, p_max, unused, j_hi);
+    if (j_lo < 0) j_lo = 0;
+    if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
+    if (j_hi < j_lo) continue;
+    tile_lo[qt] = j_lo / LN;
+    tile_hi[qt] = j_hi / LN;
+  }
+  // the CTA's key tiles: the union of the two ranges, local index t in [0, NTL)
+  const bool has0 = tile_lo[0] <= tile_hi[0], has1 = tile_lo[1] <= tile_hi[1];
+  int64_t u_lo = 0, u_hi = -1;
+  if (has0 || has1) {
+    u_lo = has0 ? tile_lo[0] : tile_lo[1];
+    u_hi = has1 ? tile_hi[1] : tile_hi[0];
+    if (has0 && has1) {
+      u_lo = tile_lo[0] < tile_lo[1] ? tile_lo[0] : tile_lo[1];
+      u_hi = tile_hi[0] > tile_hi[1] ? tile_hi[0] : tile_hi[1];
     }
   }
-  int64_t j_lo, j_hi, unused;
-  row_band(a, p_min, j_lo, unused);
-  row_band(a, p_max, unused, j_hi);
-  if (j_lo < 0) j_lo = 0;
-  if (j_hi > a.Lk - 1) j_hi = a.Lk - 1;
-  const int t_lo = static_cast<int>(j_lo / LN);
-  const int NTL = j_hi >= j_lo ? static_cast<int>(j_hi / LN) - t_lo + 1 : 0;
-  // Tile t (key tile t_lo + t) belongs to softmax group (t + e) % 2, the parity
-  // of its key tile counted from the tile of query row 0: a row's tiles then go
-  // to the same groups, in the same order, whichever rows share its CTA, so a
-  // row's result does not depend on how the rows are cut into CTAs (a query
-  // shard with a tile-aligned halo gets the bits of the whole sequence).
-  const int e = static_cast<int>((static_cast<int64_t>(t_lo) - floor_div(a.q_offset, LN)) & 1);
-  auto grp_of = [e](int t) { return (t + e) & 1; };
-  // P buffer of tile t and how many times that buffer was used before: fp16 P
-  // alternates two buffers per group, bf16 hi + lo P has one pair per group
-  auto p_idx = [grp_of](int t) { return kF16 ? 2 * grp_of(t) + ((t >> 1) & 1) : 2 * grp_of(t); };
-  auto p_use = [](int t) { return kF16 ? (t >> 2) : (t >> 1); };
-  // S buffer of tile t: each group alternates its two buffers
-  auto s_idx = [grp_of](int t) { return 2 * grp_of(t) + ((t >> 1) & 1); };
+  const int t_lo = static_cast<int>(u_lo);
+  const int NTL = static_cast<int>(u_hi - u_lo + 1);
+  // group g's local tiles [ga[g], gb[g]] (empty: ga > gb); its k-th tile uses S
+  // buffer 2g + (k & 1) for the (k >> 1)-th time
+  int ga[2], gb[2];
+#pragma unroll
+  for (int qt = 0; qt < 2; ++qt) {
+    const bool h = qt ? has1 : has0;
+    ga[qt] = h ? static_cast<int>(tile_lo[qt] - u_lo) : 1;
+    gb[qt] = h ? static_cast<int>(tile_hi[qt] - u_lo) : 0;
+  }
 
   if (tid == 0) {
     tc::mbar_init(tc::smem_addr(&sm.qfull), 1);
     for (int s = 0; s < NKS; ++s) {
       tc::mbar_init(tc::smem_addr(&sm.kfull[s]), 1);
-      tc::mbar_init(tc::smem_addr(&sm.kfree[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.kfree[s]), 2);
     }
     for (int s = 0; s < NVS; ++s) {
       tc::mbar_init(tc::smem_addr(&sm.vfull[s]), 1);
-      tc::mbar_init(tc::smem_addr(&sm.vfree[s]), 1);
+      tc::mbar_init(tc::smem_addr(&sm.vfree[s]), 2);
     }
     for (int s = 0; s < NMS; ++s) tc::mbar_init(tc::smem_addr(&sm.mfull[s]), 1);
     for (int s = 0; s < 4; ++s) {
       tc::mbar_init(tc::smem_addr(&sm.sfull[s]), 1);
-      tc::mbar_init(tc::smem_addr(&sm.sfree[s]), 4);
       tc::mbar_init(tc::smem_addr(&sm.pready[s]), 4);
       tc::mbar_init(tc::smem_addr(&sm.pfree[s]), 1);
     }
@@ -193,11 +210,12 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
-  // zero the padding rows of the Q tile (the TMA box fills rows [0, nrows)),
+  // zero the padding rows of the Q tiles (the TMA boxes fill rows [0, nrows)),
   // visible to the tensor core's async proxy
-  for (int i = tid; i < 2 * (128 - nrows) * 8; i += L_THREADS) {
+  for (int i = tid; i < 4 * (128 - nrows) * 8; i += L_THREADS) {
     const int h = i / ((128 - nrows) * 8), rem = i % ((128 - nrows) * 8);
-    *reinterpret_cast<uint4*>(sm.q[h] + (nrows + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(sm.q[h >> 1][h & 1] + (nrows + rem / 8) * 128 + (rem % 8) * 16) =
+        make_uint4(0u, 0u, 0u, 0u);
   }
   tc::fence_proxy_async();
   if (warp == 0) {
@@ -215,9 +233,12 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
     if (lane == 0) {
       tc::prefetch_tensormap(&tm_q);
       tc::prefetch_tensormap(&tm_k);
-      tc::mbar_arrive_expect_tx(qb, static_cast<uint32_t>(nrows) * 256u);
-      tc::tma_load_4d(tc::smem_addr(sm.q[0]), &tm_q, 0, hk * G, 0, static_cast<int>(b * a.Lq + q0), qb);
-      tc::tma_load_4d(tc::smem_addr(sm.q[1]), &tm_q, 0, hk * G, 1, static_cast<int>(b * a.Lq + q0), qb);
+      tc::mbar_arrive_expect_tx(qb, static_cast<uint32_t>(nrows) * 512u);
+#pragma unroll
+      for (int qt = 0; qt < 2; ++qt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          tc::tma_load_4d(tc::smem_addr(sm.q[qt][h]), &tm_q, 0, hk * G, h, static_cast<int>(b * a.Lq + q0 + qt * LQ), qb);
     }
     // key-validity bytes of tile tt (this lane's keys 32h + lane), requested one
     // tile ahead so their latency is not on the copy-issue path
@@ -236,8 +257,8 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       const int st = t % NKS;
       const uint32_t vb[2] = {vb_next[0], vb_next[1]};
       valid_bytes(t + 1, vb_next);
-      // stage st was last read by S(t - NKS); mask slot t % NMS by the softmax of
-      // tile t - NMS, which precedes the P.V(t - NMS) that S(t - NKS) is issued after
+      // stage st was released by both groups for tile t - NKS; mask slot t % NMS
+      // was last read by the softmax of tile t - NMS, which precedes that release
       if (t >= NKS && !tc::wait_bounded_warp(tc::smem_addr(&sm.kfree[st]), ((t / NKS) - 1) & 1, abort_flag)) break;
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
       // usable keys of the tile: inside the sequence, valid, and not a landmark slot when skip_inert
@@ -285,23 +306,30 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         tc::mbar_wait(tc::smem_addr(&sm.vfull[tt % NVS]), (tt / NVS) & 1);
     __syncwarp();
   } else if (warp >= L_W_MMA) {
-    // ============================ MMA issue (two converged warps) =============
-    // Warp 9 issues the MMAs of the even tiles, warp 10 those of the odd tiles
-    // (one issuing thread needs about twice the tensor pipe's time per MMA):
-    // S(t) and S(t+2) first, then per tile P.V(t) into its group's O and S(t+4)
-    // into the S buffer that tile t's softmax has released.
-    const int par = warp - L_W_MMA;
+    // ============================ MMA issue (one warp per query tile) =========
+    const int g = warp - L_W_MMA;
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, LN, 0, 0);
     // kind::f16 with fp16 A and B: the bf16 format bits cleared
     constexpr uint32_t id_o = tc::idesc_bf16_f32(128, D, 0, 1) & (kF16 ? ~((1u << 7) | (1u << 10)) : ~0u);
-    const uint64_t dq = tc::smem_desc_sw128(tc::smem_addr(sm.q[0]), 16, 1024);
+    const uint64_t dq = tc::smem_desc_sw128(tc::smem_addr(sm.q[g][0]), 16, 1024);
     const uint64_t dk0 = tc::smem_desc_sw128(tc::smem_addr(sm.k[0]), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(tc::smem_addr(sm.v[0]), 8192, 1024);
-    const uint64_t dp0 = tc::smem_desc_sw128(tc::smem_addr(sm.p[0]), 16, 1024);
+    const int t0 = g ? ga[1] : ga[0], t1 = g ? gb[1] : gb[0];
+    // the K and V stages of a tile outside this group's band, released unused (in tile order)
+    auto release = [&](int t) -> bool {
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.kfull[t % NKS]), (t / NKS) & 1, abort_flag)) return false;
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.vfull[t % NVS]), (t / NVS) & 1, abort_flag)) return false;
+      if (lane == 0) {
+        tc::mbar_arrive(tc::smem_addr(&sm.kfree[t % NKS]));
+        tc::mbar_arrive(tc::smem_addr(&sm.vfree[t % NVS]));
+      }
+      __syncwarp();
+      return true;
+    };
+    // S(t) into buffer 2g + ((t - t0) & 1)
     auto issue_s = [&](int t) -> bool {
-      const int st = t % NKS, sb = s_idx(t), use = t >> 2;
+      const int k = t - t0, sb = 2 * g + (k & 1), st = t % NKS;
       if (!tc::wait_bounded_warp(tc::smem_addr(&sm.kfull[st]), (t / NKS) & 1, abort_flag)) return false;
-      if (use >= 1 && !tc::wait_bounded_warp(tc::smem_addr(&sm.sfree[sb]), (use - 1) & 1, abort_flag)) return false;
       tc::fence_after_sync();
       const uint64_t db = tc::desc_adv(dk0, st * 16384);
       const uint32_t dS = tbase + LN * sb;
@@ -317,84 +345,82 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       __syncwarp();
       return true;
     };
+    const int pre_end = t0 < NTL ? t0 : NTL;           // tiles [0, pre_end) lie before the band
     bool ok = tc::wait_bounded_warp(tc::smem_addr(&sm.qfull), 0, abort_flag);
-    const int t0 = par ^ e;                           // this group's first tile
-    if (ok && t0 < NTL) ok = issue_s(t0);
-    if (ok && t0 + 2 < NTL) ok = issue_s(t0 + 2);
-    for (int t = t0; ok && t < NTL; t += 2) {
-      const int sv = t % NVS, pb = p_idx(t);
-      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.pready[pb]), p_use(t) & 1, abort_flag)) break;
-      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.vfull[sv]), (t / NVS) & 1, abort_flag)) break;
+    for (int t = 0; ok && t < pre_end; ++t) ok = release(t);
+    if (ok && t0 <= t1) ok = issue_s(t0);
+    if (ok && t0 + 1 <= t1) ok = issue_s(t0 + 1);
+    for (int t = t0; ok && t <= t1; ++t) {
+      const int k = t - t0, sb = 2 * g + (k & 1), sv = t % NVS;
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pready[sb]), (k >> 1) & 1, abort_flag))) break;
+      if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.vfull[sv]), (t / NVS) & 1, abort_flag))) break;
       tc::fence_after_sync();
-      const uint64_t dv = tc::desc_adv(dv0, sv * 16384), dh = tc::desc_adv(dp0, pb * 16384),
-                     dl = tc::desc_adv(dp0, (pb + 1) * 16384);
-      const uint32_t dO = tbase + kOCol + D * par;      // group par's accumulator
+      const uint64_t dv = tc::desc_adv(dv0, sv * 16384);
+      const uint32_t dO = tbase + kOCol + D * g, aP = tbase + LN * sb;
       if (tc::elect_one()) {
-        // each group's first tile overwrites its O (TMEM is not zeroed)
-        if constexpr (kF16) {
-          // P from TMEM: 16 keys (8 columns of fp16 pairs) per k-step
-          const uint32_t aP = tbase + LN * s_idx(t);
-          if (t < 2) tc::mma_f16_ts<false>(dO, aP, dv, id_o);
-          else tc::mma_f16_ts<true>(dO, aP, dv, id_o);
+        // the group's first tile overwrites its O (TMEM is not zeroed); P from
+        // TMEM, 16 keys (8 columns of 16-bit pairs) per k-step
+        if (k == 0) tc::mma_f16_ts<false>(dO, aP, dv, id_o);
+        else tc::mma_f16_ts<true>(dO, aP, dv, id_o);
 #pragma unroll
-          for (int kk = 1; kk < 4; ++kk) tc::mma_f16_ts<true>(dO, aP + 8 * kk, tc::desc_adv(dv, kk * 2048), id_o);
-        } else {
-          if (t < 2) tc::mma_bf16<false>(dO, dh, dv, id_o);
-          else tc::mma_bf16<true>(dO, dh, dv, id_o);
+        for (int kk = 1; kk < 4; ++kk) tc::mma_f16_ts<true>(dO, aP + 8 * kk, tc::desc_adv(dv, kk * 2048), id_o);
+        if constexpr (!kF16) {
+          // bf16 P's lo part, columns 32-63 of the buffer
 #pragma unroll
-          for (int kk = 1; kk < 4; ++kk) tc::mma_bf16<true>(dO, tc::desc_adv(dh, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc::mma_bf16<true>(dO, tc::desc_adv(dl, kk * 32), tc::desc_adv(dv, kk * 2048), id_o);
+          for (int kk = 0; kk < 4; ++kk) tc::mma_f16_ts<true>(dO, aP + 32 + 8 * kk, tc::desc_adv(dv, kk * 2048), id_o);
         }
-        tc::mma_commit(tc::smem_addr(&sm.pfree[pb]));
+        tc::mma_commit(tc::smem_addr(&sm.pfree[sb]));
         tc::mma_commit(tc::smem_addr(&sm.vfree[sv]));
       }
       __syncwarp();
-      // fp16 P lives in the S buffer that S(t + 4) overwrites: wait for its P.V
-      if (kF16 && t + 4 < NTL && !tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[pb]), p_use(t) & 1, abort_flag)) break;
-      if (t + 4 < NTL) ok = issue_s(t + 4);
+      if (t + 2 <= t1) {
+        // P(t) lives in the S buffer that S(t + 2) overwrites: wait for this P.V
+        if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[sb]), (k >> 1) & 1, abort_flag))) break;
+        ok = issue_s(t + 2);
+      }
     }
+    const int post_begin = (t1 + 1) > pre_end ? (t1 + 1) : pre_end;   // tiles after the band
+    for (int t = post_begin; ok && t < NTL; ++t) ok = release(t);
     if (tc::elect_one()) {
-      tc::mma_commit(tc::smem_addr(&sm.drain[par]));
-      tc::mbar_wait(tc::smem_addr(&sm.drain[par]), 0);
+      tc::mma_commit(tc::smem_addr(&sm.drain[g]));
+      tc::mbar_wait(tc::smem_addr(&sm.drain[g]), 0);
     }
     __syncwarp();
   } else {
     // ============================ softmax + epilogue (warps 0-7) ==============
-    const int grp = warp >> 2;                       // tiles t with (t + e) % 2 == grp
+    const int grp = warp >> 2;                       // this group's query tile
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t o_col = kOCol + D * grp;          // this group's O accumulator
     const int r = (warp & 3) * 32 + lane;            // MMA row = TMEM lane
     const int qi = r / G, g = r - qi * G;
-    const int64_t pos = a.qpos != nullptr ? a.qpos[q0 + (qi < rows_q ? qi : rows_q - 1)] : a.q_offset + q0 + qi;
+    const int64_t r0 = q0 + grp * LQ;                // the tile's first query
+    const int64_t nr = (a.Lq - r0) < LQ ? ((a.Lq - r0) > 0 ? (a.Lq - r0) : 0) : LQ;
+    const int64_t pos = a.qpos != nullptr ? (nr > 0 ? a.qpos[r0 + (qi < nr ? qi : nr - 1)] : 0) : a.q_offset + r0 + qi;
     const float sl2 = a.sm_scale * kLog2e;
     float m_run = -INFINITY, l_run = 0.f, o_scale = 1.f;
     int64_t band_lo, band_hi;
     row_band(a, pos, band_lo, band_hi);
     if (band_hi > a.Lk - 1) band_hi = a.Lk - 1;
     const uint32_t fill = a.exclude ? __float_as_uint(-INFINITY) : 0u;
+    const int t0 = grp ? ga[1] : ga[0], t1 = grp ? gb[1] : gb[0];
     bool ok = true;
     uint32_t x[64];
     auto load_s = [&](int tt) -> bool {
-      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.sfull[s_idx(tt)]), (tt >> 2) & 1, abort_flag)) return false;
+      const int k = tt - t0, sb = 2 * grp + (k & 1);
+      if (!tc::wait_bounded_warp(tc::smem_addr(&sm.sfull[sb]), (k >> 1) & 1, abort_flag)) return false;
       tc::fence_after_sync();
-      const uint32_t sa = tbase + lane_off + LN * s_idx(tt);
+      const uint32_t sa = tbase + lane_off + LN * sb;
       tc::tmem_ld16(sa + 0, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
       tc::tmem_ld16(sa + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
       tc::tmem_ld16(sa + 32, *reinterpret_cast<uint32_t(*)[16]>(&x[32]));
       tc::tmem_ld16(sa + 48, *reinterpret_cast<uint32_t(*)[16]>(&x[48]));
       return true;
     };
-    if ((grp ^ e) < NTL) ok = load_s(grp ^ e);
-    for (int t = grp ^ e; ok && t < NTL; t += 2) {
-      const int sb = s_idx(t), pb = p_idx(t), pu = p_use(t);
+    if (t0 <= t1) ok = load_s(t0);
+    for (int t = t0; ok && t <= t1; ++t) {
+      const int k = t - t0, sb = 2 * grp + (k & 1);
       const int64_t j0 = static_cast<int64_t>(t_lo + t) * LN;
       tc::tmem_wait_ld();
-      // the S buffer is free for S(t + 4) as soon as it is in registers
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.sfree[sb]));
       if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.mfull[t % NMS]), (t / NMS) & 1, abort_flag))) break;
       const unsigned long long km = sm.kmask[t % NMS];
       // Zeroed keys (invalid, or landmark slots) keep logit 0: their raw score is
@@ -483,38 +509,33 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
             if (!((km >> c) & 1ull)) x[c] = 0u;
         }
       }
-      uint32_t hi[32], lo[32];
+      // P as fp16, or as bf16 hi + lo parts (~16 significant bits) with bf16 V
+      uint32_t pk[32], pl[kF16 ? 1 : 32];
 #pragma unroll
       for (int h = 0; h < 32; ++h) {
         const float p0 = __uint_as_float(x[2 * h]), p1 = __uint_as_float(x[2 * h + 1]);
         if constexpr (kF16) {
-          hi[h] = pack_f16x2(p0, p1);
+          pk[h] = pack_f16x2(p0, p1);
         } else {
-          hi[h] = pack_bf16x2(p0, p1);
-          lo[h] = pack_bf16x2(p0 - __uint_as_float(hi[h] << 16), p1 - __uint_as_float(hi[h] & 0xffff0000u));
+          pk[h] = pack_bf16x2(p0, p1);
+          pl[h] = pack_bf16x2(p0 - __uint_as_float(pk[h] << 16), p1 - __uint_as_float(pk[h] & 0xffff0000u));
         }
       }
-      if constexpr (kF16) {
-        // fp16 P over the first 32 columns of its own S buffer, the A operand of
-        // P.V straight from TMEM (the buffer's next S is issued only after this
-        // P.V has completed)
-        tc::tmem_st16(tbase + lane_off + LN * sb, &hi[0]);
-        tc::tmem_st16(tbase + lane_off + LN * sb + 16, &hi[16]);
-        tc::tmem_wait_st();
-      } else {
-        // the P buffer's previous tile must have been read by its P.V
-        if (pu >= 1 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[pb]), (pu - 1) & 1, abort_flag))) break;
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-          *reinterpret_cast<uint4*>(sm.p[pb] + swz_off(r, p)) = make_uint4(hi[4 * p], hi[4 * p + 1], hi[4 * p + 2], hi[4 * p + 3]);
-          *reinterpret_cast<uint4*>(sm.p[pb + 1] + swz_off(r, p)) = make_uint4(lo[4 * p], lo[4 * p + 1], lo[4 * p + 2], lo[4 * p + 3]);
-        }
+      // P over the first 32 columns of its own S buffer (bf16: lo over the other
+      // 32), the A operand of P.V straight from TMEM (the buffer's next S is
+      // issued only after this P.V has completed)
+      tc::tmem_st16(tbase + lane_off + LN * sb, &pk[0]);
+      tc::tmem_st16(tbase + lane_off + LN * sb + 16, &pk[16]);
+      if constexpr (!kF16) {
+        tc::tmem_st16(tbase + lane_off + LN * sb + 32, &pl[0]);
+        tc::tmem_st16(tbase + lane_off + LN * sb + 48, &pl[16]);
       }
+      tc::tmem_wait_st();
       if (__any_sync(0xffffffffu, rescale)) {
         // O must hold every earlier tile of this group before it is scaled: the
-        // P.V of tile t-2 (a rescale needs an earlier tile, so t >= 2 here); with
-        // one P buffer per group that was the wait above
-        if (kF16 && !(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(t - 2)]), p_use(t - 2) & 1, abort_flag)))
+        // P.V of the previous tile (a rescale needs an earlier tile, so k >= 1)
+        if (!(ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[2 * grp + ((k - 1) & 1)]), ((k - 1) >> 1) & 1,
+                                         abort_flag)))
           break;
         tc::fence_after_sync();
         const float c = rescale ? o_scale : 1.f;
@@ -530,75 +551,47 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
         }
         tc::tmem_wait_st();
       }
-      tc::fence_proxy_async();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.pready[pb]));
-      // the group's next S: requested here, after this tile's P is handed over
-      // (waiting for it before the P store held the P.V back)
-      if (t + 2 < NTL && !(ok = load_s(t + 2))) break;
+      if (lane == 0) tc::mbar_arrive(tc::smem_addr(&sm.pready[sb]));
+      if (t + 1 <= t1 && !(ok = load_s(t + 1))) break;
     }
     tc::tmem_wait_ld();   // an S load still in flight after an abort
-    // ---- epilogue: merge the two groups' partial softmaxes, bf16 rows, LSE
-    // (natural log).  A group without tiles never wrote its O, which is then
-    // left out.  The per-row partials go to the K stages, idle once every S is
-    // done: both groups have read all their S tiles when they pass the first
-    // barrier (before it, the other group's last S may still read them).
-    const bool has0 = (0 ^ e) < NTL, has1 = (1 ^ e) < NTL;
-    float* part_m = reinterpret_cast<float*>(sm.k[0]);          // [group][row]
-    float* part_l = part_m + 2 * 128;
-    asm volatile("bar.sync 1, 256;\n" ::: "memory");
-    part_m[grp * 128 + r] = m_run;
-    part_l[grp * 128 + r] = l_run;
-    asm volatile("bar.sync 1, 256;\n" ::: "memory");
-    // each group's last P.V (group g's tiles are t = g ^ e mod 2)
-    if (ok && has0) {
-      const int tl = (NTL - 1) - (((NTL - 1) ^ e) & 1);
-      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(tl)]), p_use(tl) & 1, abort_flag);
-    }
-    if (ok && has1) {
-      const int tl = (NTL - 1) - (((NTL - 1) ^ e ^ 1) & 1);
-      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[p_idx(tl)]), p_use(tl) & 1, abort_flag);
+    // ---- epilogue: bf16 rows and the LSE (natural log) of this query tile.
+    // A group without tiles never wrote its O: its rows get zeros and -inf.
+    const bool has = t0 <= t1;
+    if (ok && has) {
+      const int kl = t1 - t0;                        // the group's last P.V
+      ok = tc::wait_bounded_warp(tc::smem_addr(&sm.pfree[2 * grp + (kl & 1)]), (kl >> 1) & 1, abort_flag);
     }
     tc::fence_after_sync();
-    if (__all_sync(0xffffffffu, ok) && !__any_sync(0xffffffffu, *abort_flag != 0)) {
-      const float m0 = part_m[r], m1 = part_m[128 + r];
-      const float m = fmaxf(m0, m1);
-      const float f0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
-      const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
-      const float l = part_l[r] * f0 + part_l[128 + r] * f1;
+    if (nr > 0 && __all_sync(0xffffffffu, ok) && !__any_sync(0xffffffffu, *abort_flag != 0)) {
+      const float l = l_run;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const float c0 = f0 * inv, c1 = f1 * inv;
-      const bool row_ok = r < nrows && qi < rows_q;
-      const int64_t orow = ((b * a.Lq + q0 + qi) * a.Hq + hk * G + g);
-      // group 0 writes dims 0-63, group 1 dims 64-127
+      const bool row_ok = r < nrows && qi < nr;
+      const int64_t orow = ((b * a.Lq + r0 + qi) * a.Hq + hk * G + g);
 #pragma unroll
-      for (int cc = grp * (D / 2); cc < (grp + 1) * (D / 2); cc += 32) {
-        uint32_t o0[32], o1[32];
-        if (has0) {
-          tc::tmem_ld16(tbase + lane_off + kOCol + cc, *reinterpret_cast<uint32_t(*)[16]>(&o0[0]));
-          tc::tmem_ld16(tbase + lane_off + kOCol + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o0[16]));
+      for (int cc = 0; cc < D; cc += 32) {
+        uint32_t o[32];
+        if (has) {
+          tc::tmem_ld16(tbase + lane_off + o_col + cc, *reinterpret_cast<uint32_t(*)[16]>(&o[0]));
+          tc::tmem_ld16(tbase + lane_off + o_col + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o[16]));
+          tc::tmem_wait_ld();
         }
-        if (has1) {
-          tc::tmem_ld16(tbase + lane_off + kOCol + D + cc, *reinterpret_cast<uint32_t(*)[16]>(&o1[0]));
-          tc::tmem_ld16(tbase + lane_off + kOCol + D + cc + 16, *reinterpret_cast<uint32_t(*)[16]>(&o1[16]));
-        }
-        tc::tmem_wait_ld();
-        float o[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          o[i] = (has0 ? __uint_as_float(o0[i]) * c0 : 0.f) + (has1 ? __uint_as_float(o1[i]) * c1 : 0.f);
         if (row_ok) {
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = has ? __uint_as_float(o[i]) * inv : 0.f;
           uint4* dst = reinterpret_cast<uint4*>(a.out + orow * D + cc);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(pack_bf16x2(o[8 * i], o[8 * i + 1]), pack_bf16x2(o[8 * i + 2], o[8 * i + 3]),
-                                pack_bf16x2(o[8 * i + 4], o[8 * i + 5]), pack_bf16x2(o[8 * i + 6], o[8 * i + 7]));
+            dst[i] = make_uint4(pack_bf16x2(f[8 * i], f[8 * i + 1]), pack_bf16x2(f[8 * i + 2], f[8 * i + 3]),
+                                pack_bf16x2(f[8 * i + 4], f[8 * i + 5]), pack_bf16x2(f[8 * i + 6], f[8 * i + 7]));
         }
       }
-      if (grp == 0 && row_ok && a.lse != nullptr)
-        a.lse[orow] = l > 0.f ? (m + log2f(l)) * kLn2 : -INFINITY;
+      if (row_ok && a.lse != nullptr) a.lse[orow] = l > 0.f ? (m_run + log2f(l)) * kLn2 : -INFINITY;
     }
+
   }
 
   tc::fence_before_sync();
@@ -690,7 +683,7 @@ int local_launch(const void* q, const void* k, const void* v, const uint8_t* key
   if (cudaFuncSetAttribute(local_tc_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return MRSA_ERR_LAUNCH;
-  const int64_t blocks = (q_len + LQ - 1) / LQ;
+  const int64_t blocks = (q_len + 2 * LQ - 1) / (2 * LQ);   // two query tiles per CTA
   if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(kv_heads), static_cast<unsigned>(batch));
   local_tc_kernel<kF16><<<grid, L_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(tm_q, tm_k, tm_v, a);
