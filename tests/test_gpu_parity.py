@@ -323,6 +323,30 @@ def test_local_attention_f16v_matches_oracle(mrsa, dev, window, skip):
     _local_case(mrsa, dev, window, skip, f16v=True)
 
 
+@pytest.mark.parametrize("hq,l", [(4, 300), (8, 157), (16, 1), (32, 200), (28, 37), (28, 73)])
+def test_local_attention_group_sizes_and_ragged_lengths(mrsa, dev, hq, l):
+    """The window kernel packs 128 // G queries x G head rows per query tile and
+    runs two tiles per CTA: group sizes 1, 2, 4, 8 and 7 (tiles of 128, 64, 32,
+    16 and 18 queries), lengths that leave a CTA's second tile partial or
+    empty, bf16 V (hi + lo P) and fp16 V."""
+    gen = torch.Generator().manual_seed(hq * 1000 + l)
+    b, hkv, d, window = 2, 4, 128, 40
+    q = torch.randn(b, l, hq, d, generator=gen).bfloat16()
+    k = torch.randn(b, l, hkv, d, generator=gen).bfloat16()
+    v = torch.randn(b, l, hkv, d, generator=gen).bfloat16()
+    valid = torch.rand(b, l, generator=gen) > 0.1
+    ro, rl = orc.local_attention(q, k, v, valid, window, 64, True)
+    # the kernel entry directly: the reference's layout check wants L % 64 == 0
+    o, lse = mrsa.window_attention(q.to(dev), k.to(dev), v.to(dev), valid.to(dev), window + 63,
+                                   skip_inert=True, chunk=64)
+    close_bf16(o, ro)
+    torch.testing.assert_close(lse.cpu(), rl, atol=2e-4, rtol=1e-5)
+    o16, lse16 = mrsa.window_attention(q.to(dev), k.to(dev), mrsa.to_f16(v.to(dev)), valid.to(dev), window + 63,
+                                       skip_inert=True, chunk=64)
+    close_bf16(o16, ro)
+    torch.testing.assert_close(lse16.cpu(), rl, atol=2e-4, rtol=1e-5)
+
+
 def _local_case(mrsa, dev, window, skip, f16v):
     gen = torch.Generator().manual_seed(window)
     b, l, hq, hkv, d = 2, 2048 + 64, 28, 4, 128
