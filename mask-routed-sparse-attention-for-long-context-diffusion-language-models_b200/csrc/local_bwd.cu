@@ -341,28 +341,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_con
 }
 
 // ============================================================ dQ
+// One CTA per 16-query tile and KV head walks the key blocks of its band.
+// Two row groups (warps 4-7 and 8-11) take the even and the odd blocks, each
+// with its own MMA warp (1 and 2), S / dP buffers and dQ accumulator in TMEM
+// and dS buffer in shared memory: a group's MMA warp issues S and dP of block
+// t+2 as soon as block t's have been read into registers, then dQ_g +=
+// dS(t) . K(t) once its dS is stored, so neither group waits for an MMA round
+// trip or for the other group.  The epilogue adds the two accumulators in a
+// fixed order.  K/V blocks use three stages.
+constexpr int DQ_THREADS = 384;              // warp 0 loads, warps 1-2 issue MMAs, warps 4-11 two row groups
+constexpr int DQ_NST = 3;                    // K/V stages
+
 struct __align__(1024) DqSmem {
   unsigned char qt[PT * 2048];               // the tile's 16 queries x 8 head rows (loaded once)
   unsigned char ot[PT * 2048];               // their dO rows
   struct Stage {
     unsigned char kt[16384];                 // K tile of one 64-key block, [half][64 keys][64 dims]
     unsigned char vt[16384];                 // V tile
-  } st[2];
-  unsigned char ds[2][16384];                // dS [128 rows x 64 keys] bf16, 128-byte swizzled rows
-  unsigned long long zm[2];                  // zeroed keys of the block in each stage
-  uint64_t bar_q, bar_full[2], bar_free[2], bar_zm[2], bar_sdone[2], bar_sfree[2], bar_pready[2], bar_pvdone[2];
-  uint64_t bar_done;
-  int last[2];
+  } st[DQ_NST];
+  unsigned char ds[2][16384];                // dS of each group [128 rows x 64 keys] bf16, 128-byte swizzled rows
+  unsigned long long zm[DQ_NST];             // zeroed keys of the block in each stage
+  uint64_t bar_q, bar_full[DQ_NST], bar_free[DQ_NST], bar_zm[DQ_NST];
+  uint64_t bar_sdone[2], bar_sfree[2], bar_pready[2], bar_pvdone[2];
+  uint64_t bar_done[2];
+  int last[DQ_NST];
   uint32_t tmem_base;
   int abort_flag;
 };
 static_assert(sizeof(DqSmem) + 1024 <= 232448, "local dQ shared memory over budget");
 
-__global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_constant__ CUtensorMap tm_k,
-                                                               const __grid_constant__ CUtensorMap tm_v,
-                                                               const __grid_constant__ CUtensorMap tm_q,
-                                                               const __grid_constant__ CUtensorMap tm_do,
-                                                               LocalBwdArgs a) {
+__global__ void __launch_bounds__(DQ_THREADS, 1) local_dq_kernel(const __grid_constant__ CUtensorMap tm_k,
+                                                                 const __grid_constant__ CUtensorMap tm_v,
+                                                                 const __grid_constant__ CUtensorMap tm_q,
+                                                                 const __grid_constant__ CUtensorMap tm_do,
+                                                                 LocalBwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   DqSmem& sm = *reinterpret_cast<DqSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -374,21 +386,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_cons
   const int64_t k_hi = q0 + nq - 1 + W < a.L - 1 ? q0 + nq - 1 + W : a.L - 1;   // inclusive
   const int kb0 = static_cast<int>(k_lo / KB), n_blocks = static_cast<int>(k_hi / KB) - kb0 + 1;
 
-  for (int e = tid; e < 2 * PT * 2048 / 16; e += NTHREADS) reinterpret_cast<uint4*>(sm.qt)[e] = make_uint4(0u, 0u, 0u, 0u);
-  for (int e = tid; e < 2 * 16384 / 16; e += NTHREADS) reinterpret_cast<uint4*>(&sm.ds[0][0])[e] = make_uint4(0u, 0u, 0u, 0u);
+  for (int e = tid; e < 2 * PT * 2048 / 16; e += DQ_THREADS) reinterpret_cast<uint4*>(sm.qt)[e] = make_uint4(0u, 0u, 0u, 0u);
+  for (int e = tid; e < 2 * 16384 / 16; e += DQ_THREADS) reinterpret_cast<uint4*>(&sm.ds[0][0])[e] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) {
     tc::mbar_init(su32(&sm.bar_q), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < DQ_NST; ++s) {
       tc::mbar_init(su32(&sm.bar_full[s]), 1);
       tc::mbar_init(su32(&sm.bar_free[s]), 1);
       tc::mbar_init(su32(&sm.bar_zm[s]), 1);
+      sm.last[s] = -1;
+    }
+    for (int s = 0; s < 2; ++s) {
       tc::mbar_init(su32(&sm.bar_sdone[s]), 1);
       tc::mbar_init(su32(&sm.bar_sfree[s]), 4);
       tc::mbar_init(su32(&sm.bar_pready[s]), 4);
       tc::mbar_init(su32(&sm.bar_pvdone[s]), 1);
-      sm.last[s] = -1;
+      tc::mbar_init(su32(&sm.bar_done[s]), 1);
     }
-    tc::mbar_init(su32(&sm.bar_done), 1);
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -402,7 +416,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_cons
   tc::fence_after_sync();
   const uint32_t tbase = sm.tmem_base;
   int* abf = &sm.abort_flag;
-  constexpr uint32_t kS = 0, kDP = 128, kDQ = 256;   // TMEM columns: S 0/64, dP 128/192, dQ 256..383
+  // TMEM columns: S of group g at 64 g, dP at 128 + 64 g, dQ_g at 256 + 128 g
+  constexpr uint32_t kS = 0, kDP = 128, kDQ = 256;
 
   if (warp == 0) {
     // ============================ loader =====================================
@@ -417,11 +432,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_cons
       tc::tma_load_3d(su32(sm.qt + lane * 2048), &tm_q, 0, qy, 0, su32(&sm.bar_q));
       tc::tma_load_3d(su32(sm.ot + lane * 2048), &tm_do, 0, qy, 0, su32(&sm.bar_q));
     }
+    // key-validity bytes of block tt (this lane's keys 32h + lane), requested one
+    // block ahead so their latency is not on the copy-issue path
+    auto valid_bytes = [&](int tt, uint32_t (&vb)[2]) {
+      const int64_t jt = static_cast<int64_t>(kb0 + tt) * KB;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        vb[h] = (a.key_valid != nullptr && tt < n_blocks) ? a.key_valid[b * a.L + jt + 32 * h + lane] : 1u;
+    };
+    uint32_t vb_next[2];
+    valid_bytes(0, vb_next);
     for (int t = 0; t < n_blocks; ++t) {
-      const int st = t & 1;
+      const int st = t % DQ_NST;
       const int64_t j0 = static_cast<int64_t>(kb0 + t) * KB;
-      if (t >= 2 && !wait_ab_warp(&sm.bar_free[st], ((t >> 1) - 1) & 1, abf)) break;
-      const unsigned long long zm = zeroed_keys(a, b, j0, lane);
+      const uint32_t vb[2] = {vb_next[0], vb_next[1]};
+      valid_bytes(t + 1, vb_next);
+      // stage st was last read by the dQ MMAs of block t - DQ_NST, and its zeroed-key
+      // word by that block's rows, which precede those MMAs
+      if (t >= DQ_NST && !wait_ab_warp(&sm.bar_free[st], ((t / DQ_NST) - 1) & 1, abf)) break;
+      bool z0 = vb[0] == 0u, z1 = vb[1] == 0u;
+      if (a.skip_inert) {
+        z0 |= ((j0 + lane + 1) % a.chunk) == 0;
+        z1 |= ((j0 + 32 + lane + 1) % a.chunk) == 0;
+      }
+      const unsigned long long zm = static_cast<unsigned long long>(__ballot_sync(0xffffffffu, z0)) |
+                                    (static_cast<unsigned long long>(__ballot_sync(0xffffffffu, z1)) << 32);
       if (lane == 0) {
         sm.zm[st] = zm;
         tc::mbar_arrive(su32(&sm.bar_zm[st]));
@@ -436,12 +471,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_cons
     __syncwarp();
     if (lane == 0) {
       tc::mbar_wait(su32(&sm.bar_q), 0);
-      for (int s2 = 0; s2 < 2; ++s2)
-        if (sm.last[s2] >= 0) tc::mbar_wait(su32(&sm.bar_full[s2]), (sm.last[s2] >> 1) & 1);
+      for (int s2 = 0; s2 < DQ_NST; ++s2)
+        if (sm.last[s2] >= 0) tc::mbar_wait(su32(&sm.bar_full[s2]), (sm.last[s2] / DQ_NST) & 1);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ============================ MMA issue ==================================
+  } else if (warp == 1 || warp == 2) {
+    // ============================ MMA issue (one warp per row group) =========
+    const int g2 = warp - 1;                      // this warp's group: blocks t with t % 2 == g2
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, 64, 0, 0);
     constexpr uint32_t id_q = tc::idesc_bf16_f32(128, 128, 0, 1);   // dS K-major, K as an MN-major B
     constexpr uint32_t kStageBytes = sizeof(DqSmem::Stage);
@@ -453,30 +489,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_cons
     const uint64_t dds0 = tc::smem_desc_sw128(su32(sm.ds[0]), 16, 1024);
     bool ok = wait_ab_warp(&sm.bar_q, 0, abf);
     tc::fence_after_sync();
-    auto dq_part = [&](int t) -> bool {      // dQ += dS(t) . K(t)
-      const int st = t & 1;
-      if (!wait_ab_warp(&sm.bar_pready[st], (t >> 1) & 1, abf)) return false;
-      tc::fence_after_sync();
-      const uint64_t da = adv(dds0, st * 16384), dbk = adv(dkm0, st * kStageBytes);
-      if (tc::elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_bf16_ss(tbase + kDQ, adv(da, kk * 32), adv(dbk, kk * 2048), id_q, t > 0 || kk > 0);
-        tc::mma_commit(su32(&sm.bar_pvdone[st]));
-        tc::mma_commit(su32(&sm.bar_free[st]));
-      }
-      __syncwarp();
-      return true;
-    };
-    for (int t = 0; ok && t < n_blocks; ++t) {
-      const int st = t & 1;
-      if (!wait_ab_warp(&sm.bar_full[st], (t >> 1) & 1, abf)) break;
-      if (t >= 2 && !wait_ab_warp(&sm.bar_sfree[st], ((t >> 1) - 1) & 1, abf)) break;
+    // S and dP of block t into its group's TMEM buffers
+    auto issue_s = [&](int t) -> bool {
+      const int st = t % DQ_NST;
+      if (!wait_ab_warp(&sm.bar_full[st], (t / DQ_NST) & 1, abf)) return false;
+      if (t >= 2 && !wait_ab_warp(&sm.bar_sfree[g2], ((t >> 1) - 1) & 1, abf)) return false;
       tc::fence_after_sync();
       const uint32_t so = st * kStageBytes;
       const uint64_t dk = adv(dk0, so), dv = adv(dv0, so);
       if (tc::elect_one()) {
-        const uint32_t tS = tbase + kS + 64 * st, tP = tbase + kDP + 64 * st;
+        const uint32_t tS = tbase + kS + 64 * g2, tP = tbase + kDP + 64 * g2;
         tc::mma_bf16<false>(tS, dq, dk, id_s);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
@@ -485,17 +507,39 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_cons
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
           tc::mma_bf16<true>(tP, adv(dob, (kk >> 2) * 1024 + (kk & 3) * 32), adv(dv, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
-        tc::mma_commit(su32(&sm.bar_sdone[st]));
+        tc::mma_commit(su32(&sm.bar_sdone[g2]));
       }
       __syncwarp();
-      if (t >= 1 && !dq_part(t - 1)) break;
-      if (t == n_blocks - 1 && !dq_part(t)) break;
+      return true;
+    };
+    // dQ_g += dS(t) . K(t)
+    auto dq_part = [&](int t) -> bool {
+      const int st = t % DQ_NST;
+      if (!wait_ab_warp(&sm.bar_pready[g2], (t >> 1) & 1, abf)) return false;
+      tc::fence_after_sync();
+      const uint64_t da = adv(dds0, g2 * 16384), dbk = adv(dkm0, st * kStageBytes);
+      if (tc::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_bf16_ss(tbase + kDQ + 128 * g2, adv(da, kk * 32), adv(dbk, kk * 2048), id_q, t > g2 || kk > 0);
+        tc::mma_commit(su32(&sm.bar_pvdone[g2]));
+        tc::mma_commit(su32(&sm.bar_free[st]));
+      }
+      __syncwarp();
+      return true;
+    };
+    if (ok && g2 < n_blocks) ok = issue_s(g2);
+    for (int t = g2; ok && t < n_blocks; t += 2) {
+      // S(t+2) as soon as block t's S and dP are in registers, then block t's dQ part
+      if (t + 2 < n_blocks && !(ok = issue_s(t + 2))) break;
+      ok = dq_part(t);
     }
-    if (tc::elect_one()) tc::mma_commit(su32(&sm.bar_done));
+    if (tc::elect_one()) tc::mma_commit(su32(&sm.bar_done[g2]));
     __syncwarp();
   } else if (warp >= 4) {
-    // ============================ rows (warps 4-7: one tile row per thread) ==
-    const int r = (warp - 4) * 32 + lane, pq = r >> 3, g = r & 7;
+    // ============================ rows (two groups, one tile row per thread) =
+    const int grp = (warp - 4) >> 2;              // blocks t with t % 2 == grp
+    const int r = (warp & 3) * 32 + lane, pq = r >> 3, g = r & 7;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float sl2 = a.sm_scale * kLog2e;
     const int64_t l = q0 + pq;
@@ -506,58 +550,94 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dq_kernel(const __grid_cons
       lse_l2 = a.lse[ri] * kLog2e;
       delta = a.delta[ri];
     }
-    for (int t = 0; t < n_blocks; ++t) {
-      const int st = t & 1;
+    bool okr = true;
+    for (int t = grp; t < n_blocks; t += 2) {
+      const int st = t % DQ_NST;
       const int64_t j0 = static_cast<int64_t>(kb0 + t) * KB;
-      if (!wait_ab_warp(&sm.bar_zm[st], (t >> 1) & 1, abf)) break;
+      if (!(okr = wait_ab_warp(&sm.bar_zm[st], (t / DQ_NST) & 1, abf))) break;
       const unsigned long long zm = sm.zm[st];
-      if (!wait_ab_warp(&sm.bar_sdone[st], (t >> 1) & 1, abf)) break;
+      if (!(okr = wait_ab_warp(&sm.bar_sdone[grp], (t >> 1) & 1, abf))) break;
       tc::fence_after_sync();
-      uint32_t x[64], y[64];
+      const int64_t rel = l - j0;                   // query position - first key of the block
+      // every column of the block in this row's band and no zeroed key: no per-key tests
+      const bool dense = row_on && zm == 0ull && rel <= W && rel - (KB - 1) >= -W;
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        tc::tmem_ld16(tbase + lane_off + kS + 64 * st + 16 * h, *reinterpret_cast<uint32_t(*)[16]>(&x[16 * h]));
-        tc::tmem_ld16(tbase + lane_off + kDP + 64 * st + 16 * h, *reinterpret_cast<uint32_t(*)[16]>(&y[16 * h]));
+      for (int half = 0; half < 2; ++half) {
+        uint32_t x[32], y[32];
+        tc::tmem_ld16(tbase + lane_off + kS + 64 * grp + 32 * half, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
+        tc::tmem_ld16(tbase + lane_off + kS + 64 * grp + 32 * half + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
+        tc::tmem_ld16(tbase + lane_off + kDP + 64 * grp + 32 * half, *reinterpret_cast<uint32_t(*)[16]>(&y[0]));
+        tc::tmem_ld16(tbase + lane_off + kDP + 64 * grp + 32 * half + 16, *reinterpret_cast<uint32_t(*)[16]>(&y[16]));
+        tc::tmem_wait_ld();
+        if (half == 1) {
+          // both halves of S and dP are in registers: the buffers take block t+2
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(su32(&sm.bar_sfree[grp]));
+        }
+        uint32_t dsv[16];
+        if (dense) {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(x[2 * h]), sl2, -lse_l2));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(x[2 * h + 1]), sl2, -lse_l2));
+            dsv[h] = pack_bf16x2(p0 * (__uint_as_float(y[2 * h]) - delta), p1 * (__uint_as_float(y[2 * h + 1]) - delta));
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            float d2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int s = 32 * half + 2 * h + e;
+              const int64_t dist = rel - s;
+              const bool zero = (zm >> s) & 1ull;
+              const bool live = row_on && dist <= W && -dist <= W;
+              const float sv = zero ? 0.f : __uint_as_float(x[2 * h + e]);
+              const float p = live ? fast_exp2(fmaf(sv, sl2, -lse_l2)) : 0.f;
+              const float dp = zero ? 0.f : __uint_as_float(y[2 * h + e]);
+              // zeroed keys contribute nothing to dQ (k' = 0 there)
+              d2[e] = zero ? 0.f : p * (dp - delta);
+            }
+            dsv[h] = pack_bf16x2(d2[0], d2[1]);
+          }
+        }
+        // dS(t) overwrites dS(t-2) once that block's dQ MMAs completed
+        if (half == 0 && t >= 2 && !(okr = wait_ab_warp(&sm.bar_pvdone[grp], ((t >> 1) - 1) & 1, abf))) break;
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+          *reinterpret_cast<uint4*>(sm.ds[grp] + swz_off(r, 4 * half + p)) =
+              make_uint4(dsv[4 * p], dsv[4 * p + 1], dsv[4 * p + 2], dsv[4 * p + 3]);
       }
-      tc::tmem_wait_ld();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_sfree[st]));
-      uint32_t pw[32], dsv[32];
-      row_grads(x, y, row_on, l - j0, W, zm, sl2, lse_l2, delta, pw, dsv);
-      // zeroed keys contribute nothing to dQ (k' = 0 there)
-#pragma unroll
-      for (int h = 0; h < 32; ++h) {
-        const uint32_t keep = (((zm >> (2 * h)) & 1ull) ? 0u : 0x0000ffffu) | (((zm >> (2 * h + 1)) & 1ull) ? 0u : 0xffff0000u);
-        dsv[h] &= keep;
-      }
-      // dS(t) overwrites dS(t-2) once that block's dQ MMAs completed
-      if (t >= 2 && !wait_ab_warp(&sm.bar_pvdone[st], ((t >> 1) - 1) & 1, abf)) break;
-#pragma unroll
-      for (int p = 0; p < 8; ++p)
-        *reinterpret_cast<uint4*>(sm.ds[st] + swz_off(r, p)) =
-            make_uint4(dsv[4 * p], dsv[4 * p + 1], dsv[4 * p + 2], dsv[4 * p + 3]);
+      if (!okr) break;
       tc::fence_proxy_async();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[st]));
+      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[grp]));
     }
     // ============================ epilogue: dQ (fp32) ========================
-    const bool ok = wait_ab_warp(&sm.bar_done, 0, abf);
+    // dQ = dQ_0 + dQ_1 (a group without blocks never wrote its accumulator);
+    // group grp writes dims [64 grp, 64 grp + 64) of the tile's rows
+    const bool has1 = n_blocks > 1;
+    bool ok = wait_ab_warp(&sm.bar_done[0], 0, abf);
+    if (ok) ok = wait_ab_warp(&sm.bar_done[1], 0, abf);
     tc::fence_after_sync();
     if (ok && !__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abf) != 0)) {
       float* dst = row_on ? a.dq + ((static_cast<int64_t>(b) * a.L + l) * Hq + hk * G + g) * D : nullptr;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 16) {
-        uint32_t v16[16];
-        tc::tmem_ld16(tbase + lane_off + kDQ + c0, v16);
+      for (int c0 = 64 * grp; c0 < 64 * grp + 64; c0 += 16) {
+        uint32_t v0[16], v1[16];
+        tc::tmem_ld16(tbase + lane_off + kDQ + c0, v0);
+        if (has1) tc::tmem_ld16(tbase + lane_off + kDQ + 128 + c0, v1);
         tc::tmem_wait_ld();
         if (dst != nullptr) {
+          float f[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            f[i] = a.sm_scale * (has1 ? __uint_as_float(v0[i]) + __uint_as_float(v1[i]) : __uint_as_float(v0[i]));
 #pragma unroll
           for (int p = 0; p < 4; ++p)
-            reinterpret_cast<float4*>(dst + c0)[p] =
-                make_float4(a.sm_scale * __uint_as_float(v16[4 * p]), a.sm_scale * __uint_as_float(v16[4 * p + 1]),
-                            a.sm_scale * __uint_as_float(v16[4 * p + 2]), a.sm_scale * __uint_as_float(v16[4 * p + 3]));
+            reinterpret_cast<float4*>(dst + c0)[p] = make_float4(f[4 * p], f[4 * p + 1], f[4 * p + 2], f[4 * p + 3]);
         }
       }
     }
@@ -684,7 +764,7 @@ extern "C" int mrsa_local_attention_backward(const void* q, const void* k, const
   MRSA_CHECK_LAUNCH();
   local_dq_kernel<<<dim3(static_cast<unsigned>((seq_len + PT - 1) / PT), static_cast<unsigned>(kv_heads),
                          static_cast<unsigned>(batch)),
-                    NTHREADS, smem_q, s>>>(tm_k, tm_v, tm_q, tm_do, a);
+                    DQ_THREADS, smem_q, s>>>(tm_k, tm_v, tm_q, tm_do, a);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
 }
