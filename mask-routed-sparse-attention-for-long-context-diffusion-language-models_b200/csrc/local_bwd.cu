@@ -12,7 +12,10 @@
 //   dQ_r = scale * sum_j dS[r, j] k'_j,  dK_j = scale * sum_r dS[r, j] q_r,
 //   dV_j = sum_r bf16(P[r, j]) dO_r     (dK_j = dV_j = 0 for zeroed keys)
 // Two kernels, both over 128-row tiles (16 queries x the 8 head rows of a KV
-// group) with S and dP as UMMA M=128 N=64 K=128 into TMEM:
+// group) with S and dP as UMMA M=128 N=64 K=128 into TMEM, each with two row
+// groups on alternate tiles, every group with its own MMA warp and TMEM
+// accumulators (added in a fixed order at the end, so the result does not
+// depend on timing):
 //  * local_dkv_kernel: one CTA per 64-key block and KV head walks the query
 //    tiles of its band; dV^T += dO^T . P and dK^T += Q^T . dS (MN-major
 //    operands) stay in TMEM and are stored once;
@@ -34,7 +37,6 @@ using namespace mrsa;
 namespace {
 
 constexpr int D = kHeadDim, KB = 64, PT = 16, GMAX = 8;
-constexpr int NTHREADS = 256;                // warp 0 loads, warp 1 issues MMAs, warps 4-7 own the tile rows
 
 __device__ int g_local_bwd_error;
 
@@ -87,54 +89,35 @@ __global__ void __launch_bounds__(256) delta_kernel(const __nv_bfloat16* __restr
   if (lane == 0) delta[row] = s - (dlse != nullptr ? dlse[row] : 0.f);
 }
 
-// P and dS of one tile row (64 keys of one block): x = S, y = dP as loaded from
-// TMEM; `rel` = query position - first key position of the block; zm = zeroed keys.
-__device__ __forceinline__ void row_grads(uint32_t (&x)[64], const uint32_t (&y)[64], bool row_on, int64_t rel,
-                                          int window, unsigned long long zm, float sl2, float lse_l2, float delta,
-                                          uint32_t (&pw)[32], uint32_t (&dsv)[32]) {
-#pragma unroll
-  for (int h = 0; h < 32; ++h) {
-    float p2[2], d2[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int s = 2 * h + e;
-      const int64_t dist = rel - s;
-      const bool zero = (zm >> s) & 1ull;
-      const bool live = row_on && dist <= window && -dist <= window;
-      const float sv = zero ? 0.f : __uint_as_float(x[s]);
-      const float p = live ? fast_exp2(fmaf(sv, sl2, -lse_l2)) : 0.f;
-      const float dp = zero ? 0.f : __uint_as_float(y[s]);
-      p2[e] = p;
-      d2[e] = p * (dp - delta);
-    }
-    pw[h] = pack_bf16x2(p2[0], p2[1]);
-    dsv[h] = pack_bf16x2(d2[0], d2[1]);
-  }
-}
-
 // ============================================================ dK / dV
+// One CTA per 64-key block and KV head walks the query tiles of its band.  Two
+// row groups (warps 4-7 and 8-11) take the even and the odd tiles, each with
+// its own MMA warp (1 and 2), Q/dO stage, P/dS buffers and S, dP, dV^T, dK^T
+// accumulators in TMEM, so the two groups' tiles overlap; the epilogue adds
+// the groups' accumulators in a fixed order.
+constexpr int DKV_THREADS = 384;             // warp 0 loads, warps 1-2 issue MMAs, warps 4-11 two row groups
+
 struct __align__(1024) DkvSmem {
   unsigned char kt[16384];                   // the block's K tile (loaded once), [half][64 keys][64 dims]
   unsigned char vt[16384];                   // and V tile
   struct Stage {
     unsigned char qt[PT * 2048];             // 16 queries x [half][8 head rows][64 dims]
     unsigned char ot[PT * 2048];             // their dO rows
-  } st[2];
-  unsigned char wp[16384];                   // bf16(P) [128 rows x 64 keys], 128-byte swizzled rows
-  unsigned char dsb[16384];                  // dS, same layout
-  uint64_t bar_kv, bar_full[2], bar_free[2], bar_sdone[2], bar_sfree[2];
-  uint64_t bar_pready, bar_pvdone, bar_done;
+  } st[2];                                   // group g's tiles use stage g
+  unsigned char wp[2][16384];                // bf16(P) of each group [128 rows x 64 keys], 128-byte swizzled rows
+  unsigned char dsb[2][16384];               // dS, same layout
+  uint64_t bar_kv, bar_full[2], bar_free[2], bar_sdone[2], bar_pready[2], bar_done[2];
   int last[2];
   uint32_t tmem_base;
   int abort_flag;
 };
 static_assert(sizeof(DkvSmem) + 1024 <= 232448, "local dK/dV shared memory over budget");
 
-__global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_constant__ CUtensorMap tm_k,
-                                                                const __grid_constant__ CUtensorMap tm_v,
-                                                                const __grid_constant__ CUtensorMap tm_q,
-                                                                const __grid_constant__ CUtensorMap tm_do,
-                                                                LocalBwdArgs a) {
+__global__ void __launch_bounds__(DKV_THREADS, 1) local_dkv_kernel(const __grid_constant__ CUtensorMap tm_k,
+                                                                   const __grid_constant__ CUtensorMap tm_v,
+                                                                   const __grid_constant__ CUtensorMap tm_q,
+                                                                   const __grid_constant__ CUtensorMap tm_do,
+                                                                   LocalBwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   DkvSmem& sm = *reinterpret_cast<DkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -146,21 +129,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_con
   const int n_tiles = static_cast<int>((q_end - q_start + PT - 1) / PT);
   const int64_t krow0 = static_cast<int64_t>(b) * a.L + j0;
 
-  for (int e = tid; e < 2 * static_cast<int>(sizeof(DkvSmem::Stage)) / 16; e += NTHREADS)
+  // query rows past the band's end stay zero (their P and dS are zero, but a
+  // NaN from stale shared memory would still reach dK through Q^T . dS)
+  for (int e = tid; e < 2 * static_cast<int>(sizeof(DkvSmem::Stage)) / 16; e += DKV_THREADS)
     reinterpret_cast<uint4*>(&sm.st[0])[e] = make_uint4(0u, 0u, 0u, 0u);
-  for (int e = tid; e < 2 * 16384 / 16; e += NTHREADS) reinterpret_cast<uint4*>(sm.wp)[e] = make_uint4(0u, 0u, 0u, 0u);
+  for (int e = tid; e < 4 * 16384 / 16; e += DKV_THREADS) reinterpret_cast<uint4*>(&sm.wp[0][0])[e] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) {
     tc::mbar_init(su32(&sm.bar_kv), 1);
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(su32(&sm.bar_full[s]), 1);
       tc::mbar_init(su32(&sm.bar_free[s]), 1);
       tc::mbar_init(su32(&sm.bar_sdone[s]), 1);
-      tc::mbar_init(su32(&sm.bar_sfree[s]), 4);
+      tc::mbar_init(su32(&sm.bar_pready[s]), 4);
+      tc::mbar_init(su32(&sm.bar_done[s]), 1);
       sm.last[s] = -1;
     }
-    tc::mbar_init(su32(&sm.bar_pready), 4);
-    tc::mbar_init(su32(&sm.bar_pvdone), 1);
-    tc::mbar_init(su32(&sm.bar_done), 1);
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -175,7 +158,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_con
   tc::fence_after_sync();
   const uint32_t tbase = sm.tmem_base;
   int* abf = &sm.abort_flag;
-  constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 320;   // TMEM columns
+  // TMEM columns: S of group g at 64 g, dP at 128 + 64 g, dV^T_g at 256 + 128 g, dK^T_g at 320 + 128 g
+  constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 320;
 
   if (warp == 0) {
     // ============================ loader =====================================
@@ -188,18 +172,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_con
     }
     __syncwarp();
     for (int t = 0; t < n_tiles; ++t) {
-      const int st = t & 1;
+      const int g2 = t & 1;
       const int64_t l0 = q_start + static_cast<int64_t>(t) * PT;
       const int nq = static_cast<int>(q_end - l0 < PT ? q_end - l0 : PT);
-      if (t >= 2 && !wait_ab_warp(&sm.bar_free[st], ((t >> 1) - 1) & 1, abf)) break;
-      if (lane == 0) tc::mbar_arrive_expect_tx(su32(&sm.bar_full[st]), static_cast<uint32_t>(nq) * 4096u);
+      // group g2's stage was last read by the gradient MMAs of tile t-2
+      if (t >= 2 && !wait_ab_warp(&sm.bar_free[g2], ((t >> 1) - 1) & 1, abf)) break;
+      if (lane == 0) tc::mbar_arrive_expect_tx(su32(&sm.bar_full[g2]), static_cast<uint32_t>(nq) * 4096u);
       __syncwarp();
       if (lane < nq) {
         const int qy = static_cast<int>((static_cast<int64_t>(b) * a.L + l0 + lane) * Hq + hk * G);
-        tc::tma_load_3d(su32(sm.st[st].qt + lane * 2048), &tm_q, 0, qy, 0, su32(&sm.bar_full[st]));
-        tc::tma_load_3d(su32(sm.st[st].ot + lane * 2048), &tm_do, 0, qy, 0, su32(&sm.bar_full[st]));
+        tc::tma_load_3d(su32(sm.st[g2].qt + lane * 2048), &tm_q, 0, qy, 0, su32(&sm.bar_full[g2]));
+        tc::tma_load_3d(su32(sm.st[g2].ot + lane * 2048), &tm_do, 0, qy, 0, su32(&sm.bar_full[g2]));
       }
-      if (lane == 0) sm.last[st] = t;
+      if (lane == 0) sm.last[g2] = t;
     }
     __syncwarp();
     if (lane == 0) {
@@ -208,50 +193,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_con
         if (sm.last[s2] >= 0) tc::mbar_wait(su32(&sm.bar_full[s2]), (sm.last[s2] >> 1) & 1);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ============================ MMA issue ==================================
+  } else if (warp == 1 || warp == 2) {
+    // ============================ MMA issue (one warp per row group) =========
+    const int g2 = warp - 1;                      // tiles t with t % 2 == g2
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, 64, 0, 0);
     constexpr uint32_t id_g = tc::idesc_bf16_f32(128, 64, 1, 1);    // MN-major A and B
-    constexpr uint32_t kStageBytes = sizeof(DkvSmem::Stage);
     const uint64_t dk = tc::smem_desc_sw128(su32(sm.kt), 16, 1024);
     const uint64_t dv = tc::smem_desc_sw128(su32(sm.vt), 16, 1024);
-    const uint64_t dqk0 = tc::smem_desc_sw128(su32(sm.st[0].qt), 16, 2048);      // Q rows, K-major
-    const uint64_t dok0 = tc::smem_desc_sw128(su32(sm.st[0].ot), 16, 2048);
-    const uint64_t dqm0 = tc::smem_desc_sw128(su32(sm.st[0].qt), 1024, 2048);    // Q^T, MN-major
-    const uint64_t dom0 = tc::smem_desc_sw128(su32(sm.st[0].ot), 1024, 2048);
+    const uint64_t dq = tc::smem_desc_sw128(su32(sm.st[g2].qt), 16, 2048);      // Q rows, K-major
+    const uint64_t dob = tc::smem_desc_sw128(su32(sm.st[g2].ot), 16, 2048);
+    const uint64_t dqm = tc::smem_desc_sw128(su32(sm.st[g2].qt), 1024, 2048);   // Q^T, MN-major
+    const uint64_t dom = tc::smem_desc_sw128(su32(sm.st[g2].ot), 1024, 2048);
     // [rows x keys] as an MN-major B: N = 64 keys is one swizzle atom wide, so
     // only the 8-row stride (1024 B) matters; both offset fields carry it
-    const uint64_t dwp = tc::smem_desc_sw128(su32(sm.wp), 1024, 1024);
-    const uint64_t dds = tc::smem_desc_sw128(su32(sm.dsb), 1024, 1024);
+    const uint64_t dwp = tc::smem_desc_sw128(su32(sm.wp[g2]), 1024, 1024);
+    const uint64_t dds = tc::smem_desc_sw128(su32(sm.dsb[g2]), 1024, 1024);
+    const uint32_t tS = tbase + kS + 64 * g2, tP = tbase + kDP + 64 * g2;
+    const uint32_t tV = tbase + kDV + 128 * g2, tK = tbase + kDK + 128 * g2;
     bool ok = wait_ab_warp(&sm.bar_kv, 0, abf);
     tc::fence_after_sync();
-    auto grads = [&](int t) -> bool {        // dV^T, dK^T += tile t's contributions
-      if (!wait_ab_warp(&sm.bar_pready, t & 1, abf)) return false;
+    for (int t = g2; ok && t < n_tiles; t += 2) {
+      if (!(ok = wait_ab_warp(&sm.bar_full[g2], (t >> 1) & 1, abf))) break;
       tc::fence_after_sync();
-      const uint32_t so = (t & 1) * kStageBytes;
-      const uint64_t dom = adv(dom0, so), dqm = adv(dqm0, so);
+      // S and dP of tile t (the group's previous P, dS and S reads all precede:
+      // its gradient MMAs were issued before, in order, and its rows read S, dP
+      // before signalling P and dS ready)
       if (tc::elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const bool acc = t > 0 || kk > 0;
-          tc::mma_bf16_ss(tbase + kDV, adv(dom, kk * 4096), adv(dwp, kk * 2048), id_g, acc);
-          tc::mma_bf16_ss(tbase + kDK, adv(dqm, kk * 4096), adv(dds, kk * 2048), id_g, acc);
-        }
-        tc::mma_commit(su32(&sm.bar_pvdone));
-        tc::mma_commit(su32(&sm.bar_free[t & 1]));
-      }
-      __syncwarp();
-      return true;
-    };
-    for (int t = 0; ok && t < n_tiles; ++t) {
-      const int st = t & 1;
-      if (!wait_ab_warp(&sm.bar_full[st], (t >> 1) & 1, abf)) break;
-      if (t >= 2 && !wait_ab_warp(&sm.bar_sfree[st], ((t >> 1) - 1) & 1, abf)) break;
-      tc::fence_after_sync();
-      const uint32_t so = st * kStageBytes;
-      const uint64_t dq = adv(dqk0, so), dob = adv(dok0, so);
-      if (tc::elect_one()) {
-        const uint32_t tS = tbase + kS + 64 * st, tP = tbase + kDP + 64 * st;
         tc::mma_bf16<false>(tS, dq, dk, id_s);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
@@ -260,21 +227,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_con
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
           tc::mma_bf16<true>(tP, adv(dob, (kk >> 2) * 1024 + (kk & 3) * 32), adv(dv, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
-        tc::mma_commit(su32(&sm.bar_sdone[st]));
+        tc::mma_commit(su32(&sm.bar_sdone[g2]));
       }
       __syncwarp();
-      if (t >= 1 && !grads(t - 1)) break;
-      if (t == n_tiles - 1 && !grads(t)) break;
+      // dV^T_g += dO^T . P and dK^T_g += Q^T . dS of tile t
+      if (!(ok = wait_ab_warp(&sm.bar_pready[g2], (t >> 1) & 1, abf))) break;
+      tc::fence_after_sync();
+      if (tc::elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const bool acc = t > g2 || kk > 0;
+          tc::mma_bf16_ss(tV, adv(dom, kk * 4096), adv(dwp, kk * 2048), id_g, acc);
+          tc::mma_bf16_ss(tK, adv(dqm, kk * 4096), adv(dds, kk * 2048), id_g, acc);
+        }
+        tc::mma_commit(su32(&sm.bar_free[g2]));
+      }
+      __syncwarp();
     }
-    if (tc::elect_one()) tc::mma_commit(su32(&sm.bar_done));
+    if (tc::elect_one()) tc::mma_commit(su32(&sm.bar_done[g2]));
     __syncwarp();
   } else if (warp >= 4) {
-    // ============================ rows (warps 4-7: one tile row per thread) ==
-    const int r = (warp - 4) * 32 + lane, pq = r >> 3, g = r & 7;
+    // ============================ rows (two groups, one tile row per thread) =
+    const int grp = (warp - 4) >> 2;              // tiles t with t % 2 == grp
+    const int r = (warp & 3) * 32 + lane, pq = r >> 3, g = r & 7;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float sl2 = a.sm_scale * kLog2e;
-    for (int t = 0; t < n_tiles; ++t) {
-      const int st = t & 1;
+    for (int t = grp; t < n_tiles; t += 2) {
       const int64_t l = q_start + static_cast<int64_t>(t) * PT + pq;
       const bool row_on = l < q_end && g < G;
       float lse_l2 = 0.f, delta = 0.f;
@@ -283,50 +261,88 @@ __global__ void __launch_bounds__(NTHREADS, 1) local_dkv_kernel(const __grid_con
         lse_l2 = a.lse[ri] * kLog2e;
         delta = a.delta[ri];
       }
-      if (!wait_ab_warp(&sm.bar_sdone[st], (t >> 1) & 1, abf)) break;
+      if (!wait_ab_warp(&sm.bar_sdone[grp], (t >> 1) & 1, abf)) break;
       tc::fence_after_sync();
-      uint32_t x[64], y[64];
+      const int64_t rel = l - j0;                   // query position - first key of the block
+      // every key of the block in this row's band and none zeroed: no per-key tests
+      const bool dense = row_on && zm == 0ull && rel <= W && rel - (KB - 1) >= -W;
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        tc::tmem_ld16(tbase + lane_off + kS + 64 * st + 16 * h, *reinterpret_cast<uint32_t(*)[16]>(&x[16 * h]));
-        tc::tmem_ld16(tbase + lane_off + kDP + 64 * st + 16 * h, *reinterpret_cast<uint32_t(*)[16]>(&y[16 * h]));
-      }
-      tc::tmem_wait_ld();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_sfree[st]));
-      uint32_t pw[32], dsv[32];
-      row_grads(x, y, row_on, l - j0, W, zm, sl2, lse_l2, delta, pw, dsv);
-      // P and dS of tile t overwrite tile t-1's once its gradient MMAs completed
-      if (t >= 1 && !wait_ab_warp(&sm.bar_pvdone, (t - 1) & 1, abf)) break;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t x[32], y[32];
+        tc::tmem_ld16(tbase + lane_off + kS + 64 * grp + 32 * half, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
+        tc::tmem_ld16(tbase + lane_off + kS + 64 * grp + 32 * half + 16, *reinterpret_cast<uint32_t(*)[16]>(&x[16]));
+        tc::tmem_ld16(tbase + lane_off + kDP + 64 * grp + 32 * half, *reinterpret_cast<uint32_t(*)[16]>(&y[0]));
+        tc::tmem_ld16(tbase + lane_off + kDP + 64 * grp + 32 * half + 16, *reinterpret_cast<uint32_t(*)[16]>(&y[16]));
+        tc::tmem_wait_ld();
+        uint32_t pw[16], dsv[16];
+        if (dense) {
 #pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        *reinterpret_cast<uint4*>(sm.wp + swz_off(r, p)) = make_uint4(pw[4 * p], pw[4 * p + 1], pw[4 * p + 2], pw[4 * p + 3]);
-        *reinterpret_cast<uint4*>(sm.dsb + swz_off(r, p)) =
-            make_uint4(dsv[4 * p], dsv[4 * p + 1], dsv[4 * p + 2], dsv[4 * p + 3]);
+          for (int h = 0; h < 16; ++h) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(x[2 * h]), sl2, -lse_l2));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(x[2 * h + 1]), sl2, -lse_l2));
+            pw[h] = pack_bf16x2(p0, p1);
+            dsv[h] = pack_bf16x2(p0 * (__uint_as_float(y[2 * h]) - delta), p1 * (__uint_as_float(y[2 * h + 1]) - delta));
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            float p2[2], d2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int s = 32 * half + 2 * h + e;
+              const int64_t dist = rel - s;
+              const bool zero = (zm >> s) & 1ull;
+              const bool live = row_on && dist <= W && -dist <= W;
+              const float sv = zero ? 0.f : __uint_as_float(x[2 * h + e]);
+              const float p = live ? fast_exp2(fmaf(sv, sl2, -lse_l2)) : 0.f;
+              const float dp = zero ? 0.f : __uint_as_float(y[2 * h + e]);
+              p2[e] = p;
+              d2[e] = p * (dp - delta);
+            }
+            pw[h] = pack_bf16x2(p2[0], p2[1]);
+            dsv[h] = pack_bf16x2(d2[0], d2[1]);
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          *reinterpret_cast<uint4*>(sm.wp[grp] + swz_off(r, 4 * half + p)) =
+              make_uint4(pw[4 * p], pw[4 * p + 1], pw[4 * p + 2], pw[4 * p + 3]);
+          *reinterpret_cast<uint4*>(sm.dsb[grp] + swz_off(r, 4 * half + p)) =
+              make_uint4(dsv[4 * p], dsv[4 * p + 1], dsv[4 * p + 2], dsv[4 * p + 3]);
+        }
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready));
+      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[grp]));
     }
     // ============================ epilogue: dK, dV (fp32) ====================
-    const bool ok = wait_ab_warp(&sm.bar_done, 0, abf);
+    // dV = dV_0 + dV_1, dK = dK_0 + dK_1 (a group without tiles never wrote its
+    // accumulators); group grp writes keys [32 grp, 32 grp + 32)
+    const bool has1 = n_tiles > 1;
+    bool ok = wait_ab_warp(&sm.bar_done[0], 0, abf);
+    if (ok) ok = wait_ab_warp(&sm.bar_done[1], 0, abf);
     tc::fence_after_sync();
     if (ok && !__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abf) != 0)) {
       const int d = (warp & 3) * 32 + lane;
 #pragma unroll 1
-      for (int s0 = 0; s0 < KB; s0 += 16) {
-        uint32_t v16[16], k16[16];
-        tc::tmem_ld16(tbase + lane_off + kDV + s0, v16);
-        tc::tmem_ld16(tbase + lane_off + kDK + s0, k16);
+      for (int s0 = 32 * grp; s0 < 32 * grp + 32; s0 += 16) {
+        uint32_t v0[16], k0[16], v1[16], k1[16];
+        tc::tmem_ld16(tbase + lane_off + kDV + s0, v0);
+        tc::tmem_ld16(tbase + lane_off + kDK + s0, k0);
+        if (has1) {
+          tc::tmem_ld16(tbase + lane_off + kDV + 128 + s0, v1);
+          tc::tmem_ld16(tbase + lane_off + kDK + 128 + s0, k1);
+        }
         tc::tmem_wait_ld();
 #pragma unroll
         for (int s = 0; s < 16; ++s) {
           const bool zero = (zm >> (s0 + s)) & 1ull;
           const int64_t o = ((krow0 + s0 + s) * a.Hkv + hk) * D + d;
-          a.dv[o] = zero ? 0.f : __uint_as_float(v16[s]);
-          a.dk[o] = zero ? 0.f : a.sm_scale * __uint_as_float(k16[s]);
+          const float vv = has1 ? __uint_as_float(v0[s]) + __uint_as_float(v1[s]) : __uint_as_float(v0[s]);
+          const float kv = has1 ? __uint_as_float(k0[s]) + __uint_as_float(k1[s]) : __uint_as_float(k0[s]);
+          a.dv[o] = zero ? 0.f : vv;
+          a.dk[o] = zero ? 0.f : a.sm_scale * kv;
         }
       }
     }
@@ -760,7 +776,7 @@ extern "C" int mrsa_local_attention_backward(const void* q, const void* k, const
   }
   local_dkv_kernel<<<dim3(static_cast<unsigned>(seq_len / KB), static_cast<unsigned>(kv_heads),
                           static_cast<unsigned>(batch)),
-                     NTHREADS, smem_kv, s>>>(tm_k, tm_v, tm_q, tm_do, a);
+                     DKV_THREADS, smem_kv, s>>>(tm_k, tm_v, tm_q, tm_do, a);
   MRSA_CHECK_LAUNCH();
   local_dq_kernel<<<dim3(static_cast<unsigned>((seq_len + PT - 1) / PT), static_cast<unsigned>(kv_heads),
                          static_cast<unsigned>(batch)),
