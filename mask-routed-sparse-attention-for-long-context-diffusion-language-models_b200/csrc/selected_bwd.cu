@@ -23,7 +23,9 @@
 //    histogram / scan / place kernels, in query order), 16 pairs (128 rows) per tile:
 //      S, dP [128 x 64] (M=128) -> rows warps: P, di, w*P and dS (bf16)
 //      dV^T [128 x 64] += dO_tile^T . (w P),  dK^T += Q_tile^T . dS   (MN-major operands)
-//    and stores dK, dV (fp32) for its 64 rows: no atomics on the gradients.
+//    with two row groups on alternate tiles, each with its own MMA warp,
+//    stage, buffers and accumulators (added in a fixed order at the end), and
+//    stores dK, dV (fp32) for its 64 rows: no atomics on the gradients.
 // A chunk listed twice by a query shares one softmax in the forward (its
 // weights summed); here the first slot carries the summed weight in the dQ
 // kernel, the dK/dV kernel sums the slots' contributions (linear in w), and
@@ -525,21 +527,23 @@ __global__ void __launch_bounds__(NTHREADS_A, 1) dq_kernel(const __grid_constant
 }
 
 // ============================================================ dK / dV kernel
-constexpr int NTHREADS_B = 256;
+constexpr int NTHREADS_B = 384;              // warp 0 loads, warps 1-2 issue MMAs, warps 4-11 two row groups
 constexpr int PT = 16;                       // (query, slot) pairs per tile: 128 rows
 
+// Two row groups (warps 4-7 and 8-11) take the even and the odd tiles, each
+// with its own MMA warp, stage, w*P / dS buffers and S, dP, dV^T, dK^T in
+// TMEM; the epilogue adds the groups' accumulators in a fixed order.
 struct __align__(1024) SmemB {
   unsigned char kt[16384];                   // this chunk's K tile (loaded once)
   unsigned char vt[16384];                   // and V tile
   struct Stage {
     unsigned char qt[PT * 2048];             // 16 pairs x [half][8 rows][64 dims]
     unsigned char ot[PT * 2048];             // their dO rows
-  } st[2];
-  unsigned char wp[16384];                   // w * P [128 rows x 64 keys] bf16, 128-byte swizzled rows
-  unsigned char dsb[16384];                  // dS, same layout
+  } st[2];                                   // group g's tiles use stage g
+  unsigned char wp[2][16384];                // w * P of each group [128 rows x 64 keys] bf16, 128-byte swizzled rows
+  unsigned char dsb[2][16384];               // dS, same layout
   int pl[2][PT], pslot[2][PT], pn[2];
-  uint64_t bar_kv, bar_full[2], bar_free[2], bar_ring[2], bar_sdone[2], bar_sfree[2];
-  uint64_t bar_pready, bar_pvdone, bar_done;
+  uint64_t bar_kv, bar_full[2], bar_free[2], bar_ring[2], bar_sdone[2], bar_pready[2], bar_done[2];
   int last[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -570,7 +574,7 @@ __global__ void __launch_bounds__(NTHREADS_B, 1) dkv_kernel(const __grid_constan
   }
   for (int e = tid; e < 2 * static_cast<int>(sizeof(SmemB::Stage)) / 16; e += NTHREADS_B)
     reinterpret_cast<uint4*>(&sm.st[0])[e] = make_uint4(0u, 0u, 0u, 0u);
-  for (int e = tid; e < 2 * 16384 / 16; e += NTHREADS_B) reinterpret_cast<uint4*>(sm.wp)[e] = make_uint4(0u, 0u, 0u, 0u);
+  for (int e = tid; e < 4 * 16384 / 16; e += NTHREADS_B) reinterpret_cast<uint4*>(&sm.wp[0][0])[e] = make_uint4(0u, 0u, 0u, 0u);
   if (tid == 0) {
     tc::mbar_init(su32(&sm.bar_kv), 1);
     for (int s = 0; s < 2; ++s) {
@@ -578,12 +582,10 @@ __global__ void __launch_bounds__(NTHREADS_B, 1) dkv_kernel(const __grid_constan
       tc::mbar_init(su32(&sm.bar_free[s]), 1);
       tc::mbar_init(su32(&sm.bar_ring[s]), 1);
       tc::mbar_init(su32(&sm.bar_sdone[s]), 1);
-      tc::mbar_init(su32(&sm.bar_sfree[s]), 4);
+      tc::mbar_init(su32(&sm.bar_pready[s]), 4);
+      tc::mbar_init(su32(&sm.bar_done[s]), 1);
       sm.last[s] = -1;
     }
-    tc::mbar_init(su32(&sm.bar_pready), 4);
-    tc::mbar_init(su32(&sm.bar_pvdone), 1);
-    tc::mbar_init(su32(&sm.bar_done), 1);
     sm.abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -605,7 +607,7 @@ __global__ void __launch_bounds__(NTHREADS_B, 1) dkv_kernel(const __grid_constan
   tc::fence_after_sync();
   const uint32_t tbase = sm.tmem_base;
   int* abf = &sm.abort_flag;
-  // TMEM columns: S 0/64, dP 128/192, dV^T 256, dK^T 320
+  // TMEM columns: S of group g at 64 g, dP at 128 + 64 g, dV^T_g at 256 + 128 g, dK^T_g at 320 + 128 g
   constexpr uint32_t kS = 0, kDP = 128, kDV = 256, kDK = 320;
 
   if (warp == 0) {
@@ -619,30 +621,32 @@ __global__ void __launch_bounds__(NTHREADS_B, 1) dkv_kernel(const __grid_constan
     }
     __syncwarp();
     for (int t = 0; t < n_tiles; ++t) {
-      const int st = t & 1;
+      const int g2 = t & 1;
       const int np = min(PT, n_pairs - t * PT);
-      if (t >= 2 && !wait_ab_warp(&sm.bar_free[st], ((t >> 1) - 1) & 1, abf)) break;
+      // group g2's stage (and its pair list) was last read for tile t-2, whose
+      // gradient MMAs have completed
+      if (t >= 2 && !wait_ab_warp(&sm.bar_free[g2], ((t >> 1) - 1) & 1, abf)) break;
       int l = 0, slot = 0;
       if (lane < np) {
         const int pr = a.pairs[p_off + t * PT + lane];
         l = pr >> 5;
         slot = pr & 31;
-        sm.pl[st][lane] = l;
-        sm.pslot[st][lane] = slot;
+        sm.pl[g2][lane] = l;
+        sm.pslot[g2][lane] = slot;
       }
-      if (lane == 0) sm.pn[st] = np;
+      if (lane == 0) sm.pn[g2] = np;
       __syncwarp();
       if (lane == 0) {
-        tc::mbar_arrive(su32(&sm.bar_ring[st]));
-        tc::mbar_arrive_expect_tx(su32(&sm.bar_full[st]), static_cast<uint32_t>(np) * 4096u);
+        tc::mbar_arrive(su32(&sm.bar_ring[g2]));
+        tc::mbar_arrive_expect_tx(su32(&sm.bar_full[g2]), static_cast<uint32_t>(np) * 4096u);
       }
       __syncwarp();
       if (lane < np) {
         const int qy = static_cast<int>((b * a.Lq + l) * Hq + hk * G);
-        tc::tma_load_3d(su32(sm.st[st].qt + lane * 2048), &tm_q, 0, qy, 0, su32(&sm.bar_full[st]));
-        tc::tma_load_3d(su32(sm.st[st].ot + lane * 2048), &tm_do, 0, qy, 0, su32(&sm.bar_full[st]));
+        tc::tma_load_3d(su32(sm.st[g2].qt + lane * 2048), &tm_q, 0, qy, 0, su32(&sm.bar_full[g2]));
+        tc::tma_load_3d(su32(sm.st[g2].ot + lane * 2048), &tm_do, 0, qy, 0, su32(&sm.bar_full[g2]));
       }
-      if (lane == 0) sm.last[st] = t;
+      if (lane == 0) sm.last[g2] = t;
     }
     __syncwarp();
     if (lane == 0) {
@@ -651,50 +655,31 @@ __global__ void __launch_bounds__(NTHREADS_B, 1) dkv_kernel(const __grid_constan
         if (sm.last[s2] >= 0) tc::mbar_wait(su32(&sm.bar_full[s2]), (sm.last[s2] >> 1) & 1);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ============================ MMA issue ==================================
+  } else if (warp == 1 || warp == 2) {
+    // ============================ MMA issue (one warp per row group) =========
+    const int g2 = warp - 1;                      // tiles t with t % 2 == g2
     constexpr uint32_t id_s = tc::idesc_bf16_f32(128, 64, 0, 0);
     constexpr uint32_t id_g = tc::idesc_bf16_f32(128, 64, 1, 1);    // MN-major A and B
-    constexpr uint32_t kStageBytes = sizeof(SmemB::Stage);
     const uint64_t dk = tc::smem_desc_sw128(su32(sm.kt), 16, 1024);
     const uint64_t dv = tc::smem_desc_sw128(su32(sm.vt), 16, 1024);
-    const uint64_t dqk0 = tc::smem_desc_sw128(su32(sm.st[0].qt), 16, 2048);      // Q rows, K-major
-    const uint64_t dok0 = tc::smem_desc_sw128(su32(sm.st[0].ot), 16, 2048);
-    const uint64_t dqm0 = tc::smem_desc_sw128(su32(sm.st[0].qt), 1024, 2048);    // Q^T, MN-major
-    const uint64_t dom0 = tc::smem_desc_sw128(su32(sm.st[0].ot), 1024, 2048);
+    const uint64_t dq = tc::smem_desc_sw128(su32(sm.st[g2].qt), 16, 2048);      // Q rows, K-major
+    const uint64_t dob = tc::smem_desc_sw128(su32(sm.st[g2].ot), 16, 2048);
+    const uint64_t dqm = tc::smem_desc_sw128(su32(sm.st[g2].qt), 1024, 2048);   // Q^T, MN-major
+    const uint64_t dom = tc::smem_desc_sw128(su32(sm.st[g2].ot), 1024, 2048);
     // [rows x keys], MN-major B: N = 64 keys is one swizzle atom wide, so only
     // the 8-row stride (1024 B) matters; both offset fields carry it
-    const uint64_t dwp = tc::smem_desc_sw128(su32(sm.wp), 1024, 1024);
-    const uint64_t dds = tc::smem_desc_sw128(su32(sm.dsb), 1024, 1024);
+    const uint64_t dwp = tc::smem_desc_sw128(su32(sm.wp[g2]), 1024, 1024);
+    const uint64_t dds = tc::smem_desc_sw128(su32(sm.dsb[g2]), 1024, 1024);
+    const uint32_t tS = tbase + kS + 64 * g2, tP = tbase + kDP + 64 * g2;
+    const uint32_t tV = tbase + kDV + 128 * g2, tK = tbase + kDK + 128 * g2;
     bool ok = wait_ab_warp(&sm.bar_kv, 0, abf);
     tc::fence_after_sync();
-    auto grads = [&](int t) -> bool {        // dV^T, dK^T += tile t's contributions
-      if (!wait_ab_warp(&sm.bar_pready, t & 1, abf)) return false;
+    for (int t = g2; ok && t < n_tiles; t += 2) {
+      if (!(ok = wait_ab_warp(&sm.bar_full[g2], (t >> 1) & 1, abf))) break;
       tc::fence_after_sync();
-      const uint32_t so = (t & 1) * kStageBytes;
-      const uint64_t dom = adv(dom0, so), dqm = adv(dqm0, so);
+      // S and dP of tile t (the group's previous gradient MMAs, issued before,
+      // and its rows' reads of S and dP precede)
       if (elect_one()) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const bool acc = t > 0 || kk > 0;
-          tc::mma_bf16_ss(tbase + kDV, adv(dom, kk * 4096), adv(dwp, kk * 2048), id_g, acc);
-          tc::mma_bf16_ss(tbase + kDK, adv(dqm, kk * 4096), adv(dds, kk * 2048), id_g, acc);
-        }
-        tc::mma_commit(su32(&sm.bar_pvdone));
-        tc::mma_commit(su32(&sm.bar_free[t & 1]));
-      }
-      __syncwarp();
-      return true;
-    };
-    for (int t = 0; ok && t < n_tiles; ++t) {
-      const int st = t & 1;
-      if (!wait_ab_warp(&sm.bar_full[st], (t >> 1) & 1, abf)) break;
-      if (t >= 2 && !wait_ab_warp(&sm.bar_sfree[st], ((t >> 1) - 1) & 1, abf)) break;
-      tc::fence_after_sync();
-      const uint32_t so = st * kStageBytes;
-      const uint64_t dq = adv(dqk0, so), dob = adv(dok0, so);
-      if (elect_one()) {
-        const uint32_t tS = tbase + kS + 64 * st, tP = tbase + kDP + 64 * st;
         tc::mma_bf16<false>(tS, dq, dk, id_s);
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
@@ -703,38 +688,46 @@ __global__ void __launch_bounds__(NTHREADS_B, 1) dkv_kernel(const __grid_constan
 #pragma unroll
         for (int kk = 1; kk < 8; ++kk)
           tc::mma_bf16<true>(tP, adv(dob, (kk >> 2) * 1024 + (kk & 3) * 32), adv(dv, (kk >> 2) * 8192 + (kk & 3) * 32), id_s);
-        tc::mma_commit(su32(&sm.bar_sdone[st]));
+        tc::mma_commit(su32(&sm.bar_sdone[g2]));
       }
       __syncwarp();
-      if (t >= 1 && !grads(t - 1)) break;
-      if (t == n_tiles - 1 && !grads(t)) break;
+      // dV^T_g += dO^T . (w P) and dK^T_g += Q^T . dS of tile t
+      if (!(ok = wait_ab_warp(&sm.bar_pready[g2], (t >> 1) & 1, abf))) break;
+      tc::fence_after_sync();
+      if (elect_one()) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const bool acc = t > g2 || kk > 0;
+          tc::mma_bf16_ss(tV, adv(dom, kk * 4096), adv(dwp, kk * 2048), id_g, acc);
+          tc::mma_bf16_ss(tK, adv(dqm, kk * 4096), adv(dds, kk * 2048), id_g, acc);
+        }
+        tc::mma_commit(su32(&sm.bar_free[g2]));
+      }
+      __syncwarp();
     }
-    if (elect_one()) tc::mma_commit(su32(&sm.bar_done));
+    if (elect_one()) tc::mma_commit(su32(&sm.bar_done[g2]));
     __syncwarp();
   } else if (warp >= 4) {
-    // ============================ rows (warps 4-7: one tile row per thread) ==
-    const int r = (warp - 4) * 32 + lane, pr = r >> 3, g = r & 7;
+    // ============================ rows (two groups, one tile row per thread) =
+    const int grp = (warp - 4) >> 2;              // tiles t with t % 2 == grp
+    const int r = (warp & 3) * 32 + lane, pr = r >> 3, g = r & 7;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float scale = a.sm_scale, sl2 = scale * kLog2e;
-    for (int t = 0; t < n_tiles; ++t) {
-      const int st = t & 1;
-      if (!wait_ab_warp(&sm.bar_ring[st], (t >> 1) & 1, abf)) break;
-      const int np = sm.pn[st];
+    const uint32_t tS = tbase + lane_off + kS + 64 * grp, tP = tbase + lane_off + kDP + 64 * grp;
+    for (int t = grp; t < n_tiles; t += 2) {
+      if (!wait_ab_warp(&sm.bar_ring[grp], (t >> 1) & 1, abf)) break;
+      const int np = sm.pn[grp];
       const bool row_on = pr < np && g < G;
       float w = 0.f;
-      if (row_on) w = bf2f(a.w[((b * a.Lq + sm.pl[st][pr]) * Hq + hk * G + g) * K + sm.pslot[st][pr]]);
-      if (!wait_ab_warp(&sm.bar_sdone[st], (t >> 1) & 1, abf)) break;
+      if (row_on) w = bf2f(a.w[((b * a.Lq + sm.pl[grp][pr]) * Hq + hk * G + g) * K + sm.pslot[grp][pr]]);
+      if (!wait_ab_warp(&sm.bar_sdone[grp], (t >> 1) & 1, abf)) break;
       tc::fence_after_sync();
-      uint32_t x[64], y[64];
+      // P of the chunk's softmax stays in registers; dP is read twice in halves
+      // (for di, then for dS) to keep the register count down
+      uint32_t x[64];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        tc::tmem_ld16(tbase + lane_off + kS + 64 * st + 16 * h, *reinterpret_cast<uint32_t(*)[16]>(&x[16 * h]));
-        tc::tmem_ld16(tbase + lane_off + kDP + 64 * st + 16 * h, *reinterpret_cast<uint32_t(*)[16]>(&y[16 * h]));
-      }
+      for (int h = 0; h < 4; ++h) tc::tmem_ld16(tS + 16 * h, *reinterpret_cast<uint32_t(*)[16]>(&x[16 * h]));
       tc::tmem_wait_ld();
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_sfree[st]));
       float mx = -INFINITY;
 #pragma unroll
       for (int s = 0; s < 64; ++s) {
@@ -752,48 +745,69 @@ __global__ void __launch_bounds__(NTHREADS_B, 1) dkv_kernel(const __grid_constan
       const float inv = sum > 0.f ? 1.f / sum : 0.f;
       float di = 0.f;
 #pragma unroll
-      for (int s = 0; s < 64; ++s) {
-        const float p = __uint_as_float(x[s]) * inv;
-        x[s] = __float_as_uint(p);
-        di = fmaf(p, __uint_as_float(y[s]), di);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t y[32];
+        tc::tmem_ld16(tP + 32 * half, *reinterpret_cast<uint32_t(*)[16]>(&y[0]));
+        tc::tmem_ld16(tP + 32 * half + 16, *reinterpret_cast<uint32_t(*)[16]>(&y[16]));
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int s = 0; s < 32; ++s) {
+          const float p = __uint_as_float(x[32 * half + s]) * inv;
+          x[32 * half + s] = __float_as_uint(p);
+          di = fmaf(p, __uint_as_float(y[s]), di);
+        }
       }
       const float f = row_on ? scale * w : 0.f, wr = row_on ? w : 0.f;
-      uint32_t pw[32], dsv[32];
 #pragma unroll
-      for (int h = 0; h < 32; ++h) {
-        const float p0 = __uint_as_float(x[2 * h]), p1 = __uint_as_float(x[2 * h + 1]);
-        pw[h] = pack_bf16x2(wr * p0, wr * p1);
-        dsv[h] = pack_bf16x2(f * p0 * (__uint_as_float(y[2 * h]) - di), f * p1 * (__uint_as_float(y[2 * h + 1]) - di));
-      }
-      // w*P and dS of tile t overwrite tile t-1's once its gradient MMAs completed
-      if (t >= 1 && !wait_ab_warp(&sm.bar_pvdone, (t - 1) & 1, abf)) break;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t y[32];
+        tc::tmem_ld16(tP + 32 * half, *reinterpret_cast<uint32_t(*)[16]>(&y[0]));
+        tc::tmem_ld16(tP + 32 * half + 16, *reinterpret_cast<uint32_t(*)[16]>(&y[16]));
+        tc::tmem_wait_ld();
+        uint32_t pw[16], dsv[16];
 #pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        *reinterpret_cast<uint4*>(sm.wp + swz_off(r, p)) = make_uint4(pw[4 * p], pw[4 * p + 1], pw[4 * p + 2], pw[4 * p + 3]);
-        *reinterpret_cast<uint4*>(sm.dsb + swz_off(r, p)) =
-            make_uint4(dsv[4 * p], dsv[4 * p + 1], dsv[4 * p + 2], dsv[4 * p + 3]);
+        for (int h = 0; h < 16; ++h) {
+          const float p0 = __uint_as_float(x[32 * half + 2 * h]), p1 = __uint_as_float(x[32 * half + 2 * h + 1]);
+          pw[h] = pack_bf16x2(wr * p0, wr * p1);
+          dsv[h] = pack_bf16x2(f * p0 * (__uint_as_float(y[2 * h]) - di), f * p1 * (__uint_as_float(y[2 * h + 1]) - di));
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          *reinterpret_cast<uint4*>(sm.wp[grp] + swz_off(r, 4 * half + p)) =
+              make_uint4(pw[4 * p], pw[4 * p + 1], pw[4 * p + 2], pw[4 * p + 3]);
+          *reinterpret_cast<uint4*>(sm.dsb[grp] + swz_off(r, 4 * half + p)) =
+              make_uint4(dsv[4 * p], dsv[4 * p + 1], dsv[4 * p + 2], dsv[4 * p + 3]);
+        }
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready));
+      if (lane == 0) tc::mbar_arrive(su32(&sm.bar_pready[grp]));
     }
     // ============================ epilogue: dK, dV (fp32) ====================
-    const bool ok = wait_ab_warp(&sm.bar_done, 0, abf);
+    // dV = dV_0 + dV_1, dK = dK_0 + dK_1 (a group without tiles never wrote its
+    // accumulators); group grp writes keys [32 grp, 32 grp + 32)
+    const bool has1 = n_tiles > 1;
+    bool ok = wait_ab_warp(&sm.bar_done[0], 0, abf);
+    if (ok) ok = wait_ab_warp(&sm.bar_done[1], 0, abf);
     tc::fence_after_sync();
     if (ok && !__any_sync(0xffffffffu, *reinterpret_cast<volatile int*>(abf) != 0)) {
       const int d = (warp & 3) * 32 + lane;
 #pragma unroll 1
-      for (int s0 = 0; s0 < S; s0 += 16) {
-        uint32_t v16[16], k16[16];
-        tc::tmem_ld16(tbase + lane_off + kDV + s0, v16);
-        tc::tmem_ld16(tbase + lane_off + kDK + s0, k16);
+      for (int s0 = 32 * grp; s0 < 32 * grp + 32; s0 += 16) {
+        uint32_t v0[16], k0[16], v1[16], k1[16];
+        tc::tmem_ld16(tbase + lane_off + kDV + s0, v0);
+        tc::tmem_ld16(tbase + lane_off + kDK + s0, k0);
+        if (has1) {
+          tc::tmem_ld16(tbase + lane_off + kDV + 128 + s0, v1);
+          tc::tmem_ld16(tbase + lane_off + kDK + 128 + s0, k1);
+        }
         tc::tmem_wait_ld();
 #pragma unroll
         for (int s = 0; s < 16; ++s) {
           const int64_t o = ((krow0 + s0 + s) * a.Hkv + hk) * D + d;
-          a.dv[o] = __uint_as_float(v16[s]);
-          a.dk[o] = __uint_as_float(k16[s]);
+          a.dv[o] = has1 ? __uint_as_float(v0[s]) + __uint_as_float(v1[s]) : __uint_as_float(v0[s]);
+          a.dk[o] = has1 ? __uint_as_float(k0[s]) + __uint_as_float(k1[s]) : __uint_as_float(k0[s]);
         }
       }
     }
