@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
       const float2 sl2x2 = make_float2(sl2, sl2), nbx2 = make_float2(nbase, nbase);
       float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       // fp16 P on a tile with no -inf column in this row (zeroed keys hold logit
-      // 0): a third of the exponentials on the FMA pipe, the rest on the
+      // 0): a quarter of the exponentials on the FMA pipe, the rest on the
       // special-function unit.  The choice is the row's own (lanes differ only on
       // the band's edge tiles), so a row's bits do not depend on which rows
       // share its warp.
@@ -483,7 +483,7 @@ __global__ void __launch_bounds__(L_THREADS, 1) local_tc_kernel(
 #pragma unroll
         for (int h = 0; h < LN / 2; ++h) {
           const float2 t2 = ffma2(make_float2(__uint_as_float(x[2 * h]), __uint_as_float(x[2 * h + 1])), sl2x2, nbx2);
-          const float2 e = (h % 3 == 2) ? exp2_poly2(t2) : make_float2(fast_exp2(t2.x), fast_exp2(t2.y));
+          const float2 e = (h % 4 == 3) ? exp2_poly2(t2) : make_float2(fast_exp2(t2.x), fast_exp2(t2.y));
           s2[h & 1] = fadd2(s2[h & 1], e);
           x[2 * h] = __float_as_uint(e.x);
           x[2 * h + 1] = __float_as_uint(e.y);
