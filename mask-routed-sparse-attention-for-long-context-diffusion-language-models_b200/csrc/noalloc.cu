@@ -74,6 +74,8 @@ int scratch_on_current_device(void** out) {
 extern "C" int mrsa_route_layer_forward_noalloc(const mrsa_route_layer_args* a,
                                                 mrsa_stream_t stream) {
   if (a == nullptr) return MRSA_ERR_NULL;
+  // the scratch of the device that holds the inputs, whichever is current on this thread
+  mrsa::DeviceScope device_scope(a->q_pre);
   const size_t need = mrsa_route_layer_workspace_size(a);
   if (need == 0) return MRSA_ERR_SHAPE;
   if (need > MRSA_NOALLOC_SCRATCH_BYTES) return MRSA_ERR_WORKSPACE;   // too large for the scratch
