@@ -529,6 +529,54 @@ def run_ops(args):
         emit("route_weights_backward", f"route-weights backward (affine gate) at L={L}", ms, L, "tokens", "hbm",
              L * HQ * TOPK * (2 + 2 + 4) + L * HKV * TOPK * 4 + L * HQ * 12, "inputs larger than L2", launches=1)
         ops = [o for o in ops if o != "backward"]
+    if "train" in ops:
+        # Not a configs[] workload: one training step of configs[1]'s route layer
+        # (L=16384, top-32) through the drop-ins under autograd -- RoPE, the local
+        # window, Q-Cal (torch, as the reference module computes it), landmark
+        # pool, routing, affine-gate route weights, selected attention and the
+        # fusion, forward and backward -- with a random output cotangent.
+        inp = {n: t.to(dev) for n, t in make_inputs(L, 0).items()}
+        inv, af = mrsa.yarn_inv_freq(D, 1.0e6, 8.0, 2048)
+        freqs = inp["position_ids"].float()[..., None] * inv.to(dev).float()
+        emb = torch.cat((freqs, freqs), dim=-1)
+        cos, sin = emb.cos() * af, emb.sin() * af
+        vd = inp["key_valid"]
+        gout = rnd(1, L, HQ, D)
+        names = ("q_pre", "k_pre", "v", "hidden", "w_in", "w_out")
+        leaves = {n: inp[n].clone().requires_grad_() for n in names}
+        gate_off, gate_sc = torch.tensor(0.3, device=dev), torch.tensor(1.2, device=dev)
+        nc = L // CHUNK
+
+        def train_step():
+            for t_ in leaves.values():
+                t_.grad = None
+            q = mrsa.single_tensor_rope_autograd(leaves["q_pre"], cos, sin)
+            k = mrsa.single_tensor_rope_autograd(leaves["k_pre"], cos, sin)
+            lo, lse = mrsa.bidir_local_attention(q, k, leaves["v"], vd, WLOC, CHUNK, skip_inert_slots=True)
+            t_ = leaves["hidden"] @ leaves["w_in"].t()
+            delta = (t_ @ leaves["w_out"].t()).view(1, L, HQ, D)
+            comb = (mrsa.single_tensor_rope_autograd(q, cos, -sin).float() + delta.float()).bfloat16()
+            cf = comb.float()
+            normed = (cf * torch.rsqrt(cf.pow(2).mean(-1, keepdim=True) + 1e-6)).bfloat16()
+            route_q = mrsa.single_tensor_rope_autograd(normed, cos, sin)
+            mu = route_q[:, CHUNK - 1::CHUNK].reshape(1, nc, HKV, HQ // HKV, D)
+            lmk, ent = mrsa.chunk_attn_pool_gqa(mu, k.view(1, nc, CHUNK, HKV, D), vd.view(1, nc, CHUNK))
+            drop = mrsa.remote_drop_mask(vd, WLOC, CHUNK)
+            idx, sc = mrsa.route_topk_g7(route_q, lmk, lse.view(1, L, HKV, HQ // HKV), ent, drop, TOPK, CHUNK, WLOC)
+            rw, lw = mrsa.route_weights_torch(sc, idx, ent, lse, temperature=1.0, gate_offset=gate_off,
+                                              gate_scale=gate_sc)
+            remote = mrsa.HiLS_block_M_head(q, k, leaves["v"], rw, idx, key_valid=vd)
+            out = mrsa.fuse_hils_outputs(remote, lo, lw)
+            out.backward(gout)
+
+        ms = timed(train_step, max(3, args.steps))
+        f_sel = L * HQ * TOPK * CHUNK * D * 4
+        pairs_loc = sum(min(L - 1, i + WLOC + CHUNK - 1) - max(0, i - WLOC - CHUNK + 1) + 1 for i in range(L))
+        f_loc = HQ * D * 4 * pairs_loc
+        emit("train", f"route-layer training step (forward + backward through the drop-ins under autograd) at "
+             f"L={L}, 28/4 heads, top-32x64 + local-256; work = 3.5 x (selected + local forward FLOPs)",
+             ms, L, "tokens", "tensor", 3.5 * (f_sel + f_loc), "inputs larger than L2", launches=None)
+        ops = [o for o in ops if o != "train"]
     if "dream" in ops:
         # the whole Dream-shaped forward, B=1, L=32768, random weights
         from mrsa_b200.dream_forward import DreamConfig, DreamForward, landmark_inputs, model_parameters
@@ -617,7 +665,7 @@ def main():
                          "(the target of the ncu captures summarised under profiles/)")
     ap.add_argument("--op", default=None,
                     choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "swa", "dream", "coherent",
-                             "backward", "gemm",
+                             "backward", "gemm", "train",
                              "all"],
                     help="time one off-path op (or all) instead of the route layer; one JSON line each")
     args = ap.parse_args()
