@@ -31,8 +31,7 @@ struct QcalSmem {
     } p2;
   } u;
   __nv_bfloat16 t[TM * RANK];   // 8 KB, bf16(h W_in^T)
-  float cs_c[TM][kHeadDim / 2];
-  float cs_s[TM][kHeadDim / 2];
+  float4 cs[TM][kHeadDim / 4 + 1];   // (cos, sin) of dims 2j, 2j+1 of token row r: {c0, s0, c1, s1}; padded row
 };
 
 // offset (elements) of 16-byte piece `p` of row `r` in a 64-column bf16 tile
@@ -65,8 +64,7 @@ __global__ void __launch_bounds__(NT) qcal_kernel(
       c *= factor;
       s *= factor;
     }
-    sm.cs_c[r][j] = c;
-    sm.cs_s[r][j] = s;
+    reinterpret_cast<float2*>(&sm.cs[r][0])[j] = make_float2(c, s);
   }
 
   // ---------------- phase 1: t = h W_in^T -----------------------------------
@@ -159,6 +157,15 @@ __global__ void __launch_bounds__(NT) qcal_kernel(
   };
 
   const int r0 = warp * 16 + g, r1 = r0 + 8;
+  // this thread's RMSNorm weights (dims n*8 + 2 tq + e and +64), held for all heads
+  float nw_lo[8][2], nw_hi[8][2];
+#pragma unroll
+  for (int n = 0; n < 8; ++n)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      nw_lo[n][e] = __ldg(norm_w + n * 8 + tq * 2 + e);
+      nw_hi[n][e] = __ldg(norm_w + n * 8 + tq * 2 + e + 64);
+    }
   load_p2(0, 0);
   for (int head = 0; head < q_heads; ++head) {
     const int st = head & 1;
@@ -196,12 +203,13 @@ __global__ void __launch_bounds__(NT) qcal_kernel(
 #pragma unroll
       for (int n = 0; n < 8; ++n) {     // n-tile n (dims < 64) pairs with n+8
         const int d = n * 8 + tq * 2;
+        const float4 cs4 = sm.cs[r][n * 4 + tq];
         float2 x_lo = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&qs[off128(r, d >> 3) + (d & 7)]));
         float2 x_hi = unpack_bf16x2(
             *reinterpret_cast<const uint32_t*>(&qs[off128(r, (d + 64) >> 3) + (d & 7)]));
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float c = sm.cs_c[r][d + e], s = sm.cs_s[r][d + e];
+          const float c = e ? cs4.z : cs4.x, s = e ? cs4.w : cs4.y;
           const float xl = e ? x_lo.y : x_lo.x, xh = e ? x_hi.y : x_hi.x;
           float dl = round_bf16(acc[n][half * 2 + e]);
           float dh = round_bf16(acc[n + 8][half * 2 + e]);
@@ -231,12 +239,13 @@ __global__ void __launch_bounds__(NT) qcal_kernel(
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         const int d = n * 8 + tq * 2;
+        const float4 cs4 = sm.cs[r][n * 4 + tq];
         float ol[2], oh[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float c = sm.cs_c[r][d + e], s = sm.cs_s[r][d + e];
-          const float nl = round_bf16(__ldg(norm_w + d + e) * (comb[half][n][e] * inv));
-          const float nh = round_bf16(__ldg(norm_w + d + e + 64) * (comb[half][n + 8][e] * inv));
+          const float c = e ? cs4.z : cs4.x, s = e ? cs4.w : cs4.y;
+          const float nl = round_bf16(nw_lo[n][e] * (comb[half][n][e] * inv));
+          const float nh = round_bf16(nw_hi[n][e] * (comb[half][n + 8][e] * inv));
           ol[e] = nl * c - nh * s;                         // apply_rotary_pos_emb
           oh[e] = nh * c + nl * s;
         }
