@@ -26,10 +26,11 @@
 //   table built once, the bias of a tile is fetched two tiles ahead from a
 //   per-lane base pointer, and the readers split each row four ways.
 // route_select_kernel: one warp per (query, KV head) holds that row's keys in
-//   registers, finds the K-th largest with a 32-step radix search over
-//   order-preserving integer keys, emits the indices in ascending chunk order
-//   (ties at the threshold: lowest chunk ids first), then computes the raw
-//   scores of its selection (lane = slot) and the route weights.
+//   registers, finds the K-th largest with a radix search over order-preserving
+//   integer keys (above 256 chunks, over the few keys a per-lane-maximum
+//   filter keeps), emits the indices in ascending chunk order (ties at the
+//   threshold: lowest chunk ids first), then gathers the raw scores of its
+//   selection (lane = slot) and computes the route weights.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -490,13 +491,60 @@ __device__ __forceinline__ void route_weights_row(float r, bool valid, float loc
 }
 
 constexpr int SEL_WARPS = 8;
+constexpr int SEL_CAND = 256;     // filtered candidates one warp keeps (8 per lane)
+
+// Largest threshold t (order-preserving key) with at least keff of the finite
+// keys in u[] >= t; the search may stop early once exactly keff keys are >= t,
+// since those keys are then the top keff and the selection takes all of them.
+// The threshold is one of the finite keys, so the high bits every finite key
+// shares are its bits from the start.  Padding slots hold 0 (below every key).
+template <int N>
+__device__ __forceinline__ uint32_t radix_threshold(const uint32_t (&u)[N], int keff) {
+  const uint32_t neg_inf_ord = f2ord(-INFINITY);
+  uint32_t orv = 0u, andv = 0xffffffffu;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (u[i] > neg_inf_ord) {
+      orv |= u[i];
+      andv &= u[i];
+    }
+  orv = __reduce_or_sync(0xffffffffu, orv);
+  andv = __reduce_and_sync(0xffffffffu, andv);
+  const uint32_t diff = orv ^ andv;
+  if (diff == 0u) return andv;           // every finite key is the same value
+  const int top = 31 - __clz(diff);
+  uint32_t thr = top == 31 ? 0u : (andv & ~((2u << top) - 1u));
+  for (int bit = top; bit >= 0; --bit) {
+    const uint32_t cand = thr | (1u << bit);
+    int cnt = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) cnt += u[i] >= cand;
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (cnt >= keff) {
+      thr = cand;
+      if (cnt == keff) break;
+    }
+  }
+  return thr;
+}
 
 // One warp per (query, KV head): top-K of the row's keys, raw scores, weights.
 // CPL = keys per lane (C <= 32 * CPL), a compile-time bound so the keys stay in
-// registers.
+// registers.  With 16 or more keys per lane the search runs on a filtered
+// candidate list: the smallest of the 32 lanes' maxima, t0, has at least 32
+// keys >= it (each lane's maximum), so when K <= 32 every selected key is >= t0
+// and only those keys (about 125 of 2048 when each key is the maximum of seven
+// Gaussian scores) are compacted into shared memory and searched.  Rows whose filter keeps fewer than K or
+// more than SEL_CAND keys take the full search.  The selection is the same set
+// either way: the K largest finite keys, ties at the threshold broken towards
+// the lowest chunk ids, emitted in ascending chunk order.
 template <int CPL>
-__global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs a) {
+__global__ void __launch_bounds__(SEL_WARPS * 32, 3) route_select_kernel(RouteArgs a) {
+  constexpr bool kFilter = CPL >= 16;
+  constexpr int NCW = kFilter ? SEL_WARPS : 1;
   __shared__ int sel_s[SEL_WARPS][32];
+  __shared__ uint32_t cand_k[NCW][kFilter ? SEL_CAND : 1];
+  __shared__ uint16_t cand_c[NCW][kFilter ? SEL_CAND : 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.y, b = blockIdx.z;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * SEL_WARPS + warp;
@@ -514,66 +562,117 @@ __global__ void __launch_bounds__(SEL_WARPS * 32) route_select_kernel(RouteArgs 
   }
   nf = __reduce_add_sync(0xffffffffu, nf);
   const int keff = nf < K ? nf : K;
-  // radix search for the largest threshold with at least keff keys >= it.
-  // The threshold is one of the finite keys, so the high bits that all finite
-  // keys share are its bits from the start; and the search may stop once
-  // exactly keff keys are >= the threshold so far: those keys are the top
-  // keff, and the selection below takes every one of them (no tie to break).
   uint32_t thr = 0;
-  if (keff > 0) {
-    uint32_t orv = 0u, andv = 0xffffffffu;
+  int csel = -1;
+  bool sorted = false;       // csel already holds the selection in ascending order
+  bool have_thr = false;
+  if (kFilter && keff > 0 && nf > K && K <= 32) {
+    uint32_t m = 0u;
 #pragma unroll
-    for (int i = 0; i < CPL; ++i)
-      if (u[i] > neg_inf_ord) {
-        orv |= u[i];
-        andv &= u[i];
+    for (int i = 0; i < CPL; ++i) m = u[i] > m ? u[i] : m;
+    const uint32_t t0 = __reduce_min_sync(0xffffffffu, m > neg_inf_ord ? m : 0xffffffffu);
+    int cl = 0;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) cl += u[i] >= t0;
+    const int n = __reduce_add_sync(0xffffffffu, cl);
+    if (n >= keff && n <= SEL_CAND) {
+      int off = cl;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, off, d);
+        if (lane >= d) off += v;
       }
-    orv = __reduce_or_sync(0xffffffffu, orv);
-    andv = __reduce_and_sync(0xffffffffu, andv);
-    const uint32_t diff = orv ^ andv;
-    int top = 31;
-    if (diff == 0u) {
-      thr = andv;                        // every finite key is the same value
-      top = -1;
-    } else {
-      top = 31 - __clz(diff);
-      thr = top == 31 ? 0u : (andv & ~((2u << top) - 1u));
-    }
-    for (int bit = top; bit >= 0; --bit) {
-      const uint32_t cand = thr | (1u << bit);
-      int cnt = 0;
+      off -= cl;
 #pragma unroll
-      for (int i = 0; i < CPL; ++i) cnt += u[i] >= cand;
-      cnt = __reduce_add_sync(0xffffffffu, cnt);
-      if (cnt >= keff) {
-        thr = cand;
-        if (cnt == keff) break;
+      for (int i = 0; i < CPL; ++i)
+        if (u[i] >= t0) {
+          cand_k[kFilter ? warp : 0][off] = u[i];
+          cand_c[kFilter ? warp : 0][off] = static_cast<uint16_t>(i * 32 + lane);
+          ++off;
+        }
+      __syncwarp();
+      constexpr int R = SEL_CAND / 32;
+      uint32_t v[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int j = r * 32 + lane;
+        v[r] = j < n ? cand_k[kFilter ? warp : 0][j] : 0u;
+      }
+      thr = radix_threshold<R>(v, keff);
+      // an early stop below t0 (only when exactly keff candidates exist) means t0 itself
+      thr = thr > t0 ? thr : t0;
+      have_thr = true;
+      int ngt = 0, neq = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        ngt += v[r] > thr;
+        neq += v[r] == thr;
+      }
+      ngt = __reduce_add_sync(0xffffffffu, ngt);
+      neq = __reduce_add_sync(0xffffffffu, neq);
+      if (ngt + neq == keff) {
+        // every key at the threshold is taken: gather the picks, sort by chunk id
+        int taken = 0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int j = r * 32 + lane;
+          const bool pick = j < n && v[r] >= thr;
+          const uint32_t pm = __ballot_sync(0xffffffffu, pick);
+          if (pick) sel_s[warp][taken + __popc(pm & ((1u << lane) - 1u))] = cand_c[kFilter ? warp : 0][j];
+          taken += __popc(pm);
+        }
+        __syncwarp();
+        int x = lane < keff ? sel_s[warp][lane] : 0x7fffffff;
+#pragma unroll
+        for (int k2 = 2; k2 <= 32; k2 <<= 1) {
+#pragma unroll
+          for (int j2 = k2 >> 1; j2 > 0; j2 >>= 1) {
+            const int o = __shfl_xor_sync(0xffffffffu, x, j2);
+            const bool up = (lane & k2) == 0, lower = (lane & j2) == 0;
+            x = (lower == up) ? min(x, o) : max(x, o);
+          }
+        }
+        csel = lane < keff ? x : -1;
+        sorted = true;
       }
     }
   }
-  int ngt = 0;
+  if (!sorted) {
+    if (kFilter) {
+      // rare rows (ties at the threshold, or a filter that kept too few or too
+      // many keys): the keys are read again from L1/L2 rather than kept live
+      // in registers across the filtered search
 #pragma unroll
-  for (int i = 0; i < CPL; ++i) ngt += u[i] > thr;
-  ngt = keff > 0 ? __reduce_add_sync(0xffffffffu, ngt) : 0;
-  int need_eq = keff - ngt, taken = 0;
-  // ascending chunk order; ties at the threshold: lowest chunk ids first
+      for (int i = 0; i < CPL; ++i) {
+        const int c = i * 32 + lane;
+        u[i] = c < C ? f2ord(krow[c]) : 0u;
+      }
+    }
+    if (keff > 0 && !have_thr) thr = radix_threshold<CPL>(u, keff);
+    int ngt = 0;
 #pragma unroll
-  for (int i = 0; i < CPL; ++i) {
-    if (keff == 0) break;
-    const int c = i * 32 + lane;
-    const bool in = c < C;
-    const bool gt = in && u[i] > thr;
-    const bool eq = in && u[i] == thr;
-    const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
-    const int eq_before = __popc(eq_mask & ((1u << lane) - 1u));
-    const bool pick = gt || (eq && eq_before < need_eq);
-    need_eq -= __popc(eq_mask) < need_eq ? __popc(eq_mask) : need_eq;
-    const uint32_t pm = __ballot_sync(0xffffffffu, pick);
-    if (pick) sel_s[warp][taken + __popc(pm & ((1u << lane) - 1u))] = c;
-    taken += __popc(pm);
+    for (int i = 0; i < CPL; ++i) ngt += u[i] > thr;
+    ngt = keff > 0 ? __reduce_add_sync(0xffffffffu, ngt) : 0;
+    int need_eq = keff - ngt, taken = 0;
+    // ascending chunk order; ties at the threshold: lowest chunk ids first
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      if (keff == 0) break;
+      const int c = i * 32 + lane;
+      const bool in = c < C;
+      const bool gt = in && u[i] > thr;
+      const bool eq = in && u[i] == thr;
+      const uint32_t eq_mask = __ballot_sync(0xffffffffu, eq);
+      const int eq_before = __popc(eq_mask & ((1u << lane) - 1u));
+      const bool pick = gt || (eq && eq_before < need_eq);
+      need_eq -= __popc(eq_mask) < need_eq ? __popc(eq_mask) : need_eq;
+      const uint32_t pm = __ballot_sync(0xffffffffu, pick);
+      if (pick) sel_s[warp][taken + __popc(pm & ((1u << lane) - 1u))] = c;
+      taken += __popc(pm);
+    }
+    __syncwarp();
+    csel = lane < keff ? sel_s[warp][lane] : -1;
   }
-  __syncwarp();
-  const int csel = lane < keff ? sel_s[warp][lane] : -1;
   if (lane < K) a.indices[(((int64_t)b * a.Lq + row) * a.Hkv + hk) * K + lane] = csel;
   // raw scores of the selection (lane = slot), gathered from the key kernel's
   // full score rows, and the route weights, head by head

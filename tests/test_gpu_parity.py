@@ -114,34 +114,86 @@ def test_route_topk_g7_matches_reference_golden(mrsa, dev):
 
 
 @pytest.mark.parametrize("c", [600, 2000])
-@pytest.mark.parametrize("tiers", [False, True])
+@pytest.mark.parametrize("tiers", [0, 1, 2])
 def test_route_ties_take_lowest_chunk_ids(mrsa, dev, c, tiers):
     """Keys equal at the top-K boundary: the lowest chunk ids win.  Zero
     landmarks make every key a function of its chunk's bias alone, so chunks
-    with equal bias tie exactly (on the GPU and in the oracle); with tiers the
-    boundary falls inside the lowest tier, without them every key ties."""
+    with equal bias tie exactly (on the GPU and in the oracle).  tiers=0: every
+    key ties; 1: the boundary falls inside the lowest of three tiers (hundreds
+    of equal keys, more than the filtered search keeps); 2: 20 chunks above
+    a tier of 40 equal keys that holds the boundary, every other key distinct
+    and lower, so the filtered candidate search finds the threshold and the
+    tie is broken by the chunk-order pass."""
     gen = torch.Generator().manual_seed(c + tiers)
     b, l, hkv, g, d, topk = 1, 96, 2, 7, 128, 32
     q = torch.randn(b, l, hkv * g, d, generator=gen).bfloat16()
     lmk = torch.zeros(b, c, hkv, g, d).bfloat16()
     lse = torch.randn(b, l, hkv, g, generator=gen)
     bias = torch.zeros(b, c, hkv, g)
-    if tiers:
+    if tiers == 1:
         perm = torch.randperm(c, generator=gen)
         bias[:, perm[:5]] = 2.0
         bias[:, perm[5:25]] = 1.0
+    elif tiers == 2:
+        perm = torch.randperm(c, generator=gen)
+        bias[:] = (-1.0 - torch.rand(c, generator=gen))[None, :, None, None]
+        bias[:, perm[:20]] = 2.0
+        bias[:, perm[20:60]] = 1.0
     drop = (torch.rand(b, l, c, generator=gen) < 0.2).int()
     idx, _ = mrsa.route_topk_g7(q.to(dev), lmk.to(dev), lse.to(dev), bias.to(dev), drop.to(dev),
                                 topk, 64, 512, training=False)
     key = orc.route_keys(q, lmk, lse, bias, drop)                      # [b, l, hkv, c]
-    ids = torch.arange(c, dtype=torch.float64)
-    # order by key descending, then chunk id ascending; dropped chunks never
-    order = (key.double() * (4 * c) - ids).argsort(dim=-1, descending=True)
+    # order by key descending, then chunk id ascending (a stable sort keeps
+    # equal keys in chunk order); dropped chunks never
+    order = torch.sort(key, dim=-1, descending=True, stable=True).indices
     top = order[..., :topk]
     top = torch.where(torch.gather(key, -1, top).isfinite(), top, torch.full_like(top, 1 << 30))
     want = top.sort(-1).values
     want = torch.where(want == (1 << 30), torch.full_like(want, -1), want)
     assert torch.equal(idx.cpu(), want)
+
+
+@pytest.mark.parametrize("c,topk,ties", [(300, 32, False), (512, 31, False), (1000, 32, False),
+                                          (2048, 32, False), (2048, 7, False), (1000, 32, True),
+                                          (2048, 32, True)])
+def test_route_selection_exact_on_the_kernels_own_keys(mrsa, dev, c, topk, ties):
+    """The selection kernel against an exact top-K of the keys the key kernel
+    wrote (read back from the workspace): bit-exact indices, ties broken
+    towards the lowest chunk ids, ascending, -1 last.  Covers the 16-, 32- and
+    64-keys-per-lane kernels and, with ``ties``, keys drawn from a few
+    distinct values so that rows also take the paths for ties at the
+    threshold and for filters that keep too many keys."""
+    lib = mrsa._lib
+    gen = torch.Generator().manual_seed(c * 3 + topk + ties)
+    b, l, hkv, g, d = 1, 80, 2, 7, 128
+    q = (torch.randn(b, l, hkv * g, d, generator=gen) * 0.3).bfloat16()
+    if ties:
+        lmk = torch.zeros(b, c, hkv, g, d).bfloat16()
+        bias = torch.randint(0, 40, (b, c, hkv, g), generator=gen).float() * 0.25
+    else:
+        lmk = (torch.randn(b, c, hkv, g, d, generator=gen) * 0.3).bfloat16()
+        bias = torch.randn(b, c, hkv, g, generator=gen) * 0.5
+    lse = torch.randn(b, l, hkv * g, generator=gen)
+    drop = (torch.rand(b, l, c, generator=gen) < 0.2).int()
+    qd, ld, lsed, bd, dd = (t.to(dev).contiguous() for t in (q, lmk, lse, bias, drop))
+    idx = torch.empty(b, l, hkv, topk, device=dev, dtype=torch.int32)
+    sc = torch.empty(b, l, hkv * g, topk, device=dev, dtype=torch.bfloat16)
+    ws_bytes = lib.load().mrsa_route_topk_workspace_size(b, l, c, hkv, g, lib.BF16)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    lib.call("mrsa_route_topk", lib.ptr(qd), lib.ptr(ld), 1, lib.ptr(lsed), lib.ptr(bd), lib.ptr(dd), None,
+             -1, 0, lib.ptr(idx), lib.ptr(sc), lib.BF16, None, None, lib.WEIGHTS_AFFINE, 1.0, 1.0, 0.0,
+             b, l, c, hkv, g, d, topk, lib.ptr(ws), ws.numel(), lib.stream_of(qd))
+    torch.cuda.synchronize(dev)
+    keys = ws[: b * l * hkv * c * 4].view(torch.float32).view(b, l, hkv, c).cpu().double()
+    assert torch.isneginf(keys[drop.bool()[:, :, None, :].expand_as(keys)]).all()
+    # the K largest finite keys, equal keys in ascending chunk id, output ascending
+    flat = keys.reshape(-1, c)
+    want = torch.full((flat.shape[0], topk), -1, dtype=torch.int64)
+    for r in range(flat.shape[0]):
+        fin = torch.nonzero(torch.isfinite(flat[r])).flatten()
+        top = sorted(fin.tolist(), key=lambda ch: (-flat[r, ch].item(), ch))[:topk]
+        want[r, :len(top)] = torch.tensor(sorted(top), dtype=torch.int64)
+    assert torch.equal(idx.cpu().long().reshape(-1, topk), want)
 
 
 def test_ref_softmax_topk_dropin_shared_landmarks(mrsa, dev):
