@@ -292,22 +292,41 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
         uint32_t s[RC];
         if (!(ok = read_tile(j, s, bias))) break;
         float y[RC], mb = -INFINITY;
+        if ((t + 1) * RN <= C) {
+          // whole tile: the same roundings as the scalar form, two columns per
+          // instruction (paired fp32 fma / mul, three-input max)
 #pragma unroll
-        for (int i = 0; i < RC; ++i) {
-          const int c = t * RN + cb + i;
-          const float x = __uint_as_float(s[i]) * scale + bias[i];
-          y[i] = c < C ? x * kLog2e : -INFINITY;
-          mb = fmaxf(mb, y[i]);
+          for (int i = 0; i < RC; i += 2) {
+            const float2 x2 = ffma2(make_float2(__uint_as_float(s[i]), __uint_as_float(s[i + 1])),
+                                    make_float2(scale, scale), make_float2(bias[i], bias[i + 1]));
+            const float2 y2 = fmul2(x2, make_float2(kLog2e, kLog2e));
+            y[i] = y2.x;
+            y[i + 1] = y2.y;
+            mb = fmax3(mb, y2.x, y2.y);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < RC; ++i) {
+            const int c = t * RN + cb + i;
+            const float x = fmaf(__uint_as_float(s[i]), scale, bias[i]);
+            y[i] = c < C ? x * kLog2e : -INFINITY;
+            mb = fmaxf(mb, y[i]);
+          }
         }
         if (mb > m) {
           l = (m == -INFINITY) ? 0.f : l * fast_exp2(m - mb);
           m = mb;
         }
         if (m != -INFINITY) {
-          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+          float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < RC; ++i) s4[i & 3] += fast_exp2(y[i] - m);
-          l += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+          for (int i = 0; i < RC; i += 4) {
+            const float2 d01 = fadd2(make_float2(y[i], y[i + 1]), make_float2(-m, -m));
+            const float2 d23 = fadd2(make_float2(y[i + 2], y[i + 3]), make_float2(-m, -m));
+            s01 = fadd2(s01, make_float2(fast_exp2(d01.x), fast_exp2(d01.y)));
+            s23 = fadd2(s23, make_float2(fast_exp2(d23.x), fast_exp2(d23.y)));
+          }
+          l += (s01.x + s01.y) + (s23.x + s23.y);
         }
       }
       // combine the two column halves held by this warp (lanes t, t+16); the
@@ -359,10 +378,17 @@ __global__ void __launch_bounds__(R_THREADS, 1) route_keys_kernel(
         float bias[RC];
         uint32_t s[RC];
         if (!(ok = read_tile(j, s, bias))) break;
+        // raw = s * scale, key = max(key, (raw + bias) - T_g): two columns per instruction
 #pragma unroll
-        for (int i = 0; i < RC; ++i) s[i] = __float_as_uint(__uint_as_float(s[i]) * scale);
-#pragma unroll
-        for (int i = 0; i < RC; ++i) key[i] = fmaxf(key[i], (__uint_as_float(s[i]) + bias[i]) - Tg);
+        for (int i = 0; i < RC; i += 2) {
+          const float2 raw2 = fmul2(make_float2(__uint_as_float(s[i]), __uint_as_float(s[i + 1])),
+                                    make_float2(scale, scale));
+          s[i] = __float_as_uint(raw2.x);
+          s[i + 1] = __float_as_uint(raw2.y);
+          const float2 k2 = fadd2(fadd2(raw2, make_float2(bias[i], bias[i + 1])), make_float2(-Tg, -Tg));
+          key[i] = fmaxf(key[i], k2.x);
+          key[i + 1] = fmaxf(key[i + 1], k2.y);
+        }
         // the raw scaled scores of every (head, chunk): the selection kernel gathers its slots from here
         if (row_ok) {
           const int c0 = t * RN + cb;
