@@ -596,6 +596,48 @@ def run_ops(args):
              # layer); the final RMSNorm and lm_head
              launches=28 * 8 + 7 * LAUNCHES_PER_STEP + 21 * 3 + 2)
         ops = [o for o in ops if o != "dream"]
+    if "decode" in ops:
+        # The Fast-dLLM cached decode step of one route layer
+        # (dream_dllm_hils/fastdllm_attention.py:70-382) on a cache of configs[1]'s
+        # length: one 32-row decode block in mid-sequence plus the landmark slot
+        # of each chunk it touches; RoPE and cache update of the block, the local
+        # branch at cache positions, Q-Cal, landmark refresh of the touched chunks,
+        # drop-mask rows, routing over all chunks, selected attention with the
+        # local merge.  The step validates its positions on the host as the
+        # reference does, so its time includes those synchronisations.
+        from mrsa_b200.fastdllm import LayerKVCache, cached_route_layer_step
+
+        c = L // CHUNK
+        gh = torch.Generator().manual_seed(5)
+        w_in = (torch.randn(RANK, HIDDEN, generator=gh) * 0.02).bfloat16().to(dev)
+        w_out = (torch.randn(HQ * D, RANK, generator=gh) * 0.02).bfloat16().to(dev)
+        layer = mrsa.RouteLayer(w_in, w_out)
+        cache = LayerKVCache(rnd(1, L, HKV, D, scale=D ** -0.5), rnd(1, L, HKV, D, scale=D ** -0.5),
+                             torch.ones(1, L, dtype=torch.bool, device=dev),
+                             rnd(1, c, HKV, HQ // HKV, D, scale=D ** -0.5),
+                             torch.zeros(1, c, HKV, HQ // HKV, device=dev))
+        blk = torch.arange(L // 2 + 16, L // 2 + 48, device=dev)
+        aff = torch.unique(blk // CHUNK)
+        qp = torch.unique(torch.cat([blk, aff * CHUNK + CHUNK - 1]))
+        m = qp.numel()
+        qpre, kpre = rnd(1, m, HQ, D, scale=D ** -0.5), rnd(1, m, HKV, D, scale=D ** -0.5)
+        vnew, hid = rnd(1, m, HKV, D, scale=D ** -0.5), rnd(1, m, HIDDEN)
+        pos = (qp - qp // CHUNK).view(1, -1)
+
+        def decode():
+            return cached_route_layer_step(layer, qpre, kpre, vnew, hid, pos, qp, blk, aff, cache)
+
+        ms = timed(decode, args.steps)
+        wf = WLOC + CHUNK - 1
+        # compulsory bytes: the selected chunks' K and V, the local window's K and
+        # V, every landmark key (routing scores all chunks), the rows' h, q and output
+        work = (m * HKV * TOPK * CHUNK * D * 2 * 2 + m * HKV * (2 * wf + 1) * D * 2 * 2 + c * HQ * D * 2
+                + m * (HIDDEN + 2 * HQ * D) * 2)
+        emit("decode", f"Fast-dLLM cached route-layer step: {m} rows ({blk.numel()}-row block + "
+             f"{aff.numel()} landmark slot(s)) against a {L}-token cache, 28/4 heads top-32x64 + local-256",
+             ms, m, "rows", "hbm", work, "decode-sized; cache K/V (33 MB) and landmarks stay in L2 across calls",
+             launches=8)
+        ops = [o for o in ops if o != "decode"]
     for op in ops:
         if op == "flex":
             w = 1280
@@ -665,6 +707,7 @@ def main():
                          "(the target of the ncu captures summarised under profiles/)")
     ap.add_argument("--op", default=None,
                     choices=["flex", "cached_local", "token_scores", "dsa", "selected_keep", "swa", "dream", "coherent",
+                             "decode",
                              "backward", "gemm", "train",
                              "all"],
                     help="time one off-path op (or all) instead of the route layer; one JSON line each")

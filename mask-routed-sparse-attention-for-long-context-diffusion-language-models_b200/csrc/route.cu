@@ -700,30 +700,110 @@ __global__ void __launch_bounds__(SEL_WARPS * 32, 3) route_select_kernel(RouteAr
     csel = lane < keff ? sel_s[warp][lane] : -1;
   }
   if (lane < K) a.indices[(((int64_t)b * a.Lq + row) * a.Hkv + hk) * K + lane] = csel;
-  // raw scores of the selection (lane = slot), gathered from the key kernel's
-  // full score rows, and the route weights, head by head
-  for (int g = 0; g < G; ++g) {
-    const int hq = hk * G + g;
-    const int64_t srow = (((int64_t)b * a.Lq + row) * Hq + hq) * C;
-    float raw = -INFINITY;
-    if (csel >= 0)
-      raw = a.scores_f32 ? static_cast<const float*>(a.raw)[srow + csel]
-                         : bf2f(static_cast<const __nv_bfloat16*>(a.raw)[srow + csel]);
-    const int64_t o = (((int64_t)b * a.Lq + row) * Hq + hq) * K + lane;
-    if (lane < K) {
-      if (a.scores_f32) static_cast<float*>(a.scores)[o] = raw;
-      else static_cast<__nv_bfloat16*>(a.scores)[o] = f2bf(raw);
-    }
-    if (a.remote_w != nullptr) {
+  // Raw scores of the selection, gathered from the key kernel's full score
+  // rows, and the route weights of all heads at once: lane (g, sg) = (lane / 4,
+  // lane % 4) takes head g's slots 8*sg .. 8*sg+7, so a head's reductions run
+  // over a group of four lanes (each lane's eight values first, then two
+  // shuffles) instead of a full-warp butterfly per head.  The slot sums are
+  // added in the tree of a 32-lane butterfly with xor 16, 8, 4, 2, 1 (slot s =
+  // 8*sg + k: s^16 and s^8 are the lanes xor 2 and xor 1, s^4, s^2, s^1 are k's
+  // bits), which is the order route_weights_row() uses.
+  __syncwarp();
+  sel_s[warp][lane] = csel;
+  __syncwarp();
+  {
+    const int g = lane >> 2, sg = lane & 3;
+    const bool gon = g < G;
+    const int hq = hk * G + (gon ? g : 0);
+    const int64_t rowhq = ((int64_t)b * a.Lq + row) * Hq + hq;
+    float rr[8];
+    bool live[8], valid[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int slot = 8 * sg + k;
+      live[k] = slot < K;
+      const int c = live[k] ? sel_s[warp][slot] : -1;
+      valid[k] = gon && c >= 0;
+      float raw = -INFINITY, bias = 0.f;
+      if (valid[k]) {
+        raw = a.scores_f32 ? static_cast<const float*>(a.raw)[rowhq * C + c]
+                           : bf2f(static_cast<const __nv_bfloat16*>(a.raw)[rowhq * C + c]);
+        if (a.bias != nullptr) bias = a.bias[((int64_t)b * C + c) * Hq + hq];
+      }
+      if (gon && live[k]) {
+        if (a.scores_f32) static_cast<float*>(a.scores)[rowhq * K + slot] = raw;
+        else static_cast<__nv_bfloat16*>(a.scores)[rowhq * K + slot] = f2bf(raw);
+      }
       // the weights see the scores as the reference stores them (bf16)
       const float sc = a.scores_f32 ? raw : round_bf16(raw);
-      const float bias = (csel >= 0 && a.bias != nullptr) ? a.bias[((int64_t)b * C + csel) * Hq + hq] : 0.f;
-      const float rr = csel >= 0 ? sc + bias : -INFINITY;
-      const float loc = a.local_lse[((int64_t)b * a.Lq + row) * Hq + hq];
-      float wr, wl;
-      route_weights_row(rr, csel >= 0, loc, K, a.weight_mode, a.temperature, a.gate_scale, a.gate_offset, wr, wl);
-      if (lane < K) a.remote_w[o] = f2bf(wr);
-      if (lane == 0) a.local_w[((int64_t)b * a.Lq + row) * Hq + hq] = f2bf(wl);
+      rr[k] = valid[k] ? sc + bias : -INFINITY;
+    }
+    if (a.remote_w != nullptr) {
+      const float local = gon ? a.local_lse[rowhq] : 0.f;
+      const float inv_t = 1.0f / a.temperature;
+      float rt[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) rt[k] = rr[k] * inv_t;     // -inf stays -inf (dead and empty slots)
+      float mx = rt[0];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) mx = fmaxf(mx, rt[k]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      const bool softmax = a.weight_mode == MRSA_WEIGHTS_SOFTMAX;
+      const float lt = softmax ? (local - a.gate_offset) * inv_t : local * inv_t;
+      const float m = softmax ? fmaxf(mx, lt) : mx;
+      float e[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) e[k] = (rt[k] == -INFINITY || m == -INFINITY) ? 0.f : expf(rt[k] - m);
+      float t[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = e[k] + __shfl_xor_sync(0xffffffffu, e[k], 2);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = t[k] + __shfl_xor_sync(0xffffffffu, t[k], 1);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) t[k] = t[k] + t[k + 4];
+      t[0] = t[0] + t[2];
+      t[1] = t[1] + t[3];
+      const float sum = t[0] + t[1];
+      float wr[8], wl;
+      if (softmax) {
+        if (m == -INFINITY) {                // every logit masked -> zeros
+#pragma unroll
+          for (int k = 0; k < 8; ++k) wr[k] = 0.f;
+          wl = 0.f;
+        } else {
+          const float el = (lt == -INFINITY) ? 0.f : expf(lt - m);
+          const float tot = sum + el;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) wr[k] = e[k] / tot;
+          wl = el / tot;
+        }
+      } else if (mx == -INFINITY && lt == -INFINITY) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wr[k] = 0.f;
+        wl = 0.f;
+      } else {
+        // affine gate (live path: fusion_gate_scale exists)
+        float inner[8], remote_lse = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) inner[k] = 0.f;
+        if (mx != -INFINITY) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) inner[k] = e[k] / sum;
+          remote_lse = mx + logf(sum);
+        }
+        const float gate = a.gate_scale * (remote_lse - lt) + a.gate_offset;
+        const float msig = 1.0f / (1.0f + expf(-gate));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wr[k] = inner[k] * msig;
+        wl = 1.0f - msig;
+      }
+      if (gon) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (live[k]) a.remote_w[rowhq * K + 8 * sg + k] = f2bf(wr[k]);
+        if (sg == 0) a.local_w[rowhq] = f2bf(wl);
+      }
     }
   }
 }
