@@ -7,6 +7,8 @@
 // delta are rounded to bf16 like the reference's bf16 linear layers.
 // One CTA owns 64 consecutive tokens; h streams once from HBM, W_in/W_out stay
 // in L2.  Tensor work is mma.sync m16n8k16 (bf16 -> fp32).
+#include <algorithm>
+
 #include "common.cuh"
 
 using namespace mrsa;
@@ -46,7 +48,7 @@ __global__ void __launch_bounds__(NT) qcal_kernel(
     const __nv_bfloat16* __restrict__ w_in, const __nv_bfloat16* __restrict__ w_out,
     const float* __restrict__ norm_w, float eps, float scale, const int64_t* __restrict__ pos_ids,
     const float* __restrict__ inv_freq, float factor, __nv_bfloat16* __restrict__ route_q,
-    int64_t tokens, int hidden, int q_heads) {
+    int64_t tokens, int hidden, int q_heads, int heads_per_cta) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   QcalSmem& sm = *reinterpret_cast<QcalSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -166,10 +168,13 @@ __global__ void __launch_bounds__(NT) qcal_kernel(
       nw_lo[n][e] = __ldg(norm_w + n * 8 + tq * 2 + e);
       nw_hi[n][e] = __ldg(norm_w + n * 8 + tq * 2 + e + 64);
     }
-  load_p2(0, 0);
-  for (int head = 0; head < q_heads; ++head) {
-    const int st = head & 1;
-    if (head + 1 < q_heads) {
+  // this CTA's heads (all of them unless few token tiles split the heads over CTAs)
+  const int h_begin = static_cast<int>(blockIdx.y) * heads_per_cta;
+  const int h_end = min(q_heads, h_begin + heads_per_cta);
+  load_p2(0, h_begin);
+  for (int head = h_begin; head < h_end; ++head) {
+    const int st = (head - h_begin) & 1;
+    if (head + 1 < h_end) {
       load_p2(st ^ 1, head + 1);
       cp_async_wait<1>();
     } else {
@@ -288,16 +293,27 @@ extern "C" int mrsa_qcal_route_query(const void* hidden, const void* q, const vo
   if (tokens == 0) return MRSA_OK;
   const int64_t blocks = (tokens + TM - 1) / TM;
   if (blocks > 0x7fffffffLL) return MRSA_ERR_SHAPE;
+  // With fewer token tiles than SMs (decode-sized calls) the heads are split
+  // over CTAs, each recomputing its tile's h W_in^T (L2-resident), so the
+  // per-head epilogues run side by side instead of in one CTA's loop; every
+  // head's result is computed exactly as in the one-CTA loop.
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int groups = 1;
+  if (blocks < sms) groups = static_cast<int>(std::min<int64_t>(q_heads, (sms + blocks - 1) / blocks));
+  const int heads_per_cta = static_cast<int>((q_heads + groups - 1) / groups);
+  groups = static_cast<int>((q_heads + heads_per_cta - 1) / heads_per_cta);
   const size_t smem = sizeof(QcalSmem);
   if (cudaFuncSetAttribute(qcal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return MRSA_ERR_LAUNCH;
-  qcal_kernel<<<static_cast<unsigned>(blocks), NT, smem, static_cast<cudaStream_t>(stream)>>>(
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(groups));
+  qcal_kernel<<<grid, NT, smem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(q),
       static_cast<const __nv_bfloat16*>(w_in), static_cast<const __nv_bfloat16*>(w_out),
       norm_weight, eps, scale, position_ids, inv_freq, attention_factor,
       static_cast<__nv_bfloat16*>(route_q), tokens, static_cast<int>(hidden_size),
-      static_cast<int>(q_heads));
+      static_cast<int>(q_heads), heads_per_cta);
   MRSA_CHECK_LAUNCH();
   return MRSA_OK;
 }

@@ -32,7 +32,7 @@ import torch
 
 from . import _lib
 from .layer import RouteLayer
-from .local_attention import cached_local_attention
+from .local_attention import positions_window_attention
 from .rope_fp32 import yarn_inv_freq, yarn_rope_qk
 from .routing import _route
 from .selected_attention import selected_attention
@@ -110,46 +110,89 @@ class CachedAttentionStats:
     routing_calls: int
 
 
-def _positions(p, name, upper, device):
+class _Checks:
+    """The validation of a cached step, read back from the GPU once.
+
+    The reference checks its position tensors one condition at a time, each
+    with a host read (``fastdllm_attention.py:34-65``, ``fastdllm_cache.py:100-127``):
+    about ten synchronisations per layer step.  Here each condition that needs
+    the tensors' values is a 0-dim bool on the device, the conditions known on
+    the host are plain bools, and ``settle()`` reads every pending device
+    condition in one transfer and raises the first failure in the order the
+    reference checks them: same exception, same message."""
+
+    def __init__(self):
+        self.items = []
+
+    def dev(self, ok: torch.Tensor, msg: str, exc=ValueError) -> None:
+        self.items.append((ok, msg, exc))
+
+    def host(self, ok: bool, msg: str, exc=ValueError) -> None:
+        """A host-side condition; a failure settles at once (later conditions
+        may not even be computable), after any earlier pending failure."""
+        self.items.append((bool(ok), msg, exc))
+        if not ok:
+            self.settle()
+
+    def settle(self) -> None:
+        pending = [ok for ok, _, _ in self.items if torch.is_tensor(ok)]
+        values = iter(torch.stack(pending).cpu().tolist()) if pending else iter(())
+        items, self.items = self.items, []
+        for ok, msg, exc in items:
+            if not (next(values) if torch.is_tensor(ok) else ok):
+                raise exc(msg)
+
+
+def _positions(p, name, upper, device, ck: _Checks):
     # mirrors fastdllm_attention.py:34-49
     p = p.to(device=device, dtype=torch.long)
-    if p.ndim != 1:
-        raise ValueError(f"{name} must be one-dimensional")
-    if torch.unique(p).numel() != p.numel():
-        raise ValueError(f"{name} must be unique")
-    if p.numel() and bool(((p < 0) | (p >= upper)).any()):
-        raise ValueError(f"{name} must be in range")
+    ck.host(p.ndim == 1, f"{name} must be one-dimensional")
+    srt = torch.sort(p).values
+    ck.dev(~(srt[1:] == srt[:-1]).any(), f"{name} must be unique")
+    ck.dev(~((p < 0) | (p >= upper)).any(), f"{name} must be in range")
     return p
 
 
-def _rows_for(query_positions, owned):
+def _rows_for(query_positions, owned, ck: _Checks):
     # mirrors fastdllm_attention.py:52-65
     if owned.numel() == 0:
         return owned
+    n = query_positions.numel()
+    if n == 0:
+        ck.host(False, "all owned positions must also be query positions")
     rows = torch.searchsorted(query_positions, owned)
-    if bool((rows >= query_positions.numel()).any()) or \
-            not torch.equal(query_positions.index_select(0, rows), owned):
-        raise ValueError("all owned positions must also be query positions")
-    return rows
+    safe = rows.clamp(max=max(n - 1, 0))
+    ck.dev(~(rows >= n).any() & (query_positions.index_select(0, safe) == owned).all(),
+           "all owned positions must also be query positions")
+    return safe
 
 
 def _prepare(q_pre, k_pre, v, position_ids, query_positions, kv_update_positions, cache, inv_freq, af):
-    if q_pre.ndim != 4 or q_pre.shape[0] != 1:
-        raise ValueError("cached attention requires partial queries [1,M,Hq,D]")
+    ck = _Checks()
+    ck.host(q_pre.ndim == 4 and q_pre.shape[0] == 1, "cached attention requires partial queries [1,M,Hq,D]")
     m = q_pre.shape[1]
     dev = q_pre.device
-    qp = _positions(query_positions, "query_positions", cache.physical_length, dev)
-    if qp.numel() != m:
-        raise ValueError("query position count must match partial hidden length")
-    if m > 1 and bool((qp[1:] <= qp[:-1]).any()):
-        raise ValueError("query_positions must be sorted")
-    up = _positions(kv_update_positions, "kv_update_positions", cache.physical_length, dev)
-    rows = _rows_for(qp, up)
-    if position_ids.shape != (1, m):
-        raise ValueError(f"position_ids must have shape {(1, m)}")
+    qp = _positions(query_positions, "query_positions", cache.physical_length, dev, ck)
+    ck.host(qp.numel() == m, "query position count must match partial hidden length")
+    if m > 1:
+        ck.dev(~(qp[1:] <= qp[:-1]).any(), "query_positions must be sorted")
+    up = _positions(kv_update_positions, "kv_update_positions", cache.physical_length, dev, ck)
+    rows = _rows_for(qp, up, ck)
+    ck.host(position_ids.shape == (1, m), f"position_ids must have shape {(1, m)}")
+    ck.settle()
     pos = position_ids.to(device=dev, dtype=torch.long).contiguous()
     q, k = yarn_rope_qk(q_pre.contiguous(), k_pre.contiguous(), pos, inv_freq, af)
-    cache.replace(up, k.index_select(1, rows), v.to(cache.value.dtype).index_select(1, rows))
+    kr, vr = k.index_select(1, rows), v.to(cache.value.dtype).index_select(1, rows)
+    # LayerKVCache.replace's remaining checks (fastdllm_cache.py:100-127); its
+    # unique / in-range conditions are the kv_update_positions ones above
+    expected = (cache.key.shape[0], up.numel(), cache.key.shape[2], cache.key.shape[3])
+    if kr.shape != expected or vr.shape != expected:
+        raise ValueError(f"replacement K/V shape must be {expected}, got "
+                         f"{tuple(kr.shape)} and {tuple(vr.shape)}")
+    if kr.dtype != cache.key.dtype or vr.dtype != cache.value.dtype:
+        raise ValueError("replacement K/V dtype must match the cache")
+    cache.key.index_copy_(1, up, kr)
+    cache.value.index_copy_(1, up, vr)
     return q, qp, up, pos
 
 
@@ -178,11 +221,17 @@ def cached_route_layer_step(layer: RouteLayer, q_pre, k_pre, v, hidden, position
     g = hq // hkv
     chunk = c.chunk
     n_chunks = cache.physical_length // chunk
-    aff = _positions(affected_chunks, "affected_chunks", n_chunks, dev)
+    ck = _Checks()
+    aff = _positions(affected_chunks, "affected_chunks", n_chunks, dev, ck)
+    lrows = _rows_for(qp, aff * chunk + (chunk - 1), ck) if aff.numel() else aff
+    ck.settle()
     kv = cache.key_valid.contiguous()
     # local branch at the rows' cache positions (fastdllm_attention.py:214-224)
-    local_o, local_lse = cached_local_attention(q, cache.key, cache.value, kv, qp, c.local_window, chunk,
-                                                skip_inert_slots=True)
+    # (the rows' positions were checked above: unique and inside the cache)
+    if c.local_window < 0 or chunk <= 0 or cache.physical_length % chunk:
+        raise ValueError(f"invalid window/chunk layout: L={cache.physical_length}, W={c.local_window}, S={chunk}")
+    local_o, local_lse = positions_window_attention(q, cache.key, cache.value, kv, qp, c.local_window, chunk,
+                                                    skip_inert_slots=True)
     # Q-Cal of the partial rows (:252)
     route_q = torch.empty_like(q)
     h = hidden.to(torch.bfloat16).contiguous()
@@ -192,7 +241,6 @@ def cached_route_layer_step(layer: RouteLayer, q_pre, k_pre, v, hidden, position
               layer.w_in.shape[0], hq, d, _lib.stream_of(q))
     # landmark refresh of the affected chunks (:254-312)
     if aff.numel():
-        lrows = _rows_for(qp, aff * chunk + (chunk - 1))
         mu = route_q.index_select(1, lrows).contiguous()                       # [1, A, Hq, D]
         span = (aff[:, None] * chunk + torch.arange(chunk, device=dev)[None]).reshape(-1)
         keys = cache.key.index_select(1, span).contiguous()                  # [1, A*chunk, Hkv, D]
@@ -237,7 +285,9 @@ def cached_swa_layer_step(q_pre, k_pre, v, position_ids, query_positions, kv_upd
         inv_freq, attention_factor = inv.to(dev), af
     q, qp, up, _ = _prepare(q_pre, k_pre, v, position_ids, query_positions, kv_update_positions, cache,
                             inv_freq, attention_factor)
-    out, _ = cached_local_attention(q, cache.key, cache.value, cache.key_valid.contiguous(), qp, window, chunk,
-                                    skip_inert_slots=False)
+    if window < 0 or chunk <= 0 or cache.physical_length % chunk:
+        raise ValueError(f"invalid window/chunk layout: L={cache.physical_length}, W={window}, S={chunk}")
+    out, _ = positions_window_attention(q, cache.key, cache.value, cache.key_valid.contiguous(), qp, window, chunk,
+                                        skip_inert_slots=False)
     return out, CachedAttentionStats(updated_positions=up.clone(), refreshed_chunks=up.new_empty(0),
                                      routing_calls=0)

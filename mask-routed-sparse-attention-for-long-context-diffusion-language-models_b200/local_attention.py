@@ -172,6 +172,18 @@ def cached_local_attention(q, k, v, key_valid, query_positions, window: int, chu
         raise ValueError("query_positions must be in cache range")
     if window < 0 or chunk_size <= 0 or seq_len % chunk_size:
         raise ValueError(f"invalid window/chunk layout: L={seq_len}, W={window}, S={chunk_size}")
+    return positions_window_attention(q, k, v, key_valid, query_positions, window, chunk_size, skip_inert_slots)
+
+
+def positions_window_attention(q, k, v, key_valid, query_positions, window: int, chunk_size: int,
+                               skip_inert_slots: bool):
+    """The launch behind :func:`cached_local_attention`, for callers that have
+    already checked the query positions (unique, inside the cache) and the
+    window layout; it reads nothing back from the GPU."""
+    batch, query_len, h_q, dim = q.shape
+    seq_len = k.shape[1]
+    if query_len == 0:
+        return q.new_empty((batch, 0, h_q, dim)), q.new_empty((batch, 0, h_q), dtype=torch.float32)
     eff = window + chunk_size - 1 if skip_inert_slots else window
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     kv = key_valid.to(device=q.device, dtype=torch.bool).contiguous()

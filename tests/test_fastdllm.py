@@ -160,3 +160,46 @@ def test_layer_kv_cache_validates_like_the_reference(mrsa):
         c.replace(torch.tensor([3, 3]), k[:, :2], k[:, :2])           # positions must be unique
     c.replace(torch.tensor([5, 9]), torch.ones(1, 2, 4, 128, dtype=torch.bfloat16), k[:, :2])
     assert c.key[0, 5].float().sum() == 512 and c.key[0, 9].float().sum() == 512 and c.key[0, 6].float().sum() == 0
+
+
+@pytest.mark.parametrize("case,msg", [
+    ("dup_query", "query_positions must be unique"),
+    ("range_query", "query_positions must be in range"),
+    ("count", "query position count must match partial hidden length"),
+    ("unsorted", "query_positions must be sorted"),
+    ("dup_update", "kv_update_positions must be unique"),
+    ("not_owned", "all owned positions must also be query positions"),
+    ("pos_shape", "position_ids must have shape (1, 4)"),
+    ("first_wins", "query_positions must be unique"),
+])
+def test_cached_step_position_checks_raise_like_the_reference(mrsa, case, msg):
+    """The cached step's position checks, read back from the device in one
+    transfer, raise the reference's first failing check (same order, same
+    message) before anything is computed or written; CPU tensors suffice."""
+    from mrsa_b200.fastdllm import LayerKVCache, _prepare
+
+    k = torch.zeros(1, 256, 4, 128, dtype=torch.bfloat16)
+    cache = LayerKVCache(k.clone(), k.clone(), torch.ones(1, 256, dtype=torch.bool))
+    q = torch.zeros(1, 4, 28, 128, dtype=torch.bfloat16)
+    kv = torch.zeros(1, 4, 4, 128, dtype=torch.bfloat16)
+    qp, up, pos = torch.tensor([3, 9, 63, 100]), torch.tensor([3, 9]), torch.zeros(1, 4, dtype=torch.long)
+    if case == "dup_query":
+        qp = torch.tensor([3, 9, 9, 100])
+    elif case == "range_query":
+        qp = torch.tensor([3, 9, 63, 256])
+    elif case == "count":
+        qp = torch.tensor([3, 9, 63])
+    elif case == "unsorted":
+        qp = torch.tensor([9, 3, 63, 100])
+    elif case == "dup_update":
+        up = torch.tensor([3, 3])
+    elif case == "not_owned":
+        up = torch.tensor([3, 10])
+    elif case == "pos_shape":
+        pos = torch.zeros(4, dtype=torch.long)
+    elif case == "first_wins":                   # also unsorted and a bad position_ids shape
+        qp, pos = torch.tensor([9, 9, 3, 100]), torch.zeros(4, dtype=torch.long)
+    before = cache.key.clone()
+    with pytest.raises(ValueError, match=msg.replace("(", r"\(").replace(")", r"\)")):
+        _prepare(q, kv, kv, pos, qp, up, cache, torch.ones(64), 1.0)
+    assert torch.equal(cache.key, before)
