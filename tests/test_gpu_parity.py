@@ -537,3 +537,37 @@ def test_no_device_side_wait_gave_up(mrsa, dev):
     """every bounded in-kernel wait of the runs above completed"""
     torch.cuda.synchronize()
     assert mrsa._lib.load().mrsa_device_error_flags(1) == 0
+
+
+@pytest.mark.parametrize("rows", [1, 33, 200, 1000])
+def test_qcal_head_split_for_few_tokens_is_bit_equal(mrsa, dev, rows):
+    """Q-Cal with fewer 64-token tiles than SMs splits the heads over CTAs
+    (each recomputing its tile's h W_in^T).  Every token's route query must be
+    the same bits as the same token computed inside a large call, where one
+    CTA walks all heads."""
+    lib = mrsa._lib
+    gen = torch.Generator().manual_seed(rows)
+    l, hq, d, hidden, rank = 16384, 28, 128, 3584, 64
+    h = torch.randn(1, l, hidden, generator=gen).bfloat16().to(dev)
+    q = (torch.randn(1, l, hq, d, generator=gen) / d ** 0.5).bfloat16().to(dev)
+    w_in = (torch.randn(rank, hidden, generator=gen) * 0.02).bfloat16().to(dev)
+    w_out = (torch.randn(hq * d, rank, generator=gen) * 0.02).bfloat16().to(dev)
+    norm = torch.ones(d, device=dev)
+    i = torch.arange(l, device=dev)
+    pos = (i - i // 64).view(1, -1).contiguous()
+    inv, af = mrsa.yarn_inv_freq(d, 1.0e6, 8.0, 2048)
+    inv = inv.to(dev)
+
+    def qcal(hh, qq, pp):
+        out = torch.empty_like(qq)
+        lib.call("mrsa_qcal_route_query", lib.ptr(hh), lib.ptr(qq), lib.ptr(w_in), lib.ptr(w_out), lib.ptr(norm),
+                 1e-6, 1.0, lib.ptr(pp), lib.ptr(inv), float(af), lib.ptr(out), 1, qq.shape[1], hidden, rank, hq, d,
+                 lib.stream_of(qq))
+        return out
+
+    full = qcal(h, q, pos)
+    start = 5000 + rows % 37                  # not on a 64-token tile boundary
+    sl = slice(start, start + rows)
+    part = qcal(h[:, sl].contiguous(), q[:, sl].contiguous(), pos[:, sl].contiguous())
+    torch.cuda.synchronize(dev)
+    assert torch.equal(part, full[:, sl])
